@@ -1,0 +1,170 @@
+/*
+ * C ABI of the B200 FP32 attention library (librocmkernels_attention.so).
+ *
+ * Every entry point below replaces the entry point of the same name in SecondNewtonLaw/ROCmKernels
+ * (HIP, gfx1031) with an sm_100a CUDA implementation. Names, argument order, argument meaning,
+ * validation and return codes are those of the reference, so existing callers (the reference's
+ * Catch2 tests and benchmark cases through the C++ wrappers in ROCmKernels/Kernels/Attention/,
+ * or a ctypes binding) work unchanged.
+ *
+ * Conventions shared by all entry points
+ *   - q, k, v, upstream (dO) and output-in (O) are read at element
+ *     b*strides.batch + h*strides.head + t*strides.token + c, feature stride 1.
+ *   - output (O) is written with the `os` strides. lse ({row max of scaled scores, sum of
+ *     exp(score - max)} per row), delta and the gradients are PACKED:
+ *     lse [batch][heads][queries][2], delta [batch][heads][queries],
+ *     gradient_q [batch][heads][queries][D], gradient_k/v [batch][heads][keys][D].
+ *   - mask is [batch][keys] bytes; nonzero = key visible. Queries are never masked.
+ *   - radius < 0 attends globally; otherwise query i sees key j only when |i - j| <= radius.
+ *   - Scores are q.k / sqrt(D). A fully masked row gives O = 0 and lse = {-inf, 0}.
+ *   - Returns 0 (cudaSuccess / hipSuccess) or an error code: 1 (cudaErrorInvalidValue, the same
+ *     value as hipErrorInvalidValue) for null pointers, non-positive sizes, an invalid radius
+ *     where the reference checks it, or an unknown selector; otherwise the launch error.
+ *   - Calls are asynchronous and ordered on `stream` (NULL = the legacy default stream); the
+ *     library never synchronizes, allocates nothing and keeps no state between calls, so it is
+ *     reentrant across host threads and devices (the caller's current device is used).
+ *   - All pointers are device pointers owned by the caller.
+ *
+ * Deliberate differences from the reference, all on inputs the reference does not handle:
+ * entries whose HIP launcher validated nothing (tiled, tuned) validate like the simple entry
+ * here instead of launching a kernel on null pointers.
+ */
+#ifndef ROCMKERNELS_ATTENTION_H
+#define ROCMKERNELS_ATTENTION_H
+
+#ifndef __cplusplus
+#include <stdbool.h>
+#endif
+
+#if defined(_WIN32)
+#define ROCMKERNELS_C_EXPORT __declspec(dllexport)
+#else
+#define ROCMKERNELS_C_EXPORT __attribute__((visibility("default")))
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element strides of a [batch][head][token] tensor; 3 ints passed by value.
+ * Replaces ROCmKernels::Kernels::Strides (ROCmKernels.Kernels/include/ROCmKernels/Kernels/Strides.hpp:5-9);
+ * the C++ name is an alias of this type. */
+typedef struct RocmKernelsStrides {
+    int batch;
+    int head;
+    int token;
+} RocmKernelsStrides;
+
+/* cudaStream_t (== hipStream_t through the HIP shim) without requiring the CUDA headers. */
+struct CUstream_st;
+typedef struct CUstream_st *RocmKernelsStream;
+
+/* 32-wide forward, "simple" entry. Replaces attention_fp32_forward
+ * (Attention.hpp:9-11; Attention.hip:194-203). Exact FP32 SIMT kernel. */
+ROCMKERNELS_C_EXPORT int attention_fp32_forward(const float *q, const float *k, const float *v, const bool *mask,
+        float *output, float *lse, int batch, int heads, int queries, int keys, int radius, RocmKernelsStrides qs,
+        RocmKernelsStrides ks, RocmKernelsStrides vs, RocmKernelsStrides os, RocmKernelsStream stream);
+
+/* 32-wide forward, tiled entry. Replaces attention_fp32_forward_tiled
+ * (Attention.hpp:12-14; Attention.hip:225-233). */
+ROCMKERNELS_C_EXPORT int attention_fp32_forward_tiled(const float *q, const float *k, const float *v, const bool *mask,
+        float *output, float *lse, int batch, int heads, int queries, int keys, int radius, RocmKernelsStrides qs,
+        RocmKernelsStrides ks, RocmKernelsStrides vs, RocmKernelsStrides os, RocmKernelsStream stream);
+
+/* 32-wide backward: delta = sum(dO * O) per row, then dQ, dK, dV from the saved {max, sum}.
+ * Replaces attention_fp32_backward (Attention.hpp:15-18; Attention.hip:205-223). */
+ROCMKERNELS_C_EXPORT int attention_fp32_backward(const float *q, const float *k, const float *v, const bool *mask,
+        const float *output, const float *lse, const float *upstream, float *gradient_q, float *gradient_k,
+        float *gradient_v, float *delta, int batch, int heads, int queries, int keys, int radius, RocmKernelsStrides qs,
+        RocmKernelsStrides ks, RocmKernelsStrides vs, RocmKernelsStrides os, RocmKernelsStrides us,
+        RocmKernelsStream stream);
+
+/* 32-wide backward, tiled entry. Replaces attention_fp32_backward_tiled
+ * (Attention.hpp:19-22; Attention.hip:235-250). */
+ROCMKERNELS_C_EXPORT int attention_fp32_backward_tiled(const float *q, const float *k, const float *v, const bool *mask,
+        const float *output, const float *lse, const float *upstream, float *gradient_q, float *gradient_k,
+        float *gradient_v, float *delta, int batch, int heads, int queries, int keys, int radius, RocmKernelsStrides qs,
+        RocmKernelsStrides ks, RocmKernelsStrides vs, RocmKernelsStrides os, RocmKernelsStrides us,
+        RocmKernelsStream stream);
+
+/* Softmax statistics only ({max, sum} per row; no V read, no O write); radius < -1 is invalid.
+ * Replaces attention_fp32_statistics (Attention.hpp:23-24; Attention.hip:252-261). */
+ROCMKERNELS_C_EXPORT int attention_fp32_statistics(const float *q, const float *k, const bool *mask, float *lse,
+        int batch, int heads, int queries, int keys, int radius, RocmKernelsStrides qs, RocmKernelsStrides ks,
+        RocmKernelsStream stream);
+
+/* Forward with a tuning selector; group in {2, 4, 8, 84, 164, 1164, 1264}, else error 1.
+ * Replaces attention_fp32_forward_tuned (Attention.hpp:25-27; Attention.hip:358-370). */
+ROCMKERNELS_C_EXPORT int attention_fp32_forward_tuned(const float *q, const float *k, const float *v, const bool *mask,
+        float *output, float *lse, int batch, int heads, int queries, int keys, int radius, int group,
+        RocmKernelsStrides qs, RocmKernelsStrides ks, RocmKernelsStrides vs, RocmKernelsStrides os,
+        RocmKernelsStream stream);
+
+/* Flash forward, the headline entry: tcgen05/TMEM 3xTF32 kernel on sm_100a; radius < -1 is
+ * invalid. Replaces attention_fp32_forward_flash (Attention.hpp:28-30; Attention.hip:372-390). */
+ROCMKERNELS_C_EXPORT int attention_fp32_forward_flash(const float *q, const float *k, const float *v, const bool *mask,
+        float *output, float *lse, int batch, int heads, int queries, int keys, int radius, RocmKernelsStrides qs,
+        RocmKernelsStrides ks, RocmKernelsStrides vs, RocmKernelsStrides os, RocmKernelsStream stream);
+
+/* Flash forward with a variant selector 0..18, else error 1; radius < -1 is invalid.
+ * Replaces attention_fp32_forward_flash_tuned (Attention.hpp:31-33; Attention.hip:392-417). */
+ROCMKERNELS_C_EXPORT int attention_fp32_forward_flash_tuned(const float *q, const float *k, const float *v,
+        const bool *mask, float *output, float *lse, int batch, int heads, int queries, int keys, int radius,
+        int variant, RocmKernelsStrides qs, RocmKernelsStrides ks, RocmKernelsStrides vs, RocmKernelsStrides os,
+        RocmKernelsStream stream);
+
+/* Backward with a tuning selector; group in {2, 4, 8, 84, 164, 1164, 1264}, else error 1.
+ * Groups 1164 and 1264 compute delta as sum_j P_ij * (dO_i . v_j) (no O read), as the
+ * reference's SOFTMAX_DELTA path does. Replaces attention_fp32_backward_tuned
+ * (Attention.hpp:34-37; Attention.hip:419-438). */
+ROCMKERNELS_C_EXPORT int attention_fp32_backward_tuned(const float *q, const float *k, const float *v, const bool *mask,
+        const float *output, const float *lse, const float *upstream, float *gradient_q, float *gradient_k,
+        float *gradient_v, float *delta, int batch, int heads, int queries, int keys, int radius, int group,
+        RocmKernelsStrides qs, RocmKernelsStrides ks, RocmKernelsStrides vs, RocmKernelsStrides os,
+        RocmKernelsStrides us, RocmKernelsStream stream);
+
+/* 64-wide forward. Replaces attention64_fp32_forward (Attention64.hpp:9-11; Attention64.hip:193-202). */
+ROCMKERNELS_C_EXPORT int attention64_fp32_forward(const float *q, const float *k, const float *v, const bool *mask,
+        float *output, float *lse, int batch, int heads, int queries, int keys, int radius, RocmKernelsStrides qs,
+        RocmKernelsStrides ks, RocmKernelsStrides vs, RocmKernelsStrides os, RocmKernelsStream stream);
+
+/* 64-wide backward. Replaces attention64_fp32_backward (Attention64.hpp:12-15; Attention64.hip:204-220). */
+ROCMKERNELS_C_EXPORT int attention64_fp32_backward(const float *q, const float *k, const float *v, const bool *mask,
+        const float *output, const float *lse, const float *upstream, float *gradient_q, float *gradient_k,
+        float *gradient_v, float *delta, int batch, int heads, int queries, int keys, int radius,
+        RocmKernelsStrides qs, RocmKernelsStrides ks, RocmKernelsStrides vs, RocmKernelsStrides os,
+        RocmKernelsStrides us, RocmKernelsStream stream);
+
+/* Backward split into stages (exported but undeclared in the reference's headers):
+ * stage 1 = delta only (softmax-weighted form, no O read), 2 = dQ only (reads delta),
+ * 3 = dK/dV only (reads delta). Requires queries >= 32; radius < -1 invalid.
+ * Replaces attention_fp32_backward_profile (Attention.hip:327-337). */
+ROCMKERNELS_C_EXPORT int attention_fp32_backward_profile(const float *q, const float *k, const float *v,
+        const bool *mask, const float *output, const float *lse, const float *upstream, float *gradient_q,
+        float *gradient_k, float *gradient_v, float *delta, int batch, int heads, int queries, int keys, int radius,
+        int stage, RocmKernelsStrides qs, RocmKernelsStrides ks, RocmKernelsStrides vs, RocmKernelsStrides os,
+        RocmKernelsStrides us, RocmKernelsStream stream);
+
+/* dQ stage only (reads delta) with a tuning selector in {14, 18, 24, 28, 44, 116}, else error 1.
+ * Requires queries >= 32; radius < -1 invalid. Exported but undeclared in the reference's
+ * headers. Replaces attention_fp32_query_profile (Attention.hip:339-356). */
+ROCMKERNELS_C_EXPORT int attention_fp32_query_profile(const float *q, const float *k, const float *v,
+        const bool *mask, const float *output, const float *lse, const float *upstream, float *gradient_q,
+        float *gradient_k, float *gradient_v, float *delta, int batch, int heads, int queries, int keys, int radius,
+        int tuning, RocmKernelsStrides qs, RocmKernelsStrides ks, RocmKernelsStrides vs, RocmKernelsStrides os,
+        RocmKernelsStrides us, RocmKernelsStream stream);
+
+/* Library build identification: a static string naming the architecture the kernels were
+ * compiled for ("sm_100a") and the kernel families present. No counterpart in the reference. */
+ROCMKERNELS_C_EXPORT const char *rocmkernels_attention_build_info(void);
+
+/* Name of the kernel attention_fp32_forward_flash selects for contiguous, 16-byte aligned
+ * tensors of this shape (for benchmarks and profiles). No counterpart in the reference. */
+ROCMKERNELS_C_EXPORT const char *rocmkernels_attention_flash_kernel(int batch, int heads, int queries, int keys,
+        int head_width);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* ROCMKERNELS_ATTENTION_H */

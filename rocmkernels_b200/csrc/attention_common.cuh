@@ -1,0 +1,80 @@
+// Shared device helpers and launch parameters for the FP32 attention kernels (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <atomic>
+
+namespace rk {
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+// A strided [batch][head][token][feature] tensor; feature stride is 1.
+// Element (b, h, t, c) is data[b*sb + h*sh + t*st + c], the addressing of the reference's
+// Input::read (Attention.hip:14-20), evaluated in 64-bit here.
+struct Tensor {
+    const float *data;
+    long long sb, sh, st;
+    __device__ __forceinline__ const float *row(int b, int h, int t) const {
+        return data + (long long)b * sb + (long long)h * sh + (long long)t * st;
+    }
+};
+
+struct OutTensor {
+    float *data;
+    long long sb, sh, st;
+    __device__ __forceinline__ float *row(int b, int h, int t) const {
+        return data + (long long)b * sb + (long long)h * sh + (long long)t * st;
+    }
+};
+
+// Everything a forward or backward launch needs. Packed outputs (lse, delta, gradients) are
+// indexed by the flattened row (b*heads + h)*tokens + t.
+struct AttentionParams {
+    Tensor q, k, v, o_in, dout;
+    OutTensor o;
+    const unsigned char *mask;  // [batch][keys], nonzero = visible
+    float *lse;                 // [batch][heads][queries][2]
+    float *delta;               // [batch][heads][queries]
+    float *dq, *dk, *dv;        // packed [batch][heads][tokens][D]
+    const float *lse_in;        // saved statistics for the backward
+    int batch, heads, queries, keys, radius;
+    float scale;                // 1/sqrt(D)
+    int vec4;                   // all strided tensors are 16-byte addressable (float4 loads)
+};
+
+// 2^x on the MUFU unit (PTX ex2.approx.ftz.f32; relative error about 2^-22).
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// Visibility of key j for query i: the selection rule of the reference
+// (AttentionFlash32.h:87-94; AttentionTests.cpp:54-59).
+__device__ __forceinline__ bool in_window(int query, int key, int radius) {
+    return radius < 0 || abs(query - key) <= radius;
+}
+
+// Key range [first, last) that can be visible from the query block [q0, q1).
+__host__ __device__ __forceinline__ void key_window(int q0, int q1, int keys, int radius, int &first, int &last) {
+    first = radius < 0 ? 0 : max(0, q0 - radius);
+    last = radius < 0 ? keys : min(keys, q1 + radius);
+}
+
+// Configures the dynamic shared memory limit of a kernel once per device.
+template <auto KernelFn>
+inline cudaError_t prepare_kernel(int shared_bytes) {
+    static std::atomic<unsigned long long> configured{0};
+    int device = 0;
+    cudaError_t status = cudaGetDevice(&device);
+    if (status != cudaSuccess) return status;
+    const unsigned long long bit = 1ull << (device & 63);
+    if (configured.load(std::memory_order_acquire) & bit) return cudaSuccess;
+    status = cudaFuncSetAttribute(KernelFn, cudaFuncAttributeMaxDynamicSharedMemorySize, shared_bytes);
+    if (status == cudaSuccess) configured.fetch_or(bit, std::memory_order_acq_rel);
+    return status;
+}
+
+}  // namespace rk

@@ -1,0 +1,19 @@
+// tcgen05 / TMEM tensor-core flash forward (sm_100a). Interface used by the entry points.
+#pragma once
+
+#include "attention_common.cuh"
+
+namespace rk {
+namespace tc {
+
+// True when the tensor-core kernel accepts the problem (head width 32, TMA-addressable tensors).
+bool flash_supported(const AttentionParams &p);
+// Launches the tensor-core flash forward; returns a cudaError_t value.
+int launch_flash_forward(const AttentionParams &p, cudaStream_t stream);
+// Static description of the build (architecture and kernel families).
+const char *build_info();
+// Name of the tensor-core flash kernel (for benchmarks and profiles).
+const char *kernel_name();
+
+}  // namespace tc
+}  // namespace rk

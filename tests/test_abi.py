@@ -1,0 +1,118 @@
+"""The C-ABI library: it loads, exports what the header declares, and rejects bad arguments
+before touching a device (no GPU needed)."""
+from __future__ import annotations
+
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+import rocmkernels_b200
+from rocmkernels_b200 import attention as api
+
+REPO = Path(__file__).resolve().parent.parent
+HEADERS = sorted((REPO / "include").glob("*.h"))
+
+
+def declared_functions():
+    names = []
+    for header in HEADERS:
+        text = header.read_text()
+        names += re.findall(r"ROCMKERNELS_C_EXPORT\s+[\w\s\*]+?\b(\w+)\s*\(", text)
+    return names
+
+
+def test_library_loads_and_reports_sm100a():
+    assert "sm_100a" in rocmkernels_b200.build_info()
+
+
+def test_every_declared_symbol_is_exported():
+    names = declared_functions()
+    assert len(names) >= 14
+    library = rocmkernels_b200.lib()
+    for name in names:
+        assert hasattr(library, name), name
+    exported = subprocess.run(["nm", "-D", "--defined-only", str(api.LIBRARY_PATH)], capture_output=True, text=True,
+                              check=True).stdout
+    for name in names:
+        assert re.search(rf"\bT {name}$", exported, re.M), name
+
+
+def test_reference_entry_points_all_declared():
+    reference_names = {
+        "attention_fp32_forward", "attention_fp32_forward_tiled", "attention_fp32_backward", "attention_fp32_backward_tiled",
+        "attention_fp32_statistics", "attention_fp32_forward_tuned", "attention_fp32_forward_flash",
+        "attention_fp32_forward_flash_tuned", "attention_fp32_backward_tuned", "attention64_fp32_forward",
+        "attention64_fp32_backward", "attention_fp32_backward_profile", "attention_fp32_query_profile",
+    }
+    assert reference_names <= set(declared_functions())
+    assert reference_names == set(api.ENTRY_POINTS)
+
+
+def test_strides_struct_layout():
+    assert ctypes.sizeof(api.Strides) == 12
+
+
+S = api.Strides(0, 0, 0)
+FWD = dict(q=1, k=1, v=1, mask=1, output=1, lse=1)
+
+
+def forward_args(**override):
+    a = dict(FWD, batch=1, heads=1, queries=4, keys=4, radius=-1)
+    a.update(override)
+    return [a["q"], a["k"], a["v"], a["mask"], a["output"], a["lse"], a["batch"], a["heads"], a["queries"], a["keys"], a["radius"]]
+
+
+@pytest.mark.parametrize("entry", ["attention_fp32_forward", "attention_fp32_forward_tiled", "attention_fp32_forward_flash",
+                                   "attention64_fp32_forward"])
+@pytest.mark.parametrize("override", [dict(q=None), dict(k=None), dict(v=None), dict(mask=None), dict(output=None),
+                                      dict(lse=None), dict(batch=0), dict(heads=-1), dict(queries=0), dict(keys=0)])
+def test_forward_rejects_invalid_arguments(entry, override):
+    assert getattr(api, entry)(*forward_args(**override), S, S, S, S) == api.INVALID_VALUE
+
+
+def test_radius_validation_matches_reference():
+    # Flash and statistics reject radius < -1 (Attention.hip:376, :255); simple/tiled/64 do not check it.
+    assert api.attention_fp32_forward_flash(*forward_args(radius=-2), S, S, S, S) == api.INVALID_VALUE
+    assert api.attention_fp32_statistics(1, 1, 1, 1, 1, 1, 4, 4, -2, S, S) == api.INVALID_VALUE
+    assert api.attention_fp32_forward_flash_tuned(*forward_args(radius=-2), 13, S, S, S, S) == api.INVALID_VALUE
+
+
+@pytest.mark.parametrize("variant", [-1, 19, 100])
+def test_flash_variant_out_of_range(variant):
+    assert api.attention_fp32_forward_flash_tuned(*forward_args(), variant, S, S, S, S) == api.INVALID_VALUE
+
+
+@pytest.mark.parametrize("group", [0, 1, 3, 16, 1165])
+def test_unknown_tuning_groups(group):
+    assert api.attention_fp32_forward_tuned(*forward_args(), group, S, S, S, S) == api.INVALID_VALUE
+    bwd = [1] * 11 + [1, 1, 4, 4, -1]
+    assert api.attention_fp32_backward_tuned(*bwd, group, S, S, S, S, S) == api.INVALID_VALUE
+
+
+@pytest.mark.parametrize("entry", ["attention_fp32_backward", "attention_fp32_backward_tiled", "attention64_fp32_backward"])
+@pytest.mark.parametrize("null_index", range(11))
+def test_backward_rejects_null_pointers(entry, null_index):
+    pointers = [1] * 11
+    pointers[null_index] = None
+    assert getattr(api, entry)(*pointers, 1, 1, 4, 4, -1, S, S, S, S, S) == api.INVALID_VALUE
+
+
+def test_profile_entries_validate_like_reference():
+    ok = [1] * 11
+    # stage outside 1..3, queries < 32, radius < -1 (Attention.hip:331-334)
+    assert api.attention_fp32_backward_profile(*ok, 1, 1, 64, 64, -1, 0, S, S, S, S, S) == api.INVALID_VALUE
+    assert api.attention_fp32_backward_profile(*ok, 1, 1, 64, 64, -1, 4, S, S, S, S, S) == api.INVALID_VALUE
+    assert api.attention_fp32_backward_profile(*ok, 1, 1, 31, 64, -1, 1, S, S, S, S, S) == api.INVALID_VALUE
+    assert api.attention_fp32_backward_profile(*ok, 1, 1, 64, 64, -2, 1, S, S, S, S, S) == api.INVALID_VALUE
+    # tuning ids accepted by the reference are 14, 18, 24, 28, 44, 116 (Attention.hip:346-353)
+    assert api.attention_fp32_query_profile(*ok, 1, 1, 64, 64, -1, 15, S, S, S, S, S) == api.INVALID_VALUE
+    assert api.attention_fp32_query_profile(*ok, 1, 1, 16, 64, -1, 14, S, S, S, S, S) == api.INVALID_VALUE
+
+
+def test_throwing_wrappers_raise_hip_error():
+    with pytest.raises(api.HipError) as error:
+        api.AttentionForwardFlash(*forward_args(q=None), S, S, S, S)
+    assert error.value.status == api.INVALID_VALUE

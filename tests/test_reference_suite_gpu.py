@@ -1,0 +1,21 @@
+"""The reference's own Catch2 attention test (ROCmKernels.Tests/AttentionTests.cpp), compiled
+unchanged from its source against this library (oracle/_ref/attention_tests, see
+oracle/Makefile), run on the GPU. Its CPU ReferenceAttention is the checker; its seven
+sections call the library through the namespaced throwing wrappers."""
+from __future__ import annotations
+
+import subprocess
+
+import pytest
+
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.skipif(not oracle.REFERENCE_TESTS.exists(), reason="reference test binary not built (needs the reference tree)")
+def test_reference_attention_tests_pass(cuda):
+    result = subprocess.run([str(oracle.REFERENCE_TESTS), "-s"], capture_output=True, text=True, timeout=300)
+    print(result.stdout)
+    assert result.returncode == 0, result.stdout + result.stderr
+    assert result.stdout.count("PASS:") == 7
