@@ -163,6 +163,11 @@ ROCMKERNELS_C_EXPORT const char *rocmkernels_attention_build_info(void);
 ROCMKERNELS_C_EXPORT const char *rocmkernels_attention_flash_kernel(int batch, int heads, int queries, int keys,
         int head_width);
 
+/* Status word of the tensor-core kernels on the current device: 0, or 1 when a bounded
+ * pipeline wait gave up (a protocol failure; the affected rows are written as NaN). Reading it
+ * synchronizes with the device; clear != 0 resets it. No counterpart in the reference. */
+ROCMKERNELS_C_EXPORT unsigned int rocmkernels_attention_device_status(int clear);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -86,6 +86,8 @@ def lib() -> ctypes.CDLL:
         library.rocmkernels_attention_build_info.restype = ctypes.c_char_p
         library.rocmkernels_attention_flash_kernel.argtypes = [ctypes.c_int] * 5
         library.rocmkernels_attention_flash_kernel.restype = ctypes.c_char_p
+        library.rocmkernels_attention_device_status.argtypes = [ctypes.c_int]
+        library.rocmkernels_attention_device_status.restype = ctypes.c_uint
         _lib = library
     return _lib
 
@@ -97,6 +99,12 @@ def build_info() -> str:
 def flash_kernel_name(batch: int, heads: int, queries: int, keys: int, head_width: int = 32) -> str:
     """Name of the kernel attention_fp32_forward_flash runs for contiguous, 16-byte aligned inputs."""
     return lib().rocmkernels_attention_flash_kernel(batch, heads, queries, keys, head_width).decode()
+
+
+def device_status(clear: bool = True) -> int:
+    """Status word of the tensor-core kernels on the current device (0 = no failed pipeline wait).
+    Synchronizes with the device."""
+    return int(lib().rocmkernels_attention_device_status(int(clear)))
 
 
 def _error_name(status: int) -> str:

@@ -121,7 +121,10 @@ int launch_backward(const AttentionParams &p, cudaStream_t stream, bool softmax_
 // The flash entry: the tcgen05 tensor-core kernel when the problem fits its contract, else the
 // exact SIMT kernel (same results within the documented tolerance; no CPU path exists).
 int launch_flash(const AttentionParams &p, cudaStream_t stream) {
-    if (rk::tc::flash_supported(p)) return rk::tc::launch_flash_forward(p, stream);
+    if (rk::tc::flash_supported(p)) {
+        const int status = rk::tc::launch_flash_forward(p, stream);
+        if (status != rk::tc::kNotEligible) return status;
+    }
     return launch_simt_forward<32, false>(p, stream);
 }
 
@@ -286,6 +289,8 @@ int attention_fp32_query_profile(const float *q, const float *k, const float *v,
 }
 
 const char *rocmkernels_attention_build_info(void) { return rk::tc::build_info(); }
+
+unsigned int rocmkernels_attention_device_status(int clear) { return rk::tc::read_device_status(clear != 0); }
 
 const char *rocmkernels_attention_flash_kernel(int batch, int heads, int queries, int keys, int head_width) {
     if (head_width != 32) return "simt-fp32-forward-d64";
