@@ -45,6 +45,14 @@ WORKLOADS = {
 }
 DEFAULT_WORKLOAD = "flash_fwd_b8h3s1024d32"
 PUBLISHED_TFLOPS = 3.36  # flash fwd d32, same FLOPs (B2 H12 L1024), RX 6700 (README.md:63)
+METRIC = "FP32 attention TFLOP/s (repo FLOP convention: 4*B*H*Q*K*d forward, 8*B*H*Q*K*d backward)"
+
+
+def workload_config(name: str, world: int) -> dict:
+    batch, heads, seq, dim, description = WORKLOADS[name]
+    return {"workload": name, "description": description, "batch_per_gpu": batch, "global_batch": batch * world,
+            "heads": heads, "seq_len": seq, "head_dim": dim, "mask": "all visible", "radius": -1,
+            "parallelism": f"batch-sharded x{world}, no collective", "l2": "flushed (256 MiB write) before every step"}
 FLUSH_BYTES = 256 << 20
 
 
@@ -174,10 +182,10 @@ def run_reference(args, rank: int) -> None:
     sample = (f"{'ReferenceAttention (AttentionTests.cpp:28-125, compiled from the reference source)' if use_ref else 'oracle port'}"
               f" forward+backward of {threads} (batch, head) slices S={seq} d={dim} per step, one slice per thread;"
               f" FLOPs counted as 12*S*S*d per slice (the function always computes forward and backward)")
-    line = {"metric": "FP32 attention TFLOP/s (repo FLOP convention)", "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
+    line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f64-accumulate/f32-storage", "data": "synthetic N(0,1), seeded",
-            "config": {"workload": args.workload, "description": description}, "impl": "reference",
+            "config": workload_config(args.workload, args.gpus), "impl": "reference",
             "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": kind, "sample": sample},
             "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -321,7 +329,7 @@ def main() -> None:
                     "kernel": path}
 
     line = {
-        "metric": "FP32 attention flash forward TFLOP/s (repo FLOP convention 4*B*H*Q*K*d)",
+        "metric": METRIC,
         "value": value,
         "unit": "TFLOP/s",
         "n_gpus": world,
@@ -333,9 +341,7 @@ def main() -> None:
         "vs_baseline": value / PUBLISHED_TFLOPS,
         "dtype": "f32",
         "data": "synthetic N(0,1) from a seeded torch generator (rank-dependent seed)",
-        "config": {"workload": args.workload, "description": description, "batch_per_gpu": batch, "global_batch": batch * world,
-                   "heads": heads, "seq_len": seq, "head_dim": dim, "mask": "all visible", "radius": -1,
-                   "parallelism": f"batch-sharded x{world}, no collective", "l2": "flushed (256 MiB write) before every step"},
+        "config": workload_config(args.workload, world),
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": d2h_bytes,
                 "steps": e2e_steps},
         "roofline": roofline,
