@@ -52,6 +52,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return done != 0;
 }
 
+// Non-blocking test of the phase with the given parity (never suspends the thread; for polling
+// several barriers from one thread).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(smem_u32(bar)), "r"(parity)
+            : "memory");
+    return done != 0;
+}
+
 // Waits for the phase with the given parity to complete; gives up after kWaitTimeoutCycles,
 // records kStatusWaitTimeout in g_device_status and returns false.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
@@ -135,6 +149,26 @@ __device__ __forceinline__ void tmem_load16x2(uint32_t a, float (&va)[16], uint3
         va[i] = __uint_as_float(r[i]);
         vb[i] = __uint_as_float(r[16 + i]);
     }
+}
+
+// 16 columns at a, 16 columns at b and the single column c with one wait.
+__device__ __forceinline__ void tmem_load16x2_1(uint32_t a, float (&va)[16], uint32_t b, float (&vb)[16], uint32_t c,
+                                                float &vc) {
+    uint32_t r[33];
+    asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%33];\n\t"
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%34];\n\t"
+            "tcgen05.ld.sync.aligned.32x32b.x1.b32 {%32}, [%35];\n\t"
+            "tcgen05.wait::ld.sync.aligned;"
+            : RK_R8(0), RK_R8(8), RK_R8(16), RK_R8(24), "=r"(r[32])
+            : "r"(a), "r"(b), "r"(c)
+            : "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        va[i] = __uint_as_float(r[i]);
+        vb[i] = __uint_as_float(r[16 + i]);
+    }
+    vc = __uint_as_float(r[32]);
 }
 
 // 16 columns at a and 16 columns at b, one wait for both stores.
@@ -224,6 +258,22 @@ __device__ __forceinline__ uint64_t sw128_descriptor(uint32_t smem_byte_address)
     return d;
 }
 
+// Instruction descriptor: F16 x F16 -> F32 (kind::f16), M x N, A and B K-major.
+__host__ __device__ constexpr uint32_t f16_instr_desc(int m, int n) {
+    return (1u << 4) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// D(tmem) (+)= A(tmem, fp16 pairs per 32-bit column) x B(smem descriptor, fp16), one thread.
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+            "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+            : "memory");
+}
+
 // Instruction descriptor: TF32 x TF32 -> F32, M x N, A K-major, B K-major or MN-major.
 __host__ __device__ constexpr uint32_t tf32_instr_desc(int m, int n, bool b_mn_major) {
     return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(b_mn_major) << 16) |
@@ -246,6 +296,40 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// Warp-collective forms: the whole warp executes the call with warp-uniform operands and one
+// lane chosen by elect.sync issues the instruction. Issuing from a full warp keeps the operand
+// arithmetic on the uniform datapath; a single lane computing them itself needs several issue
+// slots per MMA, which busy warps on the same sub-partition take (measured: 33 cycles per
+// M128 N64 K16 MMA this way, 160 from a lone lane beside two FFMA-bound warps).
+__device__ __forceinline__ void mma_f16_ts_warp(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                                uint32_t accumulate) {
+    asm volatile(
+            "{\n\t.reg .pred e, p;\n\t"
+            "elect.sync _|e, 0xffffffff;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+            "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+            : "memory");
+}
+
+__device__ __forceinline__ void mma_commit_warp(uint64_t *bar) {
+    asm volatile(
+            "{\n\t.reg .pred e;\n\t"
+            "elect.sync _|e, 0xffffffff;\n\t"
+            "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_u32(bar))
+            : "memory");
+}
+
+// Bounded wait by every lane of a warp; true only if every lane saw the phase complete.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity) {
+    return __all_sync(0xffffffffu, mbar_wait(bar, parity));
+}
+
+// Non-blocking test by every lane; true only if every lane saw the phase complete.
+__device__ __forceinline__ bool mbar_test_wait_warp(uint64_t *bar, uint32_t parity) {
+    return __all_sync(0xffffffffu, mbar_test_wait(bar, parity));
+}
+
 // Round to the nearest TF32 value (10 explicit mantissa bits, ties away from zero) with two
 // integer operations: add half an ulp of the 13 dropped bits to the magnitude, clear them. The
 // carry propagates into the exponent when needed; the sign bit is untouched; infinities stay
@@ -253,6 +337,34 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar) {
 // conversion leaves it unchanged whatever its rounding mode.
 __device__ __forceinline__ float round_tf32(float x) {
     return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
+}
+
+// Packs two FP32 values as FP16 (round to nearest): a in the low half, b in the high half (the
+// order a K-major fp16 operand stores consecutive elements in one 32-bit word).
+__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
+    uint32_t packed;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(packed) : "f"(b), "f"(a));
+    return packed;
+}
+
+// max(a, b, c) in one instruction (sm_100 three-input max; NaN operands are ignored like fmaxf).
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
+// 2^e as FP32 for integer e, exact; 0 below the normal range, +inf above it.
+__device__ __forceinline__ float exp2_int(int e) {
+    return e < -126 ? 0.f : e > 127 ? __int_as_float(0x7f800000) : __int_as_float((e + 127) << 23);
+}
+
+// Exponent that brings the largest magnitude m (> 0, finite) into [2^14, 2^15): 14 - floor(log2 m),
+// clamped to [-100, 100] so that 2^e and products of two such scales stay normal FP32 values. m == 0 (or not finite) gives 0.
+__device__ __forceinline__ int fp16_scale_exponent(float m) {
+    if (!(m > 0.f) || !isfinite(m)) return 0;
+    const int exponent = ((__float_as_int(m) >> 23) & 0xff) - 127;  // floor(log2 m) for normal m
+    return max(-100, min(100, 14 - exponent));
 }
 
 // x = hi + lo with hi = round_tf32(x) and lo = x - hi exact in FP32 (|lo| <= 2^-11 |x|). The
