@@ -9,7 +9,8 @@
 //   warps 0-3   softmax + epilogue of Q tile A (thread = query row = TMEM lane)
 //   warps 4-7   softmax + epilogue of Q tile B
 //   warp  8     TMA producer: raw FP32 K and V tiles of 64 keys x 32 features, 128B swizzle
-//   warp  9     MMA issuer: the whole warp runs the schedule, elected lanes issue tcgen05 ops
+//   warp  9     MMA issuer: the whole warp runs the schedule; one elected lane issues each group
+//               of MMAs and its commit as a single instruction sequence
 //   warps 10-11 convert each K tile to [k0 | k1] FP16 rows and each V tile to transposed
 //               [v0^T ; v1^T] FP16 rows, zero masked key rows, publish the tile's key mask and
 //               the two per-tile scale exponents
@@ -24,7 +25,8 @@
 //   rows of ones make the tensor core produce the row sums of P as well)
 // The scales are exact powers of two and are removed in FP32 by the softmax threads.
 // S is double-buffered per Q tile: the MMA warp computes S(j+2) while the softmax threads
-// work on tile j, and P(j) overwrites S(j) in TMEM (as the A operand of P.V).
+// work on tile j, and P(j) overwrites S(j) in TMEM (as the A operand of P.V), stored in chunks
+// of 16 keys as it is computed.
 // Each key tile's Ot is folded into the running output in FP32 registers (O = O * exp(m_old -
 // m_new) + Ot, with the running max and sum; online softmax as in AttentionFlash32.h:96-112).
 // Folding in registers keeps the cross-tile sum in round-to-nearest FP32; accumulating all
@@ -55,7 +57,8 @@ __device__ long long g_trace[kTraceTiles][kTraceEvents];
     do {                                                                                              \
         if (blockIdx.x == 0 && (tile_index) < kTraceTiles) g_trace[(tile_index)][(event)] = clock64(); \
     } while (0)
-// per softmax warp, tile 5 of CTA 0: events 0 s_full seen, 1 max done, 2 exp done, 3 fold done, 4 P stored
+// per softmax warp, tile 5 of CTA 0: events 0 s_full seen, 1 max done, 2 exp and P stores issued,
+// 3 fold done, 4 P stores complete
 __device__ long long g_warp_trace[8][8];
 #define RK_WARP_TRACE(tile_index, event)                                                                          \
     do {                                                                                                         \
@@ -130,28 +133,27 @@ __device__ __forceinline__ uint32_t tmem_lane_address(uint32_t base, int warp) {
 // k1 half of a K row starts 64 bytes in (+4), and consecutive stages are one tile apart.
 constexpr uint64_t kDescStep = 2, kDescHalf = 4, kDescStageK = kTileBytes / 16, kDescStageV = kVTileWords * 4 / 16;
 
-// S(buffer) = q0.k1 + q1.k0 + q0.k0 over the 32 features (two K=16 steps each); k_desc addresses
-// the stage's k16 tile. Warp-collective.
-__device__ __forceinline__ void issue_scores(uint32_t tmem, uint64_t k_desc, int tile, int buffer) {
+// S(buffer) = q0.k1 + q1.k0 + q0.k0 over the 32 features (two K=16 steps each), then a commit
+// to `bar`; k_desc addresses the stage's k16 tile. Warp-collective.
+__device__ __forceinline__ void issue_scores(uint32_t tmem, uint64_t k_desc, int tile, int buffer, uint64_t *bar) {
     const uint32_t t = tmem + tile * kColTile;
     const uint32_t d = t + kColBuffer + buffer * kBufferColumns;
-#pragma unroll
-    for (int kk = 0; kk < 2; ++kk) mma_f16_ts_warp(d, t + kColQ0 + 8 * kk, k_desc + kDescHalf + kDescStep * kk, kIdescS, kk > 0);
-#pragma unroll
-    for (int kk = 0; kk < 2; ++kk) mma_f16_ts_warp(d, t + kColQ1 + 8 * kk, k_desc + kDescStep * kk, kIdescS, 1);
-#pragma unroll
-    for (int kk = 0; kk < 2; ++kk) mma_f16_ts_warp(d, t + kColQ0 + 8 * kk, k_desc + kDescStep * kk, kIdescS, 1);
+    const uint32_t a[4] = {t + kColQ0, t + kColQ0 + 8, t + kColQ1, t + kColQ1 + 8};
+    const uint64_t bk[4] = {k_desc + kDescHalf, k_desc + kDescHalf + kDescStep, k_desc, k_desc + kDescStep};
+    mma4_f16_ts_warp(d, a, bk, kIdescS, 1);
+    mma2_f16_ts_commit_warp(d, t + kColQ0, t + kColQ0 + 8, k_desc, k_desc + kDescStep, kIdescS, bar);
 }
 
 // [Oa | Ob | sums] = p1.[v0 ; v1 ; 1] + p0.[v0 ; v1 ; 1] over the 64 keys (four K=16 steps
-// each); v_desc addresses the stage's vt16 tile. Warp-collective.
-__device__ __forceinline__ void issue_values(uint32_t tmem, uint64_t v_desc, int tile, int buffer) {
+// each), then a commit to `bar`; v_desc addresses the stage's vt16 tile. Warp-collective.
+__device__ __forceinline__ void issue_values(uint32_t tmem, uint64_t v_desc, int tile, int buffer, uint64_t *bar) {
     const uint32_t t = tmem + tile * kColTile;
     const uint32_t pbuf = t + kColBuffer + buffer * kBufferColumns;
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) mma_f16_ts_warp(t + kColO, pbuf + 32 + 8 * kk, v_desc + kDescStep * kk, kIdescPV, kk > 0);
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) mma_f16_ts_warp(t + kColO, pbuf + 8 * kk, v_desc + kDescStep * kk, kIdescPV, 1);
+    const uint64_t bv[4] = {v_desc, v_desc + kDescStep, v_desc + 2 * kDescStep, v_desc + 3 * kDescStep};
+    const uint32_t a1[4] = {pbuf + 32, pbuf + 40, pbuf + 48, pbuf + 56};
+    const uint32_t a0[4] = {pbuf, pbuf + 8, pbuf + 16, pbuf + 24};
+    mma4_f16_ts_warp(t + kColO, a1, bv, kIdescPV, 1);
+    mma4_f16_ts_commit_warp(t + kColO, a0, bv, kIdescPV, 0, bar);
 }
 
 // x' = x * scale split into (x0, x1): x0 exact in FP16, x1 = x' - x0 (rounded to FP16 on packing).
@@ -180,7 +182,7 @@ __device__ __forceinline__ void fold_output(float (&o)[32], float &row_sum, int 
     float oa[16], ob[16], sum;
     tmem_load16x2_1(lane_base + kColO, oa, lane_base + kColO + 32, ob, lane_base + kColSum, sum);
     row_sum = fmaf(row_sum, weight, sum);
-    if (tile_scale == 1.f) {
+    if (__all_sync(0xffffffffu, tile_scale == 1.f)) {  // uniform anyway; the loads inside are warp-collective
 #pragma unroll
         for (int c = 0; c < 16; ++c) o[c] = fmaf(o[c], out_weight, oa[c] + ob[c]);
         tmem_load16x2(lane_base + kColO + 16, oa, lane_base + kColO + 48, ob);
@@ -196,23 +198,31 @@ __device__ __forceinline__ void fold_output(float (&o)[32], float &row_sum, int 
 }
 
 // P' = 2^14 exp(S - max) = exp2(S * slope + offset) of 64 scores, split into FP16 pairs: p0 =
-// P' truncated to 11 significant bits (exact in FP16), p1 = FP16(P' - p0). kPlain: every score is
-// finite or -inf and the offset is finite, so exp2(-inf) = 0 covers the masked keys; otherwise
-// -inf scores are zeroed explicitly (a row without any visible key yet has an infinite offset).
+// P' truncated to 11 significant bits (exact in FP16), p1 = FP16(P' - p0), stored to the P
+// buffer (p0 pairs in columns 0-31, p1 pairs in 32-63) in chunks of 16 keys without waiting, so
+// few values are live at a time. kPlain: every score is finite or -inf and the offset is finite,
+// so exp2(-inf) = 0 covers the masked keys; otherwise -inf scores are zeroed explicitly (a row
+// without any visible key yet has an infinite offset).
 template <bool kPlain>
-__device__ __forceinline__ void exp_split(const float (&sc)[64], float slope, float offset, float (&p0)[32], float (&p1)[32]) {
+__device__ __forceinline__ void exp_split_store(const float (&sc)[64], float slope, float offset, uint32_t pbuf) {
 #pragma unroll
-    for (int c = 0; c < 32; ++c) {
-        float a = fast_exp2(fmaf(sc[2 * c], slope, offset));
-        float b = fast_exp2(fmaf(sc[2 * c + 1], slope, offset));
-        if (!kPlain) {
-            a = sc[2 * c] == -INFINITY ? 0.f : a;
-            b = sc[2 * c + 1] == -INFINITY ? 0.f : b;
+    for (int chunk = 0; chunk < 4; ++chunk) {
+        float p0[8], p1[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int c = 8 * chunk + i;
+            float a = fast_exp2(fmaf(sc[2 * c], slope, offset));
+            float b = fast_exp2(fmaf(sc[2 * c + 1], slope, offset));
+            if (!kPlain) {
+                a = sc[2 * c] == -INFINITY ? 0.f : a;
+                b = sc[2 * c + 1] == -INFINITY ? 0.f : b;
+            }
+            const float a0 = __uint_as_float(__float_as_uint(a) & 0xFFFFE000u);
+            const float b0 = __uint_as_float(__float_as_uint(b) & 0xFFFFE000u);
+            p0[i] = __uint_as_float(pack_half2(a0, b0));
+            p1[i] = __uint_as_float(pack_half2(a - a0, b - b0));
         }
-        const float a0 = __uint_as_float(__float_as_uint(a) & 0xFFFFE000u);
-        const float b0 = __uint_as_float(__float_as_uint(b) & 0xFFFFE000u);
-        p0[c] = __uint_as_float(pack_half2(a0, b0));
-        p1[c] = __uint_as_float(pack_half2(a - a0, b - b0));
+        tmem_store8x2_async(pbuf + 8 * chunk, p0, pbuf + 32 + 8 * chunk, p1);
     }
 }
 
@@ -302,8 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!ok) break;
 #pragma unroll
                 for (int t = 0; t < kQTiles; ++t) {
-                    issue_scores(tmem, k_desc0 + kDescStageK * j, t, j);
-                    mma_commit_warp(&s.s_full[t][j]);
+                    issue_scores(tmem, k_desc0 + kDescStageK * j, t, j, &s.s_full[t][j]);
                 }
             }
             for (int j = 0; j < tiles && ok; ++j) {
@@ -320,8 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (!ok || served[t] || !mbar_test_wait_warp(&s.p_full[t], j & 1)) continue;
                         if (lane == 0) RK_TRACE(j, t);
                         tc_fence_after();
-                        issue_values(tmem, v_desc0 + kDescStageV * stage, t, buffer);
-                        mma_commit_warp(&s.pv_done[t]);
+                        issue_values(tmem, v_desc0 + kDescStageV * stage, t, buffer, &s.pv_done[t]);
                         if (more) {
                             if (!next_ready) {
                                 next_ready = mbar_wait_warp(&s.kv_ready[next_stage], ((j + 2) / kStages) & 1);
@@ -331,8 +339,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 }
                                 tc_fence_after();
                             }
-                            issue_scores(tmem, k_desc0 + kDescStageK * next_stage, t, buffer);
-                            mma_commit_warp(&s.s_full[t][buffer]);
+                            issue_scores(tmem, k_desc0 + kDescStageK * next_stage, t, buffer, &s.s_full[t][buffer]);
                         }
                         served[t] = true;
                         --remaining;
@@ -522,20 +529,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float old_weight = isfinite(row_max) ? fast_exp2((row_max - next) * kLog2e) : 0.f;
             const float slope = s_scale * kLog2e;
             const float offset = fmaf(-next, kLog2e, 14.f);  // P' = 2^14 exp(S - max) = exp2(S * slope + offset)
-            float p0[32], p1[32];  // FP16 split packed in pairs: p0 (exact 11-bit part), p1 (the rest)
-            if (isfinite(offset) && slope > 0.f)
-                exp_split<true>(sc, slope, offset, p0, p1);
+            // P(j) may be written before Ot(j - 1) is folded: only the p_full arrival below lets
+            // the MMA warp start P(j).V, which overwrites Ot. The TMEM stores inside are
+            // warp-collective, so the branch is taken by the whole warp (the explicit path is
+            // exact for finite rows too).
+            if (__all_sync(0xffffffffu, isfinite(offset) && slope > 0.f))
+                exp_split_store<true>(sc, slope, offset, pbuf);
             else
-                exp_split<false>(sc, slope, offset, p0, p1);
+                exp_split_store<false>(sc, slope, offset, pbuf);
             RK_WARP_TRACE(j, 2);
             if (j > 0) {  // fold tile j-1 before P(j).V overwrites its Ot
                 ok = __all_sync(0xffffffffu, mbar_wait(&s.pv_done[tile], (j - 1) & 1));
-                if (!ok) break;
+                if (!ok) {
+                    tmem_wait_store();  // no store may be in flight when TMEM is released
+                    break;
+                }
                 tc_fence_after();
                 fold_output(o, row_sum, o_exp, lane_base, pending_weight, pending_exponent);
             }
             RK_WARP_TRACE(j, 3);
-            tmem_store32x2(pbuf, p0, pbuf + 32, p1);
+            tmem_wait_store();
             RK_WARP_TRACE(j, 4);
             tc_fence_before();
             if (tracer) RK_TRACE(j, 6 + 4 * tile);

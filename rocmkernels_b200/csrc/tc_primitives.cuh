@@ -1,5 +1,5 @@
 // sm_100a primitives written as inline PTX: mbarriers with bounded waits, TMA tensor loads,
-// tcgen05 TMEM allocation / loads / stores, UMMA descriptors and tcgen05.mma (kind::tf32).
+// tcgen05 TMEM allocation / loads / stores, UMMA descriptors and warp-issued tcgen05.mma (kind::f16).
 //
 // Encodings follow the PTX ISA for tcgen05 (shared-memory matrix descriptor: start address,
 // leading/stride byte offsets in 16-byte units, version 1 at bit 46, swizzle mode at bits 61-63;
@@ -107,33 +107,6 @@ __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::
 #define RK_R8(i) "=r"(r[i]), "=r"(r[i + 1]), "=r"(r[i + 2]), "=r"(r[i + 3]), "=r"(r[i + 4]), "=r"(r[i + 5]), "=r"(r[i + 6]), "=r"(r[i + 7])
 #define RK_W8(i) "r"(r[i]), "r"(r[i + 1]), "r"(r[i + 2]), "r"(r[i + 3]), "r"(r[i + 4]), "r"(r[i + 5]), "r"(r[i + 6]), "r"(r[i + 7])
 
-// 32 consecutive 32-bit TMEM columns of this thread's lane (32x32b shape), load + wait in one
-// statement so no use of the registers can be scheduled before the data has arrived.
-__device__ __forceinline__ void tmem_load32(uint32_t taddr, float (&v)[32]) {
-    uint32_t r[32];
-    asm volatile(
-            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-            "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
-            "tcgen05.wait::ld.sync.aligned;"
-            : RK_R8(0), RK_R8(8), RK_R8(16), RK_R8(24)
-            : "r"(taddr)
-            : "memory");
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-__device__ __forceinline__ void tmem_store32(uint32_t taddr, const float (&v)[32]) {
-    uint32_t r[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(v[i]);
-    asm volatile(
-            "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-            "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n\t"
-            "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
-            RK_W8(0), RK_W8(8), RK_W8(16), RK_W8(24)
-            : "memory");
-}
-
 // 16 columns at a and 16 columns at b with one wait.
 __device__ __forceinline__ void tmem_load16x2(uint32_t a, float (&va)[16], uint32_t b, float (&vb)[16]) {
     uint32_t r[32];
@@ -187,23 +160,20 @@ __device__ __forceinline__ void tmem_store16x2(uint32_t a, const float *va, uint
             : "memory");
 }
 
-// 32 columns at a and 32 columns at b, one wait for both stores.
-__device__ __forceinline__ void tmem_store32x2(uint32_t a, const float *va, uint32_t b, const float *vb) {
-    uint32_t r[64];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-        r[i] = __float_as_uint(va[i]);
-        r[32 + i] = __float_as_uint(vb[i]);
-    }
+// 8 columns at a and 8 columns at b without waiting: the registers are consumed at issue; the
+// data reaches TMEM by the next tmem_wait_store().
+__device__ __forceinline__ void tmem_store8x2_async(uint32_t a, const float *va, uint32_t b, const float *vb) {
     asm volatile(
-            "tcgen05.st.sync.aligned.32x32b.x32.b32 [%64], {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-            "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31};\n\t"
-            "tcgen05.st.sync.aligned.32x32b.x32.b32 [%65], {%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,"
-            "%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63};\n\t"
-            "tcgen05.wait::st.sync.aligned;" ::RK_W8(0),
-            RK_W8(8), RK_W8(16), RK_W8(24), RK_W8(32), RK_W8(40), RK_W8(48), RK_W8(56), "r"(a), "r"(b)
+            "tcgen05.st.sync.aligned.32x32b.x8.b32 [%16], {%0,%1,%2,%3,%4,%5,%6,%7};\n\t"
+            "tcgen05.st.sync.aligned.32x32b.x8.b32 [%17], {%8,%9,%10,%11,%12,%13,%14,%15};" ::"r"(__float_as_uint(va[0])),
+            "r"(__float_as_uint(va[1])), "r"(__float_as_uint(va[2])), "r"(__float_as_uint(va[3])), "r"(__float_as_uint(va[4])),
+            "r"(__float_as_uint(va[5])), "r"(__float_as_uint(va[6])), "r"(__float_as_uint(va[7])), "r"(__float_as_uint(vb[0])),
+            "r"(__float_as_uint(vb[1])), "r"(__float_as_uint(vb[2])), "r"(__float_as_uint(vb[3])), "r"(__float_as_uint(vb[4])),
+            "r"(__float_as_uint(vb[5])), "r"(__float_as_uint(vb[6])), "r"(__float_as_uint(vb[7])), "r"(a), "r"(b)
             : "memory");
 }
+
+__device__ __forceinline__ void tmem_wait_store() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // 64 columns (two 32-column blocks at taddr and taddr + 32) with one wait.
 __device__ __forceinline__ void tmem_load64(uint32_t taddr, float (&v)[64]) {
@@ -219,27 +189,6 @@ __device__ __forceinline__ void tmem_load64(uint32_t taddr, float (&v)[64]) {
             : "memory");
 #pragma unroll
     for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-// 32 columns at a and 64 columns at b (two 32-column blocks) with one wait.
-__device__ __forceinline__ void tmem_load32_64(uint32_t a, float (&va)[32], uint32_t b, float (&vb)[64]) {
-    uint32_t r[96];
-    asm volatile(
-            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-            "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%96];\n\t"
-            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
-            "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%97];\n\t"
-            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%64,%65,%66,%67,%68,%69,%70,%71,%72,%73,%74,%75,%76,%77,%78,%79,"
-            "%80,%81,%82,%83,%84,%85,%86,%87,%88,%89,%90,%91,%92,%93,%94,%95}, [%98];\n\t"
-            "tcgen05.wait::ld.sync.aligned;"
-            : RK_R8(0), RK_R8(8), RK_R8(16), RK_R8(24), RK_R8(32), RK_R8(40), RK_R8(48), RK_R8(56), RK_R8(64),
-              RK_R8(72), RK_R8(80), RK_R8(88)
-            : "r"(a), "r"(b), "r"(b + 32)
-            : "memory");
-#pragma unroll
-    for (int i = 0; i < 32; ++i) va[i] = __uint_as_float(r[i]);
-#pragma unroll
-    for (int i = 0; i < 64; ++i) vb[i] = __uint_as_float(r[32 + i]);
 }
 
 #undef RK_R8
@@ -263,60 +212,68 @@ __host__ __device__ constexpr uint32_t f16_instr_desc(int m, int n) {
     return (1u << 4) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
 }
 
-// D(tmem) (+)= A(tmem, fp16 pairs per 32-bit column) x B(smem descriptor, fp16), one thread.
-__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                           uint32_t accumulate) {
-    asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "setp.ne.b32 p, %4, 0;\n\t"
-            "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-            "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-            : "memory");
-}
-
-// Instruction descriptor: TF32 x TF32 -> F32, M x N, A K-major, B K-major or MN-major.
-__host__ __device__ constexpr uint32_t tf32_instr_desc(int m, int n, bool b_mn_major) {
-    return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(b_mn_major) << 16) |
-           (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
-}
-
-// D(tmem) (+)= A(tmem) x B(smem descriptor), issued by one thread.
-__device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                            uint32_t accumulate) {
-    asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "setp.ne.b32 p, %4, 0;\n\t"
-            "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-            "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-            : "memory");
-}
-
-// Arrives on `bar` once every tcgen05.mma issued so far by this thread has completed.
-__device__ __forceinline__ void mma_commit(uint64_t *bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
 // Warp-collective forms: the whole warp executes the call with warp-uniform operands and one
-// lane chosen by elect.sync issues the instruction. Issuing from a full warp keeps the operand
+// lane chosen by elect.sync issues the instructions. Issuing from a full warp keeps the operand
 // arithmetic on the uniform datapath; a single lane computing them itself needs several issue
-// slots per MMA, which busy warps on the same sub-partition take (measured: 33 cycles per
-// M128 N64 K16 MMA this way, 160 from a lone lane beside two FFMA-bound warps).
-__device__ __forceinline__ void mma_f16_ts_warp(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                                uint32_t accumulate) {
-    asm volatile(
-            "{\n\t.reg .pred e, p;\n\t"
-            "elect.sync _|e, 0xffffffff;\n\t"
-            "setp.ne.b32 p, %4, 0;\n\t"
-            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-            "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-            : "memory");
-}
-
+// slots per MMA, which busy warps on the same sub-partition take (measured on B200: an
+// M128 N64 K16 MMA every 33 cycles this way, N/2 cycles for any N >= 48, i.e. the full rate;
+// every 160 cycles from a lone lane beside two FFMA-bound warps).
 __device__ __forceinline__ void mma_commit_warp(uint64_t *bar) {
     asm volatile(
             "{\n\t.reg .pred e;\n\t"
             "elect.sync _|e, 0xffffffff;\n\t"
             "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_u32(bar))
+            : "memory");
+}
+
+// Warp-collective: four kind::f16 MMAs into one accumulator and a commit to `bar`, issued by one
+// elected lane in a single sequence (one warp instruction per MMA). The first MMA overwrites
+// the accumulator when `overwrite` is set; the others accumulate.
+__device__ __forceinline__ void mma4_f16_ts_commit_warp(uint32_t d, const uint32_t (&a)[4], const uint64_t (&b)[4], uint32_t idesc,
+                                                        uint32_t overwrite, uint64_t *bar) {
+    asm volatile(
+            "{\n\t.reg .pred e, first, rest;\n\t"
+            "elect.sync _|e, 0xffffffff;\n\t"
+            "setp.eq.b32 first, %10, 0;\n\t"
+            "setp.eq.b32 rest, %10, %10;\n\t"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %5, %9, first;\n\t"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%2], %6, %9, rest;\n\t"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%3], %7, %9, rest;\n\t"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%4], %8, %9, rest;\n\t"
+            "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%11];\n\t}" ::"r"(d),
+            "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "r"(idesc),
+            "r"(overwrite), "r"(smem_u32(bar))
+            : "memory");
+}
+
+// Warp-collective: four kind::f16 MMAs accumulating into one accumulator (no commit).
+__device__ __forceinline__ void mma4_f16_ts_warp(uint32_t d, const uint32_t (&a)[4], const uint64_t (&b)[4], uint32_t idesc,
+                                                 uint32_t overwrite) {
+    asm volatile(
+            "{\n\t.reg .pred e, first, rest;\n\t"
+            "elect.sync _|e, 0xffffffff;\n\t"
+            "setp.eq.b32 first, %10, 0;\n\t"
+            "setp.eq.b32 rest, %10, %10;\n\t"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %5, %9, first;\n\t"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%2], %6, %9, rest;\n\t"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%3], %7, %9, rest;\n\t"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%4], %8, %9, rest;\n\t}" ::"r"(d),
+            "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "r"(idesc),
+            "r"(overwrite)
+            : "memory");
+}
+
+// Warp-collective: two accumulating kind::f16 MMAs and a commit to `bar`, one elected sequence.
+__device__ __forceinline__ void mma2_f16_ts_commit_warp(uint32_t d, uint32_t a0, uint32_t a1, uint64_t b0, uint64_t b1,
+                                                        uint32_t idesc, uint64_t *bar) {
+    asm volatile(
+            "{\n\t.reg .pred e, rest;\n\t"
+            "elect.sync _|e, 0xffffffff;\n\t"
+            "setp.eq.b32 rest, %5, %5;\n\t"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %3, %5, rest;\n\t"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%2], %4, %5, rest;\n\t"
+            "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%6];\n\t}" ::"r"(d),
+            "r"(a0), "r"(a1), "l"(b0), "l"(b1), "r"(idesc), "r"(smem_u32(bar))
             : "memory");
 }
 
@@ -365,13 +322,6 @@ __device__ __forceinline__ int fp16_scale_exponent(float m) {
     if (!(m > 0.f) || !isfinite(m)) return 0;
     const int exponent = ((__float_as_int(m) >> 23) & 0xff) - 127;  // floor(log2 m) for normal m
     return max(-100, min(100, 14 - exponent));
-}
-
-// x = hi + lo with hi = round_tf32(x) and lo = x - hi exact in FP32 (|lo| <= 2^-11 |x|). The
-// tensor core keeps the top 11 significant bits of lo, so hi*b + lo*b carries about 22 bits.
-__device__ __forceinline__ void split_tf32(float x, float &hi, float &lo) {
-    hi = round_tf32(x);
-    lo = x - hi;
 }
 
 }  // namespace tc
