@@ -9,15 +9,22 @@ With N GPUs (torchrun) every rank runs its own B=8 batch slice of a global batch
 sequences (weak scaling; (batch, head) slices are independent, so there is no collective on
 the data path) and the reported value is all ranks' FLOPs over the slowest rank's time.
 
+The other BASELINE configs are opt-in workloads (``--workload``): forward + backward steps
+(``attention_fp32_forward_flash`` or ``attention64_fp32_forward``, then the matching backward)
+on a fixed global problem whose batch is split over the ranks (strong scaling), with the
+BASELINE key-padding lengths (seed 105) and radius. They report the repo-convention TFLOP/s
+(12*B*H*Q*K*d per step) as ``value``, the effective TFLOP/s over active (query, key) pairs, and
+the forward and backward times separately.
+
 Timing: W untimed steps, then K steps; before each step a 256 MiB buffer is written to flush
 the 126 MB L2, and the step itself is bracketed by CUDA events on the launching stream (the
 flush is outside the events). Device time is summed over the K steps; the max over ranks is
 taken with an all-reduce. FLOPs follow the reference's convention (4*B*H*Q*K*d forward,
-AttentionBenchmarks.cpp:141-142).
+8*B*H*Q*K*d backward, AttentionBenchmarks.cpp:141-142).
 
-Also reported: ``e2e`` (the same step through the public C entry point with pinned host
-buffers: H2D of q/k/v/mask and D2H of O/lse inside the timed region), ``roofline`` of the
-flash kernel, ``cpu_baseline`` (rank 0, N=1: the CPU oracle timed on this box's host cores),
+Also reported: ``e2e`` (the same step through the public C entry points with pinned host
+buffers: H2D of the inputs and D2H of the outputs inside the timed region), ``roofline`` of the
+dominant kernel, ``cpu_baseline`` (rank 0, N=1: the CPU oracle timed on this box's host cores),
 ``clocks`` sampled with nvidia-smi during the timed region, and ``gpu_launches``.
 
 ``--impl reference`` times the reference's own CPU attention (ReferenceAttention compiled from
@@ -40,19 +47,63 @@ REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
 WORKLOADS = {
-    # name: (batch per GPU, heads, seq, head_dim, description)
-    "flash_fwd_b8h3s1024d32": (8, 3, 1024, 32, "BASELINE configs[1]: 32-wide flash forward B8 H3 S1024 d32, no mask, global"),
+    # batch: per GPU (weak scaling) for the forward headline, global (split over ranks) for the
+    # forward + backward configs; lengths: per-sequence visible keys drawn U[lo, hi] (seed 105),
+    # or "c1" (batch 1 keys 112..127 masked), or None (all visible).
+    "flash_fwd_b8h3s1024d32": dict(batch=8, heads=3, seq=1024, dim=32, radius=-1, lengths=None, backward=False,
+                                   description="BASELINE configs[1]: 32-wide flash forward B8 H3 S1024 d32, no mask, global"),
+    "c1_fwd_bwd_b2h12s128d32": dict(batch=2, heads=12, seq=128, dim=32, radius=-1, lengths="c1", backward=True,
+                                    description="BASELINE configs[0]: forward+backward B2 H12 S128 d32, batch 1 keys 112..127 masked"),
+    "c3_fwd_bwd_b8h6s1024d64": dict(batch=8, heads=6, seq=1024, dim=64, radius=-1, lengths=(512, 1024), backward=True,
+                                    description="BASELINE configs[2]: 64-wide forward+backward B8 H6 S1024 d64, lengths U[512,1024]"),
+    "c4_fwd_bwd_b16h12s2048d32r128": dict(batch=16, heads=12, seq=2048, dim=32, radius=128, lengths=(1024, 2048), backward=True,
+                                          description="BASELINE configs[3]: local radius 128 forward+backward B16 H12 S2048 d32, "
+                                                      "lengths U[1024,2048]"),
+    "c5_fwd_bwd_b64h12s4096d32": dict(batch=64, heads=12, seq=4096, dim=32, radius=-1, lengths=None, backward=True,
+                                      description="BASELINE configs[4]: forward+backward B64 H12 S4096 d32, full attention"),
 }
 DEFAULT_WORKLOAD = "flash_fwd_b8h3s1024d32"
 PUBLISHED_TFLOPS = 3.36  # flash fwd d32, same FLOPs (B2 H12 L1024), RX 6700 (README.md:63)
 METRIC = "FP32 attention TFLOP/s (repo FLOP convention: 4*B*H*Q*K*d forward, 8*B*H*Q*K*d backward)"
 
 
+def key_lengths(spec: dict) -> list[int]:
+    """Visible keys per sequence of the global batch (keys [0, length) visible)."""
+    import numpy as np
+
+    batch, seq, lengths = spec["batch"], spec["seq"], spec["lengths"]
+    if lengths is None:
+        return [seq] * batch
+    if lengths == "c1":
+        return [seq if b != 1 else seq - 16 for b in range(batch)]
+    low, high = lengths
+    return [int(x) for x in np.random.default_rng(105).integers(low, high + 1, size=batch)]
+
+
+def active_pairs(seq: int, radius: int, length: int) -> int:
+    """(query, key) pairs a sequence with `length` visible keys and the radius window computes."""
+    if radius < 0:
+        return seq * length
+    total = 0
+    for i in range(seq):
+        lo, hi = max(0, i - radius), min(length - 1, i + radius)
+        total += max(0, hi - lo + 1)
+    return total
+
+
 def workload_config(name: str, world: int) -> dict:
-    batch, heads, seq, dim, description = WORKLOADS[name]
-    return {"workload": name, "description": description, "batch_per_gpu": batch, "global_batch": batch * world,
-            "heads": heads, "seq_len": seq, "head_dim": dim, "mask": "all visible", "radius": -1,
-            "parallelism": f"batch-sharded x{world}, no collective", "l2": "flushed (256 MiB write) before every step"}
+    spec = WORKLOADS[name]
+    config = {"workload": name, "description": spec["description"], "heads": spec["heads"], "seq_len": spec["seq"],
+              "head_dim": spec["dim"], "radius": spec["radius"], "l2": "flushed (256 MiB write) before every step"}
+    if spec["backward"]:
+        lengths = key_lengths(spec)
+        config.update({"global_batch": spec["batch"], "batch_per_gpu": spec["batch"] // world, "step": "forward + backward",
+                       "mask": "all visible" if spec["lengths"] is None else f"key lengths {lengths}",
+                       "parallelism": f"batch-sharded x{world} (strong scaling), no collective"})
+    else:
+        config.update({"batch_per_gpu": spec["batch"], "global_batch": spec["batch"] * world, "mask": "all visible",
+                       "parallelism": f"batch-sharded x{world}, no collective"})
+    return config
 FLUSH_BYTES = 256 << 20
 
 
@@ -119,26 +170,39 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_baseline(workload) -> dict:
-    """The oracle (C restatement, forward only) on this host's cores over the full workload."""
+def cpu_baseline(spec: dict) -> dict:
+    """The oracle (C restatement) on this host's cores: the full forward workload for the headline,
+    a bounded sample of (batch, head) slices for the forward + backward configs."""
+    import numpy as np
     from oracle import oracle
 
-    batch, heads, seq, dim, _ = workload
     threads = oracle.cpu_count()
+    seq, dim, radius = spec["seq"], spec["dim"], spec["radius"]
+    if spec["backward"]:
+        batch, heads, length = 1, threads, key_lengths(spec)[0]
+        forward_only, upstream = False, oracle.normal(heads * seq * dim, 104).reshape(1, heads, seq, dim)
+        flops = 12.0 * heads * seq * seq * dim
+        what = (f"forward+backward of {heads} (batch, head) slices (S={seq}, d={dim}, {length} visible keys, radius {radius}),"
+                f" one slice per thread; repo-convention FLOPs")
+    else:
+        batch, heads, length = spec["batch"], spec["heads"], seq
+        forward_only, upstream = True, None
+        flops = 4.0 * batch * heads * seq * seq * dim
+        what = "forward over the full workload"
     q = oracle.normal(batch * heads * seq * dim, 101).reshape(batch, heads, seq, dim)
     k = oracle.normal(batch * heads * seq * dim, 102).reshape(batch, heads, seq, dim)
     v = oracle.normal(batch * heads * seq * dim, 103).reshape(batch, heads, seq, dim)
-    mask = __import__("numpy").ones((batch, seq), dtype="uint8")
-    flops = 4.0 * batch * heads * seq * seq * dim
+    mask = np.zeros((batch, seq), dtype="uint8")
+    mask[:, :length] = 1
     reps, elapsed = 0, 0.0
     while elapsed < 10.0 and reps < 50:
         start = time.perf_counter()
-        oracle.attention(q, k, v, mask, None, -1, threads=threads, forward_only=True)
+        oracle.attention(q, k, v, mask, upstream, radius, threads=threads, forward_only=forward_only)
         elapsed += time.perf_counter() - start
         reps += 1
     return {"value": flops * reps / elapsed / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-            "sample": f"oracle/attention_oracle.c forward (double accumulation, as ReferenceAttention) over the full "
-                      f"workload x{reps}, {elapsed:.1f} s on {threads} threads"}
+            "sample": f"oracle/attention_oracle.c (double accumulation, as ReferenceAttention) {what} x{reps},"
+                      f" {elapsed:.1f} s on {threads} threads"}
 
 
 def run_reference(args, rank: int) -> None:
@@ -148,20 +212,23 @@ def run_reference(args, rank: int) -> None:
     import numpy as np
     from oracle import oracle
 
-    batch, heads, seq, dim, description = WORKLOADS[args.workload]
+    spec = WORKLOADS[args.workload]
+    seq, dim, radius = spec["seq"], spec["dim"], spec["radius"]
+    length = key_lengths(spec)[0]
     threads = oracle.cpu_count()
     use_ref = oracle.reference_available()
     q = oracle.normal(threads * seq * dim, 101).reshape(threads, 1, seq, dim)
     k = oracle.normal(threads * seq * dim, 102).reshape(threads, 1, seq, dim)
     v = oracle.normal(threads * seq * dim, 103).reshape(threads, 1, seq, dim)
     u = oracle.normal(threads * seq * dim, 104).reshape(threads, 1, seq, dim)
-    mask = np.ones((1, seq), np.uint8)
+    mask = np.zeros((1, seq), np.uint8)
+    mask[:, :length] = 1
 
     def one_slice(i):
         if use_ref:
-            oracle.reference_attention(q[i:i + 1], k[i:i + 1], v[i:i + 1], mask, u[i:i + 1], -1)
+            oracle.reference_attention(q[i:i + 1], k[i:i + 1], v[i:i + 1], mask, u[i:i + 1], radius)
         else:
-            oracle.attention(q[i:i + 1], k[i:i + 1], v[i:i + 1], mask, u[i:i + 1], -1, threads=1)
+            oracle.attention(q[i:i + 1], k[i:i + 1], v[i:i + 1], mask, u[i:i + 1], radius, threads=1)
 
     def step():
         workers = [threading.Thread(target=one_slice, args=(i,)) for i in range(threads)]
@@ -180,11 +247,13 @@ def run_reference(args, rank: int) -> None:
     value = flops / elapsed / 1e12
     kind = "reference" if use_ref else "port"
     sample = (f"{'ReferenceAttention (AttentionTests.cpp:28-125, compiled from the reference source)' if use_ref else 'oracle port'}"
-              f" forward+backward of {threads} (batch, head) slices S={seq} d={dim} per step, one slice per thread;"
-              f" FLOPs counted as 12*S*S*d per slice (the function always computes forward and backward)")
+              f" forward+backward of {threads} (batch, head) slices S={seq} d={dim} ({length} visible keys, radius {radius})"
+              f" per step, one slice per thread; FLOPs counted as 12*S*S*d per slice (the function always computes"
+              f" forward and backward)")
     line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f64-accumulate/f32-storage", "data": "synthetic N(0,1), seeded",
+            "scaling": "weak" if not spec["backward"] else "strong", "vs_baseline": None,
+            "dtype": "f64-accumulate/f32-storage", "data": "synthetic N(0,1), seeded",
             "config": workload_config(args.workload, args.gpus), "impl": "reference",
             "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": kind, "sample": sample},
             "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -231,56 +300,89 @@ def main() -> None:
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
 
-    batch, heads, seq, dim, description = WORKLOADS[args.workload]
+    spec = WORKLOADS[args.workload]
+    heads, seq, dim, radius, with_backward = spec["heads"], spec["seq"], spec["dim"], spec["radius"], spec["backward"]
+    if with_backward:
+        if spec["batch"] % world:
+            raise SystemExit(f"the global batch {spec['batch']} must be divisible by the {world} ranks")
+        batch = spec["batch"] // world
+        lengths = key_lengths(spec)[rank * batch:(rank + 1) * batch]
+    else:
+        batch = spec["batch"]
+        lengths = [seq] * batch
     generator = torch.Generator(device=device)
     generator.manual_seed(101 + rank)
     q = torch.randn(batch, heads, seq, dim, device=device, generator=generator)
     k = torch.randn(batch, heads, seq, dim, device=device, generator=generator)
     v = torch.randn(batch, heads, seq, dim, device=device, generator=generator)
-    mask = torch.ones(batch, seq, dtype=torch.uint8, device=device)
+    mask = torch.zeros(batch, seq, dtype=torch.uint8, device=device)
+    for i, length in enumerate(lengths):
+        mask[i, :length] = 1
     out = torch.empty_like(q)
     lse = torch.empty(batch, heads, seq, 2, device=device)
+    inputs, outputs = [q, k, v, mask], [out, lse]
+    if with_backward:
+        upstream = torch.randn(batch, heads, seq, dim, device=device, generator=generator)
+        gq, gk, gv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        delta = torch.empty(batch, heads, seq, device=device)
+        inputs.append(upstream)
+        outputs += [gq, gk, gv]
     flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=device)
     stream = torch.cuda.current_stream(device)
     qs, ks, vs, os_ = (api.strides_of(t) for t in (q, k, v, out))
-    flops_per_step = 4.0 * batch * heads * seq * seq * dim
+    forward_fn = api.attention_fp32_forward_flash if dim == 32 else api.attention64_fp32_forward
+    backward_fn = api.attention_fp32_backward if dim == 32 else api.attention64_fp32_backward
+    pairs = sum(active_pairs(seq, radius, length) for length in lengths) * heads
+    flops_forward, flops_backward = 4.0 * batch * heads * seq * seq * dim, 8.0 * batch * heads * seq * seq * dim
+    effective_forward, effective_backward = 4.0 * pairs * dim, 8.0 * pairs * dim
+    flops_per_step = flops_forward + (flops_backward if with_backward else 0.0)
+    effective_per_step = effective_forward + (effective_backward if with_backward else 0.0)
+    launches_per_step = 1 + (2 if with_backward else 0)
 
-    def step_device():
-        status = api.attention_fp32_forward_flash(q, k, v, mask, out, lse, batch, heads, seq, seq, -1, qs, ks, vs, os_, stream)
+    def forward():
+        status = forward_fn(q, k, v, mask, out, lse, batch, heads, seq, seq, radius, qs, ks, vs, os_, stream)
         if status != 0:
-            raise api.HipError(status, "attention_fp32_forward_flash")
+            raise api.HipError(status, forward_fn.__name__)
+
+    def backward():
+        status = backward_fn(q, k, v, mask, out, lse, upstream, gq, gk, gv, delta, batch, heads, seq, seq, radius, qs, ks, vs, os_,
+                             api.strides_of(upstream), stream)
+        if status != 0:
+            raise api.HipError(status, backward_fn.__name__)
+
+    phases = [forward, backward] if with_backward else [forward]
 
     # Host-buffer leg: pinned inputs copied in and outputs copied out every step.
-    host_q, host_k, host_v = (t.cpu().pin_memory() for t in (q, k, v))
-    host_mask = mask.cpu().pin_memory()
-    host_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    host_lse = torch.empty(lse.shape, dtype=lse.dtype).pin_memory()
-    h2d_bytes = sum(t.numel() * t.element_size() for t in (host_q, host_k, host_v, host_mask))
-    d2h_bytes = host_out.numel() * 4 + host_lse.numel() * 4
+    host_inputs = [t.cpu().pin_memory() for t in inputs]
+    host_outputs = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in outputs]
+    h2d_bytes = sum(t.numel() * t.element_size() for t in host_inputs)
+    d2h_bytes = sum(t.numel() * t.element_size() for t in host_outputs)
 
     def step_e2e():
-        q.copy_(host_q, non_blocking=True)
-        k.copy_(host_k, non_blocking=True)
-        v.copy_(host_v, non_blocking=True)
-        mask.copy_(host_mask, non_blocking=True)
-        step_device()
-        host_out.copy_(out, non_blocking=True)
-        host_lse.copy_(lse, non_blocking=True)
+        for device_tensor, host_tensor in zip(inputs, host_inputs):
+            device_tensor.copy_(host_tensor, non_blocking=True)
+        for phase in phases:
+            phase()
+        for host_tensor, device_tensor in zip(host_outputs, outputs):
+            host_tensor.copy_(device_tensor, non_blocking=True)
 
-    def timed(fn, steps):
-        starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
-        ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    def timed(fns, steps):
+        """Seconds summed over `steps`: in total and per callable of `fns` (events between them)."""
+        marks = [[torch.cuda.Event(enable_timing=True) for _ in range(len(fns) + 1)] for _ in range(steps)]
         for i in range(steps):
             flush.fill_(float(i))
-            starts[i].record(stream)
-            fn()
-            ends[i].record(stream)
+            marks[i][0].record(stream)
+            for j, fn in enumerate(fns):
+                fn()
+                marks[i][j + 1].record(stream)
         torch.cuda.synchronize(device)
-        return sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / 1e3  # seconds
+        parts = [sum(m[j].elapsed_time(m[j + 1]) for m in marks) / 1e3 for j in range(len(fns))]
+        return sum(parts), parts
 
     for _ in range(args.warmup):
         flush.fill_(0.0)
-        step_device()
+        for phase in phases:
+            phase()
     torch.cuda.synchronize(device)
 
     visible = os.environ.get("CUDA_VISIBLE_DEVICES", "")
@@ -291,7 +393,7 @@ def main() -> None:
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(device)
-    device_seconds = timed(step_device, args.steps)
+    device_seconds, part_seconds = timed(phases, args.steps)
     torch.cuda.synchronize(device)
     if world > 1:
         dist.barrier()
@@ -301,32 +403,39 @@ def main() -> None:
         step_e2e()
     torch.cuda.synchronize(device)
     e2e_steps = max(1, min(args.steps, 50))
-    e2e_seconds = timed(step_e2e, e2e_steps)
+    e2e_seconds, _ = timed([step_e2e], e2e_steps)
 
-    times = torch.tensor([device_seconds, e2e_seconds], device=device, dtype=torch.float64)
+    times = torch.tensor([device_seconds, e2e_seconds] + part_seconds, device=device, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    device_seconds, e2e_seconds = times.tolist()
+    device_seconds, e2e_seconds, *part_seconds = times.tolist()
 
     value = world * flops_per_step * args.steps / device_seconds / 1e12
     e2e_value = world * flops_per_step * e2e_steps / e2e_seconds / 1e12
-    kernel_seconds = device_seconds / args.steps
-    achieved = flops_per_step / kernel_seconds / 1e12
     peaks, peak_source = measured_peaks()
-    path = api.flash_kernel_name(batch, heads, seq, seq, dim)
-    if path.startswith("tcgen05"):
-        peak = float(peaks["bf16_tflops"])
-        roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                    "traffic": traffic_from_profiles(path),
-                    "peak_source": f"{peak_source} bf16_tflops (burst); the TF32 dense rate is half of it",
-                    "frac_of_tf32_dense": achieved / (peak / 2), "kernel": path}
-    else:
-        sm_mhz = (clocks or {}).get("sm_mhz") or float(peaks.get("sm_max_mhz", 1965.0))
-        peak = 148 * 128 * 2 * sm_mhz * 1e6 / 1e12
-        roofline = {"bound": "fp32-fma", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                    "traffic": traffic_from_profiles(path),
+    sm_mhz = (clocks or {}).get("sm_mhz") or float(peaks.get("sm_max_mhz", 1965.0))
+    fma_peak = 148 * 128 * 2 * sm_mhz * 1e6 / 1e12
+    if with_backward:
+        # The dominant kernel pair is the backward (exact FP32 SIMT); effective FLOPs per launch pair.
+        achieved = effective_backward / (part_seconds[1] / args.steps) / 1e12
+        roofline = {"bound": "fp32-fma", "achieved": achieved, "peak": fma_peak, "unit": "TFLOP/s", "frac": achieved / fma_peak,
+                    "traffic": traffic_from_profiles(f"simt-backward-d{dim}"),
                     "peak_source": "148 SMs x 128 FP32 lanes x 2 FLOP x median SM clock under load",
-                    "kernel": path}
+                    "kernel": f"simt-fp32 backward d{dim} (query-major delta+dQ, key-major dK/dV)",
+                    "flops": "effective: 8*d per active (query, key) pair"}
+    else:
+        achieved = effective_forward / (part_seconds[0] / args.steps) / 1e12
+        path = api.flash_kernel_name(batch, heads, seq, seq, dim) if dim == 32 else "simt-fp32-d64"
+        if path.startswith("tcgen05"):
+            peak = float(peaks["bf16_tflops"])
+            roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                        "traffic": traffic_from_profiles(path),
+                        "peak_source": f"{peak_source} bf16_tflops (burst); the TF32 dense rate is half of it",
+                        "frac_of_tf32_dense": achieved / (peak / 2), "kernel": path}
+        else:
+            roofline = {"bound": "fp32-fma", "achieved": achieved, "peak": fma_peak, "unit": "TFLOP/s", "frac": achieved / fma_peak,
+                        "traffic": traffic_from_profiles(path),
+                        "peak_source": "148 SMs x 128 FP32 lanes x 2 FLOP x median SM clock under load", "kernel": path}
 
     line = {
         "metric": METRIC,
@@ -337,19 +446,25 @@ def main() -> None:
         "warmup": args.warmup,
         "ms_per_step": device_seconds / args.steps * 1e3,
         "higher_is_better": True,
-        "scaling": "weak",
-        "vs_baseline": value / PUBLISHED_TFLOPS,
+        "scaling": "strong" if with_backward else "weak",
+        "vs_baseline": None if with_backward else value / PUBLISHED_TFLOPS,
         "dtype": "f32",
         "data": "synthetic N(0,1) from a seeded torch generator (rank-dependent seed)",
         "config": workload_config(args.workload, world),
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": d2h_bytes,
                 "steps": e2e_steps},
         "roofline": roofline,
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * launches_per_step,
         "clocks": clocks,
     }
+    if with_backward:
+        line["effective"] = {"value": world * effective_per_step * args.steps / device_seconds / 1e12, "unit": "TFLOP/s",
+                             "flops": "12*d per active (query, key) pair"}
+        line["parts"] = {"forward_ms": part_seconds[0] / args.steps * 1e3, "backward_ms": part_seconds[1] / args.steps * 1e3,
+                         "forward_effective_tflops": world * effective_forward * args.steps / part_seconds[0] / 1e12,
+                         "backward_effective_tflops": world * effective_backward * args.steps / part_seconds[1] / 1e12}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(WORKLOADS[args.workload])
+        line["cpu_baseline"] = cpu_baseline(spec)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
