@@ -24,6 +24,7 @@ LIBRARY = PACKAGE / "librocmkernels_attention.so"
 SOURCES = [
     "csrc/attention_abi.cu",
     "csrc/attention_tc.cu",
+    "csrc/attention_tc_backward.cu",
     "csrc/copy.cu",
     "csrc/device.cpp",
 ]

@@ -161,6 +161,12 @@ int attention_fp32_backward(const float *q, const float *k, const float *v, cons
         return cudaErrorInvalidValue;
     const AttentionParams p = backward_params(32, q, k, v, mask, output, lse, upstream, gradient_q, gradient_k, gradient_v,
                                               delta, batch, heads, queries, keys, radius, qs, ks, vs, os, us);
+    // The tensor-core backward when the tensors are TMA-addressable, else the exact SIMT pair
+    // (which the tuned entry always runs, so both stay reachable).
+    if (rk::tc::backward_supported(p)) {
+        const int status = rk::tc::launch_backward(p, stream);
+        if (status != rk::tc::kNotEligible) return status;
+    }
     return launch_backward<32>(p, stream, false);
 }
 
@@ -290,7 +296,9 @@ int attention_fp32_query_profile(const float *q, const float *k, const float *v,
 
 const char *rocmkernels_attention_build_info(void) { return rk::tc::build_info(); }
 
-unsigned int rocmkernels_attention_device_status(int clear) { return rk::tc::read_device_status(clear != 0); }
+unsigned int rocmkernels_attention_device_status(int clear) {
+    return rk::tc::read_device_status(clear != 0) | rk::tc::read_backward_status(clear != 0);
+}
 
 const char *rocmkernels_attention_flash_kernel(int batch, int heads, int queries, int keys, int head_width) {
     if (head_width != 32) return "simt-fp32-forward-d64";

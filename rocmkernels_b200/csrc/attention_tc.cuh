@@ -1,4 +1,4 @@
-// tcgen05 / TMEM tensor-core flash forward (sm_100a). Interface used by the entry points.
+// tcgen05 / TMEM tensor-core flash forward and backward (sm_100a). Interface used by the entry points.
 #pragma once
 
 #include "attention_common.cuh"
@@ -21,6 +21,15 @@ const char *build_info();
 unsigned int read_device_status(bool clear);
 // Name of the tensor-core flash kernel (for benchmarks and profiles).
 const char *kernel_name();
+
+// True when the tensor-core backward accepts the problem (head width 32, TMA-addressable q, k,
+// v, dO and 16-byte addressable O).
+bool backward_supported(const AttentionParams &p);
+// Launches the tensor-core backward: delta and dQ (query-major), then dK and dV (key-major),
+// ordered on `stream`; returns a cudaError_t value or kNotEligible.
+int launch_backward(const AttentionParams &p, cudaStream_t stream);
+// Device status word of the backward kernels (as read_device_status).
+unsigned int read_backward_status(bool clear);
 
 }  // namespace tc
 }  // namespace rk

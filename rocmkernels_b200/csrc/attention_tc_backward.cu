@@ -1,0 +1,653 @@
+// Tensor-core backward for head width 32 on sm_100a: tcgen05.mma (kind::f16) on split FP16
+// operands with TMEM accumulators, TMA-staged tiles.
+//
+// Replaces the reference's backward pair (attention_query<true> for delta and dQ,
+// Attention.hip:32-115, and attention_key_value, :117-169) with the same two-pass structure and
+// results: P_ij = exp(s_ij - max_i) / sum_i from the saved lse, dS = P (dP - delta),
+// dQ = scale dS K, dK = dS^T (scale Q), dV = P^T dO, delta_i = sum_c dO_ic O_ic; masked keys get
+// dK = dV = 0.
+//
+// One kernel template, two roles. A CTA owns 128 "rows" (TMEM lanes) and walks 64-wide "column"
+// tiles:
+//   query rows (pass 1): rows = queries, columns = key tiles.   S = Q K^T, dP = dO V^T,
+//                        X1 += dS K (dQ). Also writes delta.
+//   key rows   (pass 2): rows = keys, columns = query tiles.    S^T = K Q^T, dP^T = V dO^T,
+//                        X1 += dS^T Q (dK), X2 += P^T dO (dV).
+// Warps: 0-3 row warps (thread = row = TMEM lane), 4 TMA producer, 5 MMA issuer (whole warp,
+// elected issue), 6-7 split warps (FP16 conversion of each column tile). Two CTAs per SM
+// (256 TMEM columns each).
+//
+// Split FP16 operands as in the forward: every operand is scaled by a power of two so that its
+// largest magnitude lies in [2^14, 2^15) (row operands per row, column tiles per tile, P by
+// 2^14, dS per row and tile from the bound |dS| <= ||dO_i||_1 max|v| + |delta_i| (pass 1) or
+// ||v_j||_1 max|dO| + max|delta| (pass 2), which needs no extra pass over dS) and split into
+// x0 + x1: S = a0.b1 + a1.b0 + a0.b0 (6 MMAs N64), X = ds1.t0 + ds0.t0 + ds0.t1 per 16 columns
+// (12 MMAs N32). The per-tile products are folded into FP32 registers (the tensor core's
+// accumulation is not round-to-nearest), so the sums over column tiles are plain FP32.
+//
+// TMEM (256 columns), per row:
+//   a1 [x0 16 | x1 16] 0-31 | a2 32-63 | S then P 64-127 | dP then dS 128-191 | X1 192-223 | X2 224-255
+// P and dS overwrite S and dP chunk by chunk: 16 columns [x0 pairs 8 | x1 pairs 8], which
+// occupy exactly the 16 columns of scores the chunk has just read.
+#include "attention_tc.cuh"
+
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "tc_primitives.cuh"
+
+namespace rk {
+namespace tc {
+
+namespace {
+
+constexpr int kRows = 128;
+constexpr int kCols = 64;
+constexpr int kD = 32;
+constexpr int kStages = 2;
+constexpr int kThreads = 256;
+constexpr int kProducerWarp = 4;
+constexpr int kMmaWarp = 5;
+constexpr int kSplitWarp = 6;
+constexpr int kSplitThreads = 64;
+constexpr int kTileFloats = kCols * kD;     // 2048
+constexpr int kTileBytes = kTileFloats * 4;  // 8 KB
+constexpr uint32_t kTmemColumns = 256;
+constexpr uint32_t kColA1 = 0, kColA2 = 32, kColS = 64, kColDP = 128, kColX1 = 192, kColX2 = 224;
+constexpr uint32_t kIdescS = f16_instr_desc(128, 64);
+constexpr uint32_t kIdescX = f16_instr_desc(128, 32);
+constexpr uint64_t kDescStep = 2, kDescHalf = 4, kDescStage = kTileBytes / 16, kDescUpper = 32 * 128 / 16;
+
+template <bool kKeyRows>
+struct alignas(1024) Storage {
+    float raw1[kStages][kTileFloats];                  // TMA tile: K (query rows) or Q (key rows), 128B swizzle
+    float raw2[kStages][kTileFloats];                  // V or dO
+    uint32_t b1[kStages][kTileFloats];                 // raw1 rows as [x0 | x1] FP16 (B of S), 128B swizzle
+    uint32_t b2[kStages][kTileFloats];                 // raw2 rows as [x0 | x1] (B of dP)
+    uint32_t t1[kStages][kTileFloats];                 // raw1^T: rows 0-31 x0^T, 32-63 x1^T (B of X1)
+    uint32_t t2[kKeyRows ? kStages : 1][kTileFloats];  // raw2^T (B of X2, key rows only)
+    float col_offset[kStages][kCols];                  // key rows: 14 - max log2e - log2(sum) per query
+    float col_delta[kStages][kCols];                   // key rows: delta per query
+    uint32_t col_mask[kStages][2];                     // visible columns
+    int e1[kStages], e2[kStages];                      // tile scale exponents of raw1 (Q: of scale*Q) and raw2
+    float col_delta_max[kStages];                      // key rows: max |delta| of the tile
+    float split_max[2][2][3];                          // [tile parity][split warp]: max|raw1|, max|raw2|, max|delta|
+    int split_ok[2][2];                                // [tile parity][split warp]: its TMA wait succeeded
+    uint64_t full[kStages];                            // TMA bytes landed
+    uint64_t ready[kStages];                           // conversion done (64 arrivals)
+    uint64_t empty[kStages];                           // MMAs reading the stage finished (commit)
+    uint64_t s_full;                                   // S and dP in TMEM (commit)
+    uint64_t p_full;                                   // P / dS stored and the previous X folded (128 arrivals)
+    uint64_t x_done;                                   // X1 (X2) of the tile in TMEM (commit)
+    uint64_t rows_ready;                               // row operands in TMEM (128 arrivals)
+    uint64_t mma_done;                                 // every MMA finished (commit)
+    uint32_t tmem_base;
+};
+
+struct BackwardArgs {
+    AttentionParams p;
+    int blocks_per_head;  // row tiles per (batch, head)
+};
+
+__device__ __forceinline__ uint32_t lane_address(uint32_t base, int warp) {
+    return base + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+}
+
+// x' = x * scale split into x0 (11 significant bits, exact in FP16) and x1 = x' - x0.
+__device__ __forceinline__ void split_half(float x, float scale, float &x0, float &x1) {
+    const float scaled = x * scale;
+    x0 = round_tf32(scaled);
+    x1 = scaled - x0;
+}
+
+// Splits a 32-feature row (scaled by 2^exponent) into FP16 pairs: x0 pairs in `a`, x1 in `b`.
+__device__ __forceinline__ void split_row(const float (&x)[32], int exponent, float (&a)[16], float (&b)[16]) {
+    const float scale = exp2_int(exponent);
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+        float a0, a1, b0, b1;
+        split_half(x[2 * c], scale, a0, a1);
+        split_half(x[2 * c + 1], scale, b0, b1);
+        a[c] = __uint_as_float(pack_half2(a0, b0));
+        b[c] = __uint_as_float(pack_half2(a1, b1));
+    }
+}
+
+// Loads a 32-float row (zeros when !valid), multiplied by `scale`.
+__device__ __forceinline__ void load_row(const float *row, bool valid, float scale, float (&x)[32]) {
+    const float4 *r4 = reinterpret_cast<const float4 *>(row);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        const float4 v = valid ? __ldg(r4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+        x[4 * c] = v.x * scale;
+        x[4 * c + 1] = v.y * scale;
+        x[4 * c + 2] = v.z * scale;
+        x[4 * c + 3] = v.w * scale;
+    }
+}
+
+__device__ __forceinline__ float abs_max(const float (&x)[32]) {
+    float m = 0.f;
+#pragma unroll
+    for (int c = 0; c < 32; c += 2) m = max3(m, fabsf(x[c]), fabsf(x[c + 1]));
+    return m;
+}
+
+// X (N = 32) = x1.t0 + x0.t0 + x0.t1 over the 64 columns: A chunks of 16 columns at
+// `chunks` + 16 kk ([x0 pairs 8 | x1 pairs 8]), B = t (rows 0-31 x0^T, 32-63 x1^T). Commits to
+// `bar` when given. Warp-collective.
+__device__ __forceinline__ void issue_x(uint32_t d, uint32_t chunks, uint64_t t, uint64_t *bar) {
+    const uint64_t u = t + kDescUpper;
+    const uint32_t g1a[4] = {chunks, chunks + 8, chunks, chunks + 16};
+    const uint64_t g1b[4] = {t, t, u, t + kDescStep};
+    mma4_f16_ts_warp(d, g1a, g1b, kIdescX, 1);
+    const uint32_t g2a[4] = {chunks + 24, chunks + 16, chunks + 32, chunks + 40};
+    const uint64_t g2b[4] = {t + kDescStep, u + kDescStep, t + 2 * kDescStep, t + 2 * kDescStep};
+    mma4_f16_ts_warp(d, g2a, g2b, kIdescX, 0);
+    const uint32_t g3a[4] = {chunks + 32, chunks + 48, chunks + 56, chunks + 48};
+    const uint64_t g3b[4] = {u + 2 * kDescStep, t + 3 * kDescStep, t + 3 * kDescStep, u + 3 * kDescStep};
+    if (bar != nullptr)
+        mma4_f16_ts_commit_warp(d, g3a, g3b, kIdescX, 0, bar);
+    else
+        mma4_f16_ts_warp(d, g3a, g3b, kIdescX, 0);
+}
+
+// S (N = 64) = a0.b1 + a1.b0 + a0.b0 over the 32 features; a at TMEM `a` ([x0 16 | x1 16]),
+// b = [x0 | x1] rows. Warp-collective.
+__device__ __forceinline__ void issue_product(uint32_t d, uint32_t a, uint64_t b, uint64_t *bar) {
+    const uint32_t ga[4] = {a, a + 8, a + 16, a + 24};
+    const uint64_t gb[4] = {b + kDescHalf, b + kDescHalf + kDescStep, b, b + kDescStep};
+    mma4_f16_ts_warp(d, ga, gb, kIdescS, 1);
+    if (bar != nullptr)
+        mma2_f16_ts_commit_warp(d, a, a + 8, b, b + kDescStep, kIdescS, bar);
+    else
+        mma2_f16_ts_warp(d, a, a + 8, b, b + kDescStep, kIdescS);
+}
+
+// Splits 16 values (columns of a chunk) into FP16 pairs and stores them, without waiting, as
+// [x0 pairs 8 | x1 pairs 8] at TMEM `chunk` (the A layout of one K=16 step).
+__device__ __forceinline__ void store_split_chunk(uint32_t chunk, const float (&v)[16]) {
+    float q0[8], q1[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        const float x0 = __uint_as_float(__float_as_uint(v[2 * c]) & 0xFFFFE000u);
+        const float y0 = __uint_as_float(__float_as_uint(v[2 * c + 1]) & 0xFFFFE000u);
+        q0[c] = __uint_as_float(pack_half2(x0, y0));
+        q1[c] = __uint_as_float(pack_half2(v[2 * c] - x0, v[2 * c + 1] - y0));
+    }
+    tmem_store8x2_async(chunk, q0, chunk + 8, q1);
+}
+
+// acc1 += X1 * scale1 (and acc2 += X2 * scale2 for key rows), eight columns at a time.
+template <bool kKeyRows>
+__device__ __forceinline__ void fold_x(float (&acc1)[32], float (&acc2)[kKeyRows ? 32 : 1], uint32_t lanes, float scale1,
+                                       float scale2) {
+#pragma unroll
+    for (int quarter = 0; quarter < 4; ++quarter) {
+        float xa[8], xb[8];
+        tmem_load8x2(lanes + kColX1 + 8 * quarter, xa, lanes + (kKeyRows ? kColX2 : kColX1) + 8 * quarter, xb);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            acc1[8 * quarter + c] = fmaf(xa[c], scale1, acc1[8 * quarter + c]);
+            if constexpr (kKeyRows) acc2[8 * quarter + c] = fmaf(xb[c], scale2, acc2[8 * quarter + c]);
+        }
+    }
+}
+
+template <bool kKeyRows>
+__global__ void __launch_bounds__(kThreads, 2)
+        backward_kernel(const BackwardArgs args, const __grid_constant__ CUtensorMap tmap1,
+                        const __grid_constant__ CUtensorMap tmap2) {
+    using S = Storage<kKeyRows>;
+    extern __shared__ uint8_t shared_raw[];
+    S &s = *reinterpret_cast<S *>((reinterpret_cast<uintptr_t>(shared_raw) + 1023) & ~uintptr_t(1023));
+    const AttentionParams &p = args.p;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    int block = blockIdx.x;
+    const int row_tile = block % args.blocks_per_head;
+    block /= args.blocks_per_head;
+    const int h = block % p.heads;
+    const int b = block / p.heads;
+    const int r0 = row_tile * kRows;
+    const int row_count = kKeyRows ? p.keys : p.queries;
+    const int column_count = kKeyRows ? p.queries : p.keys;
+    int first, last;  // columns that can see (or be seen by) the row tile
+    key_window(r0, min(r0 + kRows, row_count), column_count, p.radius, first, last);
+    const int tiles = last > first ? (last - first + kCols - 1) / kCols : 0;
+    const long long query_base = (static_cast<long long>(b) * p.heads + h) * p.queries;
+    const long long key_base = (static_cast<long long>(b) * p.heads + h) * p.keys;
+    const unsigned char *mask = p.mask + static_cast<long long>(b) * p.keys;
+
+    if (warp == 0) {
+        tmem_alloc(&s.tmem_base, kTmemColumns);
+        tmem_relinquish();
+    }
+    if (threadIdx.x == kProducerWarp * 32) {
+        for (int i = 0; i < kStages; ++i) {
+            mbar_init(&s.full[i], 1);
+            mbar_init(&s.ready[i], kSplitThreads);
+            mbar_init(&s.empty[i], 1);
+        }
+        mbar_init(&s.s_full, 1);
+        mbar_init(&s.p_full, kRows);
+        mbar_init(&s.x_done, 1);
+        mbar_init(&s.rows_ready, kRows);
+        mbar_init(&s.mma_done, 1);
+        mbar_fence_init();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s.tmem_base;
+
+    if (warp == kProducerWarp) {
+        // ---------------------------------------------------------------- TMA producer
+        if (lane == 0) {
+            int issued = 0;
+            bool ok = true;
+            for (int j = 0; j < tiles && ok; ++j) {
+                const int stage = j % kStages;
+                if (j >= kStages) ok = mbar_wait(&s.empty[stage], ((j / kStages) - 1) & 1);
+                if (!ok) break;
+                mbar_arrive_expect_tx(&s.full[stage], 2 * kTileBytes);
+                tma_load_4d(s.raw1[stage], &tmap1, &s.full[stage], 0, first + j * kCols, h, b);
+                tma_load_4d(s.raw2[stage], &tmap2, &s.full[stage], 0, first + j * kCols, h, b);
+                ++issued;
+            }
+            if (!ok) {
+                for (int j = max(0, issued - kStages); j < issued; ++j) mbar_wait(&s.full[j % kStages], (j / kStages) & 1);
+            }
+        }
+    } else if (warp == kMmaWarp) {
+        // ---------------------------------------------------------------- MMA issuer
+        if (tiles > 0) {
+            const uint64_t b1_desc = sw128_descriptor(smem_u32(s.b1[0]));
+            const uint64_t b2_desc = sw128_descriptor(smem_u32(s.b2[0]));
+            const uint64_t t1_desc = sw128_descriptor(smem_u32(s.t1[0]));
+            const uint64_t t2_desc = sw128_descriptor(smem_u32(s.t2[0]));
+            bool ok = mbar_wait_warp(&s.rows_ready, 0);
+            for (int j = 0; j < tiles && ok; ++j) {
+                const int stage = j % kStages;
+                ok = mbar_wait_warp(&s.ready[stage], (j / kStages) & 1);
+                if (!ok) break;
+                tc_fence_after();
+                issue_product(tmem + kColS, tmem + kColA1, b1_desc + kDescStage * stage, nullptr);
+                issue_product(tmem + kColDP, tmem + kColA2, b2_desc + kDescStage * stage, &s.s_full);
+                ok = mbar_wait_warp(&s.p_full, j & 1);
+                if (!ok) break;
+                tc_fence_after();
+                if (kKeyRows) {
+                    issue_x(tmem + kColX1, tmem + kColDP, t1_desc + kDescStage * stage, nullptr);
+                    issue_x(tmem + kColX2, tmem + kColS, t2_desc + kDescStage * stage, &s.x_done);
+                } else {
+                    issue_x(tmem + kColX1, tmem + kColDP, t1_desc + kDescStage * stage, &s.x_done);
+                }
+                mma_commit_warp(&s.empty[stage]);
+            }
+            mma_commit_warp(&s.mma_done);
+            mbar_wait_warp(&s.mma_done, 0);
+        }
+    } else if (warp >= kSplitWarp) {
+        // ---------------------------------------------------------------- FP16 split
+        // Split warp w owns rows [32w, 32w + 32) of each column tile for the row layouts and the
+        // column statistics; for the transposed layouts lane = (group of 8 rows, chunk of 4
+        // features), as in the forward's V conversion.
+        const int w = warp - kSplitWarp;
+        const int row = 32 * w + lane;
+        const int group = 4 * w + (lane >> 3);
+        const int fchunk = lane & 7;
+        const float scale1 = kKeyRows ? p.scale : 1.f;  // Q enters the products as scale * Q
+        for (int j = 0; j < tiles; ++j) {
+            const int stage = j % kStages, parity = j & 1;
+            const bool landed = __all_sync(0xffffffffu, mbar_wait(&s.full[stage], (j / kStages) & 1));
+            const int column = first + j * kCols + row;
+            bool visible;
+            float delta_abs = 0.f;
+            if (kKeyRows) {  // column = query: visible if it exists and has a finite row max
+                const bool exists = column < last;
+                const float maximum = exists ? p.lse_in[(query_base + column) * 2] : -INFINITY;
+                const float total = exists ? p.lse_in[(query_base + column) * 2 + 1] : 0.f;
+                const float delta = exists ? p.delta[query_base + column] : 0.f;
+                visible = exists && maximum != -INFINITY;
+                s.col_offset[stage][row] = visible ? 14.f - maximum * kLog2e - __log2f(total) : -INFINITY;
+                s.col_delta[stage][row] = delta;
+                delta_abs = visible ? fabsf(delta) : 0.f;
+            } else {  // column = key
+                visible = column < last && mask[column] != 0;
+            }
+            const uint32_t bits = __ballot_sync(0xffffffffu, visible);
+            // Row-layout rows of key columns that are masked are zeroed (query rows only).
+            const bool keep_row = kKeyRows || ((bits >> lane) & 1);
+            const float4 *r1 = reinterpret_cast<const float4 *>(s.raw1[stage]);
+            const float4 *r2 = reinterpret_cast<const float4 *>(s.raw2[stage]);
+            float max1 = 0.f, max2 = 0.f;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                const float4 x = r1[row * 8 + (c ^ (row & 7))];
+                const float4 y = r2[row * 8 + (c ^ (row & 7))];
+                if (keep_row) {
+                    max1 = max3(max1, fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
+                    max2 = max3(max2, fmaxf(fabsf(y.x), fabsf(y.y)), fmaxf(fabsf(y.z), fabsf(y.w)));
+                }
+            }
+#pragma unroll
+            for (int offset = 16; offset; offset >>= 1) {
+                max1 = fmaxf(max1, __shfl_xor_sync(0xffffffffu, max1, offset));
+                max2 = fmaxf(max2, __shfl_xor_sync(0xffffffffu, max2, offset));
+                delta_abs = fmaxf(delta_abs, __shfl_xor_sync(0xffffffffu, delta_abs, offset));
+            }
+            if (lane == 0) {
+                s.split_max[parity][w][0] = max1;
+                s.split_max[parity][w][1] = max2;
+                s.split_max[parity][w][2] = delta_abs;
+                s.split_ok[parity][w] = landed;
+                s.col_mask[stage][w] = bits;
+            }
+            // One barrier per tile: the maxima are double-buffered by tile parity.
+            asm volatile("bar.sync 1, 64;" ::: "memory");
+            if (!(s.split_ok[parity][0] && s.split_ok[parity][1])) break;
+            const int e1 = fp16_scale_exponent(fmaxf(s.split_max[parity][0][0], s.split_max[parity][1][0]) * scale1);
+            const int e2 = fp16_scale_exponent(fmaxf(s.split_max[parity][0][1], s.split_max[parity][1][1]));
+            if (threadIdx.x == kSplitWarp * 32) {
+                s.e1[stage] = e1;
+                s.e2[stage] = e2;
+                s.col_delta_max[stage] = fmaxf(s.split_max[parity][0][2], s.split_max[parity][1][2]);
+            }
+            const float scale_1 = exp2_int(e1) * scale1, scale_2 = exp2_int(e2);
+            const uint32_t tile_bits0 = s.col_mask[stage][0], tile_bits1 = s.col_mask[stage][1];
+            // Row layouts: features 8m..8m+7 -> x0 chunk m, x1 chunk 4 + m (swizzled by row % 8).
+#pragma unroll
+            for (int which = 0; which < 2; ++which) {
+                const float4 *raw = which == 0 ? r1 : r2;
+                uint4 *dst = reinterpret_cast<uint4 *>(which == 0 ? s.b1[stage] : s.b2[stage]);
+                const float scale = which == 0 ? scale_1 : scale_2;
+#pragma unroll
+                for (int m = 0; m < 4; ++m) {
+                    float4 lo = raw[row * 8 + ((2 * m) ^ (row & 7))], hi = raw[row * 8 + ((2 * m + 1) ^ (row & 7))];
+                    if (!keep_row) lo = hi = make_float4(0.f, 0.f, 0.f, 0.f);
+                    const float x[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+                    float x0[8], x1[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) split_half(x[e], scale, x0[e], x1[e]);
+                    dst[row * 8 + (m ^ (row & 7))] = make_uint4(pack_half2(x0[0], x0[1]), pack_half2(x0[2], x0[3]),
+                                                                pack_half2(x0[4], x0[5]), pack_half2(x0[6], x0[7]));
+                    dst[row * 8 + ((4 + m) ^ (row & 7))] = make_uint4(pack_half2(x1[0], x1[1]), pack_half2(x1[2], x1[3]),
+                                                                      pack_half2(x1[4], x1[5]), pack_half2(x1[6], x1[7]));
+                }
+            }
+            // Transposed layouts: feature rows f (x0) and 32 + f (x1); rows 8g..8g+7 of the tile
+            // are 16-byte chunk g (swizzled by f % 8).
+#pragma unroll
+            for (int which = 0; which < (kKeyRows ? 2 : 1); ++which) {
+                const float4 *raw = which == 0 ? r1 : r2;
+                uint4 *dst = reinterpret_cast<uint4 *>(which == 0 ? s.t1[stage] : s.t2[kKeyRows ? stage : 0]);
+                const float scale = which == 0 ? scale_1 : scale_2;
+                float4 items[8];
+#pragma unroll
+                for (int r = 0; r < 8; ++r) {
+                    const int trow = 8 * group + r;
+                    items[r] = raw[trow * 8 + (fchunk ^ (trow & 7))];
+                    const uint32_t word = trow < 32 ? tile_bits0 : tile_bits1;
+                    if (!kKeyRows && !((word >> (trow & 31)) & 1)) items[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int f = 4 * fchunk + e;
+                    float x0[8], x1[8];
+#pragma unroll
+                    for (int r = 0; r < 8; ++r) {
+                        const float value = e == 0 ? items[r].x : e == 1 ? items[r].y : e == 2 ? items[r].z : items[r].w;
+                        split_half(value, scale, x0[r], x1[r]);
+                    }
+                    dst[f * 8 + (group ^ (f & 7))] = make_uint4(pack_half2(x0[0], x0[1]), pack_half2(x0[2], x0[3]),
+                                                                pack_half2(x0[4], x0[5]), pack_half2(x0[6], x0[7]));
+                    dst[(32 + f) * 8 + (group ^ (f & 7))] = make_uint4(pack_half2(x1[0], x1[1]), pack_half2(x1[2], x1[3]),
+                                                                       pack_half2(x1[4], x1[5]), pack_half2(x1[6], x1[7]));
+                }
+            }
+            fence_proxy_async_shared();
+            mbar_arrive(&s.ready[stage]);
+        }
+    } else {
+        // ---------------------------------------------------------------- row warps
+        const int r = threadIdx.x;  // row within the tile = TMEM lane
+        const int row = r0 + r;
+        const bool row_valid = row < row_count;
+        const uint32_t lanes = lane_address(tmem, warp);
+        bool row_active;  // the row takes part at all (query: finite max; key: visible)
+        float row_offset = -INFINITY, row_delta = 0.f, row_l1;
+        int ea1, ea2;
+        {
+            float x[32], y[32];
+            if (kKeyRows) {
+                row_active = row_valid && mask[row] != 0;
+                load_row(p.k.row(b, h, row_valid ? row : 0), row_active, 1.f, x);
+                load_row(p.v.row(b, h, row_valid ? row : 0), row_active, 1.f, y);
+                row_l1 = 0.f;
+#pragma unroll
+                for (int c = 0; c < 32; ++c) row_l1 += fabsf(y[c]);
+            } else {
+                const float maximum = row_valid ? p.lse_in[(query_base + row) * 2] : -INFINITY;
+                const float total = row_valid ? p.lse_in[(query_base + row) * 2 + 1] : 0.f;
+                row_active = row_valid && maximum != -INFINITY;
+                if (row_active) row_offset = 14.f - maximum * kLog2e - __log2f(total);
+                float o[32];
+                load_row(p.dout.row(b, h, row_valid ? row : 0), row_valid, 1.f, y);
+                load_row(p.o_in.row(b, h, row_valid ? row : 0), row_valid, 1.f, o);
+                float delta = 0.f;
+                row_l1 = 0.f;
+#pragma unroll
+                for (int c = 0; c < 32; ++c) {
+                    delta = fmaf(y[c], o[c], delta);
+                    row_l1 += fabsf(y[c]);
+                }
+                row_delta = delta;
+                if (row_valid) p.delta[query_base + row] = delta;
+                load_row(p.q.row(b, h, row_valid ? row : 0), row_valid, p.scale, x);
+            }
+            ea1 = fp16_scale_exponent(abs_max(x));
+            ea2 = fp16_scale_exponent(abs_max(y));
+            float a0[16], a1[16];
+            split_row(x, ea1, a0, a1);
+            tmem_store16x2(lanes + kColA1, a0, lanes + kColA1 + 16, a1);
+            split_row(y, ea2, a0, a1);
+            tmem_store16x2(lanes + kColA2, a0, lanes + kColA2 + 16, a1);
+            tc_fence_before();
+            mbar_arrive(&s.rows_ready);
+        }
+
+        float acc1[32], acc2[kKeyRows ? 32 : 1];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) acc1[c] = 0.f;
+#pragma unroll
+        for (int c = 0; c < (kKeyRows ? 32 : 1); ++c) acc2[c] = 0.f;
+        float pending_scale1 = 0.f, pending_scale2 = 0.f;  // 2^-(scales) of the last tile's X1, X2
+        bool ok = true;
+        for (int j = 0; j < tiles && ok; ++j) {
+            const int stage = j % kStages;
+            ok = __all_sync(0xffffffffu, mbar_wait(&s.s_full, j & 1) && mbar_wait(&s.ready[stage], (j / kStages) & 1));
+            if (!ok) break;
+            tc_fence_after();
+            const int c0 = first + j * kCols;
+            const int e1 = s.e1[stage], e2 = s.e2[stage];
+            const float slope = kLog2e * exp2_int(-(ea1 + e1));  // TMEM S -> log2e * score
+            const float dp_scale = exp2_int(-(ea2 + e2));        // TMEM dP -> dP
+            // |dS| <= ||row operand 2||_1 * max|column operand 2| + |delta| (P <= 1)
+            const float bound = row_l1 * exp2_int(15 - e2) + (kKeyRows ? s.col_delta_max[stage] : fabsf(row_delta));
+            const int g = fp16_scale_exponent(bound);
+            const float to_ds = exp2_int(g - 14);  // P' (= 2^14 P) * (dP - delta) * to_ds = 2^g dS
+            const float w_scale = dp_scale * to_ds;
+            uint64_t active = row_active ? (static_cast<uint64_t>(s.col_mask[stage][0]) |
+                                            (static_cast<uint64_t>(s.col_mask[stage][1]) << 32))
+                                         : 0ull;
+            if (p.radius >= 0) {
+                const int lo_col = max(0, row - p.radius - c0), hi_col = min(kCols - 1, row + p.radius - c0);
+                active &= lo_col > hi_col ? 0ull : ((~0ull) >> (63 - (hi_col - lo_col))) << lo_col;
+            }
+            const bool all_active = __all_sync(0xffffffffu, active == ~0ull);
+#pragma unroll 1
+            for (int chunk = 0; chunk < 4; ++chunk) {  // rolled: keeps one chunk's values live
+                float sv[16], dv[16];  // scores, then P'; dP, then dS'
+                tmem_load16x2(lanes + kColS + 16 * chunk, sv, lanes + kColDP + 16 * chunk, dv);
+#pragma unroll
+                for (int c = 0; c < 16; ++c) {
+                    const int col = 16 * chunk + c;
+                    const float offset = kKeyRows ? s.col_offset[stage][col] : row_offset;
+                    const float delta = kKeyRows ? s.col_delta[stage][col] : row_delta;
+                    float pv = fast_exp2(fmaf(sv[c], slope, offset));
+                    if (!all_active) pv = (active >> col) & 1 ? pv : 0.f;
+                    sv[c] = pv;
+                    dv[c] = pv * fmaf(dv[c], w_scale, -delta * to_ds);
+                }
+                store_split_chunk(lanes + kColDP + 16 * chunk, dv);
+                if (kKeyRows) store_split_chunk(lanes + kColS + 16 * chunk, sv);
+            }
+            // Fold the previous tile's X before the P(j)/dS(j) arrival lets the MMA warp
+            // overwrite it.
+            if (j > 0) {
+                ok = __all_sync(0xffffffffu, mbar_wait(&s.x_done, (j - 1) & 1));
+                if (!ok) {
+                    tmem_wait_store();
+                    break;
+                }
+                tc_fence_after();
+                fold_x<kKeyRows>(acc1, acc2, lanes, pending_scale1, pending_scale2);
+            }
+            tmem_wait_store();
+            tc_fence_before();
+            mbar_arrive(&s.p_full);
+            // X1 = 2^(g + e1) * (dS . column operand 1); X2 = 2^(14 + e2) * (P . dO)
+            pending_scale1 = exp2_int(-(g + e1));
+            pending_scale2 = exp2_int(-(14 + e2));
+        }
+        if (tiles > 0 && ok) {
+            ok = __all_sync(0xffffffffu, mbar_wait(&s.x_done, (tiles - 1) & 1));
+            tc_fence_after();
+            if (ok) fold_x<kKeyRows>(acc1, acc2, lanes, pending_scale1, pending_scale2);
+        }
+        // Outputs (packed [batch][heads][tokens][32]); a failed wait leaves NaN.
+        if (row_valid) {
+            const float bad = ok ? 1.f : NAN;
+            if (kKeyRows) {
+                float4 *dk = reinterpret_cast<float4 *>(p.dk + (key_base + row) * kD);
+                float4 *dv = reinterpret_cast<float4 *>(p.dv + (key_base + row) * kD);
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    if (row_active) {
+                        dk[c] = make_float4(acc1[4 * c] * bad, acc1[4 * c + 1] * bad, acc1[4 * c + 2] * bad, acc1[4 * c + 3] * bad);
+                        dv[c] = make_float4(acc2[(4 * c) % (kKeyRows ? 32 : 1)] * bad, acc2[(4 * c + 1) % (kKeyRows ? 32 : 1)] * bad,
+                                            acc2[(4 * c + 2) % (kKeyRows ? 32 : 1)] * bad, acc2[(4 * c + 3) % (kKeyRows ? 32 : 1)] * bad);
+                    } else {
+                        dk[c] = dv[c] = make_float4(0.f, 0.f, 0.f, 0.f);  // masked key: exactly zero
+                    }
+                }
+            } else {
+                float4 *dq = reinterpret_cast<float4 *>(p.dq + (query_base + row) * kD);
+                const float scale = p.scale * bad;
+#pragma unroll
+                for (int c = 0; c < 8; ++c)
+                    dq[c] = make_float4(acc1[4 * c] * scale, acc1[4 * c + 1] * scale, acc1[4 * c + 2] * scale, acc1[4 * c + 3] * scale);
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemColumns);
+    }
+}
+
+// ---- host side ----------------------------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_function() {
+    static PFN_cuTensorMapEncodeTiled_v12000 function = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *pointer = nullptr;
+        cudaDriverEntryPointQueryResult query;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &pointer, cudaEnableDefault, &query) == cudaSuccess &&
+            query == cudaDriverEntryPointSuccess)
+            function = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(pointer);
+    });
+    return function;
+}
+
+// [batch][heads][tokens][32] FP32 with the given element strides; box = 32 features x 64 tokens.
+bool make_tensor_map(CUtensorMap *map, const Tensor &t, int batch, int heads, int tokens) {
+    auto encode = encode_function();
+    if (encode == nullptr) return false;
+    const cuuint64_t dims[4] = {kD, static_cast<cuuint64_t>(tokens), static_cast<cuuint64_t>(heads), static_cast<cuuint64_t>(batch)};
+    const cuuint64_t strides[3] = {static_cast<cuuint64_t>(t.st) * 4, static_cast<cuuint64_t>(t.sh) * 4,
+                                   static_cast<cuuint64_t>(t.sb) * 4};
+    const cuuint32_t box[4] = {kD, static_cast<cuuint32_t>(kCols), 1, 1};
+    const cuuint32_t element_strides[4] = {1, 1, 1, 1};
+    return encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float *>(t.data), dims, strides, box, element_strides,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool tma_addressable(const Tensor &t) {
+    const long long limit = 1ll << 38;
+    return t.st > 0 && t.sh > 0 && t.sb > 0 && t.st % 4 == 0 && t.sh % 4 == 0 && t.sb % 4 == 0 && t.st < limit &&
+           t.sh < limit && t.sb < limit && (reinterpret_cast<uintptr_t>(t.data) & 15u) == 0;
+}
+
+bool rows_addressable(const Tensor &t) {
+    return t.st % 4 == 0 && t.sh % 4 == 0 && t.sb % 4 == 0 && (reinterpret_cast<uintptr_t>(t.data) & 15u) == 0;
+}
+
+template <bool kKeyRows>
+constexpr int shared_bytes() {
+    return static_cast<int>(sizeof(Storage<kKeyRows>)) + 1024;
+}
+static_assert(shared_bytes<false>() <= 113 * 1024 && shared_bytes<true>() <= 113 * 1024, "two CTAs per SM");
+
+template <bool kKeyRows>
+int launch_pass(const AttentionParams &p, const CUtensorMap &map1, const CUtensorMap &map2, cudaStream_t stream) {
+    cudaError_t status = prepare_kernel<backward_kernel<kKeyRows>>(shared_bytes<kKeyRows>());
+    if (status != cudaSuccess) return status;
+    BackwardArgs args{};
+    args.p = p;
+    const int rows = kKeyRows ? p.keys : p.queries;
+    args.blocks_per_head = (rows + kRows - 1) / kRows;
+    const unsigned blocks = static_cast<unsigned>(args.blocks_per_head) * static_cast<unsigned>(p.heads) * static_cast<unsigned>(p.batch);
+    backward_kernel<kKeyRows><<<blocks, kThreads, shared_bytes<kKeyRows>(), stream>>>(args, map1, map2);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+bool backward_supported(const AttentionParams &p) {
+    return tma_addressable(p.q) && tma_addressable(p.k) && tma_addressable(p.v) && tma_addressable(p.dout) &&
+           rows_addressable(p.o_in) && (reinterpret_cast<uintptr_t>(p.dq) & 15u) == 0 &&
+           (reinterpret_cast<uintptr_t>(p.dk) & 15u) == 0 && (reinterpret_cast<uintptr_t>(p.dv) & 15u) == 0;
+}
+
+int launch_backward(const AttentionParams &p, cudaStream_t stream) {
+    CUtensorMap map_k, map_v, map_q, map_dout;
+    if (!make_tensor_map(&map_k, p.k, p.batch, p.heads, p.keys) || !make_tensor_map(&map_v, p.v, p.batch, p.heads, p.keys) ||
+        !make_tensor_map(&map_q, p.q, p.batch, p.heads, p.queries) ||
+        !make_tensor_map(&map_dout, p.dout, p.batch, p.heads, p.queries))
+        return kNotEligible;
+    const int status = launch_pass<false>(p, map_k, map_v, stream);  // delta, dQ
+    if (status != cudaSuccess) return status;
+    return launch_pass<true>(p, map_q, map_dout, stream);  // dK, dV (reads delta)
+}
+
+unsigned int read_backward_status(bool clear) {
+    unsigned int value = 0;
+    if (cudaMemcpyFromSymbol(&value, g_device_status, sizeof(value)) != cudaSuccess) return ~0u;
+    if (clear && value != 0) {
+        const unsigned int zero = 0;
+        cudaMemcpyToSymbol(g_device_status, &zero, sizeof(zero));
+    }
+    return value;
+}
+
+}  // namespace tc
+}  // namespace rk

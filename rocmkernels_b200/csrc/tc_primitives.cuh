@@ -124,6 +124,23 @@ __device__ __forceinline__ void tmem_load16x2(uint32_t a, float (&va)[16], uint3
     }
 }
 
+// 8 columns at a and 8 columns at b with one wait.
+__device__ __forceinline__ void tmem_load8x2(uint32_t a, float (&va)[8], uint32_t b, float (&vb)[8]) {
+    uint32_t r[16];
+    asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%16];\n\t"
+            "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%8,%9,%10,%11,%12,%13,%14,%15}, [%17];\n\t"
+            "tcgen05.wait::ld.sync.aligned;"
+            : RK_R8(0), RK_R8(8)
+            : "r"(a), "r"(b)
+            : "memory");
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        va[i] = __uint_as_float(r[i]);
+        vb[i] = __uint_as_float(r[8 + i]);
+    }
+}
+
 // 16 columns at a, 16 columns at b and the single column c with one wait.
 __device__ __forceinline__ void tmem_load16x2_1(uint32_t a, float (&va)[16], uint32_t b, float (&vb)[16], uint32_t c,
                                                 float &vc) {
@@ -274,6 +291,18 @@ __device__ __forceinline__ void mma2_f16_ts_commit_warp(uint32_t d, uint32_t a0,
             "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%2], %4, %5, rest;\n\t"
             "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%6];\n\t}" ::"r"(d),
             "r"(a0), "r"(a1), "l"(b0), "l"(b1), "r"(idesc), "r"(smem_u32(bar))
+            : "memory");
+}
+
+// Warp-collective: two accumulating kind::f16 MMAs, one elected sequence (no commit).
+__device__ __forceinline__ void mma2_f16_ts_warp(uint32_t d, uint32_t a0, uint32_t a1, uint64_t b0, uint64_t b1, uint32_t idesc) {
+    asm volatile(
+            "{\n\t.reg .pred e, rest;\n\t"
+            "elect.sync _|e, 0xffffffff;\n\t"
+            "setp.eq.b32 rest, %5, %5;\n\t"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %3, %5, rest;\n\t"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%2], %4, %5, rest;\n\t}" ::"r"(d),
+            "r"(a0), "r"(a1), "l"(b0), "l"(b1), "r"(idesc)
             : "memory");
 }
 
