@@ -61,6 +61,8 @@ WORKLOADS = {
                                                       "lengths U[1024,2048]"),
     "c5_fwd_bwd_b64h12s4096d32": dict(batch=64, heads=12, seq=4096, dim=32, radius=-1, lengths=None, backward=True,
                                       description="BASELINE configs[4]: forward+backward B64 H12 S4096 d32, full attention"),
+    "fwd_bwd_b4h12s4096d32": dict(batch=4, heads=12, seq=4096, dim=32, radius=-1, lengths=None, backward=True,
+                                  description="profiling case: C5's shape at B=4 (inputs above L2, a few hundred MB)"),
 }
 DEFAULT_WORKLOAD = "flash_fwd_b8h3s1024d32"
 PUBLISHED_TFLOPS = 3.36  # flash fwd d32, same FLOPs (B2 H12 L1024), RX 6700 (README.md:63)
