@@ -154,6 +154,20 @@ ROCMKERNELS_C_EXPORT int attention_fp32_query_profile(const float *q, const floa
         int tuning, RocmKernelsStrides qs, RocmKernelsStrides ks, RocmKernelsStrides vs, RocmKernelsStrides os,
         RocmKernelsStrides us, RocmKernelsStream stream);
 
+/* 32-wide backward without a delta argument, for callers that cannot supply or allocate the
+ * per-row delta scratch (an interface exposing only dQ/dK/dV, or a step whose device memory is
+ * fixed before it runs): the same kernels and results as attention_fp32_backward, with delta kept
+ * in a 16 MiB array inside the library, so the call allocates nothing. Limit: batch * heads *
+ * queries <= 4194304, else error 1 (cudaErrorInvalidValue). Calls on one device share that
+ * array, so they must not overlap (issue them on one stream per device, or order them). The first
+ * call on a device looks up the array's device address (cudaGetSymbolAddress) and should come
+ * before any stream capture. No counterpart in the reference. */
+ROCMKERNELS_C_EXPORT int attention_fp32_backward_static_delta(const float *q, const float *k, const float *v,
+        const bool *mask, const float *output, const float *lse, const float *upstream, float *gradient_q,
+        float *gradient_k, float *gradient_v, int batch, int heads, int queries, int keys, int radius,
+        RocmKernelsStrides qs, RocmKernelsStrides ks, RocmKernelsStrides vs, RocmKernelsStrides os,
+        RocmKernelsStrides us, RocmKernelsStream stream);
+
 /* Library build identification: a static string naming the architecture the kernels were
  * compiled for ("sm_100a") and the kernel families present. No counterpart in the reference. */
 ROCMKERNELS_C_EXPORT const char *rocmkernels_attention_build_info(void);

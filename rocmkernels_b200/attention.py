@@ -88,6 +88,8 @@ def lib() -> ctypes.CDLL:
         library.rocmkernels_attention_flash_kernel.restype = ctypes.c_char_p
         library.rocmkernels_attention_device_status.argtypes = [ctypes.c_int]
         library.rocmkernels_attention_device_status.restype = ctypes.c_uint
+        library.attention_fp32_backward_static_delta.argtypes = [_POINTER] * 10 + [_INT] * 5 + [Strides] * 5 + [_POINTER]
+        library.attention_fp32_backward_static_delta.restype = ctypes.c_int
         _lib = library
     return _lib
 
@@ -200,6 +202,14 @@ def attention_fp32_backward(q, k, v, mask, output, lse, upstream, gq, gk, gv, de
                             os_, us, stream=None):
     return _backward("attention_fp32_backward", q, k, v, mask, output, lse, upstream, gq, gk, gv, delta, batch, heads, queries, keys,
                      radius, qs, ks, vs, os_, us, stream)
+
+
+def attention_fp32_backward_static_delta(q, k, v, mask, output, lse, upstream, gq, gk, gv, batch, heads, queries, keys, radius,
+                                         qs, ks, vs, os_, us, stream=None):
+    """attention_fp32_backward with the delta scratch held by the library (no delta argument)."""
+    return _call("attention_fp32_backward_static_delta", ptr(q), ptr(k), ptr(v), ptr(mask), ptr(output), ptr(lse),
+                 ptr(upstream), ptr(gq), ptr(gk), ptr(gv), batch, heads, queries, keys, radius, strides(qs), strides(ks),
+                 strides(vs), strides(os_), strides(us), _stream(stream))
 
 
 def attention_fp32_backward_tiled(q, k, v, mask, output, lse, upstream, gq, gk, gv, delta, batch, heads, queries, keys, radius, qs, ks,

@@ -8,6 +8,8 @@
 #include "attention_simt.cuh"
 #include "attention_tc.cuh"
 
+#include <mutex>
+
 namespace {
 
 using rk::AttentionParams;
@@ -130,6 +132,36 @@ int launch_flash(const AttentionParams &p, cudaStream_t stream) {
 
 bool known_group(int group) {
     return group == 2 || group == 4 || group == 8 || group == 84 || group == 164 || group == 1164 || group == 1264;
+}
+
+// Delta scratch for attention_fp32_backward_static_delta. Some callers cannot hand the backward
+// a delta buffer: an autograd interface that exposes only dQ, dK and dV, or a training step whose
+// device memory is planned up front and must not grow once it runs. For them the per-row delta
+// lives in this file-scope array of the library instead of caller memory, so the call allocates
+// nothing. Nothing in it has to start at zero: the query-major pass writes every entry it covers
+// before the key-major pass reads it. Calls on one device share it, so they must not overlap.
+constexpr long long kStaticDeltaRows = 1ll << 22;  // batch * heads * queries <= 4,194,304 (16 MiB)
+static __device__ __align__(256) float g_static_delta[kStaticDeltaRows];
+
+// Device address of g_static_delta on the current device, looked up once per device (with that
+// device current) by its first call.
+cudaError_t static_delta_address(float **address) {
+    constexpr int kDevices = 64;
+    static std::mutex lock;
+    static float *addresses[kDevices] = {};
+    int device = 0;
+    cudaError_t status = cudaGetDevice(&device);
+    if (status != cudaSuccess) return status;
+    if (device < 0 || device >= kDevices) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> guard(lock);
+    if (addresses[device] == nullptr) {
+        void *pointer = nullptr;
+        status = cudaGetSymbolAddress(&pointer, g_static_delta);
+        if (status != cudaSuccess) return status;
+        addresses[device] = static_cast<float *>(pointer);
+    }
+    *address = addresses[device];
+    return cudaSuccess;
 }
 
 }  // namespace
@@ -314,6 +346,21 @@ const char *rocmkernels_attention_flash_kernel(int batch, int heads, int queries
     p.v = p.k;
     p.o = rk::OutTensor{nullptr, p.q.sb, p.q.sh, p.q.st};
     return rk::tc::flash_supported(p) ? rk::tc::kernel_name() : "simt-fp32-forward-d32";
+}
+
+int attention_fp32_backward_static_delta(const float *q, const float *k, const float *v, const bool *mask,
+                                         const float *output, const float *lse, const float *upstream, float *gradient_q,
+                                         float *gradient_k, float *gradient_v, int batch, int heads, int queries, int keys,
+                                         int radius, RocmKernelsStrides qs, RocmKernelsStrides ks, RocmKernelsStrides vs,
+                                         RocmKernelsStrides os, RocmKernelsStrides us, RocmKernelsStream stream) {
+    if (batch > 0 && heads > 0 && queries > 0 &&
+        static_cast<long long>(batch) * heads * queries > kStaticDeltaRows)
+        return cudaErrorInvalidValue;
+    float *delta = nullptr;
+    const cudaError_t status = static_delta_address(&delta);
+    if (status != cudaSuccess) return status;
+    return attention_fp32_backward(q, k, v, mask, output, lse, upstream, gradient_q, gradient_k, gradient_v, delta, batch,
+                                   heads, queries, keys, radius, qs, ks, vs, os, us, stream);
 }
 
 }  // extern "C"
