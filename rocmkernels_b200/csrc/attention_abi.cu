@@ -196,7 +196,7 @@ int attention_fp32_backward(const float *q, const float *k, const float *v, cons
     // The tensor-core backward when the tensors are TMA-addressable, else the exact SIMT pair
     // (which the tuned entry always runs, so both stay reachable).
     if (rk::tc::backward_supported(p)) {
-        const int status = rk::tc::launch_backward(p, stream);
+        const int status = rk::tc::launch_backward(p, 32, stream);
         if (status != rk::tc::kNotEligible) return status;
     }
     return launch_backward<32>(p, stream, false);
@@ -289,6 +289,10 @@ int attention64_fp32_backward(const float *q, const float *k, const float *v, co
         return cudaErrorInvalidValue;
     const AttentionParams p = backward_params(64, q, k, v, mask, output, lse, upstream, gradient_q, gradient_k, gradient_v,
                                               delta, batch, heads, queries, keys, radius, qs, ks, vs, os, us);
+    if (rk::tc::backward_supported(p)) {  // else (strides not TMA-addressable) the exact SIMT pair
+        const int status = rk::tc::launch_backward(p, 64, stream);
+        if (status != rk::tc::kNotEligible) return status;
+    }
     return launch_backward<64>(p, stream, false);
 }
 

@@ -22,12 +22,12 @@ unsigned int read_device_status(bool clear);
 // Name of the tensor-core flash kernel (for benchmarks and profiles).
 const char *kernel_name();
 
-// True when the tensor-core backward accepts the problem (head width 32, TMA-addressable q, k,
-// v, dO and 16-byte addressable O).
+// True when the tensor-core backward accepts the tensors (TMA-addressable q, k, v, dO; 16-byte
+// addressable O and gradients).
 bool backward_supported(const AttentionParams &p);
-// Launches the tensor-core backward: delta and dQ (query-major), then dK and dV (key-major),
-// ordered on `stream`; returns a cudaError_t value or kNotEligible.
-int launch_backward(const AttentionParams &p, cudaStream_t stream);
+// Launches the tensor-core backward for head width 32 or 64: delta and dQ (query-major), then
+// dK and dV (key-major), ordered on `stream`; returns a cudaError_t value or kNotEligible.
+int launch_backward(const AttentionParams &p, int head_width, cudaStream_t stream);
 // Device status word of the backward kernels (as read_device_status).
 unsigned int read_backward_status(bool clear);
 

@@ -44,44 +44,61 @@ namespace {
 
 constexpr int kRows = 128;
 constexpr int kCols = 64;
-constexpr int kD = 32;
 constexpr int kStages = 2;
 constexpr int kThreads = 256;
 constexpr int kProducerWarp = 4;
 constexpr int kMmaWarp = 5;
 constexpr int kSplitWarp = 6;
 constexpr int kSplitThreads = 64;
-constexpr int kTileFloats = kCols * kD;     // 2048
-constexpr int kTileBytes = kTileFloats * 4;  // 8 KB
-constexpr uint32_t kTmemColumns = 256;
-constexpr uint32_t kColA1 = 0, kColA2 = 32, kColS = 64, kColDP = 128, kColX1 = 192, kColX2 = 224;
+constexpr int kBoxFloats = kCols * 32;     // one TMA box: 64 rows x 32 features (128 B), 8 KB
+constexpr int kBoxBytes = kBoxFloats * 4;
 constexpr uint32_t kIdescS = f16_instr_desc(128, 64);
-constexpr uint32_t kIdescX = f16_instr_desc(128, 32);
-constexpr uint64_t kDescStep = 2, kDescHalf = 4, kDescStage = kTileBytes / 16, kDescUpper = 32 * 128 / 16;
+constexpr uint64_t kDescStep = 2;  // one K=16 step of FP16 = 32 bytes
 
-template <bool kKeyRows>
+// Layout constants for head width D (32 or 64).
+template <int D>
+struct Geometry {
+    static constexpr int kBoxes = D / 32;                   // TMA boxes per tile row
+    static constexpr int kRawFloats = kBoxes * kBoxFloats;   // FP32 tile: kBoxes boxes of 64 x 32
+    static constexpr int kRowWords = 64 * D;                // row layout: 64 rows x [x0 | x1] (2 D fp16 each)
+    static constexpr int kTWords = 2 * D * 32;              // transposed: 2 D rows x 64 fp16
+    static constexpr int kKSteps = D / 16;                  // K=16 steps over the features
+    // Row layout: D = 32 keeps [x0 | x1] in one 128-byte row; D = 64 uses an x0 tile and an x1
+    // tile of 64 rows x 128 bytes each. Descriptor offset (16-byte units) of the x1 part.
+    static constexpr uint64_t kDescX1 = D == 32 ? 4 : kBoxBytes / 16;
+    static constexpr uint64_t kDescUpper = D * 128 / 16;   // transposed: x1^T rows start
+    // TMEM columns
+    static constexpr uint32_t kColA1 = 0, kColA2 = D, kColS = 2 * D, kColDP = 2 * D + 64, kColX1 = 2 * D + 128,
+                              kColX2 = 3 * D + 128;
+    static constexpr uint32_t kTmemColumns = D == 32 ? 256 : 512;
+    static constexpr int kCtasPerSm = D == 32 ? 2 : 1;
+    static constexpr uint32_t kIdescX = f16_instr_desc(128, D);
+};
+
+template <int D, bool kKeyRows>
 struct alignas(1024) Storage {
-    float raw1[kStages][kTileFloats];                  // TMA tile: K (query rows) or Q (key rows), 128B swizzle
-    float raw2[kStages][kTileFloats];                  // V or dO
-    uint32_t b1[kStages][kTileFloats];                 // raw1 rows as [x0 | x1] FP16 (B of S), 128B swizzle
-    uint32_t b2[kStages][kTileFloats];                 // raw2 rows as [x0 | x1] (B of dP)
-    uint32_t t1[kStages][kTileFloats];                 // raw1^T: rows 0-31 x0^T, 32-63 x1^T (B of X1)
-    uint32_t t2[kKeyRows ? kStages : 1][kTileFloats];  // raw2^T (B of X2, key rows only)
-    float col_offset[kStages][kCols];                  // key rows: 14 - max log2e - log2(sum) per query
-    float col_delta[kStages][kCols];                   // key rows: delta per query
-    uint32_t col_mask[kStages][2];                     // visible columns
-    int e1[kStages], e2[kStages];                      // tile scale exponents of raw1 (Q: of scale*Q) and raw2
-    float col_delta_max[kStages];                      // key rows: max |delta| of the tile
-    float split_max[2][2][3];                          // [tile parity][split warp]: max|raw1|, max|raw2|, max|delta|
-    int split_ok[2][2];                                // [tile parity][split warp]: its TMA wait succeeded
-    uint64_t full[kStages];                            // TMA bytes landed
-    uint64_t ready[kStages];                           // conversion done (64 arrivals)
-    uint64_t empty[kStages];                           // MMAs reading the stage finished (commit)
-    uint64_t s_full;                                   // S and dP in TMEM (commit)
-    uint64_t p_full;                                   // P / dS stored and the previous X folded (128 arrivals)
-    uint64_t x_done;                                   // X1 (X2) of the tile in TMEM (commit)
-    uint64_t rows_ready;                               // row operands in TMEM (128 arrivals)
-    uint64_t mma_done;                                 // every MMA finished (commit)
+    using G = Geometry<D>;
+    float raw1[kStages][G::kRawFloats];                    // TMA tile: K (query rows) or Q (key rows), 128B swizzle
+    float raw2[kStages][G::kRawFloats];                    // V or dO
+    uint32_t b1[kStages][G::kRowWords];                    // raw1 rows as split FP16 (B of S), 128B swizzle
+    uint32_t b2[kStages][G::kRowWords];                    // raw2 rows (B of dP)
+    uint32_t t1[kStages][G::kTWords];                      // raw1^T: rows 0..D-1 x0^T, D..2D-1 x1^T (B of X1)
+    uint32_t t2[kKeyRows ? kStages : 1][G::kTWords];       // raw2^T (B of X2, key rows only)
+    float col_offset[kStages][kCols];                      // key rows: 14 - max log2e - log2(sum) per query
+    float col_delta[kStages][kCols];                       // key rows: delta per query
+    uint32_t col_mask[kStages][2];                         // visible columns
+    int e1[kStages], e2[kStages];                          // tile scale exponents of raw1 (Q: of scale*Q) and raw2
+    float col_delta_max[kStages];                          // key rows: max |delta| of the tile
+    float split_max[2][2][3];                              // [tile parity][split warp]: max|raw1|, max|raw2|, max|delta|
+    int split_ok[2][2];                                    // [tile parity][split warp]: its TMA wait succeeded
+    uint64_t full[kStages];                                // TMA bytes landed
+    uint64_t ready[kStages];                               // conversion done (64 arrivals)
+    uint64_t empty[kStages];                               // MMAs reading the stage finished (commit)
+    uint64_t s_full;                                       // S and dP in TMEM (commit)
+    uint64_t p_full;                                       // P / dS stored and the previous X folded (128 arrivals)
+    uint64_t x_done;                                       // X1 (X2) of the tile in TMEM (commit)
+    uint64_t rows_ready;                                   // row operands in TMEM (128 arrivals)
+    uint64_t mma_done;                                     // every MMA finished (commit)
     uint32_t tmem_base;
 };
 
@@ -101,24 +118,32 @@ __device__ __forceinline__ void split_half(float x, float scale, float &x0, floa
     x1 = scaled - x0;
 }
 
-// Splits a 32-feature row (scaled by 2^exponent) into FP16 pairs: x0 pairs in `a`, x1 in `b`.
-__device__ __forceinline__ void split_row(const float (&x)[32], int exponent, float (&a)[16], float (&b)[16]) {
+// Splits a D-feature row (scaled by 2^exponent) and stores it to TMEM at `column` as FP16 pairs:
+// x0 pairs in columns [0, D/2), x1 pairs in [D/2, D).
+template <int D>
+__device__ __forceinline__ void store_row_operand(const float (&x)[D], int exponent, uint32_t column) {
     const float scale = exp2_int(exponent);
 #pragma unroll
-    for (int c = 0; c < 16; ++c) {
-        float a0, a1, b0, b1;
-        split_half(x[2 * c], scale, a0, a1);
-        split_half(x[2 * c + 1], scale, b0, b1);
-        a[c] = __uint_as_float(pack_half2(a0, b0));
-        b[c] = __uint_as_float(pack_half2(a1, b1));
+    for (int half = 0; half < D / 32; ++half) {
+        float a[16], b[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+            float a0, a1, b0, b1;
+            split_half(x[32 * half + 2 * c], scale, a0, a1);
+            split_half(x[32 * half + 2 * c + 1], scale, b0, b1);
+            a[c] = __uint_as_float(pack_half2(a0, b0));
+            b[c] = __uint_as_float(pack_half2(a1, b1));
+        }
+        tmem_store16x2(column + 16 * half, a, column + D / 2 + 16 * half, b);
     }
 }
 
-// Loads a 32-float row (zeros when !valid), multiplied by `scale`.
-__device__ __forceinline__ void load_row(const float *row, bool valid, float scale, float (&x)[32]) {
+// Loads a D-float row (zeros when !valid), multiplied by `scale`.
+template <int D>
+__device__ __forceinline__ void load_row(const float *row, bool valid, float scale, float (&x)[D]) {
     const float4 *r4 = reinterpret_cast<const float4 *>(row);
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
+    for (int c = 0; c < D / 4; ++c) {
         const float4 v = valid ? __ldg(r4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
         x[4 * c] = v.x * scale;
         x[4 * c + 1] = v.y * scale;
@@ -127,42 +152,81 @@ __device__ __forceinline__ void load_row(const float *row, bool valid, float sca
     }
 }
 
-__device__ __forceinline__ float abs_max(const float (&x)[32]) {
+template <int D>
+__device__ __forceinline__ float abs_max(const float (&x)[D]) {
     float m = 0.f;
 #pragma unroll
-    for (int c = 0; c < 32; c += 2) m = max3(m, fabsf(x[c]), fabsf(x[c + 1]));
+    for (int c = 0; c < D; c += 2) m = max3(m, fabsf(x[c]), fabsf(x[c + 1]));
     return m;
 }
 
-// X (N = 32) = x1.t0 + x0.t0 + x0.t1 over the 64 columns: A chunks of 16 columns at
-// `chunks` + 16 kk ([x0 pairs 8 | x1 pairs 8]), B = t (rows 0-31 x0^T, 32-63 x1^T). Commits to
-// `bar` when given. Warp-collective.
+// 16-byte chunk `chunk` (features 4 chunk .. 4 chunk + 3) of row `row` of an FP32 tile: D = 64
+// tiles are two 64 x 32 boxes side by side.
+template <int D>
+__device__ __forceinline__ float4 raw_chunk(const float *tile, int row, int chunk) {
+    const float4 *box = reinterpret_cast<const float4 *>(tile) + (chunk >> 3) * (kBoxFloats / 4);
+    return box[row * 8 + ((chunk & 7) ^ (row & 7))];
+}
+
+// Row layout: the 16-byte FP16 chunk m (features 8m..8m+7) of part x0 (part 0) or x1 (part 1)
+// of row `row`, 128B-swizzled.
+template <int D>
+__device__ __forceinline__ uint4 *row_chunk(uint32_t *tile, int row, int part, int m) {
+    if constexpr (D == 32)
+        return reinterpret_cast<uint4 *>(tile) + row * 8 + ((4 * part + m) ^ (row & 7));
+    else
+        return reinterpret_cast<uint4 *>(tile) + part * (kBoxBytes / 16) + row * 8 + (m ^ (row & 7));
+}
+
+// X (N = D) = x1.t0 + x0.t0 + x0.t1 over the 64 columns: A chunks of 16 columns at
+// `chunks` + 16 kk ([x0 pairs 8 | x1 pairs 8]), B = t (rows 0..D-1 x0^T, D..2D-1 x1^T). Commits
+// to `bar` when given. Warp-collective.
+template <int D>
 __device__ __forceinline__ void issue_x(uint32_t d, uint32_t chunks, uint64_t t, uint64_t *bar) {
-    const uint64_t u = t + kDescUpper;
+    constexpr uint32_t idesc = Geometry<D>::kIdescX;
+    const uint64_t u = t + Geometry<D>::kDescUpper;
     const uint32_t g1a[4] = {chunks, chunks + 8, chunks, chunks + 16};
     const uint64_t g1b[4] = {t, t, u, t + kDescStep};
-    mma4_f16_ts_warp(d, g1a, g1b, kIdescX, 1);
+    mma4_f16_ts_warp(d, g1a, g1b, idesc, 1);
     const uint32_t g2a[4] = {chunks + 24, chunks + 16, chunks + 32, chunks + 40};
     const uint64_t g2b[4] = {t + kDescStep, u + kDescStep, t + 2 * kDescStep, t + 2 * kDescStep};
-    mma4_f16_ts_warp(d, g2a, g2b, kIdescX, 0);
+    mma4_f16_ts_warp(d, g2a, g2b, idesc, 0);
     const uint32_t g3a[4] = {chunks + 32, chunks + 48, chunks + 56, chunks + 48};
     const uint64_t g3b[4] = {u + 2 * kDescStep, t + 3 * kDescStep, t + 3 * kDescStep, u + 3 * kDescStep};
     if (bar != nullptr)
-        mma4_f16_ts_commit_warp(d, g3a, g3b, kIdescX, 0, bar);
+        mma4_f16_ts_commit_warp(d, g3a, g3b, idesc, 0, bar);
     else
-        mma4_f16_ts_warp(d, g3a, g3b, kIdescX, 0);
+        mma4_f16_ts_warp(d, g3a, g3b, idesc, 0);
 }
 
-// S (N = 64) = a0.b1 + a1.b0 + a0.b0 over the 32 features; a at TMEM `a` ([x0 16 | x1 16]),
-// b = [x0 | x1] rows. Warp-collective.
+// S (N = 64) = a0.b1 + a1.b0 + a0.b0 over the D features; a at TMEM `a` ([x0 D/2 | x1 D/2]),
+// b = the row layout (x0 part at b, x1 part at b + kDescX1). Commits to `bar` when given.
+// Warp-collective.
+template <int D>
 __device__ __forceinline__ void issue_product(uint32_t d, uint32_t a, uint64_t b, uint64_t *bar) {
-    const uint32_t ga[4] = {a, a + 8, a + 16, a + 24};
-    const uint64_t gb[4] = {b + kDescHalf, b + kDescHalf + kDescStep, b, b + kDescStep};
-    mma4_f16_ts_warp(d, ga, gb, kIdescS, 1);
-    if (bar != nullptr)
-        mma2_f16_ts_commit_warp(d, a, a + 8, b, b + kDescStep, kIdescS, bar);
-    else
-        mma2_f16_ts_warp(d, a, a + 8, b, b + kDescStep, kIdescS);
+    constexpr uint64_t x1 = Geometry<D>::kDescX1;
+    constexpr uint32_t h = D / 2;
+    if constexpr (D == 32) {
+        const uint32_t ga[4] = {a, a + 8, a + h, a + h + 8};
+        const uint64_t gb[4] = {b + x1, b + x1 + kDescStep, b, b + kDescStep};
+        mma4_f16_ts_warp(d, ga, gb, kIdescS, 1);
+        if (bar != nullptr)
+            mma2_f16_ts_commit_warp(d, a, a + 8, b, b + kDescStep, kIdescS, bar);
+        else
+            mma2_f16_ts_warp(d, a, a + 8, b, b + kDescStep, kIdescS);
+    } else {
+        const uint32_t g1a[4] = {a, a + 8, a + 16, a + 24};  // a0 . b1
+        const uint64_t g1b[4] = {b + x1, b + x1 + kDescStep, b + x1 + 2 * kDescStep, b + x1 + 3 * kDescStep};
+        mma4_f16_ts_warp(d, g1a, g1b, kIdescS, 1);
+        const uint32_t g2a[4] = {a + h, a + h + 8, a + h + 16, a + h + 24};  // a1 . b0
+        const uint64_t g2b[4] = {b, b + kDescStep, b + 2 * kDescStep, b + 3 * kDescStep};
+        mma4_f16_ts_warp(d, g2a, g2b, kIdescS, 0);
+        const uint32_t g3a[4] = {a, a + 8, a + 16, a + 24};  // a0 . b0
+        if (bar != nullptr)
+            mma4_f16_ts_commit_warp(d, g3a, g2b, kIdescS, 0, bar);
+        else
+            mma4_f16_ts_warp(d, g3a, g2b, kIdescS, 0);
+    }
 }
 
 // Splits 16 values (columns of a chunk) into FP16 pairs and stores them, without waiting, as
@@ -180,13 +244,14 @@ __device__ __forceinline__ void store_split_chunk(uint32_t chunk, const float (&
 }
 
 // acc1 += X1 * scale1 (and acc2 += X2 * scale2 for key rows), eight columns at a time.
-template <bool kKeyRows>
-__device__ __forceinline__ void fold_x(float (&acc1)[32], float (&acc2)[kKeyRows ? 32 : 1], uint32_t lanes, float scale1,
+template <int D, bool kKeyRows>
+__device__ __forceinline__ void fold_x(float (&acc1)[D], float (&acc2)[kKeyRows ? D : 1], uint32_t lanes, float scale1,
                                        float scale2) {
+    using G = Geometry<D>;
 #pragma unroll
-    for (int quarter = 0; quarter < 4; ++quarter) {
+    for (int quarter = 0; quarter < D / 8; ++quarter) {
         float xa[8], xb[8];
-        tmem_load8x2(lanes + kColX1 + 8 * quarter, xa, lanes + (kKeyRows ? kColX2 : kColX1) + 8 * quarter, xb);
+        tmem_load8x2(lanes + G::kColX1 + 8 * quarter, xa, lanes + (kKeyRows ? G::kColX2 : G::kColX1) + 8 * quarter, xb);
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
             acc1[8 * quarter + c] = fmaf(xa[c], scale1, acc1[8 * quarter + c]);
@@ -195,11 +260,79 @@ __device__ __forceinline__ void fold_x(float (&acc1)[32], float (&acc2)[kKeyRows
     }
 }
 
-template <bool kKeyRows>
-__global__ void __launch_bounds__(kThreads, 2)
+// Converts the two FP32 tiles of one stage (split warps, 64 threads): row layouts of both
+// (B of S and dP), transposed layouts of raw1 (and of raw2 for key rows), masked key rows zeroed
+// (query rows). Lane layout: row = 32 w + lane for the row layouts; (group of 8 rows, chunk of 4
+// features) items for the transposed ones.
+template <int D, bool kKeyRows>
+__device__ __forceinline__ void convert_stage(Storage<D, kKeyRows> &s, int stage, int w, int lane, bool keep_row, float scale_1,
+                                              float scale_2) {
+    using G = Geometry<D>;
+    const int row = 32 * w + lane;
+    const uint32_t bits0 = s.col_mask[stage][0], bits1 = s.col_mask[stage][1];
+#pragma unroll
+    for (int which = 0; which < 2; ++which) {
+        const float *raw = which == 0 ? s.raw1[stage] : s.raw2[stage];
+        uint32_t *dst = which == 0 ? s.b1[stage] : s.b2[stage];
+        const float scale = which == 0 ? scale_1 : scale_2;
+#pragma unroll
+        for (int m = 0; m < D / 8; ++m) {
+            float4 lo = raw_chunk<D>(raw, row, 2 * m), hi = raw_chunk<D>(raw, row, 2 * m + 1);
+            if (!keep_row) lo = hi = make_float4(0.f, 0.f, 0.f, 0.f);
+            const float x[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+            float x0[8], x1[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) split_half(x[e], scale, x0[e], x1[e]);
+            *row_chunk<D>(dst, row, 0, m) = make_uint4(pack_half2(x0[0], x0[1]), pack_half2(x0[2], x0[3]),
+                                                       pack_half2(x0[4], x0[5]), pack_half2(x0[6], x0[7]));
+            *row_chunk<D>(dst, row, 1, m) = make_uint4(pack_half2(x1[0], x1[1]), pack_half2(x1[2], x1[3]),
+                                                       pack_half2(x1[4], x1[5]), pack_half2(x1[6], x1[7]));
+        }
+    }
+    // Transposed: feature rows f (x0) and D + f (x1); tile rows 8g..8g+7 are 16-byte chunk g
+    // (swizzled by f % 8). Item = (group g, feature chunk fc of 4 features).
+#pragma unroll
+    for (int which = 0; which < (kKeyRows ? 2 : 1); ++which) {
+        const float *raw = which == 0 ? s.raw1[stage] : s.raw2[stage];
+        uint4 *dst = reinterpret_cast<uint4 *>(which == 0 ? s.t1[stage] : s.t2[kKeyRows ? stage : 0]);
+        const float scale = which == 0 ? scale_1 : scale_2;
+#pragma unroll
+        for (int item = 0; item < D / 32; ++item) {
+            const int index = 64 * item + 32 * w + lane;  // 0 .. 2D - 1
+            const int group = index >> 3 & 7;
+            const int fchunk = (index & 7) + 8 * (index >> 6);
+            float4 values[8];
+#pragma unroll
+            for (int r = 0; r < 8; ++r) {
+                const int trow = 8 * group + r;
+                values[r] = raw_chunk<D>(raw, trow, fchunk);
+                const uint32_t word = trow < 32 ? bits0 : bits1;
+                if (!kKeyRows && !((word >> (trow & 31)) & 1)) values[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int f = 4 * fchunk + e;
+                float x0[8], x1[8];
+#pragma unroll
+                for (int r = 0; r < 8; ++r) {
+                    const float value = e == 0 ? values[r].x : e == 1 ? values[r].y : e == 2 ? values[r].z : values[r].w;
+                    split_half(value, scale, x0[r], x1[r]);
+                }
+                dst[f * 8 + (group ^ (f & 7))] = make_uint4(pack_half2(x0[0], x0[1]), pack_half2(x0[2], x0[3]),
+                                                            pack_half2(x0[4], x0[5]), pack_half2(x0[6], x0[7]));
+                dst[(D + f) * 8 + (group ^ (f & 7))] = make_uint4(pack_half2(x1[0], x1[1]), pack_half2(x1[2], x1[3]),
+                                                                  pack_half2(x1[4], x1[5]), pack_half2(x1[6], x1[7]));
+            }
+        }
+    }
+}
+
+template <int D, bool kKeyRows>
+__global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
         backward_kernel(const BackwardArgs args, const __grid_constant__ CUtensorMap tmap1,
                         const __grid_constant__ CUtensorMap tmap2) {
-    using S = Storage<kKeyRows>;
+    using G = Geometry<D>;
+    using S = Storage<D, kKeyRows>;
     extern __shared__ uint8_t shared_raw[];
     S &s = *reinterpret_cast<S *>((reinterpret_cast<uintptr_t>(shared_raw) + 1023) & ~uintptr_t(1023));
     const AttentionParams &p = args.p;
@@ -222,7 +355,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     const unsigned char *mask = p.mask + static_cast<long long>(b) * p.keys;
 
     if (warp == 0) {
-        tmem_alloc(&s.tmem_base, kTmemColumns);
+        tmem_alloc(&s.tmem_base, G::kTmemColumns);
         tmem_relinquish();
     }
     if (threadIdx.x == kProducerWarp * 32) {
@@ -252,9 +385,12 @@ __global__ void __launch_bounds__(kThreads, 2)
                 const int stage = j % kStages;
                 if (j >= kStages) ok = mbar_wait(&s.empty[stage], ((j / kStages) - 1) & 1);
                 if (!ok) break;
-                mbar_arrive_expect_tx(&s.full[stage], 2 * kTileBytes);
-                tma_load_4d(s.raw1[stage], &tmap1, &s.full[stage], 0, first + j * kCols, h, b);
-                tma_load_4d(s.raw2[stage], &tmap2, &s.full[stage], 0, first + j * kCols, h, b);
+                mbar_arrive_expect_tx(&s.full[stage], 2 * G::kBoxes * kBoxBytes);
+#pragma unroll
+                for (int box = 0; box < G::kBoxes; ++box) {
+                    tma_load_4d(s.raw1[stage] + box * kBoxFloats, &tmap1, &s.full[stage], 32 * box, first + j * kCols, h, b);
+                    tma_load_4d(s.raw2[stage] + box * kBoxFloats, &tmap2, &s.full[stage], 32 * box, first + j * kCols, h, b);
+                }
                 ++issued;
             }
             if (!ok) {
@@ -264,6 +400,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     } else if (warp == kMmaWarp) {
         // ---------------------------------------------------------------- MMA issuer
         if (tiles > 0) {
+            constexpr uint64_t row_stage = G::kRowWords * 4 / 16, t_stage = G::kTWords * 4 / 16;
             const uint64_t b1_desc = sw128_descriptor(smem_u32(s.b1[0]));
             const uint64_t b2_desc = sw128_descriptor(smem_u32(s.b2[0]));
             const uint64_t t1_desc = sw128_descriptor(smem_u32(s.t1[0]));
@@ -274,16 +411,16 @@ __global__ void __launch_bounds__(kThreads, 2)
                 ok = mbar_wait_warp(&s.ready[stage], (j / kStages) & 1);
                 if (!ok) break;
                 tc_fence_after();
-                issue_product(tmem + kColS, tmem + kColA1, b1_desc + kDescStage * stage, nullptr);
-                issue_product(tmem + kColDP, tmem + kColA2, b2_desc + kDescStage * stage, &s.s_full);
+                issue_product<D>(tmem + G::kColS, tmem + G::kColA1, b1_desc + row_stage * stage, nullptr);
+                issue_product<D>(tmem + G::kColDP, tmem + G::kColA2, b2_desc + row_stage * stage, &s.s_full);
                 ok = mbar_wait_warp(&s.p_full, j & 1);
                 if (!ok) break;
                 tc_fence_after();
                 if (kKeyRows) {
-                    issue_x(tmem + kColX1, tmem + kColDP, t1_desc + kDescStage * stage, nullptr);
-                    issue_x(tmem + kColX2, tmem + kColS, t2_desc + kDescStage * stage, &s.x_done);
+                    issue_x<D>(tmem + G::kColX1, tmem + G::kColDP, t1_desc + t_stage * stage, nullptr);
+                    issue_x<D>(tmem + G::kColX2, tmem + G::kColS, t2_desc + t_stage * stage, &s.x_done);
                 } else {
-                    issue_x(tmem + kColX1, tmem + kColDP, t1_desc + kDescStage * stage, &s.x_done);
+                    issue_x<D>(tmem + G::kColX1, tmem + G::kColDP, t1_desc + t_stage * stage, &s.x_done);
                 }
                 mma_commit_warp(&s.empty[stage]);
             }
@@ -292,13 +429,10 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
     } else if (warp >= kSplitWarp) {
         // ---------------------------------------------------------------- FP16 split
-        // Split warp w owns rows [32w, 32w + 32) of each column tile for the row layouts and the
-        // column statistics; for the transposed layouts lane = (group of 8 rows, chunk of 4
-        // features), as in the forward's V conversion.
+        // Split warp w owns rows [32w, 32w + 32) of each column tile for the maxima, the masks and
+        // the column statistics; convert_stage writes the operand layouts.
         const int w = warp - kSplitWarp;
         const int row = 32 * w + lane;
-        const int group = 4 * w + (lane >> 3);
-        const int fchunk = lane & 7;
         const float scale1 = kKeyRows ? p.scale : 1.f;  // Q enters the products as scale * Q
         for (int j = 0; j < tiles; ++j) {
             const int stage = j % kStages, parity = j & 1;
@@ -319,15 +453,13 @@ __global__ void __launch_bounds__(kThreads, 2)
                 visible = column < last && mask[column] != 0;
             }
             const uint32_t bits = __ballot_sync(0xffffffffu, visible);
-            // Row-layout rows of key columns that are masked are zeroed (query rows only).
+            // Rows of masked key columns are zeroed (query rows only).
             const bool keep_row = kKeyRows || ((bits >> lane) & 1);
-            const float4 *r1 = reinterpret_cast<const float4 *>(s.raw1[stage]);
-            const float4 *r2 = reinterpret_cast<const float4 *>(s.raw2[stage]);
             float max1 = 0.f, max2 = 0.f;
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                const float4 x = r1[row * 8 + (c ^ (row & 7))];
-                const float4 y = r2[row * 8 + (c ^ (row & 7))];
+            for (int c = 0; c < D / 4; ++c) {
+                const float4 x = raw_chunk<D>(s.raw1[stage], row, c);
+                const float4 y = raw_chunk<D>(s.raw2[stage], row, c);
                 if (keep_row) {
                     max1 = max3(max1, fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
                     max2 = max3(max2, fmaxf(fabsf(y.x), fabsf(y.y)), fmaxf(fabsf(y.z), fabsf(y.w)));
@@ -356,58 +488,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                 s.e2[stage] = e2;
                 s.col_delta_max[stage] = fmaxf(s.split_max[parity][0][2], s.split_max[parity][1][2]);
             }
-            const float scale_1 = exp2_int(e1) * scale1, scale_2 = exp2_int(e2);
-            const uint32_t tile_bits0 = s.col_mask[stage][0], tile_bits1 = s.col_mask[stage][1];
-            // Row layouts: features 8m..8m+7 -> x0 chunk m, x1 chunk 4 + m (swizzled by row % 8).
-#pragma unroll
-            for (int which = 0; which < 2; ++which) {
-                const float4 *raw = which == 0 ? r1 : r2;
-                uint4 *dst = reinterpret_cast<uint4 *>(which == 0 ? s.b1[stage] : s.b2[stage]);
-                const float scale = which == 0 ? scale_1 : scale_2;
-#pragma unroll
-                for (int m = 0; m < 4; ++m) {
-                    float4 lo = raw[row * 8 + ((2 * m) ^ (row & 7))], hi = raw[row * 8 + ((2 * m + 1) ^ (row & 7))];
-                    if (!keep_row) lo = hi = make_float4(0.f, 0.f, 0.f, 0.f);
-                    const float x[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
-                    float x0[8], x1[8];
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) split_half(x[e], scale, x0[e], x1[e]);
-                    dst[row * 8 + (m ^ (row & 7))] = make_uint4(pack_half2(x0[0], x0[1]), pack_half2(x0[2], x0[3]),
-                                                                pack_half2(x0[4], x0[5]), pack_half2(x0[6], x0[7]));
-                    dst[row * 8 + ((4 + m) ^ (row & 7))] = make_uint4(pack_half2(x1[0], x1[1]), pack_half2(x1[2], x1[3]),
-                                                                      pack_half2(x1[4], x1[5]), pack_half2(x1[6], x1[7]));
-                }
-            }
-            // Transposed layouts: feature rows f (x0) and 32 + f (x1); rows 8g..8g+7 of the tile
-            // are 16-byte chunk g (swizzled by f % 8).
-#pragma unroll
-            for (int which = 0; which < (kKeyRows ? 2 : 1); ++which) {
-                const float4 *raw = which == 0 ? r1 : r2;
-                uint4 *dst = reinterpret_cast<uint4 *>(which == 0 ? s.t1[stage] : s.t2[kKeyRows ? stage : 0]);
-                const float scale = which == 0 ? scale_1 : scale_2;
-                float4 items[8];
-#pragma unroll
-                for (int r = 0; r < 8; ++r) {
-                    const int trow = 8 * group + r;
-                    items[r] = raw[trow * 8 + (fchunk ^ (trow & 7))];
-                    const uint32_t word = trow < 32 ? tile_bits0 : tile_bits1;
-                    if (!kKeyRows && !((word >> (trow & 31)) & 1)) items[r] = make_float4(0.f, 0.f, 0.f, 0.f);
-                }
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int f = 4 * fchunk + e;
-                    float x0[8], x1[8];
-#pragma unroll
-                    for (int r = 0; r < 8; ++r) {
-                        const float value = e == 0 ? items[r].x : e == 1 ? items[r].y : e == 2 ? items[r].z : items[r].w;
-                        split_half(value, scale, x0[r], x1[r]);
-                    }
-                    dst[f * 8 + (group ^ (f & 7))] = make_uint4(pack_half2(x0[0], x0[1]), pack_half2(x0[2], x0[3]),
-                                                                pack_half2(x0[4], x0[5]), pack_half2(x0[6], x0[7]));
-                    dst[(32 + f) * 8 + (group ^ (f & 7))] = make_uint4(pack_half2(x1[0], x1[1]), pack_half2(x1[2], x1[3]),
-                                                                       pack_half2(x1[4], x1[5]), pack_half2(x1[6], x1[7]));
-                }
-            }
+            convert_stage<D, kKeyRows>(s, stage, w, lane, keep_row, exp2_int(e1) * scale1, exp2_int(e2));
             fence_proxy_async_shared();
             mbar_arrive(&s.ready[stage]);
         }
@@ -418,52 +499,53 @@ __global__ void __launch_bounds__(kThreads, 2)
         const bool row_valid = row < row_count;
         const uint32_t lanes = lane_address(tmem, warp);
         bool row_active;  // the row takes part at all (query: finite max; key: visible)
-        float row_offset = -INFINITY, row_delta = 0.f, row_l1;
+        float row_offset = -INFINITY, row_delta = 0.f, row_l1 = 0.f;
         int ea1, ea2;
         {
-            float x[32], y[32];
+            float x[D];
             if (kKeyRows) {
                 row_active = row_valid && mask[row] != 0;
-                load_row(p.k.row(b, h, row_valid ? row : 0), row_active, 1.f, x);
-                load_row(p.v.row(b, h, row_valid ? row : 0), row_active, 1.f, y);
-                row_l1 = 0.f;
+                load_row<D>(p.v.row(b, h, row_valid ? row : 0), row_active, 1.f, x);
 #pragma unroll
-                for (int c = 0; c < 32; ++c) row_l1 += fabsf(y[c]);
+                for (int c = 0; c < D; ++c) row_l1 += fabsf(x[c]);
+                ea2 = fp16_scale_exponent(abs_max<D>(x));
+                store_row_operand<D>(x, ea2, lanes + G::kColA2);
+                load_row<D>(p.k.row(b, h, row_valid ? row : 0), row_active, 1.f, x);
             } else {
                 const float maximum = row_valid ? p.lse_in[(query_base + row) * 2] : -INFINITY;
                 const float total = row_valid ? p.lse_in[(query_base + row) * 2 + 1] : 0.f;
                 row_active = row_valid && maximum != -INFINITY;
                 if (row_active) row_offset = 14.f - maximum * kLog2e - __log2f(total);
-                float o[32];
-                load_row(p.dout.row(b, h, row_valid ? row : 0), row_valid, 1.f, y);
-                load_row(p.o_in.row(b, h, row_valid ? row : 0), row_valid, 1.f, o);
+                load_row<D>(p.dout.row(b, h, row_valid ? row : 0), row_valid, 1.f, x);
+                const float4 *o4 = reinterpret_cast<const float4 *>(p.o_in.row(b, h, row_valid ? row : 0));
                 float delta = 0.f;
-                row_l1 = 0.f;
 #pragma unroll
-                for (int c = 0; c < 32; ++c) {
-                    delta = fmaf(y[c], o[c], delta);
-                    row_l1 += fabsf(y[c]);
+                for (int c = 0; c < D / 4; ++c) {
+                    const float4 o = row_valid ? __ldg(o4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    delta = fmaf(x[4 * c], o.x, delta);
+                    delta = fmaf(x[4 * c + 1], o.y, delta);
+                    delta = fmaf(x[4 * c + 2], o.z, delta);
+                    delta = fmaf(x[4 * c + 3], o.w, delta);
                 }
+#pragma unroll
+                for (int c = 0; c < D; ++c) row_l1 += fabsf(x[c]);
                 row_delta = delta;
                 if (row_valid) p.delta[query_base + row] = delta;
-                load_row(p.q.row(b, h, row_valid ? row : 0), row_valid, p.scale, x);
+                ea2 = fp16_scale_exponent(abs_max<D>(x));
+                store_row_operand<D>(x, ea2, lanes + G::kColA2);
+                load_row<D>(p.q.row(b, h, row_valid ? row : 0), row_valid, p.scale, x);
             }
-            ea1 = fp16_scale_exponent(abs_max(x));
-            ea2 = fp16_scale_exponent(abs_max(y));
-            float a0[16], a1[16];
-            split_row(x, ea1, a0, a1);
-            tmem_store16x2(lanes + kColA1, a0, lanes + kColA1 + 16, a1);
-            split_row(y, ea2, a0, a1);
-            tmem_store16x2(lanes + kColA2, a0, lanes + kColA2 + 16, a1);
+            ea1 = fp16_scale_exponent(abs_max<D>(x));
+            store_row_operand<D>(x, ea1, lanes + G::kColA1);
             tc_fence_before();
             mbar_arrive(&s.rows_ready);
         }
 
-        float acc1[32], acc2[kKeyRows ? 32 : 1];
+        float acc1[D], acc2[kKeyRows ? D : 1];
 #pragma unroll
-        for (int c = 0; c < 32; ++c) acc1[c] = 0.f;
+        for (int c = 0; c < D; ++c) acc1[c] = 0.f;
 #pragma unroll
-        for (int c = 0; c < (kKeyRows ? 32 : 1); ++c) acc2[c] = 0.f;
+        for (int c = 0; c < (kKeyRows ? D : 1); ++c) acc2[c] = 0.f;
         float pending_scale1 = 0.f, pending_scale2 = 0.f;  // 2^-(scales) of the last tile's X1, X2
         bool ok = true;
         for (int j = 0; j < tiles && ok; ++j) {
@@ -491,7 +573,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll 1
             for (int chunk = 0; chunk < 4; ++chunk) {  // rolled: keeps one chunk's values live
                 float sv[16], dv[16];  // scores, then P'; dP, then dS'
-                tmem_load16x2(lanes + kColS + 16 * chunk, sv, lanes + kColDP + 16 * chunk, dv);
+                tmem_load16x2(lanes + G::kColS + 16 * chunk, sv, lanes + G::kColDP + 16 * chunk, dv);
 #pragma unroll
                 for (int c = 0; c < 16; ++c) {
                     const int col = 16 * chunk + c;
@@ -502,8 +584,8 @@ __global__ void __launch_bounds__(kThreads, 2)
                     sv[c] = pv;
                     dv[c] = pv * fmaf(dv[c], w_scale, -delta * to_ds);
                 }
-                store_split_chunk(lanes + kColDP + 16 * chunk, dv);
-                if (kKeyRows) store_split_chunk(lanes + kColS + 16 * chunk, sv);
+                store_split_chunk(lanes + G::kColDP + 16 * chunk, dv);
+                if (kKeyRows) store_split_chunk(lanes + G::kColS + 16 * chunk, sv);
             }
             // Fold the previous tile's X before the P(j)/dS(j) arrival lets the MMA warp
             // overwrite it.
@@ -514,7 +596,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                     break;
                 }
                 tc_fence_after();
-                fold_x<kKeyRows>(acc1, acc2, lanes, pending_scale1, pending_scale2);
+                fold_x<D, kKeyRows>(acc1, acc2, lanes, pending_scale1, pending_scale2);
             }
             tmem_wait_store();
             tc_fence_before();
@@ -526,29 +608,28 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (tiles > 0 && ok) {
             ok = __all_sync(0xffffffffu, mbar_wait(&s.x_done, (tiles - 1) & 1));
             tc_fence_after();
-            if (ok) fold_x<kKeyRows>(acc1, acc2, lanes, pending_scale1, pending_scale2);
+            if (ok) fold_x<D, kKeyRows>(acc1, acc2, lanes, pending_scale1, pending_scale2);
         }
-        // Outputs (packed [batch][heads][tokens][32]); a failed wait leaves NaN.
+        // Outputs (packed [batch][heads][tokens][D]); a failed wait leaves NaN.
         if (row_valid) {
             const float bad = ok ? 1.f : NAN;
-            if (kKeyRows) {
-                float4 *dk = reinterpret_cast<float4 *>(p.dk + (key_base + row) * kD);
-                float4 *dv = reinterpret_cast<float4 *>(p.dv + (key_base + row) * kD);
+            if constexpr (kKeyRows) {
+                float4 *dk = reinterpret_cast<float4 *>(p.dk + (key_base + row) * D);
+                float4 *dv = reinterpret_cast<float4 *>(p.dv + (key_base + row) * D);
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
+                for (int c = 0; c < D / 4; ++c) {
                     if (row_active) {
                         dk[c] = make_float4(acc1[4 * c] * bad, acc1[4 * c + 1] * bad, acc1[4 * c + 2] * bad, acc1[4 * c + 3] * bad);
-                        dv[c] = make_float4(acc2[(4 * c) % (kKeyRows ? 32 : 1)] * bad, acc2[(4 * c + 1) % (kKeyRows ? 32 : 1)] * bad,
-                                            acc2[(4 * c + 2) % (kKeyRows ? 32 : 1)] * bad, acc2[(4 * c + 3) % (kKeyRows ? 32 : 1)] * bad);
+                        dv[c] = make_float4(acc2[4 * c] * bad, acc2[4 * c + 1] * bad, acc2[4 * c + 2] * bad, acc2[4 * c + 3] * bad);
                     } else {
                         dk[c] = dv[c] = make_float4(0.f, 0.f, 0.f, 0.f);  // masked key: exactly zero
                     }
                 }
             } else {
-                float4 *dq = reinterpret_cast<float4 *>(p.dq + (query_base + row) * kD);
+                float4 *dq = reinterpret_cast<float4 *>(p.dq + (query_base + row) * D);
                 const float scale = p.scale * bad;
 #pragma unroll
-                for (int c = 0; c < 8; ++c)
+                for (int c = 0; c < D / 4; ++c)
                     dq[c] = make_float4(acc1[4 * c] * scale, acc1[4 * c + 1] * scale, acc1[4 * c + 2] * scale, acc1[4 * c + 3] * scale);
             }
         }
@@ -558,7 +639,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        tmem_dealloc(tmem, kTmemColumns);
+        tmem_dealloc(tmem, G::kTmemColumns);
     }
 }
 
@@ -577,14 +658,15 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_function() {
     return function;
 }
 
-// [batch][heads][tokens][32] FP32 with the given element strides; box = 32 features x 64 tokens.
-bool make_tensor_map(CUtensorMap *map, const Tensor &t, int batch, int heads, int tokens) {
+// [batch][heads][tokens][D] FP32 with the given element strides; box = 32 features x 64 tokens.
+bool make_tensor_map(CUtensorMap *map, const Tensor &t, int width, int batch, int heads, int tokens) {
     auto encode = encode_function();
     if (encode == nullptr) return false;
-    const cuuint64_t dims[4] = {kD, static_cast<cuuint64_t>(tokens), static_cast<cuuint64_t>(heads), static_cast<cuuint64_t>(batch)};
+    const cuuint64_t dims[4] = {static_cast<cuuint64_t>(width), static_cast<cuuint64_t>(tokens), static_cast<cuuint64_t>(heads),
+                                static_cast<cuuint64_t>(batch)};
     const cuuint64_t strides[3] = {static_cast<cuuint64_t>(t.st) * 4, static_cast<cuuint64_t>(t.sh) * 4,
                                    static_cast<cuuint64_t>(t.sb) * 4};
-    const cuuint32_t box[4] = {kD, static_cast<cuuint32_t>(kCols), 1, 1};
+    const cuuint32_t box[4] = {32, static_cast<cuuint32_t>(kCols), 1, 1};
     const cuuint32_t element_strides[4] = {1, 1, 1, 1};
     return encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float *>(t.data), dims, strides, box, element_strides,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
@@ -601,23 +683,36 @@ bool rows_addressable(const Tensor &t) {
     return t.st % 4 == 0 && t.sh % 4 == 0 && t.sb % 4 == 0 && (reinterpret_cast<uintptr_t>(t.data) & 15u) == 0;
 }
 
-template <bool kKeyRows>
+template <int D, bool kKeyRows>
 constexpr int shared_bytes() {
-    return static_cast<int>(sizeof(Storage<kKeyRows>)) + 1024;
+    return static_cast<int>(sizeof(Storage<D, kKeyRows>)) + 1024;
 }
-static_assert(shared_bytes<false>() <= 113 * 1024 && shared_bytes<true>() <= 113 * 1024, "two CTAs per SM");
+static_assert(shared_bytes<32, false>() <= 113 * 1024 && shared_bytes<32, true>() <= 113 * 1024, "d=32: two CTAs per SM");
+static_assert(shared_bytes<64, false>() <= 227 * 1024 && shared_bytes<64, true>() <= 227 * 1024, "d=64: one CTA per SM");
 
-template <bool kKeyRows>
+template <int D, bool kKeyRows>
 int launch_pass(const AttentionParams &p, const CUtensorMap &map1, const CUtensorMap &map2, cudaStream_t stream) {
-    cudaError_t status = prepare_kernel<backward_kernel<kKeyRows>>(shared_bytes<kKeyRows>());
+    cudaError_t status = prepare_kernel<backward_kernel<D, kKeyRows>>(shared_bytes<D, kKeyRows>());
     if (status != cudaSuccess) return status;
     BackwardArgs args{};
     args.p = p;
     const int rows = kKeyRows ? p.keys : p.queries;
     args.blocks_per_head = (rows + kRows - 1) / kRows;
     const unsigned blocks = static_cast<unsigned>(args.blocks_per_head) * static_cast<unsigned>(p.heads) * static_cast<unsigned>(p.batch);
-    backward_kernel<kKeyRows><<<blocks, kThreads, shared_bytes<kKeyRows>(), stream>>>(args, map1, map2);
+    backward_kernel<D, kKeyRows><<<blocks, kThreads, shared_bytes<D, kKeyRows>(), stream>>>(args, map1, map2);
     return cudaGetLastError();
+}
+
+template <int D>
+int launch_both(const AttentionParams &p, cudaStream_t stream) {
+    CUtensorMap map_k, map_v, map_q, map_dout;
+    if (!make_tensor_map(&map_k, p.k, D, p.batch, p.heads, p.keys) || !make_tensor_map(&map_v, p.v, D, p.batch, p.heads, p.keys) ||
+        !make_tensor_map(&map_q, p.q, D, p.batch, p.heads, p.queries) ||
+        !make_tensor_map(&map_dout, p.dout, D, p.batch, p.heads, p.queries))
+        return kNotEligible;
+    const int status = launch_pass<D, false>(p, map_k, map_v, stream);  // delta, dQ
+    if (status != cudaSuccess) return status;
+    return launch_pass<D, true>(p, map_q, map_dout, stream);  // dK, dV (reads delta)
 }
 
 }  // namespace
@@ -628,15 +723,10 @@ bool backward_supported(const AttentionParams &p) {
            (reinterpret_cast<uintptr_t>(p.dk) & 15u) == 0 && (reinterpret_cast<uintptr_t>(p.dv) & 15u) == 0;
 }
 
-int launch_backward(const AttentionParams &p, cudaStream_t stream) {
-    CUtensorMap map_k, map_v, map_q, map_dout;
-    if (!make_tensor_map(&map_k, p.k, p.batch, p.heads, p.keys) || !make_tensor_map(&map_v, p.v, p.batch, p.heads, p.keys) ||
-        !make_tensor_map(&map_q, p.q, p.batch, p.heads, p.queries) ||
-        !make_tensor_map(&map_dout, p.dout, p.batch, p.heads, p.queries))
-        return kNotEligible;
-    const int status = launch_pass<false>(p, map_k, map_v, stream);  // delta, dQ
-    if (status != cudaSuccess) return status;
-    return launch_pass<true>(p, map_q, map_dout, stream);  // dK, dV (reads delta)
+int launch_backward(const AttentionParams &p, int head_width, cudaStream_t stream) {
+    if (head_width == 32) return launch_both<32>(p, stream);
+    if (head_width == 64) return launch_both<64>(p, stream);
+    return kNotEligible;
 }
 
 unsigned int read_backward_status(bool clear) {
