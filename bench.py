@@ -427,7 +427,7 @@ def main() -> None:
                     "flops": "effective: 8*d per active (query, key) pair"}
     else:
         achieved = effective_forward / (part_seconds[0] / args.steps) / 1e12
-        path = api.flash_kernel_name(batch, heads, seq, seq, dim) if dim == 32 else "simt-fp32-d64"
+        path = api.flash_kernel_name(batch, heads, seq, seq, dim)
         if path.startswith("tcgen05"):
             peak = float(peaks["bf16_tflops"])
             roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,

@@ -172,8 +172,9 @@ ROCMKERNELS_C_EXPORT int attention_fp32_backward_static_delta(const float *q, co
  * compiled for ("sm_100a") and the kernel families present. No counterpart in the reference. */
 ROCMKERNELS_C_EXPORT const char *rocmkernels_attention_build_info(void);
 
-/* Name of the kernel attention_fp32_forward_flash selects for contiguous, 16-byte aligned
- * tensors of this shape (for benchmarks and profiles). No counterpart in the reference. */
+/* Name of the kernel the flash forward (head_width 32: attention_fp32_forward_flash; 64:
+ * attention64_fp32_forward) selects for contiguous, 16-byte aligned tensors of this shape (for
+ * benchmarks and profiles). No counterpart in the reference. */
 ROCMKERNELS_C_EXPORT const char *rocmkernels_attention_flash_kernel(int batch, int heads, int queries, int keys,
         int head_width);
 

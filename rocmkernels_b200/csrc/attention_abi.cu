@@ -124,7 +124,7 @@ int launch_backward(const AttentionParams &p, cudaStream_t stream, bool softmax_
 // exact SIMT kernel (same results within the documented tolerance; no CPU path exists).
 int launch_flash(const AttentionParams &p, cudaStream_t stream) {
     if (rk::tc::flash_supported(p)) {
-        const int status = rk::tc::launch_flash_forward(p, stream);
+        const int status = rk::tc::launch_flash_forward(p, 32, stream);
         if (status != rk::tc::kNotEligible) return status;
     }
     return launch_simt_forward<32, false>(p, stream);
@@ -276,6 +276,10 @@ int attention64_fp32_forward(const float *q, const float *k, const float *v, con
                              RocmKernelsStream stream) {
     if (forward_args_bad(q, k, v, mask, output, lse, batch, heads, queries, keys)) return cudaErrorInvalidValue;
     const AttentionParams p = forward_params(64, q, k, v, mask, output, lse, batch, heads, queries, keys, radius, qs, ks, vs, os);
+    if (rk::tc::flash_supported(p)) {  // else (tensors not TMA-addressable) the exact SIMT kernel
+        const int status = rk::tc::launch_flash_forward(p, 64, stream);
+        if (status != rk::tc::kNotEligible) return status;
+    }
     return launch_simt_forward<64, false>(p, stream);
 }
 
@@ -337,7 +341,7 @@ unsigned int rocmkernels_attention_device_status(int clear) {
 }
 
 const char *rocmkernels_attention_flash_kernel(int batch, int heads, int queries, int keys, int head_width) {
-    if (head_width != 32) return "simt-fp32-forward-d64";
+    if (head_width != 32 && head_width != 64) return "unsupported";
     AttentionParams p{};
     p.batch = batch;
     p.heads = heads;
@@ -345,11 +349,13 @@ const char *rocmkernels_attention_flash_kernel(int batch, int heads, int queries
     p.keys = keys;
     p.radius = -1;
     p.vec4 = 1;
-    p.q = rk::Tensor{nullptr, (long long)heads * queries * 32, (long long)queries * 32, 32};
-    p.k = rk::Tensor{nullptr, (long long)heads * keys * 32, (long long)keys * 32, 32};
+    const long long w = head_width;
+    p.q = rk::Tensor{nullptr, (long long)heads * queries * w, (long long)queries * w, w};
+    p.k = rk::Tensor{nullptr, (long long)heads * keys * w, (long long)keys * w, w};
     p.v = p.k;
     p.o = rk::OutTensor{nullptr, p.q.sb, p.q.sh, p.q.st};
-    return rk::tc::flash_supported(p) ? rk::tc::kernel_name() : "simt-fp32-forward-d32";
+    if (rk::tc::flash_supported(p)) return rk::tc::kernel_name(head_width);
+    return head_width == 64 ? "simt-fp32-forward-d64" : "simt-fp32-forward-d32";
 }
 
 int attention_fp32_backward_static_delta(const float *q, const float *k, const float *v, const bool *mask,

@@ -41,7 +41,7 @@
 
 #include <mutex>
 
-#include "tc_primitives.cuh"
+#include "tc_operands.cuh"
 
 namespace rk {
 namespace tc {
@@ -74,54 +74,64 @@ __device__ long long g_warp_trace[8][8];
 #endif
 
 constexpr int kQTile = 128;
-constexpr int kQTiles = 2;
-constexpr int kCtaQueries = kQTile * kQTiles;
 constexpr int kKeyTile = 64;
-constexpr int kD = 32;
-constexpr int kStages = 4;
-constexpr int kThreads = 384;
-constexpr int kProducerWarp = 8;
-constexpr int kMmaWarp = 9;
-constexpr int kSplitWarp = 10;
-constexpr int kSplitThreads = 64;
-constexpr int kTileFloats = kKeyTile * kD;  // 2048
-constexpr int kTileBytes = kTileFloats * 4;  // 8 KB
-constexpr int kVRows = 2 * kD + 16;          // B of P.V: v0^T, v1^T and 16 rows of ones (row sums)
-constexpr int kVTileWords = kVRows * 32;     // 80 rows x 128 bytes
-constexpr uint32_t kTmemColumns = 512;
-constexpr uint32_t kColQ0 = 0, kColQ1 = 16, kColBuffer = 32, kBufferColumns = 64, kColO = 160, kColTile = 256;
-constexpr uint32_t kColSum = kColO + 2 * kD;  // first of the 16 row-sum columns
-constexpr uint32_t kIdescS = f16_instr_desc(128, 64);       // S: 64 keys
-constexpr uint32_t kIdescPV = f16_instr_desc(128, kVRows);  // P.V: [v0 ; v1 ; ones] = 80 rows
-constexpr float kPScale = 16384.f;                          // P is split as P * 2^14
-constexpr int kNoExponent = 1000;                           // outside every clamped scale exponent
+constexpr float kPScale = 16384.f;  // P is split as P * 2^14
+constexpr int kNoExponent = 1000;   // outside every clamped scale exponent
+constexpr uint32_t kIdescS = f16_instr_desc(128, 64);  // S: 64 keys
+constexpr uint64_t kDescStep = 2;                      // one K=16 step of FP16 = 32 bytes
 
-// Every tile buffer is 8 KB (64 rows x 128 bytes) and 1024-byte aligned (the 128B swizzle atom).
+// Configuration per head width. d = 32: two Q tiles of 128 queries per CTA sharing each K/V tile
+// (12 warps, 4 stages); d = 64: one Q tile per CTA (8 warps, 3 stages), its operands twice as wide.
+template <int D>
+struct Forward {
+    static constexpr int kQTiles = D == 32 ? 2 : 1;
+    static constexpr int kCtaQueries = kQTile * kQTiles;
+    static constexpr int kStages = D == 32 ? 4 : 3;
+    static constexpr int kSoftmaxWarps = 4 * kQTiles;
+    static constexpr int kProducerWarp = kSoftmaxWarps, kMmaWarp = kSoftmaxWarps + 1, kSplitWarp = kSoftmaxWarps + 2;
+    static constexpr int kThreads = 32 * (kSoftmaxWarps + 4);
+    static constexpr int kSplitThreads = 64;
+    static constexpr int kBoxes = D / 32;
+    static constexpr int kRawFloats = kBoxes * kBoxFloats;  // FP32 tile of 64 keys x D
+    static constexpr int kKWords = 64 * D;                   // row layout [k0 | k1] of 64 keys
+    static constexpr int kVRows = 2 * D + 16;                // B of P.V: v0^T, v1^T and 16 rows of ones (row sums)
+    static constexpr int kVWords = kVRows * 32;              // kVRows x 128 bytes
+    // TMEM per Q tile: q0 pairs | q1 pairs | S/P buffer 0 | S/P buffer 1 | Oa | Ob | row sums
+    static constexpr uint32_t kColQ0 = 0, kColQ1 = D / 2, kColBuffer = D, kBufferColumns = 64, kColO = D + 128,
+                              kColSum = kColO + 2 * D, kColTile = D == 32 ? 256 : 512;
+    static constexpr uint32_t kTmemColumns = 512;
+    static constexpr uint32_t kIdescPV = f16_instr_desc(128, kVRows);
+    static constexpr uint64_t kDescStageK = kKWords * 4 / 16, kDescStageV = kVWords * 4 / 16;
+};
+
+// Operand tiles are rows of 128 bytes in 1024-byte aligned 8-row atoms (the 128B swizzle).
+template <int D>
 struct alignas(1024) SharedStorage {
-    float k_raw[kStages][kTileFloats];       // FP32 K tile as TMA lands it (64 rows x 128 B, swizzled)
-    float v_raw[kStages][kTileFloats];       // FP32 V tile
-    uint32_t k16[kStages][kTileFloats];      // 64 key rows x 128 B: [k0 (32 fp16) | k1 (32 fp16)], K-major 128B swizzle
-    uint32_t vt16[kStages][kVTileWords];     // 80 rows x 128 B: rows 0-31 v0^T, 32-63 v1^T (64 keys each, 128B
-                                             // swizzle), 64-79 FP16 ones (written once)
-    uint32_t key_mask[kStages][2];           // bit c: key k0 + c visible
-    int k_exponent[kStages];                 // K tile scaled by 2^k_exponent
-    int v_exponent[kStages];                 // V tile scaled by 2^v_exponent
-    float split_max[2][2];                   // per split warp: max |K|, max |V| of its rows
-    int split_ok[2];                         // per split warp: its kv_full wait succeeded
-    uint64_t kv_full[kStages];               // TMA bytes landed
-    uint64_t kv_ready[kStages];              // conversion done (64 arrivals)
-    uint64_t kv_empty[kStages];              // MMAs reading the stage finished (commit)
-    uint64_t s_full[kQTiles][2];             // S of a buffer is in TMEM (commit)
-    uint64_t p_full[kQTiles];                // P of the current tile is in TMEM (128 arrivals)
-    uint64_t pv_done[kQTiles];               // Ot of the current tile is in TMEM (commit)
-    uint64_t q_ready;                        // q0/q1 of both tiles in TMEM (256 arrivals)
-    uint64_t mma_done;                       // every MMA of the CTA finished (commit)
+    using F = Forward<D>;
+    float k_raw[F::kStages][F::kRawFloats];    // FP32 K tile as TMA lands it (swizzled boxes of 64 x 32)
+    float v_raw[F::kStages][F::kRawFloats];    // FP32 V tile
+    uint32_t k16[F::kStages][F::kKWords];      // 64 key rows as [k0 | k1] FP16 (row layout), K-major 128B swizzle
+    uint32_t vt16[F::kStages][F::kVWords];     // rows 0..D-1 v0^T, D..2D-1 v1^T (64 keys each, 128B swizzle),
+                                               // 2D..2D+15 FP16 ones (written once)
+    uint32_t key_mask[F::kStages][2];          // bit c: key k0 + c visible
+    int k_exponent[F::kStages];                // K tile scaled by 2^k_exponent
+    int v_exponent[F::kStages];                // V tile scaled by 2^v_exponent
+    float split_max[2][2];                     // per split warp: max |K|, max |V| of its rows
+    int split_ok[2];                           // per split warp: its kv_full wait succeeded
+    uint64_t kv_full[F::kStages];              // TMA bytes landed
+    uint64_t kv_ready[F::kStages];             // conversion done (64 arrivals)
+    uint64_t kv_empty[F::kStages];             // MMAs reading the stage finished (commit)
+    uint64_t s_full[F::kQTiles][2];            // S of a buffer is in TMEM (commit)
+    uint64_t p_full[F::kQTiles];               // P of the current tile is in TMEM (128 arrivals)
+    uint64_t pv_done[F::kQTiles];              // Ot of the current tile is in TMEM (commit)
+    uint64_t q_ready;                          // q0/q1 of every Q tile in TMEM (128 arrivals per tile)
+    uint64_t mma_done;                         // every MMA of the CTA finished (commit)
     uint32_t tmem_base;
 };
 
 struct FlashArgs {
     AttentionParams p;
-    int cta_per_head;  // ceil(queries / 256)
+    int cta_per_head;  // ceil(queries / queries per CTA)
     int vec_out;       // output rows 16-byte addressable
 };
 
@@ -129,38 +139,43 @@ __device__ __forceinline__ uint32_t tmem_lane_address(uint32_t base, int warp) {
     return base + (static_cast<uint32_t>((warp & 3) * 32) << 16);
 }
 
-// Descriptor start addresses count 16-byte units: one K=16 step of FP16 is 32 bytes (+2), the
-// k1 half of a K row starts 64 bytes in (+4), and consecutive stages are one tile apart.
-constexpr uint64_t kDescStep = 2, kDescHalf = 4, kDescStageK = kTileBytes / 16, kDescStageV = kVTileWords * 4 / 16;
-
-// S(buffer) = q0.k1 + q1.k0 + q0.k0 over the 32 features (two K=16 steps each), then a commit
-// to `bar`; k_desc addresses the stage's k16 tile. Warp-collective.
+// S(buffer) = q0.k1 + q1.k0 + q0.k0 over the D features (D/16 K=16 steps each), then a commit to
+// `bar`; k_desc addresses the stage's k16 tile. Warp-collective.
+template <int D>
 __device__ __forceinline__ void issue_scores(uint32_t tmem, uint64_t k_desc, int tile, int buffer, uint64_t *bar) {
-    const uint32_t t = tmem + tile * kColTile;
-    const uint32_t d = t + kColBuffer + buffer * kBufferColumns;
-    const uint32_t a[4] = {t + kColQ0, t + kColQ0 + 8, t + kColQ1, t + kColQ1 + 8};
-    const uint64_t bk[4] = {k_desc + kDescHalf, k_desc + kDescHalf + kDescStep, k_desc, k_desc + kDescStep};
-    mma4_f16_ts_warp(d, a, bk, kIdescS, 1);
-    mma2_f16_ts_commit_warp(d, t + kColQ0, t + kColQ0 + 8, k_desc, k_desc + kDescStep, kIdescS, bar);
+    using F = Forward<D>;
+    constexpr uint64_t x1 = row_x1_offset<D>();
+    const uint32_t t = tmem + tile * F::kColTile;
+    const uint32_t d = t + F::kColBuffer + buffer * F::kBufferColumns;
+    const uint32_t a0 = t + F::kColQ0, a1 = t + F::kColQ1;
+    if constexpr (D == 32) {
+        const uint32_t a[4] = {a0, a0 + 8, a1, a1 + 8};
+        const uint64_t bk[4] = {k_desc + x1, k_desc + x1 + kDescStep, k_desc, k_desc + kDescStep};
+        mma4_f16_ts_warp(d, a, bk, kIdescS, 1);
+        mma2_f16_ts_commit_warp(d, a0, a0 + 8, k_desc, k_desc + kDescStep, kIdescS, bar);
+    } else {
+        const uint32_t g1a[4] = {a0, a0 + 8, a0 + 16, a0 + 24};  // q0 . k1
+        const uint64_t g1b[4] = {k_desc + x1, k_desc + x1 + kDescStep, k_desc + x1 + 2 * kDescStep, k_desc + x1 + 3 * kDescStep};
+        mma4_f16_ts_warp(d, g1a, g1b, kIdescS, 1);
+        const uint32_t g2a[4] = {a1, a1 + 8, a1 + 16, a1 + 24};  // q1 . k0
+        const uint64_t g2b[4] = {k_desc, k_desc + kDescStep, k_desc + 2 * kDescStep, k_desc + 3 * kDescStep};
+        mma4_f16_ts_warp(d, g2a, g2b, kIdescS, 0);
+        mma4_f16_ts_commit_warp(d, g1a, g2b, kIdescS, 0, bar);  // q0 . k0
+    }
 }
 
 // [Oa | Ob | sums] = p1.[v0 ; v1 ; 1] + p0.[v0 ; v1 ; 1] over the 64 keys (four K=16 steps
 // each), then a commit to `bar`; v_desc addresses the stage's vt16 tile. Warp-collective.
+template <int D>
 __device__ __forceinline__ void issue_values(uint32_t tmem, uint64_t v_desc, int tile, int buffer, uint64_t *bar) {
-    const uint32_t t = tmem + tile * kColTile;
-    const uint32_t pbuf = t + kColBuffer + buffer * kBufferColumns;
+    using F = Forward<D>;
+    const uint32_t t = tmem + tile * F::kColTile;
+    const uint32_t pbuf = t + F::kColBuffer + buffer * F::kBufferColumns;
     const uint64_t bv[4] = {v_desc, v_desc + kDescStep, v_desc + 2 * kDescStep, v_desc + 3 * kDescStep};
     const uint32_t a1[4] = {pbuf + 32, pbuf + 40, pbuf + 48, pbuf + 56};
     const uint32_t a0[4] = {pbuf, pbuf + 8, pbuf + 16, pbuf + 24};
-    mma4_f16_ts_warp(t + kColO, a1, bv, kIdescPV, 1);
-    mma4_f16_ts_commit_warp(t + kColO, a0, bv, kIdescPV, 0, bar);
-}
-
-// x' = x * scale split into (x0, x1): x0 exact in FP16, x1 = x' - x0 (rounded to FP16 on packing).
-__device__ __forceinline__ void split_half(float x, float scale, float &x0, float &x1) {
-    const float scaled = x * scale;
-    x0 = round_tf32(scaled);  // 10 explicit mantissa bits, the FP16 precision
-    x1 = scaled - x0;
+    mma4_f16_ts_warp(t + F::kColO, a1, bv, F::kIdescPV, 1);
+    mma4_f16_ts_commit_warp(t + F::kColO, a0, bv, F::kIdescPV, 0, bar);
 }
 
 // Folds the last finished key tile into the running output and row sum. In TMEM, Oa + Ob is the
@@ -169,8 +184,10 @@ __device__ __forceinline__ void split_half(float x, float scale, float &x0, floa
 // a tile with that exponent (the usual case, warp-uniform) costs one add and one FMA per column;
 // a tile with another exponent moves whichever side has the larger one down, so no value is
 // ever scaled up.
-__device__ __forceinline__ void fold_output(float (&o)[32], float &row_sum, int &o_exp, uint32_t lane_base, float weight,
+template <int D>
+__device__ __forceinline__ void fold_output(float (&o)[D], float &row_sum, int &o_exp, uint32_t lane_base, float weight,
                                             int c) {
+    using F = Forward<D>;
     if (o_exp == kNoExponent) o_exp = c;
     float out_weight = weight, tile_scale = 1.f;
     if (c > o_exp) {
@@ -180,20 +197,19 @@ __device__ __forceinline__ void fold_output(float (&o)[32], float &row_sum, int 
         o_exp = c;
     }
     float oa[16], ob[16], sum;
-    tmem_load16x2_1(lane_base + kColO, oa, lane_base + kColO + 32, ob, lane_base + kColSum, sum);
+    tmem_load16x2_1(lane_base + F::kColO, oa, lane_base + F::kColO + D, ob, lane_base + F::kColSum, sum);
     row_sum = fmaf(row_sum, weight, sum);
-    if (__all_sync(0xffffffffu, tile_scale == 1.f)) {  // uniform anyway; the loads inside are warp-collective
+    const bool unscaled = __all_sync(0xffffffffu, tile_scale == 1.f);  // uniform anyway
 #pragma unroll
-        for (int c = 0; c < 16; ++c) o[c] = fmaf(o[c], out_weight, oa[c] + ob[c]);
-        tmem_load16x2(lane_base + kColO + 16, oa, lane_base + kColO + 48, ob);
+    for (int part = 0; part < D / 16; ++part) {
+        if (part > 0) tmem_load16x2(lane_base + F::kColO + 16 * part, oa, lane_base + F::kColO + D + 16 * part, ob);
+        if (unscaled) {
 #pragma unroll
-        for (int c = 0; c < 16; ++c) o[16 + c] = fmaf(o[16 + c], out_weight, oa[c] + ob[c]);
-    } else {
+            for (int i = 0; i < 16; ++i) o[16 * part + i] = fmaf(o[16 * part + i], out_weight, oa[i] + ob[i]);
+        } else {
 #pragma unroll
-        for (int c = 0; c < 16; ++c) o[c] = fmaf(o[c], out_weight, (oa[c] + ob[c]) * tile_scale);
-        tmem_load16x2(lane_base + kColO + 16, oa, lane_base + kColO + 48, ob);
-#pragma unroll
-        for (int c = 0; c < 16; ++c) o[16 + c] = fmaf(o[16 + c], out_weight, (oa[c] + ob[c]) * tile_scale);
+            for (int i = 0; i < 16; ++i) o[16 * part + i] = fmaf(o[16 * part + i], out_weight, (oa[i] + ob[i]) * tile_scale);
+        }
     }
 }
 
@@ -226,11 +242,14 @@ __device__ __forceinline__ void exp_split_store(const float (&sc)[64], float slo
     }
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+template <int D>
+__global__ void __launch_bounds__(Forward<D>::kThreads, 1)
         flash_forward_kernel(const FlashArgs args, const __grid_constant__ CUtensorMap tmap_k,
                              const __grid_constant__ CUtensorMap tmap_v) {
+    using F = Forward<D>;
+    constexpr int kStages = F::kStages;
     extern __shared__ uint8_t shared_raw[];
-    SharedStorage &s = *reinterpret_cast<SharedStorage *>((reinterpret_cast<uintptr_t>(shared_raw) + 1023) & ~uintptr_t(1023));
+    SharedStorage<D> &s = *reinterpret_cast<SharedStorage<D> *>((reinterpret_cast<uintptr_t>(shared_raw) + 1023) & ~uintptr_t(1023));
     const AttentionParams &p = args.p;
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -240,41 +259,41 @@ __global__ void __launch_bounds__(kThreads, 1)
     block /= args.cta_per_head;
     const int h = block % p.heads;
     const int b = block / p.heads;
-    const int q0 = cta_tile * kCtaQueries;
+    const int q0 = cta_tile * F::kCtaQueries;
     int first, last;
-    key_window(q0, min(q0 + kCtaQueries, p.queries), p.keys, p.radius, first, last);
+    key_window(q0, min(q0 + F::kCtaQueries, p.queries), p.keys, p.radius, first, last);
     const int tiles = last > first ? (last - first + kKeyTile - 1) / kKeyTile : 0;
 
     if (warp == 0) {
-        tmem_alloc(&s.tmem_base, kTmemColumns);
+        tmem_alloc(&s.tmem_base, F::kTmemColumns);
         tmem_relinquish();
     }
-    if (threadIdx.x == kProducerWarp * 32) {
+    if (threadIdx.x == F::kProducerWarp * 32) {
         for (int i = 0; i < kStages; ++i) {
             mbar_init(&s.kv_full[i], 1);
-            mbar_init(&s.kv_ready[i], kSplitThreads);
+            mbar_init(&s.kv_ready[i], F::kSplitThreads);
             mbar_init(&s.kv_empty[i], 1);
         }
-        for (int t = 0; t < kQTiles; ++t) {
+        for (int t = 0; t < F::kQTiles; ++t) {
             mbar_init(&s.s_full[t][0], 1);
             mbar_init(&s.s_full[t][1], 1);
             mbar_init(&s.p_full[t], kQTile);
             mbar_init(&s.pv_done[t], 1);
         }
-        mbar_init(&s.q_ready, kQTile * kQTiles);
+        mbar_init(&s.q_ready, kQTile * F::kQTiles);
         mbar_init(&s.mma_done, 1);
         mbar_fence_init();
     }
-    // Rows 64-79 of every V operand tile are FP16 ones, so P.V also yields the row sums of P.
-    for (int i = threadIdx.x; i < kStages * 16 * 32; i += kThreads)
-        s.vt16[i / (16 * 32)][2 * kD * 32 + i % (16 * 32)] = 0x3C003C00u;
+    // Rows 2D..2D+15 of every V operand tile are FP16 ones, so P.V also yields the row sums of P.
+    for (int i = threadIdx.x; i < kStages * 16 * 32; i += F::kThreads)
+        s.vt16[i / (16 * 32)][2 * D * 32 + i % (16 * 32)] = 0x3C003C00u;
     fence_proxy_async_shared();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = s.tmem_base;
 
-    if (warp == kProducerWarp) {
+    if (warp == F::kProducerWarp) {
         // ---------------------------------------------------------------- TMA producer
         if (lane == 0) {
             int issued = 0;
@@ -284,9 +303,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (j >= kStages) ok = mbar_wait(&s.kv_empty[stage], (use - 1) & 1);
                 if (!ok) break;
                 RK_TRACE(j, 12);
-                mbar_arrive_expect_tx(&s.kv_full[stage], 2 * kTileBytes);
-                tma_load_4d(s.k_raw[stage], &tmap_k, &s.kv_full[stage], 0, first + j * kKeyTile, h, b);
-                tma_load_4d(s.v_raw[stage], &tmap_v, &s.kv_full[stage], 0, first + j * kKeyTile, h, b);
+                mbar_arrive_expect_tx(&s.kv_full[stage], 2 * F::kBoxes * kBoxBytes);
+#pragma unroll
+                for (int box = 0; box < F::kBoxes; ++box) {
+                    tma_load_4d(s.k_raw[stage] + box * kBoxFloats, &tmap_k, &s.kv_full[stage], 32 * box, first + j * kKeyTile, h, b);
+                    tma_load_4d(s.v_raw[stage] + box * kBoxFloats, &tmap_v, &s.kv_full[stage], 32 * box, first + j * kKeyTile, h, b);
+                }
                 ++issued;
             }
             if (!ok) {
@@ -295,11 +317,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mbar_wait(&s.kv_full[j % kStages], (j / kStages) & 1);
             }
         }
-    } else if (warp == kMmaWarp) {
+    } else if (warp == F::kMmaWarp) {
         // ---------------------------------------------------------------- MMA issuer
         // S(t, 0) and S(t, 1) first; then for every key tile j, whichever Q tile's P is ready
         // first gets P(j).V and S(j + 2) (into the buffer P(j) occupied) issued first; the K/V
-        // stage of tile j is released once both P.V products are issued. The whole warp runs
+        // stage of tile j is released once every P.V product is issued. The whole warp runs
         // the loop (uniform control flow and descriptors); elected lanes issue the tcgen05 ops.
         if (tiles > 0) {
             const uint64_t k_desc0 = sw128_descriptor(smem_u32(s.k16[0]));
@@ -311,25 +333,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
                 if (!ok) break;
 #pragma unroll
-                for (int t = 0; t < kQTiles; ++t) {
-                    issue_scores(tmem, k_desc0 + kDescStageK * j, t, j, &s.s_full[t][j]);
-                }
+                for (int t = 0; t < F::kQTiles; ++t) issue_scores<D>(tmem, k_desc0 + F::kDescStageK * j, t, j, &s.s_full[t][j]);
             }
             for (int j = 0; j < tiles && ok; ++j) {
                 const int stage = j % kStages, buffer = j & 1;
                 const bool more = j + 2 < tiles;
                 const int next_stage = (j + 2) % kStages;
                 bool next_ready = !more;
-                bool served[kQTiles] = {false, false};
+                bool served[F::kQTiles] = {};
                 const long long start_clock = clock64();
-                int remaining = kQTiles;
+                int remaining = F::kQTiles;
                 while (remaining > 0 && ok) {
 #pragma unroll
-                    for (int t = 0; t < kQTiles; ++t) {
+                    for (int t = 0; t < F::kQTiles; ++t) {
                         if (!ok || served[t] || !mbar_test_wait_warp(&s.p_full[t], j & 1)) continue;
                         if (lane == 0) RK_TRACE(j, t);
                         tc_fence_after();
-                        issue_values(tmem, v_desc0 + kDescStageV * stage, t, buffer, &s.pv_done[t]);
+                        issue_values<D>(tmem, v_desc0 + F::kDescStageV * stage, t, buffer, &s.pv_done[t]);
                         if (more) {
                             if (!next_ready) {
                                 next_ready = mbar_wait_warp(&s.kv_ready[next_stage], ((j + 2) / kStages) & 1);
@@ -339,7 +359,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 }
                                 tc_fence_after();
                             }
-                            issue_scores(tmem, k_desc0 + kDescStageK * next_stage, t, buffer, &s.s_full[t][buffer]);
+                            issue_scores<D>(tmem, k_desc0 + F::kDescStageK * next_stage, t, buffer, &s.s_full[t][buffer]);
                         }
                         served[t] = true;
                         --remaining;
@@ -355,17 +375,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_commit_warp(&s.mma_done);
             mbar_wait_warp(&s.mma_done, 0);
         }
-    } else if (warp >= kSplitWarp) {
+    } else if (warp >= F::kSplitWarp) {
         // ---------------------------------------------------------------- FP16 split
         // Split warp w owns key rows [32w, 32w + 32) of every tile; its ballot is their mask.
-        // K: lane = one key row (8 raw 16-byte chunks in, 8 FP16 chunks [k0 | k1] out).
-        // V: lane = (key group of 8 rows, chunk of 4 features): 8 raw chunks in, the 4 features'
-        // 8-key FP16 chunks of v0^T and v1^T out.
-        const int w = warp - kSplitWarp;
+        // K: lane = one key row -> its row-layout chunks [k0 | k1]. V: item = (key group of 8 rows,
+        // chunk of 4 features) -> the 4 features' 8-key FP16 chunks of v0^T and v1^T.
+        const int w = warp - F::kSplitWarp;
         const unsigned char *mask = p.mask + static_cast<long long>(b) * p.keys;
-        const int row = 32 * w + lane;          // K row of this lane
-        const int group = 4 * w + (lane >> 3);  // V key group (rows 8g..8g+7)
-        const int fchunk = lane & 7;            // V logical feature chunk (features 4f..4f+3)
+        const int row = 32 * w + lane;  // K row of this lane
         for (int j = 0; j < tiles; ++j) {
             const int stage = j % kStages, use = j / kStages;
             // Both split warps pass the named barrier below before either may give up, so a
@@ -374,19 +391,28 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int key = first + j * kKeyTile + row;
             const uint32_t bits = __ballot_sync(0xffffffffu, key < last && mask[key] != 0);
             const bool keep_row = (bits >> lane) & 1;
-            const float4 *k4 = reinterpret_cast<const float4 *>(s.k_raw[stage]);
-            const float4 *v4 = reinterpret_cast<const float4 *>(s.v_raw[stage]);
-            float4 kx[8], vx[8];
+            // This lane's K row and V items stay in registers from the max pass to the conversion.
+            // V item (group, fchunk) covers rows 8 group .. 8 group + 7, all rows of this warp.
+            float4 kx[D / 4], vx[D / 32][8];
             float kmax = 0.f, vmax = 0.f;
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                kx[c] = k4[row * 8 + (c ^ (row & 7))];  // logical chunk c of the row
+            for (int c = 0; c < D / 4; ++c) {
+                kx[c] = raw_chunk<D>(s.k_raw[stage], row, c);
                 if (!keep_row) kx[c] = make_float4(0.f, 0.f, 0.f, 0.f);
-                kmax = fmaxf(kmax, fmaxf(fmaxf(fabsf(kx[c].x), fabsf(kx[c].y)), fmaxf(fabsf(kx[c].z), fabsf(kx[c].w))));
-                const int vrow = 8 * group + c;
-                vx[c] = v4[vrow * 8 + (fchunk ^ (vrow & 7))];
-                if (!((bits >> (vrow & 31)) & 1)) vx[c] = make_float4(0.f, 0.f, 0.f, 0.f);
-                vmax = fmaxf(vmax, fmaxf(fmaxf(fabsf(vx[c].x), fabsf(vx[c].y)), fmaxf(fabsf(vx[c].z), fabsf(vx[c].w))));
+                kmax = max3(kmax, fmaxf(fabsf(kx[c].x), fabsf(kx[c].y)), fmaxf(fabsf(kx[c].z), fabsf(kx[c].w)));
+            }
+#pragma unroll
+            for (int item = 0; item < D / 32; ++item) {
+                const int index = 64 * item + row;  // 0 .. 2D - 1
+                const int group = index >> 3 & 7, fchunk = (index & 7) + 8 * (index >> 6);
+#pragma unroll
+                for (int r = 0; r < 8; ++r) {
+                    const int vrow = 8 * group + r;
+                    vx[item][r] = raw_chunk<D>(s.v_raw[stage], vrow, fchunk);
+                    if (!((bits >> (vrow & 31)) & 1)) vx[item][r] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    vmax = max3(vmax, fmaxf(fabsf(vx[item][r].x), fabsf(vx[item][r].y)),
+                                fmaxf(fabsf(vx[item][r].z), fabsf(vx[item][r].w)));
+                }
             }
 #pragma unroll
             for (int offset = 16; offset; offset >>= 1) {
@@ -404,40 +430,41 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int k_exponent = fp16_scale_exponent(fmaxf(s.split_max[0][0], s.split_max[1][0]));
             const int v_exponent = fp16_scale_exponent(fmaxf(s.split_max[0][1], s.split_max[1][1]));
             asm volatile("bar.sync 1, 64;" ::: "memory");  // split_max is rewritten for the next tile
-            if (threadIdx.x == kSplitWarp * 32) {
+            if (threadIdx.x == F::kSplitWarp * 32) {
                 s.k_exponent[stage] = k_exponent;
                 s.v_exponent[stage] = v_exponent;
             }
             const float k_scale = exp2_int(k_exponent), v_scale = exp2_int(v_exponent);
-            // K row: features 8m..8m+7 -> k0 chunk m, k1 chunk 4 + m (16-byte chunks, swizzled by row % 8)
-            uint4 *k16 = reinterpret_cast<uint4 *>(s.k16[stage]);
+            // K row: features 8m..8m+7 -> k0 chunk m and k1 chunk m of the row layout
 #pragma unroll
-            for (int m = 0; m < 4; ++m) {
+            for (int m = 0; m < D / 8; ++m) {
                 const float x[8] = {kx[2 * m].x, kx[2 * m].y, kx[2 * m].z, kx[2 * m].w,
                                     kx[2 * m + 1].x, kx[2 * m + 1].y, kx[2 * m + 1].z, kx[2 * m + 1].w};
                 float x0[8], x1[8];
 #pragma unroll
                 for (int e = 0; e < 8; ++e) split_half(x[e], k_scale, x0[e], x1[e]);
-                k16[row * 8 + (m ^ (row & 7))] = make_uint4(pack_half2(x0[0], x0[1]), pack_half2(x0[2], x0[3]),
-                                                            pack_half2(x0[4], x0[5]), pack_half2(x0[6], x0[7]));
-                k16[row * 8 + ((4 + m) ^ (row & 7))] = make_uint4(pack_half2(x1[0], x1[1]), pack_half2(x1[2], x1[3]),
-                                                                  pack_half2(x1[4], x1[5]), pack_half2(x1[6], x1[7]));
+                *row_chunk<D>(s.k16[stage], row, 0, m) = pack_chunk(x0);
+                *row_chunk<D>(s.k16[stage], row, 1, m) = pack_chunk(x1);
             }
-            // V^T rows f (v0) and 32 + f (v1), keys 8g..8g+7 = 16-byte chunk g (swizzled by f % 8)
+            // V^T rows f (v0) and D + f (v1), keys 8g..8g+7 = 16-byte chunk g (swizzled by f % 8)
             uint4 *vt16 = reinterpret_cast<uint4 *>(s.vt16[stage]);
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int f = 4 * fchunk + e;
-                float v0[8], v1[8];
+            for (int item = 0; item < D / 32; ++item) {
+                const int index = 64 * item + row;
+                const int group = index >> 3 & 7, fchunk = (index & 7) + 8 * (index >> 6);
 #pragma unroll
-                for (int r = 0; r < 8; ++r) {
-                    const float value = e == 0 ? vx[r].x : e == 1 ? vx[r].y : e == 2 ? vx[r].z : vx[r].w;
-                    split_half(value, v_scale, v0[r], v1[r]);
+                for (int e = 0; e < 4; ++e) {
+                    const int f = 4 * fchunk + e;
+                    float v0[8], v1[8];
+#pragma unroll
+                    for (int r = 0; r < 8; ++r) {
+                        const float4 &x = vx[item][r];
+                        const float value = e == 0 ? x.x : e == 1 ? x.y : e == 2 ? x.z : x.w;
+                        split_half(value, v_scale, v0[r], v1[r]);
+                    }
+                    vt16[f * 8 + (group ^ (f & 7))] = pack_chunk(v0);
+                    vt16[(D + f) * 8 + (group ^ (f & 7))] = pack_chunk(v1);
                 }
-                vt16[f * 8 + (group ^ (f & 7))] = make_uint4(pack_half2(v0[0], v0[1]), pack_half2(v0[2], v0[3]),
-                                                             pack_half2(v0[4], v0[5]), pack_half2(v0[6], v0[7]));
-                vt16[(32 + f) * 8 + (group ^ (f & 7))] = make_uint4(pack_half2(v1[0], v1[1]), pack_half2(v1[2], v1[3]),
-                                                                    pack_half2(v1[4], v1[5]), pack_half2(v1[6], v1[7]));
             }
             fence_proxy_async_shared();
             if (lane == 0 && w == 0) RK_TRACE(j, 3);
@@ -445,20 +472,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         // ---------------------------------------------------------------- softmax / epilogue
-        const int tile = warp >> 2;  // 0 = A, 1 = B
+        const int tile = warp >> 2;  // Q tile (0 = A, 1 = B)
         const int row_in_tile = threadIdx.x & (kQTile - 1);
         const int query = q0 + tile * kQTile + row_in_tile;
         const bool row_valid = query < p.queries;
-        const uint32_t lane_base = tmem_lane_address(tmem, warp) + tile * kColTile;
+        const uint32_t lane_base = tmem_lane_address(tmem, warp) + tile * F::kColTile;
         const bool tracer = row_in_tile == 0;
 
         int q_exponent;
         {  // Q row -> scaled by 1/sqrt(D) and 2^q_exponent, split into FP16 q0/q1 pairs in TMEM
-            float x[32];
+            float x[D];
             const float4 *q4 = reinterpret_cast<const float4 *>(p.q.row(b, h, row_valid ? query : 0));
             float qmax = 0.f;
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
+            for (int c = 0; c < D / 4; ++c) {
                 const float4 v = row_valid ? __ldg(q4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
                 x[4 * c] = v.x * p.scale;
                 x[4 * c + 1] = v.y * p.scale;
@@ -469,31 +496,34 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             q_exponent = fp16_scale_exponent(qmax);
             const float q_scale = exp2_int(q_exponent);
-            float packed0[16], packed1[16];
 #pragma unroll
-            for (int c = 0; c < 16; ++c) {
-                float a0, a1, b0, b1;
-                split_half(x[2 * c], q_scale, a0, a1);
-                split_half(x[2 * c + 1], q_scale, b0, b1);
-                packed0[c] = __uint_as_float(pack_half2(a0, b0));
-                packed1[c] = __uint_as_float(pack_half2(a1, b1));
+            for (int half = 0; half < D / 32; ++half) {
+                float packed0[16], packed1[16];
+#pragma unroll
+                for (int c = 0; c < 16; ++c) {
+                    float a0, a1, b0, b1;
+                    split_half(x[32 * half + 2 * c], q_scale, a0, a1);
+                    split_half(x[32 * half + 2 * c + 1], q_scale, b0, b1);
+                    packed0[c] = __uint_as_float(pack_half2(a0, b0));
+                    packed1[c] = __uint_as_float(pack_half2(a1, b1));
+                }
+                tmem_store16x2(lane_base + F::kColQ0 + 16 * half, packed0, lane_base + F::kColQ1 + 16 * half, packed1);
             }
-            tmem_store16x2(lane_base + kColQ0, packed0, lane_base + kColQ1, packed1);
             tc_fence_before();
             mbar_arrive(&s.q_ready);
         }
 
         float row_max = -INFINITY, row_sum = 0.f;  // row_sum carries the 2^14 of P
-        float o[32];                               // running output, scaled by 2^o_exp
+        float o[D];                                // running output, scaled by 2^o_exp
 #pragma unroll
-        for (int c = 0; c < 32; ++c) o[c] = 0.f;
+        for (int c = 0; c < D; ++c) o[c] = 0.f;
         int o_exp = kNoExponent;
         float pending_weight = 0.f;  // exp(m_(j-2) - m_(j-1)), applied when tile j-1 is folded
         int pending_exponent = 0;    // c_(j-1): the V exponent of tile j-1
         bool ok = true;
         for (int j = 0; j < tiles && ok; ++j) {
             const int stage = j % kStages, use = j / kStages, buffer = j & 1;
-            const uint32_t pbuf = lane_base + kColBuffer + buffer * kBufferColumns;
+            const uint32_t pbuf = lane_base + F::kColBuffer + buffer * F::kBufferColumns;
             ok = __all_sync(0xffffffffu, mbar_wait(&s.s_full[tile][buffer], (j >> 1) & 1) &&
                                                  mbar_wait(&s.kv_ready[stage], use & 1));
             if (!ok) break;
@@ -545,7 +575,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                fold_output(o, row_sum, o_exp, lane_base, pending_weight, pending_exponent);
+                fold_output<D>(o, row_sum, o_exp, lane_base, pending_weight, pending_exponent);
             }
             RK_WARP_TRACE(j, 3);
             tmem_wait_store();
@@ -562,21 +592,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (tiles > 0 && ok) {
             ok = __all_sync(0xffffffffu, mbar_wait(&s.pv_done[tile], (tiles - 1) & 1));
             tc_fence_after();
-            if (ok) fold_output(o, row_sum, o_exp, lane_base, pending_weight, pending_exponent);
+            if (ok) fold_output<D>(o, row_sum, o_exp, lane_base, pending_weight, pending_exponent);
         }
         if (row_valid) {
             const float total = ok ? row_sum : NAN;
             float *out = p.o.row(b, h, query);
             const float out_scale = exp2_int(-o_exp) / total;
 #pragma unroll
-            for (int c = 0; c < 32; ++c) o[c] = total > 0.f ? o[c] * out_scale : isnan(total) ? NAN : 0.f;
+            for (int c = 0; c < D; ++c) o[c] = total > 0.f ? o[c] * out_scale : isnan(total) ? NAN : 0.f;
             if (args.vec_out) {
 #pragma unroll
-                for (int c = 0; c < 8; ++c)
+                for (int c = 0; c < D / 4; ++c)
                     reinterpret_cast<float4 *>(out)[c] = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
             } else {
 #pragma unroll
-                for (int c = 0; c < 32; ++c) out[c] = o[c];
+                for (int c = 0; c < D; ++c) out[c] = o[c];
             }
             const long long row = (static_cast<long long>(b) * p.heads + h) * p.queries + query;
             p.lse[row * 2] = total > 0.f ? row_max : isnan(total) ? NAN : -INFINITY;
@@ -588,7 +618,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        tmem_dealloc(tmem, kTmemColumns);
+        tmem_dealloc(tmem, F::kTmemColumns);
     }
 }
 
@@ -607,14 +637,15 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_function() {
     return function;
 }
 
-// [batch][heads][tokens][32] FP32 with the given element strides; box = 32 features x rows tokens.
-bool make_tensor_map(CUtensorMap *map, const Tensor &t, int batch, int heads, int tokens, int rows) {
+// [batch][heads][tokens][width] FP32 with the given element strides; box = 32 features x 64 tokens.
+bool make_tensor_map(CUtensorMap *map, const Tensor &t, int width, int batch, int heads, int tokens) {
     auto encode = encode_function();
     if (encode == nullptr) return false;
-    const cuuint64_t dims[4] = {kD, static_cast<cuuint64_t>(tokens), static_cast<cuuint64_t>(heads), static_cast<cuuint64_t>(batch)};
+    const cuuint64_t dims[4] = {static_cast<cuuint64_t>(width), static_cast<cuuint64_t>(tokens), static_cast<cuuint64_t>(heads),
+                                static_cast<cuuint64_t>(batch)};
     const cuuint64_t strides[3] = {static_cast<cuuint64_t>(t.st) * 4, static_cast<cuuint64_t>(t.sh) * 4,
                                    static_cast<cuuint64_t>(t.sb) * 4};
-    const cuuint32_t box[4] = {kD, static_cast<cuuint32_t>(rows), 1, 1};
+    const cuuint32_t box[4] = {32, static_cast<cuuint32_t>(kKeyTile), 1, 1};
     const cuuint32_t element_strides[4] = {1, 1, 1, 1};
     return encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float *>(t.data), dims, strides, box, element_strides,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
@@ -627,12 +658,35 @@ bool positive_tma_strides(const Tensor &t) {
            t.sh < limit && t.sb < limit && (reinterpret_cast<uintptr_t>(t.data) & 15u) == 0;
 }
 
-constexpr int kSharedBytes = static_cast<int>(sizeof(SharedStorage)) + 1024;
-static_assert(sizeof(SharedStorage::k16[0]) == 64 * 128 && sizeof(SharedStorage::vt16[0]) == kVRows * 128,
-              "FP16 operand tiles are rows of 128 bytes");
-static_assert(sizeof(SharedStorage::vt16[0]) % 1024 == 0, "V operand tiles stay 1024-byte aligned");
-static_assert(kColSum + 16 <= kColTile, "Q tile TMEM columns");
-static_assert(kSharedBytes <= 227 * 1024, "shared memory budget");
+template <int D>
+constexpr int shared_bytes() {
+    return static_cast<int>(sizeof(SharedStorage<D>)) + 1024;
+}
+template <int D>
+constexpr bool layout_ok() {
+    using F = Forward<D>;
+    return sizeof(SharedStorage<D>::k16[0]) == 64 * 2 * D * 2 && sizeof(SharedStorage<D>::vt16[0]) == F::kVRows * 128 &&
+           sizeof(SharedStorage<D>::vt16[0]) % 1024 == 0 && F::kColSum + 16 <= (F::kQTiles == 2 ? F::kColTile : F::kTmemColumns) &&
+           shared_bytes<D>() <= 227 * 1024;
+}
+static_assert(layout_ok<32>() && layout_ok<64>(), "operand tiles, TMEM columns and shared memory budget");
+
+template <int D>
+int launch(const AttentionParams &p, cudaStream_t stream) {
+    using F = Forward<D>;
+    CUtensorMap tmap_k, tmap_v;
+    if (!make_tensor_map(&tmap_k, p.k, D, p.batch, p.heads, p.keys) || !make_tensor_map(&tmap_v, p.v, D, p.batch, p.heads, p.keys))
+        return kNotEligible;
+    cudaError_t status = prepare_kernel<flash_forward_kernel<D>>(shared_bytes<D>());
+    if (status != cudaSuccess) return status;
+    FlashArgs args{};
+    args.p = p;
+    args.cta_per_head = (p.queries + F::kCtaQueries - 1) / F::kCtaQueries;
+    args.vec_out = (reinterpret_cast<uintptr_t>(p.o.data) & 15u) == 0 && p.o.sb % 4 == 0 && p.o.sh % 4 == 0 && p.o.st % 4 == 0;
+    const unsigned blocks = static_cast<unsigned>(args.cta_per_head) * static_cast<unsigned>(p.heads) * static_cast<unsigned>(p.batch);
+    flash_forward_kernel<D><<<blocks, F::kThreads, shared_bytes<D>(), stream>>>(args, tmap_k, tmap_v);
+    return cudaGetLastError();
+}
 
 }  // namespace
 
@@ -641,20 +695,10 @@ bool flash_supported(const AttentionParams &p) {
            (reinterpret_cast<uintptr_t>(p.q.data) & 15u) == 0;
 }
 
-int launch_flash_forward(const AttentionParams &p, cudaStream_t stream) {
-    CUtensorMap tmap_k, tmap_v;
-    if (!make_tensor_map(&tmap_k, p.k, p.batch, p.heads, p.keys, kKeyTile) ||
-        !make_tensor_map(&tmap_v, p.v, p.batch, p.heads, p.keys, kKeyTile))
-        return kNotEligible;
-    cudaError_t status = prepare_kernel<flash_forward_kernel>(kSharedBytes);
-    if (status != cudaSuccess) return status;
-    FlashArgs args{};
-    args.p = p;
-    args.cta_per_head = (p.queries + kCtaQueries - 1) / kCtaQueries;
-    args.vec_out = (reinterpret_cast<uintptr_t>(p.o.data) & 15u) == 0 && p.o.sb % 4 == 0 && p.o.sh % 4 == 0 && p.o.st % 4 == 0;
-    const unsigned blocks = static_cast<unsigned>(args.cta_per_head) * static_cast<unsigned>(p.heads) * static_cast<unsigned>(p.batch);
-    flash_forward_kernel<<<blocks, kThreads, kSharedBytes, stream>>>(args, tmap_k, tmap_v);
-    return cudaGetLastError();
+int launch_flash_forward(const AttentionParams &p, int head_width, cudaStream_t stream) {
+    if (head_width == 32) return launch<32>(p, stream);
+    if (head_width == 64) return launch<64>(p, stream);
+    return kNotEligible;
 }
 
 unsigned int read_device_status(bool clear) {
@@ -667,7 +711,7 @@ unsigned int read_device_status(bool clear) {
     return value;
 }
 
-const char *kernel_name() { return "tcgen05-f16x2-flash-d32"; }
+const char *kernel_name(int head_width) { return head_width == 64 ? "tcgen05-f16x2-flash-d64" : "tcgen05-f16x2-flash-d32"; }
 
 #ifdef RK_TC_TRACE
 extern "C" __attribute__((visibility("default"))) int rocmkernels_attention_trace(long long *out, int capacity) {
@@ -680,8 +724,8 @@ extern "C" __attribute__((visibility("default"))) int rocmkernels_attention_trac
 #endif
 
 const char *build_info() {
-    return "sm_100a; tcgen05-f16x2-flash-d32 forward (TMA + TMEM, split FP16 operands, double-buffered S, tensor-core row sums); "
-           "simt-fp32 d32/d64 forward+backward";
+    return "sm_100a; tcgen05-f16x2-flash-d32/d64 forward (TMA + TMEM, split FP16 operands, double-buffered S, tensor-core row "
+           "sums); tcgen05 split-FP16 backward d32/d64 (query-major delta+dQ, key-major dK/dV); simt-fp32 d32/d64 forward+backward";
 }
 
 }  // namespace tc

@@ -10,17 +10,19 @@ namespace tc {
 // caller then runs the SIMT kernel instead.
 constexpr int kNotEligible = -1;
 
-// True when the tensor-core kernel accepts the problem (head width 32, TMA-addressable tensors).
+// True when the tensor-core flash forward accepts the tensors (TMA-addressable K and V, 16-byte
+// addressable Q rows).
 bool flash_supported(const AttentionParams &p);
-// Launches the tensor-core flash forward; returns a cudaError_t value.
-int launch_flash_forward(const AttentionParams &p, cudaStream_t stream);
+// Launches the tensor-core flash forward for head width 32 or 64; returns a cudaError_t value or
+// kNotEligible.
+int launch_flash_forward(const AttentionParams &p, int head_width, cudaStream_t stream);
 // Static description of the build (architecture and kernel families).
 const char *build_info();
 // Reads (and optionally clears) the device status word set by a failed bounded wait;
 // synchronizes with the device. 0 = no failure recorded.
 unsigned int read_device_status(bool clear);
-// Name of the tensor-core flash kernel (for benchmarks and profiles).
-const char *kernel_name();
+// Name of the tensor-core flash kernel for a head width (for benchmarks and profiles).
+const char *kernel_name(int head_width);
 
 // True when the tensor-core backward accepts the tensors (TMA-addressable q, k, v, dO; 16-byte
 // addressable O and gradients).

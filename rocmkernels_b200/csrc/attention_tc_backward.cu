@@ -35,7 +35,7 @@
 
 #include <mutex>
 
-#include "tc_primitives.cuh"
+#include "tc_operands.cuh"
 
 namespace rk {
 namespace tc {
@@ -50,8 +50,6 @@ constexpr int kProducerWarp = 4;
 constexpr int kMmaWarp = 5;
 constexpr int kSplitWarp = 6;
 constexpr int kSplitThreads = 64;
-constexpr int kBoxFloats = kCols * 32;     // one TMA box: 64 rows x 32 features (128 B), 8 KB
-constexpr int kBoxBytes = kBoxFloats * 4;
 constexpr uint32_t kIdescS = f16_instr_desc(128, 64);
 constexpr uint64_t kDescStep = 2;  // one K=16 step of FP16 = 32 bytes
 
@@ -65,7 +63,7 @@ struct Geometry {
     static constexpr int kKSteps = D / 16;                  // K=16 steps over the features
     // Row layout: D = 32 keeps [x0 | x1] in one 128-byte row; D = 64 uses an x0 tile and an x1
     // tile of 64 rows x 128 bytes each. Descriptor offset (16-byte units) of the x1 part.
-    static constexpr uint64_t kDescX1 = D == 32 ? 4 : kBoxBytes / 16;
+    static constexpr uint64_t kDescX1 = row_x1_offset<D>();
     static constexpr uint64_t kDescUpper = D * 128 / 16;   // transposed: x1^T rows start
     // TMEM columns
     static constexpr uint32_t kColA1 = 0, kColA2 = D, kColS = 2 * D, kColDP = 2 * D + 64, kColX1 = 2 * D + 128,
@@ -111,13 +109,6 @@ __device__ __forceinline__ uint32_t lane_address(uint32_t base, int warp) {
     return base + (static_cast<uint32_t>((warp & 3) * 32) << 16);
 }
 
-// x' = x * scale split into x0 (11 significant bits, exact in FP16) and x1 = x' - x0.
-__device__ __forceinline__ void split_half(float x, float scale, float &x0, float &x1) {
-    const float scaled = x * scale;
-    x0 = round_tf32(scaled);
-    x1 = scaled - x0;
-}
-
 // Splits a D-feature row (scaled by 2^exponent) and stores it to TMEM at `column` as FP16 pairs:
 // x0 pairs in columns [0, D/2), x1 pairs in [D/2, D).
 template <int D>
@@ -158,24 +149,6 @@ __device__ __forceinline__ float abs_max(const float (&x)[D]) {
 #pragma unroll
     for (int c = 0; c < D; c += 2) m = max3(m, fabsf(x[c]), fabsf(x[c + 1]));
     return m;
-}
-
-// 16-byte chunk `chunk` (features 4 chunk .. 4 chunk + 3) of row `row` of an FP32 tile: D = 64
-// tiles are two 64 x 32 boxes side by side.
-template <int D>
-__device__ __forceinline__ float4 raw_chunk(const float *tile, int row, int chunk) {
-    const float4 *box = reinterpret_cast<const float4 *>(tile) + (chunk >> 3) * (kBoxFloats / 4);
-    return box[row * 8 + ((chunk & 7) ^ (row & 7))];
-}
-
-// Row layout: the 16-byte FP16 chunk m (features 8m..8m+7) of part x0 (part 0) or x1 (part 1)
-// of row `row`, 128B-swizzled.
-template <int D>
-__device__ __forceinline__ uint4 *row_chunk(uint32_t *tile, int row, int part, int m) {
-    if constexpr (D == 32)
-        return reinterpret_cast<uint4 *>(tile) + row * 8 + ((4 * part + m) ^ (row & 7));
-    else
-        return reinterpret_cast<uint4 *>(tile) + part * (kBoxBytes / 16) + row * 8 + (m ^ (row & 7));
 }
 
 // X (N = D) = x1.t0 + x0.t0 + x0.t1 over the 64 columns: A chunks of 16 columns at

@@ -1,0 +1,59 @@
+// Shared-memory layouts of the split-FP16 tensor-core operands (sm_100a), shared by the flash
+// forward and the backward.
+//
+//   FP32 tiles as TMA lands them: 64 rows x D features as D / 32 boxes of 64 rows x 32 features
+//   (128 bytes per row, 128B swizzle: 16-byte chunk c of row r at r * 8 + (c ^ (r % 8))).
+//   Row layout (K-major B operand over the features): row r holds x0 (D FP16) and x1 (D FP16);
+//   for D = 32 both halves share one 128-byte row ([x0 | x1]), for D = 64 x0 and x1 are separate
+//   64 x 128-byte tiles. 128B swizzle.
+//   Transposed layout (K-major B operand over the 64 rows): feature rows f (x0) and D + f (x1),
+//   each 64 FP16 (128 bytes), rows 8g..8g+7 of the source tile in 16-byte chunk g. 128B swizzle.
+#pragma once
+
+#include "tc_primitives.cuh"
+
+namespace rk {
+namespace tc {
+
+constexpr int kBoxRows = 64;
+constexpr int kBoxFloats = kBoxRows * 32;  // one TMA box: 64 rows x 32 FP32 (8 KB)
+constexpr int kBoxBytes = kBoxFloats * 4;
+
+// x' = x * scale split into x0 (11 significant bits, exact in FP16) and x1 = x' - x0 (rounded to
+// FP16 when packed).
+__device__ __forceinline__ void split_half(float x, float scale, float &x0, float &x1) {
+    const float scaled = x * scale;
+    x0 = round_tf32(scaled);
+    x1 = scaled - x0;
+}
+
+// 16-byte chunk `chunk` (features 4 chunk .. 4 chunk + 3) of row `row` of an FP32 tile.
+template <int D>
+__device__ __forceinline__ float4 raw_chunk(const float *tile, int row, int chunk) {
+    const float4 *box = reinterpret_cast<const float4 *>(tile) + (chunk >> 3) * (kBoxFloats / 4);
+    return box[row * 8 + ((chunk & 7) ^ (row & 7))];
+}
+
+// Row layout: the 16-byte FP16 chunk m (features 8m..8m+7) of part x0 (part 0) or x1 (part 1)
+// of row `row`.
+template <int D>
+__device__ __forceinline__ uint4 *row_chunk(uint32_t *tile, int row, int part, int m) {
+    if constexpr (D == 32)
+        return reinterpret_cast<uint4 *>(tile) + row * 8 + ((4 * part + m) ^ (row & 7));
+    else
+        return reinterpret_cast<uint4 *>(tile) + part * (kBoxBytes / 16) + row * 8 + (m ^ (row & 7));
+}
+
+// Descriptor offset (16-byte units) of the x1 part of a row-layout tile.
+template <int D>
+constexpr uint64_t row_x1_offset() {
+    return D == 32 ? 4 : kBoxBytes / 16;
+}
+
+// Packs eight FP32 values into one 16-byte FP16 chunk (element i at byte 2 i).
+__device__ __forceinline__ uint4 pack_chunk(const float (&x)[8]) {
+    return make_uint4(pack_half2(x[0], x[1]), pack_half2(x[2], x[3]), pack_half2(x[4], x[5]), pack_half2(x[6], x[7]));
+}
+
+}  // namespace tc
+}  // namespace rk

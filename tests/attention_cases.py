@@ -99,6 +99,13 @@ class Device:
     def get(tensor):
         return tensor.detach().cpu().numpy()
 
+    def padded(self, array):
+        """[B, H, S, D] view of [B, H, S, D + 1] storage (token stride D + 1 floats)."""
+        B, H, S, D = array.shape
+        storage = self.torch.zeros((B, H, S, D + 1), device=self.device)
+        storage[..., :D] = self.put(array)
+        return storage[..., :D]
+
     def forward(self, entry, q, k, v, mask, radius=-1, selector=None, layout="bhsd", queries_first=False):
         """Runs a forward entry point. layout="bshd" stores q/k/v/O token-major (strided heads)."""
         import rocmkernels_b200.attention as api
@@ -109,6 +116,10 @@ class Device:
         if layout == "bhsd":
             dq, dk, dv = self.put(q), self.put(k), self.put(v)
             out = torch.full((B, H, Q, D), float("nan"), device=self.device)
+            views = dq, dk, dv, out
+        elif layout == "padded":  # token stride D + 1: not TMA-addressable, exercises the SIMT fallbacks
+            dq, dk, dv = (self.padded(x) for x in (q, k, v))
+            out = self.padded(np.full((B, H, Q, D), np.nan, np.float32))
             views = dq, dk, dv, out
         else:  # [B, S, H, D] storage viewed as [B, H, S, D]
             dq, dk, dv = (self.put(np.ascontiguousarray(x.transpose(0, 2, 1, 3))).transpose(1, 2) for x in (q, k, v))
@@ -132,6 +143,8 @@ class Device:
         K = k.shape[2]
         if layout == "bhsd":
             tensors = [self.put(x) for x in (q, k, v, output, upstream)]
+        elif layout == "padded":
+            tensors = [self.padded(x) for x in (q, k, v, output, upstream)]
         else:
             tensors = [self.put(np.ascontiguousarray(x.transpose(0, 2, 1, 3))).transpose(1, 2) for x in (q, k, v, output, upstream)]
         dq_, dk_, dv_, do_, du_ = tensors

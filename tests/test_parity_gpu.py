@@ -91,7 +91,7 @@ SHAPES = [
 
 
 @pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "b{}h{}q{}k{}d{}r{}m{}".format(*s[:7]))
-@pytest.mark.parametrize("layout", ["bhsd", "bshd"])
+@pytest.mark.parametrize("layout", ["bhsd", "bshd", "padded"])
 def test_random_shapes_forward_backward(dev, shape, layout):
     B, H, Q, K, D, radius, fraction, masked = shape
     q, k, v, upstream, mask = make_inputs(B, H, Q, K, D, seed=7 + Q, dist="normal", mask_fraction=fraction,
