@@ -300,7 +300,19 @@ def main() -> None:
     if world > 1:
         import datetime
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+        # NCCL may print a banner to stdout when its communicator starts; stdout carries only the
+        # JSON line, so everything written during set-up (and the first collective) goes to stderr.
+        sys.stdout.flush()
+        saved_stdout = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+            dist.barrier()
+            torch.cuda.synchronize(device)
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved_stdout, 1)
+            os.close(saved_stdout)
 
     spec = WORKLOADS[args.workload]
     heads, seq, dim, radius, with_backward = spec["heads"], spec["seq"], spec["dim"], spec["radius"], spec["backward"]
