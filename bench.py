@@ -14,7 +14,10 @@ The other BASELINE configs are opt-in workloads (``--workload``): forward + back
 on a fixed global problem whose batch is split over the ranks (strong scaling), with the
 BASELINE key-padding lengths (seed 105) and radius. They report the repo-convention TFLOP/s
 (12*B*H*Q*K*d per step) as ``value``, the effective TFLOP/s over active (query, key) pairs, and
-the forward and backward times separately.
+the forward and backward times separately. The ``generic_*`` workloads are the reference's
+AttentionGeneric benchmark cases (AttentionGenericBenchmarks.cpp:14-18, 100-110: B2 H8 L512,
+d = 16/32/64, fp32 or fp16 storage): a step is one ``attention_generic_forward`` call, per GPU
+(weak scaling), 4*B*H*Q*K*d FLOPs (the reference's operation count, :96).
 
 Timing: W untimed steps, then K steps; before each step a 256 MiB buffer is written to flush
 the 126 MB L2, and the step itself is bracketed by CUDA events on the launching stream (the
@@ -64,6 +67,12 @@ WORKLOADS = {
     "fwd_bwd_b4h12s4096d32": dict(batch=4, heads=12, seq=4096, dim=32, radius=-1, lengths=None, backward=True,
                                   description="profiling case: C5's shape at B=4 (inputs above L2, a few hundred MB)"),
 }
+for _width in (16, 32, 64):
+    for _storage in ("fp32", "fp16"):
+        WORKLOADS[f"generic_fwd_b2h8s512d{_width}_{_storage}"] = dict(
+                batch=2, heads=8, seq=512, dim=_width, radius=-1, lengths=None, backward=False, generic=_storage,
+                description=f"AttentionGeneric{_width} {_storage} b2 h8 l512 (AttentionGenericBenchmarks.cpp:79-110), "
+                            f"attention_generic_forward")
 DEFAULT_WORKLOAD = "flash_fwd_b8h3s1024d32"
 PUBLISHED_TFLOPS = 3.36  # flash fwd d32, same FLOPs (B2 H12 L1024), RX 6700 (README.md:63)
 METRIC = "FP32 attention TFLOP/s (repo FLOP convention: 4*B*H*Q*K*d forward, 8*B*H*Q*K*d backward)"
@@ -97,6 +106,8 @@ def workload_config(name: str, world: int) -> dict:
     spec = WORKLOADS[name]
     config = {"workload": name, "description": spec["description"], "heads": spec["heads"], "seq_len": spec["seq"],
               "head_dim": spec["dim"], "radius": spec["radius"], "l2": "flushed (256 MiB write) before every step"}
+    if spec.get("generic"):
+        config["storage"] = spec["generic"]
     if spec["backward"]:
         lengths = key_lengths(spec)
         config.update({"global_batch": spec["batch"], "batch_per_gpu": spec["batch"] // world, "step": "forward + backward",
@@ -194,6 +205,8 @@ def cpu_baseline(spec: dict) -> dict:
     q = oracle.normal(batch * heads * seq * dim, 101).reshape(batch, heads, seq, dim)
     k = oracle.normal(batch * heads * seq * dim, 102).reshape(batch, heads, seq, dim)
     v = oracle.normal(batch * heads * seq * dim, 103).reshape(batch, heads, seq, dim)
+    if spec.get("generic") == "fp16":  # the values FP16 storage holds, widened (AttentionGenericTests.cpp:118-119)
+        q, k, v = (x.astype(np.float16).astype(np.float32) for x in (q, k, v))
     mask = np.zeros((batch, seq), dtype="uint8")
     mask[:, :length] = 1
     reps, elapsed = 0, 0.0
@@ -215,6 +228,9 @@ def run_reference(args, rank: int) -> None:
     from oracle import oracle
 
     spec = WORKLOADS[args.workload]
+    if spec.get("generic"):
+        run_reference_generic(args, spec)
+        return
     seq, dim, radius = spec["seq"], spec["dim"], spec["radius"]
     length = key_lengths(spec)[0]
     threads = oracle.cpu_count()
@@ -259,6 +275,22 @@ def run_reference(args, rank: int) -> None:
             "config": workload_config(args.workload, args.gpus), "impl": "reference",
             "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": kind, "sample": sample},
             "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_reference_generic(args, spec: dict) -> None:
+    """--impl reference for the generic workloads: the reference has no CPU implementation of the
+    generic forward besides its test's double-precision ComputeReference
+    (AttentionGenericTests.cpp:45-104), which the oracle's forward restates; it runs on the full
+    workload with all host threads."""
+    base = cpu_baseline(spec)
+    elapsed_per_step = 4.0 * spec["batch"] * spec["heads"] * spec["seq"] ** 2 * spec["dim"] / (base["value"] * 1e12)
+    line = {"metric": METRIC, "value": base["value"], "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": elapsed_per_step * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f64-accumulate", "data": "synthetic N(0,1), seeded",
+            "config": workload_config(args.workload, args.gpus), "impl": "reference",
+            "cpu_baseline": base,
+            "e2e": {"value": base["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
@@ -316,6 +348,8 @@ def main() -> None:
 
     spec = WORKLOADS[args.workload]
     heads, seq, dim, radius, with_backward = spec["heads"], spec["seq"], spec["dim"], spec["radius"], spec["backward"]
+    generic = spec.get("generic")  # None, or the generic forward's storage type
+    storage = torch.float16 if generic == "fp16" else torch.float32
     if with_backward:
         if spec["batch"] % world:
             raise SystemExit(f"the global batch {spec['batch']} must be divisible by the {world} ranks")
@@ -326,9 +360,9 @@ def main() -> None:
         lengths = [seq] * batch
     generator = torch.Generator(device=device)
     generator.manual_seed(101 + rank)
-    q = torch.randn(batch, heads, seq, dim, device=device, generator=generator)
-    k = torch.randn(batch, heads, seq, dim, device=device, generator=generator)
-    v = torch.randn(batch, heads, seq, dim, device=device, generator=generator)
+    q = torch.randn(batch, heads, seq, dim, device=device, generator=generator).to(storage)
+    k = torch.randn(batch, heads, seq, dim, device=device, generator=generator).to(storage)
+    v = torch.randn(batch, heads, seq, dim, device=device, generator=generator).to(storage)
     mask = torch.zeros(batch, seq, dtype=torch.uint8, device=device)
     for i, length in enumerate(lengths):
         mask[i, :length] = 1
@@ -354,9 +388,13 @@ def main() -> None:
     launches_per_step = 1 + (2 if with_backward else 0)
 
     def forward():
-        status = forward_fn(q, k, v, mask, out, lse, batch, heads, seq, seq, radius, qs, ks, vs, os_, stream)
+        if generic:
+            status = api.attention_generic_forward(q, k, v, mask, out, lse, batch, heads, seq, seq, dim, radius, qs, ks, vs, os_,
+                                                   api.DType.Float16 if generic == "fp16" else api.DType.Float32, stream)
+        else:
+            status = forward_fn(q, k, v, mask, out, lse, batch, heads, seq, seq, radius, qs, ks, vs, os_, stream)
         if status != 0:
-            raise api.HipError(status, forward_fn.__name__)
+            raise api.HipError(status, "attention_generic_forward" if generic else forward_fn.__name__)
 
     def backward():
         status = backward_fn(q, k, v, mask, out, lse, upstream, gq, gk, gv, delta, batch, heads, seq, seq, radius, qs, ks, vs, os_,
@@ -430,22 +468,33 @@ def main() -> None:
     sm_mhz = (clocks or {}).get("sm_mhz") or float(peaks.get("sm_max_mhz", 1965.0))
     fma_peak = 148 * 128 * 2 * sm_mhz * 1e6 / 1e12
     if with_backward:
-        # The dominant kernel pair is the backward (exact FP32 SIMT); effective FLOPs per launch pair.
+        # The dominant kernel pair is the backward (the tcgen05 split-FP16 query-major delta + dQ
+        # pass and key-major dK/dV pass); effective FLOPs per launch pair, against the measured
+        # dense bf16 rate (the kind::f16 MMAs' rate) and the FP32 CUDA-core rate for context.
         achieved = effective_backward / (part_seconds[1] / args.steps) / 1e12
-        roofline = {"bound": "fp32-fma", "achieved": achieved, "peak": fma_peak, "unit": "TFLOP/s", "frac": achieved / fma_peak,
-                    "traffic": traffic_from_profiles(f"simt-backward-d{dim}"),
-                    "peak_source": "148 SMs x 128 FP32 lanes x 2 FLOP x median SM clock under load",
-                    "kernel": f"simt-fp32 backward d{dim} (query-major delta+dQ, key-major dK/dV)",
+        peak = float(peaks["bf16_tflops"])
+        roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                    "traffic": traffic_from_profiles(f"tcgen05-backward-d{dim}"),
+                    "peak_source": f"{peak_source} bf16_tflops (burst); the TF32 dense rate is half of it",
+                    "frac_of_tf32_dense": achieved / (peak / 2), "frac_of_fp32_fma": achieved / fma_peak,
+                    "kernel": f"tcgen05 split-FP16 backward d{dim} (query-major delta+dQ, key-major dK/dV)",
                     "flops": "effective: 8*d per active (query, key) pair"}
     else:
         achieved = effective_forward / (part_seconds[0] / args.steps) / 1e12
-        path = api.flash_kernel_name(batch, heads, seq, seq, dim)
+        if generic:
+            path = api.generic_kernel_name(batch, heads, seq, seq, dim,
+                                           api.DType.Float16 if generic == "fp16" else api.DType.Float32)
+        else:
+            path = api.flash_kernel_name(batch, heads, seq, seq, dim)
         if path.startswith("tcgen05"):
             peak = float(peaks["bf16_tflops"])
             roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                        "traffic": traffic_from_profiles(path),
-                        "peak_source": f"{peak_source} bf16_tflops (burst); the TF32 dense rate is half of it",
-                        "frac_of_tf32_dense": achieved / (peak / 2), "kernel": path}
+                        "traffic": traffic_from_profiles(path), "kernel": path}
+            if path.startswith("tcgen05-f16x2"):  # FP32 storage: compare with the TF32 dense rate as well
+                roofline["peak_source"] = f"{peak_source} bf16_tflops (burst); the TF32 dense rate is half of it"
+                roofline["frac_of_tf32_dense"] = achieved / (peak / 2)
+            else:
+                roofline["peak_source"] = f"{peak_source} bf16_tflops (burst), the FP16 dense rate"
         else:
             roofline = {"bound": "fp32-fma", "achieved": achieved, "peak": fma_peak, "unit": "TFLOP/s", "frac": achieved / fma_peak,
                         "traffic": traffic_from_profiles(path),
@@ -461,8 +510,8 @@ def main() -> None:
         "ms_per_step": device_seconds / args.steps * 1e3,
         "higher_is_better": True,
         "scaling": "strong" if with_backward else "weak",
-        "vs_baseline": None if with_backward else value / PUBLISHED_TFLOPS,
-        "dtype": "f32",
+        "vs_baseline": None if with_backward or generic else value / PUBLISHED_TFLOPS,
+        "dtype": generic or "f32",
         "data": "synthetic N(0,1) from a seeded torch generator (rank-dependent seed)",
         "config": workload_config(args.workload, world),
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": d2h_bytes,

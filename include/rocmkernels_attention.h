@@ -55,6 +55,14 @@ typedef struct RocmKernelsStrides {
     int token;
 } RocmKernelsStrides;
 
+/* Storage type of the generic forward's q, k, v and output, passed as one byte. The values of
+ * ROCmKernels::Kernels::DType (ROCmKernels.Kernels/include/ROCmKernels/Kernels/DType.hpp:10,
+ * `enum class DType : unsigned char { Float32, Float16 }`); the C++ enum of the same name converts
+ * to this type. */
+typedef unsigned char RocmKernelsDType;
+#define ROCMKERNELS_DTYPE_FLOAT32 ((RocmKernelsDType)0)
+#define ROCMKERNELS_DTYPE_FLOAT16 ((RocmKernelsDType)1)
+
 /* cudaStream_t (== hipStream_t through the HIP shim) without requiring the CUDA headers. */
 struct CUstream_st;
 typedef struct CUstream_st *RocmKernelsStream;
@@ -168,6 +176,22 @@ ROCMKERNELS_C_EXPORT int attention_fp32_backward_static_delta(const float *q, co
         RocmKernelsStrides qs, RocmKernelsStrides ks, RocmKernelsStrides vs, RocmKernelsStrides os,
         RocmKernelsStrides us, RocmKernelsStream stream);
 
+/* Generic forward for 16-, 32- or 64-wide heads with FP32 or FP16 storage (accumulation FP32),
+ * forward only. Replaces attention_generic_forward (Generic/AttentionGeneric.hpp:10-13;
+ * AttentionGeneric.hip:292-309): q, k, v and output are `dtype` elements with the given strides
+ * (in elements), lse is FP32 {row max, exp sum}. Scores are (q.k) * (1/sqrt(head_width)); a row
+ * whose exp sum is not positive (fully masked, or NaN) gives O = 0 and lse = {-inf, 0}, the
+ * reference's epilogue (AttentionGeneric.hip:119-128). Returns 1 for null pointers, non-positive
+ * sizes, head_width outside {16, 32, 64}, radius < -1 or an unknown dtype.
+ * Kernels: FP16 storage runs a tcgen05 kernel with FP16 operands (P rounded to FP16 once, as
+ * the reference rounds it for its v_dot2 P.V); FP32 storage with head width 32 or 64 runs the
+ * split-FP16 tcgen05 flash kernel; everything else (FP32 with head width 16, or tensors the
+ * tensor maps cannot describe) the exact FP32 SIMT kernel. */
+ROCMKERNELS_C_EXPORT int attention_generic_forward(const void *q, const void *k, const void *v, const bool *mask,
+        void *output, float *lse, int batch, int heads, int queries, int keys, int head_width, int radius,
+        RocmKernelsStrides qs, RocmKernelsStrides ks, RocmKernelsStrides vs, RocmKernelsStrides os,
+        RocmKernelsDType dtype, RocmKernelsStream stream);
+
 /* Library build identification: a static string naming the architecture the kernels were
  * compiled for ("sm_100a") and the kernel families present. No counterpart in the reference. */
 ROCMKERNELS_C_EXPORT const char *rocmkernels_attention_build_info(void);
@@ -177,6 +201,11 @@ ROCMKERNELS_C_EXPORT const char *rocmkernels_attention_build_info(void);
  * benchmarks and profiles). No counterpart in the reference. */
 ROCMKERNELS_C_EXPORT const char *rocmkernels_attention_flash_kernel(int batch, int heads, int queries, int keys,
         int head_width);
+
+/* Name of the kernel attention_generic_forward runs for contiguous [batch][heads][tokens][head_width]
+ * tensors of the given dtype (no reference counterpart; for benchmarks and tests). */
+ROCMKERNELS_C_EXPORT const char *rocmkernels_attention_generic_kernel(int batch, int heads, int queries, int keys,
+        int head_width, RocmKernelsDType dtype);
 
 /* Status word of the tensor-core kernels on the current device: 0, or 1 when a bounded
  * pipeline wait gave up (a protocol failure; the affected rows are written as NaN). Reading it

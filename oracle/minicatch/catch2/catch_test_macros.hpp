@@ -3,16 +3,20 @@
 // not available offline; this header lets ROCmKernels.Tests/AttentionTests.cpp compile unchanged.
 // TEST INFRASTRUCTURE: built only into the oracle/_ref test binary.
 //
-// Semantics kept from Catch2: a TEST_CASE body is run once per SECTION, each run entering exactly
-// one section (sections are flat here: nesting is not supported); CHECK records a failure and
-// continues; REQUIRE records a failure and leaves the current run; INFO messages in scope are
-// printed with a failure. Command line: `-c <section>` runs one section, `-s` also prints INFO
-// messages of passing checks, `--list` lists test names.
+// Semantics kept from Catch2: a TEST_CASE body is run once per leaf SECTION; each run enters, at
+// every nesting level, the first section that is not complete yet and skips its siblings (a
+// section is complete once it has run without discovering unfinished child sections). CHECK
+// records a failure and continues; REQUIRE records a failure and leaves the current run; INFO
+// messages in scope are printed with a failure. Command line: `-c <section>` runs only the
+// sections of that name (and everything inside them), `-s` also prints INFO messages of passing
+// checks, `--list` lists test names.
 #pragma once
 
 #include <cstdio>
 #include <exception>
 #include <functional>
+#include <map>
+#include <set>
 #include <sstream>
 #include <string>
 #include <vector>
@@ -34,10 +38,14 @@ struct Registrar {
 };
 
 struct RunState {
-    int encountered = 0;       // sections seen in this run
-    int target = 0;            // index of the section this run enters
+    // Section paths are the names from the test case down, joined by " / ".
+    std::set<std::string> completed;                     // sections finished (this test case)
+    std::map<std::string, std::set<std::string>> children;  // section path -> child paths seen
+    std::set<std::string> entered_parents;               // this run: parents that entered a child
+    std::vector<std::string> stack;                      // this run: entered sections, outermost first
+    std::vector<bool> matched;                           // per stack entry: inside a filtered section
     std::string filter;        // only enter sections with this name (empty = all)
-    std::string current;       // name of the section entered in this run
+    std::string current;       // deepest section entered in this run
     bool show_success = false; // print INFO for passing checks too
     int failed_checks = 0;
     int passed_checks = 0;
@@ -49,14 +57,44 @@ inline RunState &state() {
     return run;
 }
 
+inline std::string join(const std::vector<std::string> &names) {
+    std::string path;
+    for (const std::string &name : names) path += (path.empty() ? "" : " / ") + name;
+    return path;
+}
+
 struct Section {
-    bool active;
+    bool active = false;
+    std::string path;
     explicit Section(const char *name) {
         RunState &s = state();
-        active = s.encountered == s.target && (s.filter.empty() || s.filter == name);
-        if (active) s.current = name;
-        ++s.encountered;
+        const std::string parent = join(s.stack);
+        path = parent.empty() ? std::string(name) : parent + " / " + name;
+        s.children[parent].insert(path);
+        const bool inside = !s.matched.empty() && s.matched.back();
+        const bool matches = s.filter.empty() || inside || s.filter == name;
+        if (!matches) {
+            s.completed.insert(path);  // filtered out: never entered
+            return;
+        }
+        active = !s.completed.count(path) && !s.entered_parents.count(parent);
+        if (!active) return;
+        s.entered_parents.insert(parent);
+        s.stack.push_back(name);
+        s.matched.push_back(inside || s.filter == name);
+        s.current = path;
     }
+    ~Section() {
+        if (!active) return;
+        RunState &s = state();
+        bool done = true;
+        for (const std::string &child : s.children[path]) done = done && s.completed.count(child) > 0;
+        if (done) s.completed.insert(path);
+        s.stack.pop_back();
+        s.matched.pop_back();
+    }
+    Section(const Section &) = delete;
+    Section &operator=(const Section &) = delete;
     explicit operator bool() const { return active; }
 };
 
@@ -94,9 +132,12 @@ inline int run(int argc, char **argv) {
     }
     int sections_run = 0;
     for (const TestCase &test : registry()) {
-        for (int target = 0;; ++target) {
-            s.encountered = 0;
-            s.target = target;
+        s.completed.clear();
+        s.children.clear();
+        for (;;) {
+            s.entered_parents.clear();
+            s.stack.clear();
+            s.matched.clear();
             s.current.clear();
             s.info.clear();
             const int failed_before = s.failed_checks;
@@ -111,7 +152,9 @@ inline int run(int argc, char **argv) {
                 ++sections_run;
                 std::printf("%s: %s / %s\n", s.failed_checks == failed_before ? "PASS" : "FAIL", test.name, s.current.c_str());
             }
-            if (s.encountered == 0 || target + 1 >= s.encountered) break;
+            bool finished = true;  // every top-level section complete (or none exists)
+            for (const std::string &child : s.children[""]) finished = finished && s.completed.count(child) > 0;
+            if (finished || s.current.empty()) break;
         }
     }
     std::printf("%d section(s), %d check(s) passed, %d failed\n", sections_run, s.passed_checks, s.failed_checks);

@@ -25,6 +25,8 @@ ORACLE_LIBRARY = ORACLE_DIR / "_build" / "liboracle_attention.so"
 REFERENCE_LIBRARY = ORACLE_DIR / "_ref" / "libref_attention.so"
 REFERENCE_TESTS = ORACLE_DIR / "_ref" / "attention_tests"
 REFERENCE_BENCH = ORACLE_DIR / "_ref" / "attention_bench"
+REFERENCE_GENERIC_TESTS = ORACLE_DIR / "_ref" / "generic_tests"
+REFERENCE_GENERIC_BENCH = ORACLE_DIR / "_ref" / "generic_bench"
 
 _F32 = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
 _U8 = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")

@@ -2,7 +2,8 @@
 
 The reference's host API is C++: ``extern "C"`` launchers plus namespaced wrappers that throw
 ``ROCmKernels::HipError`` (ROCmKernels.Kernels/include/ROCmKernels/Kernels/Attention/Attention.hpp:44-108,
-Attention64.hpp:19-32). This module exposes both layers under the same names:
+Attention64.hpp:19-32, Generic/AttentionGeneric.hpp:15-25). This module exposes both layers under
+the same names:
 
 * ``lib()`` returns the loaded library whose ``attention_fp32_*`` / ``attention64_fp32_*``
   functions return the raw status code (0 = success, 1 = invalid value, else a CUDA error);
@@ -17,6 +18,7 @@ There is no CPU fallback: if the CUDA library is missing, :func:`lib` raises.
 from __future__ import annotations
 
 import ctypes
+import enum
 import os
 from pathlib import Path
 
@@ -34,6 +36,13 @@ class Strides(ctypes.Structure):
 
     def __repr__(self) -> str:
         return f"Strides(batch={self.batch}, head={self.head}, token={self.token})"
+
+
+class DType(enum.IntEnum):
+    """Storage type of the generic forward (ROCmKernels::Kernels::DType, passed as one byte)."""
+
+    Float32 = 0
+    Float16 = 1
 
 
 class HipError(RuntimeError):
@@ -64,6 +73,7 @@ _SIGNATURES = {
     "attention_fp32_backward_profile": _BACKWARD_SELECT_ARGS,
     "attention_fp32_query_profile": _BACKWARD_SELECT_ARGS,
     "attention_fp32_statistics": [_POINTER] * 4 + [_INT] * 5 + [Strides] * 2 + [_POINTER],
+    "attention_generic_forward": [_POINTER] * 6 + [_INT] * 6 + [Strides] * 4 + [ctypes.c_ubyte, _POINTER],
 }
 ENTRY_POINTS = tuple(_SIGNATURES)
 
@@ -86,6 +96,8 @@ def lib() -> ctypes.CDLL:
         library.rocmkernels_attention_build_info.restype = ctypes.c_char_p
         library.rocmkernels_attention_flash_kernel.argtypes = [ctypes.c_int] * 5
         library.rocmkernels_attention_flash_kernel.restype = ctypes.c_char_p
+        library.rocmkernels_attention_generic_kernel.argtypes = [ctypes.c_int] * 5 + [ctypes.c_ubyte]
+        library.rocmkernels_attention_generic_kernel.restype = ctypes.c_char_p
         library.rocmkernels_attention_device_status.argtypes = [ctypes.c_int]
         library.rocmkernels_attention_device_status.restype = ctypes.c_uint
         library.attention_fp32_backward_static_delta.argtypes = [_POINTER] * 10 + [_INT] * 5 + [Strides] * 5 + [_POINTER]
@@ -101,6 +113,11 @@ def build_info() -> str:
 def flash_kernel_name(batch: int, heads: int, queries: int, keys: int, head_width: int = 32) -> str:
     """Name of the kernel attention_fp32_forward_flash runs for contiguous, 16-byte aligned inputs."""
     return lib().rocmkernels_attention_flash_kernel(batch, heads, queries, keys, head_width).decode()
+
+
+def generic_kernel_name(batch: int, heads: int, queries: int, keys: int, head_width: int, dtype: DType) -> str:
+    """Name of the kernel attention_generic_forward runs for contiguous, 16-byte aligned inputs."""
+    return lib().rocmkernels_attention_generic_kernel(batch, heads, queries, keys, head_width, int(dtype)).decode()
 
 
 def device_status(clear: bool = True) -> int:
@@ -242,6 +259,12 @@ def attention_fp32_query_profile(q, k, v, mask, output, lse, upstream, gq, gk, g
                      keys, radius, qs, ks, vs, os_, us, stream, tuning)
 
 
+def attention_generic_forward(q, k, v, mask, output, lse, batch, heads, queries, keys, head_width, radius, qs, ks, vs, os_, dtype,
+                              stream=None):
+    return _call("attention_generic_forward", ptr(q), ptr(k), ptr(v), ptr(mask), ptr(output), ptr(lse), batch, heads, queries,
+                 keys, head_width, radius, strides(qs), strides(ks), strides(vs), strides(os_), int(dtype), _stream(stream))
+
+
 def _check(status: int, function: str) -> None:
     if status != SUCCESS:
         raise HipError(status, function)
@@ -304,3 +327,9 @@ def Attention64Backward(q, k, v, mask, output, lse, upstream, gq, gk, gv, delta,
                         us, stream=None):
     _check(attention64_fp32_backward(q, k, v, mask, output, lse, upstream, gq, gk, gv, delta, batch, heads, queries, keys, radius, qs,
                                      ks, vs, os_, us, stream), "attention64_fp32_backward")
+
+
+def AttentionGenericForward(q, k, v, mask, output, lse, batch, heads, queries, keys, head_width, radius, qs, ks, vs, os_, dtype,
+                            stream=None):
+    _check(attention_generic_forward(q, k, v, mask, output, lse, batch, heads, queries, keys, head_width, radius, qs, ks, vs, os_,
+                                     dtype, stream), "attention_generic_forward")

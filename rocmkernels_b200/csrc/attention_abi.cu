@@ -8,7 +8,9 @@
 #include "attention_simt.cuh"
 #include "attention_tc.cuh"
 
+#include <cmath>
 #include <mutex>
+#include <type_traits>
 
 namespace {
 
@@ -73,12 +75,12 @@ unsigned blocks_for(int tokens, int tile, int heads, int batch) {
     return static_cast<unsigned>((tokens + tile - 1) / tile) * static_cast<unsigned>(heads) * static_cast<unsigned>(batch);
 }
 
-template <int D, bool STATS_ONLY>
+template <int D, bool STATS_ONLY, class T = float>
 int launch_simt_forward(const AttentionParams &p, cudaStream_t stream) {
     constexpr int bytes = rk::simt::ForwardSmem<D, STATS_ONLY>::bytes;
-    cudaError_t status = rk::prepare_kernel<rk::simt::forward_kernel<D, STATS_ONLY>>(bytes);
+    cudaError_t status = rk::prepare_kernel<rk::simt::forward_kernel<D, STATS_ONLY, T>>(bytes);
     if (status != cudaSuccess) return status;
-    rk::simt::forward_kernel<D, STATS_ONLY>
+    rk::simt::forward_kernel<D, STATS_ONLY, T>
             <<<blocks_for(p.queries, rk::simt::kBlockQ, p.heads, p.batch), rk::simt::kThreads, bytes, stream>>>(p);
     return cudaGetLastError();
 }
@@ -128,6 +130,54 @@ int launch_flash(const AttentionParams &p, cudaStream_t stream) {
         if (status != rk::tc::kNotEligible) return status;
     }
     return launch_simt_forward<32, false>(p, stream);
+}
+
+// Parameters of the generic forward: T-typed tensors addressed through row_as<T> (strides in
+// elements of T), scale 1/sqrt(D) computed as the reference does (AttentionGeneric.hip:245),
+// the generic epilogue (NaN totals give 0), 4-element vector loads where every row allows them.
+template <class T>
+AttentionParams generic_params(int D, const void *q, const void *k, const void *v, const bool *mask, void *output,
+                               float *lse, int batch, int heads, int queries, int keys, int radius, RocmKernelsStrides qs,
+                               RocmKernelsStrides ks, RocmKernelsStrides vs, RocmKernelsStrides os) {
+    AttentionParams p{};
+    p.q = make_tensor(static_cast<const float *>(q), qs);
+    p.k = make_tensor(static_cast<const float *>(k), ks);
+    p.v = make_tensor(static_cast<const float *>(v), vs);
+    p.o = rk::OutTensor{static_cast<float *>(output), os.batch, os.head, os.token};
+    p.mask = reinterpret_cast<const unsigned char *>(mask);
+    p.lse = lse;
+    p.batch = batch;
+    p.heads = heads;
+    p.queries = queries;
+    p.keys = keys;
+    p.radius = radius;
+    p.scale = 1.0f / std::sqrt(static_cast<float>(D));
+    p.zero_nan_rows = 1;
+    const auto aligned = [](const void *pointer) { return (reinterpret_cast<uintptr_t>(pointer) & (4 * sizeof(T) - 1)) == 0; };
+    p.vec4 = aligned(q) && aligned(k) && aligned(v) && strides4(qs) && strides4(ks) && strides4(vs);
+    return p;
+}
+
+// Generic forward dispatch. FP32 storage: the split-FP16 tensor-core flash kernel (D = 16 on its
+// 32-wide form) when its tensor maps describe the tensors, else the exact SIMT kernel.
+// FP16 storage: the single-term FP16 tensor-core kernel when K, V and Q rows are 16-byte
+// addressable, else the SIMT kernel widening the FP16 values.
+template <class T>
+int launch_generic(const AttentionParams &p, int D, cudaStream_t stream) {
+    if constexpr (std::is_same_v<T, float>) {
+        if (rk::tc::flash_supported(p)) {
+            const int status = rk::tc::launch_flash_forward(p, D, stream);
+            if (status != rk::tc::kNotEligible) return status;
+        }
+    } else {
+        if (rk::tc::half_flash_supported(p)) {
+            const int status = rk::tc::launch_half_flash_forward(p, D, stream);
+            if (status != rk::tc::kNotEligible) return status;
+        }
+    }
+    if (D == 16) return launch_simt_forward<16, false, T>(p, stream);
+    if (D == 32) return launch_simt_forward<32, false, T>(p, stream);
+    return launch_simt_forward<64, false, T>(p, stream);
 }
 
 bool known_group(int group) {
@@ -356,6 +406,56 @@ const char *rocmkernels_attention_flash_kernel(int batch, int heads, int queries
     p.o = rk::OutTensor{nullptr, p.q.sb, p.q.sh, p.q.st};
     if (rk::tc::flash_supported(p)) return rk::tc::kernel_name(head_width);
     return head_width == 64 ? "simt-fp32-forward-d64" : "simt-fp32-forward-d32";
+}
+
+int attention_generic_forward(const void *q, const void *k, const void *v, const bool *mask, void *output, float *lse,
+                              int batch, int heads, int queries, int keys, int head_width, int radius, RocmKernelsStrides qs,
+                              RocmKernelsStrides ks, RocmKernelsStrides vs, RocmKernelsStrides os, RocmKernelsDType dtype,
+                              RocmKernelsStream stream) {
+    if (!q || !k || !v || !mask || !output || !lse || batch <= 0 || heads <= 0 || queries <= 0 || keys <= 0)
+        return cudaErrorInvalidValue;
+    if (head_width != 16 && head_width != 32 && head_width != 64) return cudaErrorInvalidValue;
+    if (radius < -1) return cudaErrorInvalidValue;
+    if (dtype == ROCMKERNELS_DTYPE_FLOAT32) {
+        const AttentionParams p = generic_params<float>(head_width, q, k, v, mask, output, lse, batch, heads, queries, keys,
+                                                        radius, qs, ks, vs, os);
+        return launch_generic<float>(p, head_width, stream);
+    }
+    if (dtype == ROCMKERNELS_DTYPE_FLOAT16) {
+        const AttentionParams p = generic_params<__half>(head_width, q, k, v, mask, output, lse, batch, heads, queries, keys,
+                                                         radius, qs, ks, vs, os);
+        return launch_generic<__half>(p, head_width, stream);
+    }
+    return cudaErrorInvalidValue;
+}
+
+const char *rocmkernels_attention_generic_kernel(int batch, int heads, int queries, int keys, int head_width,
+                                                 RocmKernelsDType dtype) {
+    if ((head_width != 16 && head_width != 32 && head_width != 64) ||
+        (dtype != ROCMKERNELS_DTYPE_FLOAT32 && dtype != ROCMKERNELS_DTYPE_FLOAT16))
+        return "unsupported";
+    const bool half = dtype == ROCMKERNELS_DTYPE_FLOAT16;
+    const long long w = head_width;
+    AttentionParams p{};
+    p.batch = batch;
+    p.heads = heads;
+    p.queries = queries;
+    p.keys = keys;
+    p.radius = -1;
+    p.vec4 = 1;
+    p.q = rk::Tensor{nullptr, (long long)heads * queries * w, (long long)queries * w, w};
+    p.k = rk::Tensor{nullptr, (long long)heads * keys * w, (long long)keys * w, w};
+    p.v = p.k;
+    p.o = rk::OutTensor{nullptr, p.q.sb, p.q.sh, p.q.st};
+    // A 256-byte aligned stand-in address: the tensor-map check reads no memory.
+    p.q.data = p.k.data = p.v.data = reinterpret_cast<const float *>(uintptr_t{1} << 20);
+    p.o.data = reinterpret_cast<float *>(uintptr_t{1} << 20);
+    if (half && rk::tc::half_flash_supported(p) && rk::tc::tensor_maps_encodable(p, head_width, true))
+        return rk::tc::half_kernel_name(head_width);
+    if (!half && rk::tc::flash_supported(p) && rk::tc::tensor_maps_encodable(p, head_width, false))
+        return rk::tc::kernel_name(head_width);
+    if (half) return head_width == 16 ? "simt-fp16-forward-d16" : head_width == 32 ? "simt-fp16-forward-d32" : "simt-fp16-forward-d64";
+    return head_width == 16 ? "simt-fp32-forward-d16" : head_width == 32 ? "simt-fp32-forward-d32" : "simt-fp32-forward-d64";
 }
 
 int attention_fp32_backward_static_delta(const float *q, const float *k, const float *v, const bool *mask,

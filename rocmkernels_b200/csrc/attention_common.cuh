@@ -1,6 +1,7 @@
 // Shared device helpers and launch parameters for the FP32 attention kernels (sm_100a).
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -12,20 +13,26 @@ constexpr float kLog2e = 1.4426950408889634f;
 
 // A strided [batch][head][token][feature] tensor; feature stride is 1.
 // Element (b, h, t, c) is data[b*sb + h*sh + t*st + c], the addressing of the reference's
-// Input::read (Attention.hip:14-20), evaluated in 64-bit here.
+// Input::read (Attention.hip:14-20), evaluated in 64-bit here. The strides count elements of the
+// storage type: FP32 everywhere except the FP16 tensors of the generic forward, which read them
+// through row_as<__half>.
 struct Tensor {
     const float *data;
     long long sb, sh, st;
-    __device__ __forceinline__ const float *row(int b, int h, int t) const {
-        return data + (long long)b * sb + (long long)h * sh + (long long)t * st;
+    __device__ __forceinline__ const float *row(int b, int h, int t) const { return row_as<float>(b, h, t); }
+    template <class T>
+    __device__ __forceinline__ const T *row_as(int b, int h, int t) const {
+        return reinterpret_cast<const T *>(data) + (long long)b * sb + (long long)h * sh + (long long)t * st;
     }
 };
 
 struct OutTensor {
     float *data;
     long long sb, sh, st;
-    __device__ __forceinline__ float *row(int b, int h, int t) const {
-        return data + (long long)b * sb + (long long)h * sh + (long long)t * st;
+    __device__ __forceinline__ float *row(int b, int h, int t) const { return row_as<float>(b, h, t); }
+    template <class T>
+    __device__ __forceinline__ T *row_as(int b, int h, int t) const {
+        return reinterpret_cast<T *>(data) + (long long)b * sb + (long long)h * sh + (long long)t * st;
     }
 };
 
@@ -41,8 +48,23 @@ struct AttentionParams {
     const float *lse_in;        // saved statistics for the backward
     int batch, heads, queries, keys, radius;
     float scale;                // 1/sqrt(D)
-    int vec4;                   // all strided tensors are 16-byte addressable (float4 loads)
+    int vec4;                   // every strided row starts 4-element aligned (float4 / 4 x FP16 loads)
+    int zero_nan_rows;          // a row whose exponent sum is NaN gives O = 0 and {-inf, 0} (the generic
+                                // forward's epilogue, AttentionGeneric.hip:119-128) instead of NaN
 };
+
+// Four consecutive elements widened to FP32: one 16-byte load for FP32, one 8-byte load for FP16.
+__device__ __forceinline__ float4 load4(const float *src) { return __ldg(reinterpret_cast<const float4 *>(src)); }
+__device__ __forceinline__ float4 load4(const __half *src) {
+    const uint2 raw = __ldg(reinterpret_cast<const uint2 *>(src));
+    const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
+    const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
+    return make_float4(lo.x, lo.y, hi.x, hi.y);
+}
+__device__ __forceinline__ float load1(const float *src) { return __ldg(src); }
+__device__ __forceinline__ float load1(const __half *src) { return __half2float(__ldg(src)); }
+__device__ __forceinline__ void store1(float *dst, float value) { *dst = value; }
+__device__ __forceinline__ void store1(__half *dst, float value) { *dst = __float2half_rn(value); }
 
 // 2^x on the MUFU unit (PTX ex2.approx.ftz.f32; relative error about 2^-22).
 __device__ __forceinline__ float fast_exp2(float x) {

@@ -28,14 +28,15 @@ constexpr int kPitchP = kBlockK + 4;
 
 template <int D> struct Shape {
     static constexpr int pitch = D + 4;    // padded row pitch of a [rows][D] tile (keeps float4 alignment)
-    static constexpr int features = D / 16; // O / dQ / dK / dV features per thread
+    static constexpr int features = D / 16; // O / dQ / dK / dV features per thread (D = 16 only in the forward)
     static constexpr int tile = 64 * pitch; // floats in one 64-row tile
 };
 
-// dst[r][c] = scale * src(row0 + r, c) for rows below `limit` whose flag is set, else 0.
-template <int D, int ROWS>
-__device__ __forceinline__ void load_rows(float *dst, const float *src, long long stride, int row0, int limit,
-                                          float scale, bool vec4, const int *flags) {
+// dst[r][c] = scale * src(row0 + r, c) for rows below `limit` whose flag is set, else 0; T is the
+// storage type (FP32, or FP16 widened to FP32).
+template <int D, int ROWS, class T>
+__device__ __forceinline__ void load_rows(float *dst, const T *src, long long stride, int row0, int limit, float scale,
+                                          bool vec4, const int *flags) {
     constexpr int pitch = Shape<D>::pitch;
     if (vec4) {
         constexpr int per_row = D / 4;
@@ -44,7 +45,7 @@ __device__ __forceinline__ void load_rows(float *dst, const float *src, long lon
             const int row = row0 + r;
             float4 value = make_float4(0.f, 0.f, 0.f, 0.f);
             if (row < limit && (flags == nullptr || flags[r])) {
-                value = __ldg(reinterpret_cast<const float4 *>(src + (long long)row * stride) + c4);
+                value = load4(src + (long long)row * stride + 4 * c4);
                 value.x *= scale; value.y *= scale; value.z *= scale; value.w *= scale;
             }
             *reinterpret_cast<float4 *>(dst + r * pitch + c4 * 4) = value;
@@ -54,7 +55,7 @@ __device__ __forceinline__ void load_rows(float *dst, const float *src, long lon
             const int r = index / D, c = index % D;
             const int row = row0 + r;
             float value = 0.f;
-            if (row < limit && (flags == nullptr || flags[r])) value = __ldg(src + (long long)row * stride + c) * scale;
+            if (row < limit && (flags == nullptr || flags[r])) value = load1(src + (long long)row * stride + c) * scale;
             dst[r * pitch + c] = value;
         }
     }
@@ -97,7 +98,9 @@ __device__ __forceinline__ void tile_accumulate(float (&out)[4][Shape<D>::featur
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) {
             float x[F];
-            if constexpr (F == 2) {
+            if constexpr (F == 1) {
+                x[0] = X[(j + jj) * pitch + tx];
+            } else if constexpr (F == 2) {
                 const float2 t = *reinterpret_cast<const float2 *>(X + (j + jj) * pitch + tx * 2);
                 x[0] = t.x; x[1] = t.y;
             } else {
@@ -136,7 +139,10 @@ __device__ __forceinline__ void decode_block(int block, int blocks_per_head, int
 // ------------------------------------------------------------------------------------------
 // Forward: O = softmax(scale * Q K^T, masked) V and lse = {max, sum}; STATS_ONLY skips V and O.
 // Replaces attention_query<false> (Attention.hip:32-115), attention_query_tiled<false>
-// (AttentionTile32.h:12-217) and attention64_query<false> (Attention64.hip:34-129).
+// (AttentionTile32.h:12-217) and attention64_query<false> (Attention64.hip:34-129); with T =
+// __half or D = 16 it is the exact-FP32 path of the generic forward (attention_generic_query and
+// attention_generic_query_half, AttentionGeneric.hip:36-237): FP16 storage is widened on load,
+// every product and sum is FP32, O is rounded to the storage type on the store.
 // ------------------------------------------------------------------------------------------
 template <int D, bool STATS_ONLY>
 struct ForwardSmem {
@@ -144,7 +150,7 @@ struct ForwardSmem {
     static constexpr int bytes = floats * 4;
 };
 
-template <int D, bool STATS_ONLY>
+template <int D, bool STATS_ONLY, class T = float>
 __global__ void __launch_bounds__(kThreads) forward_kernel(AttentionParams p) {
     extern __shared__ float4 shared_raw[];
     float *Qs = reinterpret_cast<float *>(shared_raw);
@@ -161,7 +167,7 @@ __global__ void __launch_bounds__(kThreads) forward_kernel(AttentionParams p) {
     const int q0 = tile * kBlockQ;
     const unsigned char *mask = p.mask + (long long)b * p.keys;
 
-    load_rows<D, kBlockQ>(Qs, p.q.row(b, h, 0), p.q.st, q0, p.queries, p.scale, p.vec4, nullptr);
+    load_rows<D, kBlockQ>(Qs, p.q.row_as<T>(b, h, 0), p.q.st, q0, p.queries, p.scale, p.vec4, nullptr);
 
     float m[4], l[4], o[4][F];
 #pragma unroll
@@ -183,8 +189,8 @@ __global__ void __launch_bounds__(kThreads) forward_kernel(AttentionParams p) {
             flags[threadIdx.x] = visible;
         }
         if (!__syncthreads_or(visible)) continue;  // whole tile masked: contributes nothing
-        load_rows<D, kBlockK>(Ks, p.k.row(b, h, 0), p.k.st, k0, last, 1.f, p.vec4, flags);
-        if constexpr (!STATS_ONLY) load_rows<D, kBlockK>(Vs, p.v.row(b, h, 0), p.v.st, k0, last, 1.f, p.vec4, flags);
+        load_rows<D, kBlockK>(Ks, p.k.row_as<T>(b, h, 0), p.k.st, k0, last, 1.f, p.vec4, flags);
+        if constexpr (!STATS_ONLY) load_rows<D, kBlockK>(Vs, p.v.row_as<T>(b, h, 0), p.v.st, k0, last, 1.f, p.vec4, flags);
         __syncthreads();
 
         float s[4][4] = {};
@@ -226,21 +232,22 @@ __global__ void __launch_bounds__(kThreads) forward_kernel(AttentionParams p) {
     }
 
     // Epilogue (AttentionFlash32.h:157-169): O = acc / total; fully masked rows give O = 0 and
-    // {-inf, 0}; a NaN total propagates.
+    // {-inf, 0}; a NaN total propagates, or gives 0 and {-inf, 0} when p.zero_nan_rows is set.
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const int query = q0 + ty * 4 + i;
         if (query >= p.queries) continue;
         const float total = l[i];
+        const bool nan_out = isnan(total) && !p.zero_nan_rows;
         if constexpr (!STATS_ONLY) {
-            float *out = p.o.row(b, h, query) + tx * F;
+            T *out = p.o.row_as<T>(b, h, query) + tx * F;
 #pragma unroll
-            for (int f = 0; f < F; ++f) out[f] = total > 0.f ? o[i][f] / total : isnan(total) ? NAN : 0.f;
+            for (int f = 0; f < F; ++f) store1(out + f, total > 0.f ? o[i][f] / total : nan_out ? NAN : 0.f);
         }
         if (tx == 0) {
             const long long row = ((long long)b * p.heads + h) * p.queries + query;
-            p.lse[row * 2] = total > 0.f ? m[i] : isnan(total) ? NAN : -INFINITY;
-            p.lse[row * 2 + 1] = total > 0.f ? total : isnan(total) ? NAN : 0.f;
+            p.lse[row * 2] = total > 0.f ? m[i] : nan_out ? NAN : -INFINITY;
+            p.lse[row * 2 + 1] = total > 0.f ? total : nan_out ? NAN : 0.f;
         }
     }
 }

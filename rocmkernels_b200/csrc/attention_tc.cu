@@ -35,6 +35,17 @@
 // TMEM (512 columns, one CTA per SM), Q tile t uses [256t, 256t + 240):
 //   q0 0-15 | q1 16-31 | S/P buffer 0: 32-95 | S/P buffer 1: 96-159 | Oa 160-191 | Ob 192-223 |
 //   row sums 224-239 (P in a buffer: p0 pairs in its first 32 columns, p1 pairs in the next 32)
+//
+// FP16 storage (the generic forward's DType::Float16, attention_generic_query_half,
+// AttentionGeneric.hip:141-237; head width 16, 32 or 64). The same pipeline with one FP16 term
+// per operand and no scale exponents: the inputs already are FP16, so S = q.k is one product per
+// K=16 step, read by the MMAs straight from the TMA tile of K (64 keys x 64 FP16, 128B swizzle;
+// the features past D are the TMA's zero fill), and P is rounded to FP16 once for P.V (as the
+// reference rounds it before its v_dot2 P.V) while the row sum adds the unrounded FP32 values
+// (as the reference's total does). One Q tile per CTA; the split warps only transpose V and
+// publish the key mask. The 1/sqrt(D) scale multiplies the FP32 scores, as in the reference.
+// TMEM (256 columns): q 0..D/2-1 | S/P buffers 32-95, 96-159 (P in the first 32 columns) |
+// O 160..160+D-1.
 #include "attention_tc.cuh"
 
 #include <cudaTypedefs.h>
@@ -80,39 +91,45 @@ constexpr int kNoExponent = 1000;   // outside every clamped scale exponent
 constexpr uint32_t kIdescS = f16_instr_desc(128, 64);  // S: 64 keys
 constexpr uint64_t kDescStep = 2;                      // one K=16 step of FP16 = 32 bytes
 
-// Configuration per head width. d = 32: two Q tiles of 128 queries per CTA sharing each K/V tile
-// (12 warps, 4 stages); d = 64: one Q tile per CTA (8 warps, 3 stages), its operands twice as wide.
-template <int D>
+// Configuration per storage mode and head width. Split FP32 (kHalf false): d = 32 has two Q tiles
+// of 128 queries per CTA sharing each K/V tile (12 warps, 4 stages), d = 64 one Q tile per CTA
+// (8 warps, 3 stages) with operands twice as wide. FP16 storage (kHalf true, d = 16, 32 or 64):
+// one Q tile, 3 stages, one FP16 term per operand.
+template <int D, bool kHalf>
 struct Forward {
-    static constexpr int kQTiles = D == 32 ? 2 : 1;
+    static constexpr int kTerms = kHalf ? 1 : 2;  // FP16 terms per operand
+    static constexpr int kQTiles = !kHalf && D == 32 ? 2 : 1;
     static constexpr int kCtaQueries = kQTile * kQTiles;
-    static constexpr int kStages = D == 32 ? 4 : 3;
+    static constexpr int kStages = !kHalf && D == 32 ? 4 : 3;
     static constexpr int kSoftmaxWarps = 4 * kQTiles;
     static constexpr int kProducerWarp = kSoftmaxWarps, kMmaWarp = kSoftmaxWarps + 1, kSplitWarp = kSoftmaxWarps + 2;
     static constexpr int kThreads = 32 * (kSoftmaxWarps + 4);
     static constexpr int kSplitThreads = 64;
-    static constexpr int kBoxes = D / 32;
-    static constexpr int kRawFloats = kBoxes * kBoxFloats;  // FP32 tile of 64 keys x D
-    static constexpr int kKWords = 64 * D;                   // row layout [k0 | k1] of 64 keys
-    static constexpr int kVRows = 2 * D + 16;                // B of P.V: v0^T, v1^T and 16 rows of ones (row sums)
+    static constexpr int kBoxes = kHalf ? 1 : D / 32;        // TMA boxes of 64 rows x 128 bytes per raw tile
+    static constexpr int kRawFloats = kBoxes * kBoxFloats;  // raw tile of 64 keys in 32-bit words
+    static constexpr int kKWords = kHalf ? 0 : 64 * D;       // row layout [k0 | k1] of 64 keys (FP16: the raw tile)
+    static constexpr int kVRows = kHalf ? D : 2 * D + 16;    // B of P.V: v0^T, v1^T and 16 rows of ones (row sums);
+                                                             // FP16: v^T only
     static constexpr int kVWords = kVRows * 32;              // kVRows x 128 bytes
     // TMEM per Q tile: q0 pairs | q1 pairs | S/P buffer 0 | S/P buffer 1 | Oa | Ob | row sums
-    static constexpr uint32_t kColQ0 = 0, kColQ1 = D / 2, kColBuffer = D, kBufferColumns = 64, kColO = D + 128,
-                              kColSum = kColO + 2 * D, kColTile = D == 32 ? 256 : 512;
-    static constexpr uint32_t kTmemColumns = 512;
+    static constexpr uint32_t kColQ0 = 0, kColQ1 = D / 2, kColBuffer = kHalf ? 32 : D, kBufferColumns = 64,
+                              kColO = kColBuffer + 128, kColSum = kColO + kTerms * D,
+                              kColTile = kHalf || D == 32 ? 256 : 512;
+    static constexpr uint32_t kTmemColumns = kHalf ? 256 : 512;
     static constexpr uint32_t kIdescPV = f16_instr_desc(128, kVRows);
-    static constexpr uint64_t kDescStageK = kKWords * 4 / 16, kDescStageV = kVWords * 4 / 16;
+    static constexpr uint64_t kDescStageK = (kHalf ? kRawFloats : kKWords) * 4 / 16, kDescStageV = kVWords * 4 / 16;
 };
 
 // Operand tiles are rows of 128 bytes in 1024-byte aligned 8-row atoms (the 128B swizzle).
-template <int D>
+template <int D, bool kHalf>
 struct alignas(1024) SharedStorage {
-    using F = Forward<D>;
-    float k_raw[F::kStages][F::kRawFloats];    // FP32 K tile as TMA lands it (swizzled boxes of 64 x 32)
-    float v_raw[F::kStages][F::kRawFloats];    // FP32 V tile
-    uint32_t k16[F::kStages][F::kKWords];      // 64 key rows as [k0 | k1] FP16 (row layout), K-major 128B swizzle
-    uint32_t vt16[F::kStages][F::kVWords];     // rows 0..D-1 v0^T, D..2D-1 v1^T (64 keys each, 128B swizzle),
-                                               // 2D..2D+15 FP16 ones (written once)
+    using F = Forward<D, kHalf>;
+    float k_raw[F::kStages][F::kRawFloats];    // K tile as TMA lands it (FP32: swizzled boxes of 64 x 32; FP16: 64 x 64)
+    float v_raw[F::kStages][F::kRawFloats];    // V tile
+    uint32_t k16[F::kStages][F::kKWords > 0 ? F::kKWords : 1];  // 64 key rows as [k0 | k1] FP16 (row layout),
+                                                                // K-major 128B swizzle (unused for FP16 storage)
+    alignas(1024) uint32_t vt16[F::kStages][F::kVWords];  // rows 0..D-1 v0^T, D..2D-1 v1^T (64 keys each, 128B
+                                                          // swizzle), 2D..2D+15 FP16 ones (written once); FP16: v^T
     uint32_t key_mask[F::kStages][2];          // bit c: key k0 + c visible
     int k_exponent[F::kStages];                // K tile scaled by 2^k_exponent
     int v_exponent[F::kStages];                // V tile scaled by 2^v_exponent
@@ -140,14 +157,27 @@ __device__ __forceinline__ uint32_t tmem_lane_address(uint32_t base, int warp) {
 }
 
 // S(buffer) = q0.k1 + q1.k0 + q0.k0 over the D features (D/16 K=16 steps each), then a commit to
-// `bar`; k_desc addresses the stage's k16 tile. Warp-collective.
-template <int D>
+// `bar`; k_desc addresses the stage's k16 tile. FP16 storage: S = q.k, k_desc addressing the raw
+// K tile. Warp-collective.
+template <int D, bool kHalf>
 __device__ __forceinline__ void issue_scores(uint32_t tmem, uint64_t k_desc, int tile, int buffer, uint64_t *bar) {
-    using F = Forward<D>;
-    constexpr uint64_t x1 = row_x1_offset<D>();
+    using F = Forward<D, kHalf>;
     const uint32_t t = tmem + tile * F::kColTile;
     const uint32_t d = t + F::kColBuffer + buffer * F::kBufferColumns;
     const uint32_t a0 = t + F::kColQ0, a1 = t + F::kColQ1;
+    if constexpr (kHalf) {
+        if constexpr (D == 16) {
+            mma1_f16_ts_commit_warp(d, a0, k_desc, kIdescS, 1, bar);
+        } else if constexpr (D == 32) {
+            mma2_f16_ts_first_commit_warp(d, a0, a0 + 8, k_desc, k_desc + kDescStep, kIdescS, 1, bar);
+        } else {
+            const uint32_t a[4] = {a0, a0 + 8, a0 + 16, a0 + 24};
+            const uint64_t bk[4] = {k_desc, k_desc + kDescStep, k_desc + 2 * kDescStep, k_desc + 3 * kDescStep};
+            mma4_f16_ts_commit_warp(d, a, bk, kIdescS, 1, bar);
+        }
+        return;
+    }
+    constexpr uint64_t x1 = row_x1_offset<D>();
     if constexpr (D == 32) {
         const uint32_t a[4] = {a0, a0 + 8, a1, a1 + 8};
         const uint64_t bk[4] = {k_desc + x1, k_desc + x1 + kDescStep, k_desc, k_desc + kDescStep};
@@ -165,17 +195,20 @@ __device__ __forceinline__ void issue_scores(uint32_t tmem, uint64_t k_desc, int
 }
 
 // [Oa | Ob | sums] = p1.[v0 ; v1 ; 1] + p0.[v0 ; v1 ; 1] over the 64 keys (four K=16 steps
-// each), then a commit to `bar`; v_desc addresses the stage's vt16 tile. Warp-collective.
-template <int D>
+// each), then a commit to `bar`; v_desc addresses the stage's vt16 tile. FP16 storage:
+// [O | sums] = p.[v ; 1]. Warp-collective.
+template <int D, bool kHalf>
 __device__ __forceinline__ void issue_values(uint32_t tmem, uint64_t v_desc, int tile, int buffer, uint64_t *bar) {
-    using F = Forward<D>;
+    using F = Forward<D, kHalf>;
     const uint32_t t = tmem + tile * F::kColTile;
     const uint32_t pbuf = t + F::kColBuffer + buffer * F::kBufferColumns;
     const uint64_t bv[4] = {v_desc, v_desc + kDescStep, v_desc + 2 * kDescStep, v_desc + 3 * kDescStep};
-    const uint32_t a1[4] = {pbuf + 32, pbuf + 40, pbuf + 48, pbuf + 56};
     const uint32_t a0[4] = {pbuf, pbuf + 8, pbuf + 16, pbuf + 24};
-    mma4_f16_ts_warp(t + F::kColO, a1, bv, F::kIdescPV, 1);
-    mma4_f16_ts_commit_warp(t + F::kColO, a0, bv, F::kIdescPV, 0, bar);
+    if constexpr (!kHalf) {
+        const uint32_t a1[4] = {pbuf + 32, pbuf + 40, pbuf + 48, pbuf + 56};
+        mma4_f16_ts_warp(t + F::kColO, a1, bv, F::kIdescPV, 1);
+    }
+    mma4_f16_ts_commit_warp(t + F::kColO, a0, bv, F::kIdescPV, kHalf ? 1 : 0, bar);
 }
 
 // Folds the last finished key tile into the running output and row sum. In TMEM, Oa + Ob is the
@@ -184,10 +217,35 @@ __device__ __forceinline__ void issue_values(uint32_t tmem, uint64_t v_desc, int
 // a tile with that exponent (the usual case, warp-uniform) costs one add and one FMA per column;
 // a tile with another exponent moves whichever side has the larger one down, so no value is
 // ever scaled up.
-template <int D>
+// FP16 storage has no exponents (c = o_exp = 0) and keeps its row sum itself: O = O * weight + Ot
+// over the D columns.
+template <int D, bool kHalf>
 __device__ __forceinline__ void fold_output(float (&o)[D], float &row_sum, int &o_exp, uint32_t lane_base, float weight,
                                             int c) {
-    using F = Forward<D>;
+    using F = Forward<D, kHalf>;
+    if constexpr (kHalf) {
+        o_exp = 0;
+        float ta[16], tb[16];
+        if constexpr (D == 16)
+            tmem_load16(lane_base + F::kColO, ta);
+        else
+            tmem_load16x2(lane_base + F::kColO, ta, lane_base + F::kColO + 16, tb);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) o[i] = fmaf(o[i], weight, ta[i]);
+        if constexpr (D >= 32) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) o[16 + i] = fmaf(o[16 + i], weight, tb[i]);
+        }
+        if constexpr (D == 64) {
+            tmem_load16x2(lane_base + F::kColO + 32, ta, lane_base + F::kColO + 48, tb);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                o[32 + i] = fmaf(o[32 + i], weight, ta[i]);
+                o[48 + i] = fmaf(o[48 + i], weight, tb[i]);
+            }
+        }
+        return;
+    }
     if (o_exp == kNoExponent) o_exp = c;
     float out_weight = weight, tile_scale = 1.f;
     if (c > o_exp) {
@@ -218,9 +276,11 @@ __device__ __forceinline__ void fold_output(float (&o)[D], float &row_sum, int &
 // buffer (p0 pairs in columns 0-31, p1 pairs in 32-63) in chunks of 16 keys without waiting, so
 // few values are live at a time. kPlain: every score is finite or -inf and the offset is finite,
 // so exp2(-inf) = 0 covers the masked keys; otherwise -inf scores are zeroed explicitly (a row
-// without any visible key yet has an infinite offset).
-template <bool kPlain>
-__device__ __forceinline__ void exp_split_store(const float (&sc)[64], float slope, float offset, uint32_t pbuf) {
+// without any visible key yet has an infinite offset). kHalf: P' rounded to FP16 once, pairs in
+// columns 0-31, and the FP32 sum of the unrounded P' returned (0 otherwise).
+template <bool kPlain, bool kHalf>
+__device__ __forceinline__ float exp_split_store(const float (&sc)[64], float slope, float offset, uint32_t pbuf) {
+    float sum[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int chunk = 0; chunk < 4; ++chunk) {
         float p0[8], p1[8];
@@ -233,23 +293,70 @@ __device__ __forceinline__ void exp_split_store(const float (&sc)[64], float slo
                 a = sc[2 * c] == -INFINITY ? 0.f : a;
                 b = sc[2 * c + 1] == -INFINITY ? 0.f : b;
             }
-            const float a0 = __uint_as_float(__float_as_uint(a) & 0xFFFFE000u);
-            const float b0 = __uint_as_float(__float_as_uint(b) & 0xFFFFE000u);
-            p0[i] = __uint_as_float(pack_half2(a0, b0));
-            p1[i] = __uint_as_float(pack_half2(a - a0, b - b0));
+            if constexpr (kHalf) {
+                p0[i] = __uint_as_float(pack_half2(a, b));
+                sum[i & 3] += a + b;
+            } else {
+                const float a0 = __uint_as_float(__float_as_uint(a) & 0xFFFFE000u);
+                const float b0 = __uint_as_float(__float_as_uint(b) & 0xFFFFE000u);
+                p0[i] = __uint_as_float(pack_half2(a0, b0));
+                p1[i] = __uint_as_float(pack_half2(a - a0, b - b0));
+            }
         }
-        tmem_store8x2_async(pbuf + 8 * chunk, p0, pbuf + 32 + 8 * chunk, p1);
+        if constexpr (kHalf)
+            tmem_store8_async(pbuf + 8 * chunk, p0);
+        else
+            tmem_store8x2_async(pbuf + 8 * chunk, p0, pbuf + 32 + 8 * chunk, p1);
+    }
+    return (sum[0] + sum[1]) + (sum[2] + sum[3]);
+}
+
+// V tile -> V^T operand rows for FP16 storage. Split warp w transposes the key groups 4w..4w+3
+// (its own 32 rows, whose mask bits are `bits`); lane -> (group g = 4w + lane % 4, feature chunk
+// fc = lane / 4 < D / 8): the 8 x 8 FP16 block of rows 8g..8g+7 and features 8fc..8fc+7, masked
+// rows zeroed, becomes chunk g of the V^T rows 8fc..8fc+7 (pairs regrouped with byte permutes).
+template <int D>
+__device__ __forceinline__ void transpose_values(const float *v_raw, uint32_t *vt16, int w, int lane, uint32_t bits) {
+    const int fc = lane >> 2;
+    if (fc >= D / 8) return;
+    const int g = 4 * w + (lane & 3);
+    const uint4 *raw = reinterpret_cast<const uint4 *>(v_raw);
+    uint32_t x[8][4];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+        const int vrow = 8 * g + r;
+        uint4 chunk = raw[vrow * 8 + (fc ^ (vrow & 7))];
+        if (!((bits >> (vrow & 31)) & 1)) chunk = make_uint4(0u, 0u, 0u, 0u);
+        x[r][0] = chunk.x;
+        x[r][1] = chunk.y;
+        x[r][2] = chunk.z;
+        x[r][3] = chunk.w;
+    }
+    uint4 *vt = reinterpret_cast<uint4 *>(vt16);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        const uint32_t select = (e & 1) ? 0x7632u : 0x5410u;  // high or low halves of two words
+        const int f = 8 * fc + e;
+        vt[f * 8 + (g ^ (f & 7))] = make_uint4(__byte_perm(x[0][e >> 1], x[1][e >> 1], select),
+                                               __byte_perm(x[2][e >> 1], x[3][e >> 1], select),
+                                               __byte_perm(x[4][e >> 1], x[5][e >> 1], select),
+                                               __byte_perm(x[6][e >> 1], x[7][e >> 1], select));
     }
 }
 
-template <int D>
-__global__ void __launch_bounds__(Forward<D>::kThreads, 1)
+// kWidth: the tensors' head width when it is below the kernel's D (FP32 storage with 16 features
+// on the D = 32 kernel): the tensor maps are kWidth wide, so the TMA fills features kWidth..D-1
+// of K and V with zeros, Q rows are read and O rows written kWidth wide.
+template <int D, bool kHalf, int kWidth = D>
+__global__ void __launch_bounds__(Forward<D, kHalf>::kThreads, 1)
         flash_forward_kernel(const FlashArgs args, const __grid_constant__ CUtensorMap tmap_k,
                              const __grid_constant__ CUtensorMap tmap_v) {
-    using F = Forward<D>;
+    static_assert(kWidth == D || (!kHalf && kWidth % 4 == 0 && kWidth < D), "narrow rows: FP32 storage only");
+    using F = Forward<D, kHalf>;
+    using Storage = SharedStorage<D, kHalf>;
     constexpr int kStages = F::kStages;
     extern __shared__ uint8_t shared_raw[];
-    SharedStorage<D> &s = *reinterpret_cast<SharedStorage<D> *>((reinterpret_cast<uintptr_t>(shared_raw) + 1023) & ~uintptr_t(1023));
+    Storage &s = *reinterpret_cast<Storage *>((reinterpret_cast<uintptr_t>(shared_raw) + 1023) & ~uintptr_t(1023));
     const AttentionParams &p = args.p;
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -285,8 +392,10 @@ __global__ void __launch_bounds__(Forward<D>::kThreads, 1)
         mbar_fence_init();
     }
     // Rows 2D..2D+15 of every V operand tile are FP16 ones, so P.V also yields the row sums of P.
-    for (int i = threadIdx.x; i < kStages * 16 * 32; i += F::kThreads)
-        s.vt16[i / (16 * 32)][2 * D * 32 + i % (16 * 32)] = 0x3C003C00u;
+    if constexpr (!kHalf) {
+        for (int i = threadIdx.x; i < kStages * 16 * 32; i += F::kThreads)
+            s.vt16[i / (16 * 32)][2 * D * 32 + i % (16 * 32)] = 0x3C003C00u;
+    }
     fence_proxy_async_shared();
     tc_fence_before();
     __syncthreads();
@@ -324,7 +433,7 @@ __global__ void __launch_bounds__(Forward<D>::kThreads, 1)
         // stage of tile j is released once every P.V product is issued. The whole warp runs
         // the loop (uniform control flow and descriptors); elected lanes issue the tcgen05 ops.
         if (tiles > 0) {
-            const uint64_t k_desc0 = sw128_descriptor(smem_u32(s.k16[0]));
+            const uint64_t k_desc0 = sw128_descriptor(smem_u32(kHalf ? static_cast<const void *>(s.k_raw[0]) : s.k16[0]));
             const uint64_t v_desc0 = sw128_descriptor(smem_u32(s.vt16[0]));
             bool ok = mbar_wait_warp(&s.q_ready, 0);
             tc_fence_after();
@@ -333,7 +442,7 @@ __global__ void __launch_bounds__(Forward<D>::kThreads, 1)
                 tc_fence_after();
                 if (!ok) break;
 #pragma unroll
-                for (int t = 0; t < F::kQTiles; ++t) issue_scores<D>(tmem, k_desc0 + F::kDescStageK * j, t, j, &s.s_full[t][j]);
+                for (int t = 0; t < F::kQTiles; ++t) issue_scores<D, kHalf>(tmem, k_desc0 + F::kDescStageK * j, t, j, &s.s_full[t][j]);
             }
             for (int j = 0; j < tiles && ok; ++j) {
                 const int stage = j % kStages, buffer = j & 1;
@@ -349,7 +458,7 @@ __global__ void __launch_bounds__(Forward<D>::kThreads, 1)
                         if (!ok || served[t] || !mbar_test_wait_warp(&s.p_full[t], j & 1)) continue;
                         if (lane == 0) RK_TRACE(j, t);
                         tc_fence_after();
-                        issue_values<D>(tmem, v_desc0 + F::kDescStageV * stage, t, buffer, &s.pv_done[t]);
+                        issue_values<D, kHalf>(tmem, v_desc0 + F::kDescStageV * stage, t, buffer, &s.pv_done[t]);
                         if (more) {
                             if (!next_ready) {
                                 next_ready = mbar_wait_warp(&s.kv_ready[next_stage], ((j + 2) / kStages) & 1);
@@ -359,7 +468,7 @@ __global__ void __launch_bounds__(Forward<D>::kThreads, 1)
                                 }
                                 tc_fence_after();
                             }
-                            issue_scores<D>(tmem, k_desc0 + F::kDescStageK * next_stage, t, buffer, &s.s_full[t][buffer]);
+                            issue_scores<D, kHalf>(tmem, k_desc0 + F::kDescStageK * next_stage, t, buffer, &s.s_full[t][buffer]);
                         }
                         served[t] = true;
                         --remaining;
@@ -385,6 +494,17 @@ __global__ void __launch_bounds__(Forward<D>::kThreads, 1)
         const int row = 32 * w + lane;  // K row of this lane
         for (int j = 0; j < tiles; ++j) {
             const int stage = j % kStages, use = j / kStages;
+            if constexpr (kHalf) {
+                // FP16 storage: the MMAs read K from the TMA tile; V is transposed, masked rows zeroed.
+                if (!__all_sync(0xffffffffu, mbar_wait(&s.kv_full[stage], use & 1))) break;
+                const int key = first + j * kKeyTile + row;
+                const uint32_t bits = __ballot_sync(0xffffffffu, key < last && mask[key] != 0);
+                if (lane == 0) s.key_mask[stage][w] = bits;
+                transpose_values<D>(s.v_raw[stage], s.vt16[stage], w, lane, bits);
+                fence_proxy_async_shared();
+                mbar_arrive(&s.kv_ready[stage]);
+                continue;
+            } else {
             // Both split warps pass the named barrier below before either may give up, so a
             // failed wait can never leave one of them blocked in bar.sync.
             const bool landed = __all_sync(0xffffffffu, mbar_wait(&s.kv_full[stage], use & 1));
@@ -469,6 +589,7 @@ __global__ void __launch_bounds__(Forward<D>::kThreads, 1)
             fence_proxy_async_shared();
             if (lane == 0 && w == 0) RK_TRACE(j, 3);
             mbar_arrive(&s.kv_ready[stage]);
+            }
         }
     } else {
         // ---------------------------------------------------------------- softmax / epilogue
@@ -479,14 +600,35 @@ __global__ void __launch_bounds__(Forward<D>::kThreads, 1)
         const uint32_t lane_base = tmem_lane_address(tmem, warp) + tile * F::kColTile;
         const bool tracer = row_in_tile == 0;
 
-        int q_exponent;
-        {  // Q row -> scaled by 1/sqrt(D) and 2^q_exponent, split into FP16 q0/q1 pairs in TMEM
+        int q_exponent = 0;
+        if constexpr (kHalf) {  // Q row as FP16 pairs in TMEM, unscaled
+            const uint4 *q8 = reinterpret_cast<const uint4 *>(p.q.row_as<__half>(b, h, row_valid ? query : 0));
+            float packed[D / 2];
+#pragma unroll
+            for (int c = 0; c < D / 8; ++c) {
+                const uint4 v = row_valid ? __ldg(q8 + c) : make_uint4(0u, 0u, 0u, 0u);
+                packed[4 * c] = __uint_as_float(v.x);
+                packed[4 * c + 1] = __uint_as_float(v.y);
+                packed[4 * c + 2] = __uint_as_float(v.z);
+                packed[4 * c + 3] = __uint_as_float(v.w);
+            }
+#pragma unroll
+            for (int c = 0; c < D / 2; c += 16) {
+                if constexpr (D == 16)
+                    tmem_store8_async(lane_base + F::kColQ0, packed);
+                else
+                    tmem_store8x2_async(lane_base + F::kColQ0 + c, packed + c, lane_base + F::kColQ0 + c + 8, packed + c + 8);
+            }
+            tmem_wait_store();
+            tc_fence_before();
+            mbar_arrive(&s.q_ready);
+        } else {  // Q row -> scaled by 1/sqrt(D) and 2^q_exponent, split into FP16 q0/q1 pairs in TMEM
             float x[D];
             const float4 *q4 = reinterpret_cast<const float4 *>(p.q.row(b, h, row_valid ? query : 0));
             float qmax = 0.f;
 #pragma unroll
             for (int c = 0; c < D / 4; ++c) {
-                const float4 v = row_valid ? __ldg(q4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+                const float4 v = row_valid && c < kWidth / 4 ? __ldg(q4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
                 x[4 * c] = v.x * p.scale;
                 x[4 * c + 1] = v.y * p.scale;
                 x[4 * c + 2] = v.z * p.scale;
@@ -541,8 +683,9 @@ __global__ void __launch_bounds__(Forward<D>::kThreads, 1)
                 const int lo_col = max(0, query - p.radius - k0), hi_col = min(kKeyTile - 1, query + p.radius - k0);
                 active &= lo_col > hi_col ? 0ull : ((~0ull) >> (63 - (hi_col - lo_col))) << lo_col;
             }
-            const float s_scale = exp2_int(-(q_exponent + s.k_exponent[stage]));  // TMEM S -> scaled score
-            const int v_exponent = s.v_exponent[stage];
+            // TMEM S -> scaled score (FP16 storage: S is the plain dot product)
+            const float s_scale = kHalf ? p.scale : exp2_int(-(q_exponent + s.k_exponent[stage]));
+            const int v_exponent = kHalf ? 0 : s.v_exponent[stage];
             // Row max (four independent three-input max chains).
             if (active != ~0ull) {
 #pragma unroll
@@ -563,10 +706,10 @@ __global__ void __launch_bounds__(Forward<D>::kThreads, 1)
             // the MMA warp start P(j).V, which overwrites Ot. The TMEM stores inside are
             // warp-collective, so the branch is taken by the whole warp (the explicit path is
             // exact for finite rows too).
-            if (__all_sync(0xffffffffu, isfinite(offset) && slope > 0.f))
-                exp_split_store<true>(sc, slope, offset, pbuf);
-            else
-                exp_split_store<false>(sc, slope, offset, pbuf);
+            const float tile_sum = __all_sync(0xffffffffu, isfinite(offset) && slope > 0.f)
+                                           ? exp_split_store<true, kHalf>(sc, slope, offset, pbuf)
+                                           : exp_split_store<false, kHalf>(sc, slope, offset, pbuf);
+            if constexpr (kHalf) row_sum = fmaf(row_sum, old_weight, tile_sum);  // kept in units of the new max
             RK_WARP_TRACE(j, 2);
             if (j > 0) {  // fold tile j-1 before P(j).V overwrites its Ot
                 ok = __all_sync(0xffffffffu, mbar_wait(&s.pv_done[tile], (j - 1) & 1));
@@ -575,7 +718,7 @@ __global__ void __launch_bounds__(Forward<D>::kThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                fold_output<D>(o, row_sum, o_exp, lane_base, pending_weight, pending_exponent);
+                fold_output<D, kHalf>(o, row_sum, o_exp, lane_base, pending_weight, pending_exponent);
             }
             RK_WARP_TRACE(j, 3);
             tmem_wait_store();
@@ -592,25 +735,40 @@ __global__ void __launch_bounds__(Forward<D>::kThreads, 1)
         if (tiles > 0 && ok) {
             ok = __all_sync(0xffffffffu, mbar_wait(&s.pv_done[tile], (tiles - 1) & 1));
             tc_fence_after();
-            if (ok) fold_output<D>(o, row_sum, o_exp, lane_base, pending_weight, pending_exponent);
+            if (ok) fold_output<D, kHalf>(o, row_sum, o_exp, lane_base, pending_weight, pending_exponent);
         }
         if (row_valid) {
             const float total = ok ? row_sum : NAN;
-            float *out = p.o.row(b, h, query);
+            const bool nan_out = isnan(total) && !p.zero_nan_rows;
             const float out_scale = exp2_int(-o_exp) / total;
 #pragma unroll
-            for (int c = 0; c < D; ++c) o[c] = total > 0.f ? o[c] * out_scale : isnan(total) ? NAN : 0.f;
-            if (args.vec_out) {
+            for (int c = 0; c < D; ++c) o[c] = total > 0.f ? o[c] * out_scale : nan_out ? NAN : 0.f;
+            if constexpr (kHalf) {
+                __half *out = p.o.row_as<__half>(b, h, query);
+                if (args.vec_out) {
 #pragma unroll
-                for (int c = 0; c < D / 4; ++c)
-                    reinterpret_cast<float4 *>(out)[c] = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+                    for (int c = 0; c < D / 8; ++c)
+                        reinterpret_cast<uint4 *>(out)[c] =
+                                make_uint4(pack_half2(o[8 * c], o[8 * c + 1]), pack_half2(o[8 * c + 2], o[8 * c + 3]),
+                                           pack_half2(o[8 * c + 4], o[8 * c + 5]), pack_half2(o[8 * c + 6], o[8 * c + 7]));
+                } else {
+#pragma unroll
+                    for (int c = 0; c < D; ++c) out[c] = __float2half_rn(o[c]);
+                }
             } else {
+                float *out = p.o.row(b, h, query);
+                if (args.vec_out) {
 #pragma unroll
-                for (int c = 0; c < D; ++c) out[c] = o[c];
+                    for (int c = 0; c < kWidth / 4; ++c)
+                        reinterpret_cast<float4 *>(out)[c] = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+                } else {
+#pragma unroll
+                    for (int c = 0; c < kWidth; ++c) out[c] = o[c];
+                }
             }
             const long long row = (static_cast<long long>(b) * p.heads + h) * p.queries + query;
-            p.lse[row * 2] = total > 0.f ? row_max : isnan(total) ? NAN : -INFINITY;
-            p.lse[row * 2 + 1] = total > 0.f ? total * (1.f / kPScale) : isnan(total) ? NAN : 0.f;
+            p.lse[row * 2] = total > 0.f ? row_max : nan_out ? NAN : -INFINITY;
+            p.lse[row * 2 + 1] = total > 0.f ? total * (1.f / kPScale) : nan_out ? NAN : 0.f;
         }
     }
 
@@ -637,68 +795,105 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_function() {
     return function;
 }
 
-// [batch][heads][tokens][width] FP32 with the given element strides; box = 32 features x 64 tokens.
-bool make_tensor_map(CUtensorMap *map, const Tensor &t, int width, int batch, int heads, int tokens) {
+// [batch][heads][tokens][width] with the given element strides, FP32 (box = 32 features x 64
+// tokens) or FP16 (box = 64 features x 64 tokens; for width < 64 the features past the width
+// are the TMA's zero fill). 128-byte box rows, 128B swizzle.
+bool make_tensor_map(CUtensorMap *map, const Tensor &t, int width, int batch, int heads, int tokens, bool half) {
     auto encode = encode_function();
     if (encode == nullptr) return false;
+    const cuuint64_t element = half ? 2 : 4;
     const cuuint64_t dims[4] = {static_cast<cuuint64_t>(width), static_cast<cuuint64_t>(tokens), static_cast<cuuint64_t>(heads),
                                 static_cast<cuuint64_t>(batch)};
-    const cuuint64_t strides[3] = {static_cast<cuuint64_t>(t.st) * 4, static_cast<cuuint64_t>(t.sh) * 4,
-                                   static_cast<cuuint64_t>(t.sb) * 4};
-    const cuuint32_t box[4] = {32, static_cast<cuuint32_t>(kKeyTile), 1, 1};
+    const cuuint64_t strides[3] = {static_cast<cuuint64_t>(t.st) * element, static_cast<cuuint64_t>(t.sh) * element,
+                                   static_cast<cuuint64_t>(t.sb) * element};
+    const cuuint32_t box[4] = {half ? 64u : 32u, static_cast<cuuint32_t>(kKeyTile), 1, 1};
     const cuuint32_t element_strides[4] = {1, 1, 1, 1};
-    return encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float *>(t.data), dims, strides, box, element_strides,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    return encode(map, half ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float *>(t.data), dims,
+                  strides, box, element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-bool positive_tma_strides(const Tensor &t) {
-    const long long limit = 1ll << 38;  // strides below 2^40 bytes
-    return t.st > 0 && t.sh > 0 && t.sb > 0 && t.st % 4 == 0 && t.sh % 4 == 0 && t.sb % 4 == 0 && t.st < limit &&
+// Strides that TMA accepts (positive multiples of 16 bytes below 2^40 bytes) and a 16-byte aligned
+// base; `per16` = elements per 16 bytes.
+bool positive_tma_strides(const Tensor &t, int per16) {
+    const long long limit = 1ll << 38;
+    return t.st > 0 && t.sh > 0 && t.sb > 0 && t.st % per16 == 0 && t.sh % per16 == 0 && t.sb % per16 == 0 && t.st < limit &&
            t.sh < limit && t.sb < limit && (reinterpret_cast<uintptr_t>(t.data) & 15u) == 0;
 }
 
-template <int D>
+template <int D, bool kHalf>
 constexpr int shared_bytes() {
-    return static_cast<int>(sizeof(SharedStorage<D>)) + 1024;
+    return static_cast<int>(sizeof(SharedStorage<D, kHalf>)) + 1024;
 }
-template <int D>
+template <int D, bool kHalf>
 constexpr bool layout_ok() {
-    using F = Forward<D>;
-    return sizeof(SharedStorage<D>::k16[0]) == 64 * 2 * D * 2 && sizeof(SharedStorage<D>::vt16[0]) == F::kVRows * 128 &&
-           sizeof(SharedStorage<D>::vt16[0]) % 1024 == 0 && F::kColSum + 16 <= (F::kQTiles == 2 ? F::kColTile : F::kTmemColumns) &&
-           shared_bytes<D>() <= 227 * 1024;
+    using F = Forward<D, kHalf>;
+    using S = SharedStorage<D, kHalf>;
+    return (kHalf || sizeof(S::k16[0]) == 64 * 2 * D * 2) && sizeof(S::vt16[0]) == F::kVRows * 128 &&
+           sizeof(S::vt16[0]) % 1024 == 0 && sizeof(S::k_raw[0]) % 1024 == 0 &&
+           F::kColSum + (kHalf ? 0 : 16) <= (F::kQTiles == 2 ? F::kColTile : F::kTmemColumns) &&
+           shared_bytes<D, kHalf>() <= 227 * 1024;
 }
-static_assert(layout_ok<32>() && layout_ok<64>(), "operand tiles, TMEM columns and shared memory budget");
+static_assert(layout_ok<32, false>() && layout_ok<64, false>() && layout_ok<16, true>() && layout_ok<32, true>() &&
+                      layout_ok<64, true>(),
+              "operand tiles, TMEM columns and shared memory budget");
 
-template <int D>
+template <int D, bool kHalf, int kWidth = D>
 int launch(const AttentionParams &p, cudaStream_t stream) {
-    using F = Forward<D>;
+    using F = Forward<D, kHalf>;
     CUtensorMap tmap_k, tmap_v;
-    if (!make_tensor_map(&tmap_k, p.k, D, p.batch, p.heads, p.keys) || !make_tensor_map(&tmap_v, p.v, D, p.batch, p.heads, p.keys))
+    if (!make_tensor_map(&tmap_k, p.k, kWidth, p.batch, p.heads, p.keys, kHalf) ||
+        !make_tensor_map(&tmap_v, p.v, kWidth, p.batch, p.heads, p.keys, kHalf))
         return kNotEligible;
-    cudaError_t status = prepare_kernel<flash_forward_kernel<D>>(shared_bytes<D>());
+    cudaError_t status = prepare_kernel<flash_forward_kernel<D, kHalf, kWidth>>(shared_bytes<D, kHalf>());
     if (status != cudaSuccess) return status;
+    constexpr int per16 = kHalf ? 8 : 4;
     FlashArgs args{};
     args.p = p;
     args.cta_per_head = (p.queries + F::kCtaQueries - 1) / F::kCtaQueries;
-    args.vec_out = (reinterpret_cast<uintptr_t>(p.o.data) & 15u) == 0 && p.o.sb % 4 == 0 && p.o.sh % 4 == 0 && p.o.st % 4 == 0;
+    args.vec_out = (reinterpret_cast<uintptr_t>(p.o.data) & 15u) == 0 && p.o.sb % per16 == 0 && p.o.sh % per16 == 0 &&
+                   p.o.st % per16 == 0;
     const unsigned blocks = static_cast<unsigned>(args.cta_per_head) * static_cast<unsigned>(p.heads) * static_cast<unsigned>(p.batch);
-    flash_forward_kernel<D><<<blocks, F::kThreads, shared_bytes<D>(), stream>>>(args, tmap_k, tmap_v);
+    flash_forward_kernel<D, kHalf, kWidth><<<blocks, F::kThreads, shared_bytes<D, kHalf>(), stream>>>(args, tmap_k, tmap_v);
     return cudaGetLastError();
 }
 
 }  // namespace
 
 bool flash_supported(const AttentionParams &p) {
-    return p.vec4 && positive_tma_strides(p.k) && positive_tma_strides(p.v) && (p.q.st % 4 == 0) &&
+    return p.vec4 && positive_tma_strides(p.k, 4) && positive_tma_strides(p.v, 4) && (p.q.st % 4 == 0) &&
            (reinterpret_cast<uintptr_t>(p.q.data) & 15u) == 0;
 }
 
 int launch_flash_forward(const AttentionParams &p, int head_width, cudaStream_t stream) {
-    if (head_width == 32) return launch<32>(p, stream);
-    if (head_width == 64) return launch<64>(p, stream);
+    if (head_width == 16) return launch<32, false, 16>(p, stream);
+    if (head_width == 32) return launch<32, false>(p, stream);
+    if (head_width == 64) return launch<64, false>(p, stream);
     return kNotEligible;
+}
+
+bool half_flash_supported(const AttentionParams &p) {
+    const Tensor &q = p.q;
+    return positive_tma_strides(p.k, 8) && positive_tma_strides(p.v, 8) && q.st % 8 == 0 && q.sh % 8 == 0 && q.sb % 8 == 0 &&
+           (reinterpret_cast<uintptr_t>(q.data) & 15u) == 0;
+}
+
+int launch_half_flash_forward(const AttentionParams &p, int head_width, cudaStream_t stream) {
+    if (head_width == 16) return launch<16, true>(p, stream);
+    if (head_width == 32) return launch<32, true>(p, stream);
+    if (head_width == 64) return launch<64, true>(p, stream);
+    return kNotEligible;
+}
+
+bool tensor_maps_encodable(const AttentionParams &p, int head_width, bool half) {
+    if (encode_function() == nullptr) return true;  // no driver here: nothing to ask
+    CUtensorMap map_k, map_v;
+    return make_tensor_map(&map_k, p.k, head_width, p.batch, p.heads, p.keys, half) &&
+           make_tensor_map(&map_v, p.v, head_width, p.batch, p.heads, p.keys, half);
+}
+
+const char *half_kernel_name(int head_width) {
+    return head_width == 16 ? "tcgen05-f16-flash-d16" : head_width == 32 ? "tcgen05-f16-flash-d32" : "tcgen05-f16-flash-d64";
 }
 
 unsigned int read_device_status(bool clear) {
@@ -711,7 +906,9 @@ unsigned int read_device_status(bool clear) {
     return value;
 }
 
-const char *kernel_name(int head_width) { return head_width == 64 ? "tcgen05-f16x2-flash-d64" : "tcgen05-f16x2-flash-d32"; }
+const char *kernel_name(int head_width) {
+    return head_width == 64 ? "tcgen05-f16x2-flash-d64" : head_width == 16 ? "tcgen05-f16x2-flash-d16" : "tcgen05-f16x2-flash-d32";
+}
 
 #ifdef RK_TC_TRACE
 extern "C" __attribute__((visibility("default"))) int rocmkernels_attention_trace(long long *out, int capacity) {
@@ -724,8 +921,9 @@ extern "C" __attribute__((visibility("default"))) int rocmkernels_attention_trac
 #endif
 
 const char *build_info() {
-    return "sm_100a; tcgen05-f16x2-flash-d32/d64 forward (TMA + TMEM, split FP16 operands, double-buffered S, tensor-core row "
-           "sums); tcgen05 split-FP16 backward d32/d64 (query-major delta+dQ, key-major dK/dV); simt-fp32 d32/d64 forward+backward";
+    return "sm_100a; tcgen05-f16x2-flash-d16/d32/d64 forward (TMA + TMEM, split FP16 operands, double-buffered S, tensor-core row "
+           "sums); tcgen05-f16-flash-d16/d32/d64 generic forward for FP16 storage; tcgen05 split-FP16 backward d32/d64 "
+           "(query-major delta+dQ, key-major dK/dV); simt-fp32 d16/d32/d64 forward (FP32 or FP16 storage), d32/d64 backward";
 }
 
 }  // namespace tc

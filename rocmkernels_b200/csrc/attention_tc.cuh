@@ -13,9 +13,20 @@ constexpr int kNotEligible = -1;
 // True when the tensor-core flash forward accepts the tensors (TMA-addressable K and V, 16-byte
 // addressable Q rows).
 bool flash_supported(const AttentionParams &p);
-// Launches the tensor-core flash forward for head width 32 or 64; returns a cudaError_t value or
-// kNotEligible.
+// Launches the tensor-core flash forward for head width 32 or 64 (16: the 32-wide kernel over
+// zero-filled features 16-31); returns a cudaError_t value or kNotEligible.
 int launch_flash_forward(const AttentionParams &p, int head_width, cudaStream_t stream);
+// True when the FP16-storage tensor-core forward accepts the tensors (TMA-addressable K and V,
+// 16-byte addressable Q rows).
+bool half_flash_supported(const AttentionParams &p);
+// Launches the FP16-storage tensor-core forward (the generic forward's DType::Float16) for head
+// width 16, 32 or 64; returns a cudaError_t value or kNotEligible.
+int launch_half_flash_forward(const AttentionParams &p, int head_width, cudaStream_t stream);
+// False when the driver rejects the tensor maps the tensor-core forward would use for these
+// tensors (the launch then falls back to SIMT); true when it accepts them or no driver is loaded.
+bool tensor_maps_encodable(const AttentionParams &p, int head_width, bool half);
+// Name of the FP16-storage tensor-core kernel for a head width.
+const char *half_kernel_name(int head_width);
 // Static description of the build (architecture and kernel families).
 const char *build_info();
 // Reads (and optionally clears) the device status word set by a failed bounded wait;

@@ -161,6 +161,19 @@ __device__ __forceinline__ void tmem_load16x2_1(uint32_t a, float (&va)[16], uin
     vc = __uint_as_float(r[32]);
 }
 
+// 16 columns at a with one wait.
+__device__ __forceinline__ void tmem_load16(uint32_t a, float (&va)[16]) {
+    uint32_t r[16];
+    asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
+            "tcgen05.wait::ld.sync.aligned;"
+            : RK_R8(0), RK_R8(8)
+            : "r"(a)
+            : "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) va[i] = __uint_as_float(r[i]);
+}
+
 // 16 columns at a and 16 columns at b, one wait for both stores.
 __device__ __forceinline__ void tmem_store16x2(uint32_t a, const float *va, uint32_t b, const float *vb) {
     uint32_t r[32];
@@ -188,6 +201,15 @@ __device__ __forceinline__ void tmem_store8x2_async(uint32_t a, const float *va,
             "r"(__float_as_uint(vb[1])), "r"(__float_as_uint(vb[2])), "r"(__float_as_uint(vb[3])), "r"(__float_as_uint(vb[4])),
             "r"(__float_as_uint(vb[5])), "r"(__float_as_uint(vb[6])), "r"(__float_as_uint(vb[7])), "r"(a), "r"(b)
             : "memory");
+}
+
+// 8 columns at a without waiting (see tmem_store8x2_async).
+__device__ __forceinline__ void tmem_store8_async(uint32_t a, const float *va) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%8], {%0,%1,%2,%3,%4,%5,%6,%7};" ::"r"(__float_as_uint(va[0])),
+                 "r"(__float_as_uint(va[1])), "r"(__float_as_uint(va[2])), "r"(__float_as_uint(va[3])),
+                 "r"(__float_as_uint(va[4])), "r"(__float_as_uint(va[5])), "r"(__float_as_uint(va[6])),
+                 "r"(__float_as_uint(va[7])), "r"(a)
+                 : "memory");
 }
 
 __device__ __forceinline__ void tmem_wait_store() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
@@ -277,6 +299,36 @@ __device__ __forceinline__ void mma4_f16_ts_warp(uint32_t d, const uint32_t (&a)
             "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%4], %8, %9, rest;\n\t}" ::"r"(d),
             "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "r"(idesc),
             "r"(overwrite)
+            : "memory");
+}
+
+// Warp-collective: one kind::f16 MMA (overwriting the accumulator when `overwrite` is set) and a
+// commit to `bar`, one elected sequence.
+__device__ __forceinline__ void mma1_f16_ts_commit_warp(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, uint32_t overwrite,
+                                                        uint64_t *bar) {
+    asm volatile(
+            "{\n\t.reg .pred e, first;\n\t"
+            "elect.sync _|e, 0xffffffff;\n\t"
+            "setp.eq.b32 first, %4, 0;\n\t"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, first;\n\t"
+            "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%5];\n\t}" ::"r"(d),
+            "r"(a), "l"(b), "r"(idesc), "r"(overwrite), "r"(smem_u32(bar))
+            : "memory");
+}
+
+// Warp-collective: two kind::f16 MMAs into one accumulator (the first overwriting it when
+// `overwrite` is set) and a commit to `bar`, one elected sequence.
+__device__ __forceinline__ void mma2_f16_ts_first_commit_warp(uint32_t d, uint32_t a0, uint32_t a1, uint64_t b0, uint64_t b1,
+                                                              uint32_t idesc, uint32_t overwrite, uint64_t *bar) {
+    asm volatile(
+            "{\n\t.reg .pred e, first, rest;\n\t"
+            "elect.sync _|e, 0xffffffff;\n\t"
+            "setp.eq.b32 first, %6, 0;\n\t"
+            "setp.eq.b32 rest, %6, %6;\n\t"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %3, %5, first;\n\t"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%2], %4, %5, rest;\n\t"
+            "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%7];\n\t}" ::"r"(d),
+            "r"(a0), "r"(a1), "l"(b0), "l"(b1), "r"(idesc), "r"(overwrite), "r"(smem_u32(bar))
             : "memory");
 }
 

@@ -46,6 +46,7 @@ def test_reference_entry_points_all_declared():
         "attention_fp32_statistics", "attention_fp32_forward_tuned", "attention_fp32_forward_flash",
         "attention_fp32_forward_flash_tuned", "attention_fp32_backward_tuned", "attention64_fp32_forward",
         "attention64_fp32_backward", "attention_fp32_backward_profile", "attention_fp32_query_profile",
+        "attention_generic_forward",
     }
     assert reference_names <= set(declared_functions())
     assert reference_names == set(api.ENTRY_POINTS)
@@ -116,3 +117,42 @@ def test_throwing_wrappers_raise_hip_error():
     with pytest.raises(api.HipError) as error:
         api.AttentionForwardFlash(*forward_args(q=None), S, S, S, S)
     assert error.value.status == api.INVALID_VALUE
+
+
+def generic_args(head_width=32, dtype=api.DType.Float32, **override):
+    return [*forward_args(**override)[:10], head_width, override.get("radius", -1), S, S, S, S, dtype]
+
+
+@pytest.mark.parametrize("override", [dict(q=None), dict(k=None), dict(v=None), dict(mask=None), dict(output=None),
+                                      dict(lse=None), dict(batch=0), dict(heads=-1), dict(queries=0), dict(keys=0),
+                                      dict(radius=-2)])
+@pytest.mark.parametrize("dtype", list(api.DType))
+def test_generic_forward_rejects_invalid_arguments(override, dtype):
+    # AttentionGeneric.hip:295-297: null pointers, non-positive sizes, radius < -1
+    assert api.attention_generic_forward(*generic_args(dtype=dtype, **override)) == api.INVALID_VALUE
+
+
+@pytest.mark.parametrize("head_width", [0, 8, 17, 48, 128])
+def test_generic_forward_rejects_head_width(head_width):
+    # AttentionGeneric.hip:296: only 16, 32 and 64
+    assert api.attention_generic_forward(*generic_args(head_width=head_width)) == api.INVALID_VALUE
+
+
+@pytest.mark.parametrize("dtype", [2, 3, 255])
+def test_generic_forward_rejects_unknown_dtype(dtype):
+    # AttentionGeneric.hip:306-307: any other DType value
+    assert api.attention_generic_forward(*generic_args(dtype=dtype)) == api.INVALID_VALUE
+
+
+def test_generic_wrapper_raises_hip_error():
+    with pytest.raises(api.HipError) as error:
+        api.AttentionGenericForward(*generic_args(head_width=24))
+    assert error.value.status == api.INVALID_VALUE
+
+
+@pytest.mark.parametrize("head_width", [16, 32, 64])
+def test_generic_dispatch_names(head_width):
+    # Contiguous tensors: FP16 storage on the FP16 tensor-core kernel, FP32 on the split one.
+    assert api.generic_kernel_name(2, 8, 512, 512, head_width, api.DType.Float16) == f"tcgen05-f16-flash-d{head_width}"
+    assert api.generic_kernel_name(2, 8, 512, 512, head_width, api.DType.Float32) == f"tcgen05-f16x2-flash-d{head_width}"
+    assert api.generic_kernel_name(1, 1, 4, 4, 24, api.DType.Float16) == "unsupported"

@@ -19,3 +19,15 @@ def test_reference_attention_tests_pass(cuda):
     print(result.stdout)
     assert result.returncode == 0, result.stdout + result.stderr
     assert result.stdout.count("PASS:") == 7
+
+
+@pytest.mark.skipif(not oracle.REFERENCE_GENERIC_TESTS.exists(),
+                    reason="reference generic test binary not built (needs the reference tree)")
+def test_reference_generic_tests_pass(cuda):
+    """ROCmKernels.Tests/Generic/AttentionGenericTests.cpp, unchanged: head widths 16/32/64 x
+    fp32/fp16, each leaf section two cases against its double-precision ComputeReference with
+    its own max-abs tolerances (5e-4 fp32, 2e-3 fp16)."""
+    result = subprocess.run([str(oracle.REFERENCE_GENERIC_TESTS), "-s"], capture_output=True, text=True, timeout=300)
+    print(result.stdout)
+    assert result.returncode == 0, result.stdout + result.stderr
+    assert result.stdout.count("PASS:") == 6
