@@ -17,7 +17,12 @@ BASELINE key-padding lengths (seed 105) and radius. They report the repo-convent
 the forward and backward times separately. The ``generic_*`` workloads are the reference's
 AttentionGeneric benchmark cases (AttentionGenericBenchmarks.cpp:14-18, 100-110: B2 H8 L512,
 d = 16/32/64, fp32 or fp16 storage): a step is one ``attention_generic_forward`` call, per GPU
-(weak scaling), 4*B*H*Q*K*d FLOPs (the reference's operation count, :96).
+(weak scaling), 4*B*H*Q*K*d FLOPs (the reference's operation count, :96). ``rotary_*`` are the
+reference's Rotary benchmark cases (RotaryBenchmarks.cpp:75-76: B2 H12 L1024, token-major q and
+k, 0.5-valued inputs): one ``rotary_fp32`` call per step, GB/s over the reference's byte count
+(4 x elements x 4 B, :68). ``flash_rotary_fwd_b8h3s1024d32`` is the headline forward with the
+rotary prologue fused in (``attention_fp32_forward_flash_rotary``); its line also carries the
+time of the unfused sequence (``rotary_fp32`` then ``attention_fp32_forward_flash``).
 
 Timing: W untimed steps, then K steps; before each step a 256 MiB buffer is written to flush
 the 126 MB L2, and the step itself is bracketed by CUDA events on the launching stream (the
@@ -67,6 +72,14 @@ WORKLOADS = {
     "fwd_bwd_b4h12s4096d32": dict(batch=4, heads=12, seq=4096, dim=32, radius=-1, lengths=None, backward=True,
                                   description="profiling case: C5's shape at B=4 (inputs above L2, a few hundred MB)"),
 }
+WORKLOADS["flash_rotary_fwd_b8h3s1024d32"] = dict(
+        batch=8, heads=3, seq=1024, dim=32, radius=-1, lengths=None, backward=False, rotary=True,
+        description="headline flash forward B8 H3 S1024 d32 with the rotary prologue fused (attention_fp32_forward_flash_rotary)")
+for _direction in ("fwd", "bwd"):
+    WORKLOADS[f"rotary_{_direction}_b2h12l1024"] = dict(
+            batch=2, heads=12, seq=1024, dim=32, radius=-1, lengths=None, backward=_direction == "bwd", kind="rotary",
+            description=f"Rotary {'backward' if _direction == 'bwd' else 'forward'} b2 h12 l1024 (RotaryBenchmarks.cpp:75-76), "
+                        f"rotary_fp32")
 for _width in (16, 32, 64):
     for _storage in ("fp32", "fp16"):
         WORKLOADS[f"generic_fwd_b2h8s512d{_width}_{_storage}"] = dict(
@@ -231,6 +244,16 @@ def run_reference(args, rank: int) -> None:
     if spec.get("generic"):
         run_reference_generic(args, spec)
         return
+    if spec.get("kind") == "rotary":
+        base = rotary_cpu_baseline(spec)
+        print(json.dumps({"metric": "rotary GB/s (4 x elements x 4 B per step: q, k read, oq, ok written; RotaryBenchmarks.cpp:68)",
+                          "value": base["value"], "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
+                          "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                          "dtype": "f32", "data": "seeded uniform", "config": workload_config(args.workload, args.gpus),
+                          "impl": "reference", "cpu_baseline": base,
+                          "e2e": {"value": base["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+              flush=True)
+        return
     seq, dim, radius = spec["seq"], spec["dim"], spec["radius"]
     length = key_lengths(spec)[0]
     threads = oracle.cpu_count()
@@ -276,6 +299,127 @@ def run_reference(args, rank: int) -> None:
             "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": kind, "sample": sample},
             "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def rotary_cpu_baseline(spec: dict) -> dict:
+    """The rotary oracle (ReferenceRotary restated, one thread) over the full workload."""
+    from oracle import oracle
+
+    batch, heads, length = spec["batch"], spec["heads"], spec["seq"]
+    x = oracle.uniform(batch * length * heads * 32, 21, -2, 2).reshape(batch, length, heads, 32)
+    cos = oracle.uniform(batch * length * 32, 23).reshape(batch, length, 32)
+    sin = oracle.uniform(batch * length * 32, 24).reshape(batch, length, 32)
+    reps, elapsed = 0, 0.0
+    while elapsed < 5.0 and reps < 200:
+        start = time.perf_counter()
+        oracle.rotary(x, cos, sin, spec["backward"])
+        oracle.rotary(x, cos, sin, spec["backward"])  # q and k
+        elapsed += time.perf_counter() - start
+        reps += 1
+    moved = 4.0 * batch * heads * length * 32 * 4
+    return {"value": moved * reps / elapsed / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"oracle_rotary (ReferenceRotary, PositionalTests.cpp:18-50) on q and k of the full workload x{reps},"
+                      f" {elapsed:.1f} s on 1 thread"}
+
+
+def run_rotary(args, spec: dict, device, world: int, rank: int, dist) -> None:
+    """Rotary workloads: rotary_fp32 on token-major q, k (the reference's benchmark layout)."""
+    import torch
+
+    import rocmkernels_b200.attention as api
+
+    batch, heads, length = spec["batch"], spec["heads"], spec["seq"]
+    backward = 1 if spec["backward"] else 0
+    generator = torch.Generator(device=device)
+    generator.manual_seed(301 + rank)
+    q = torch.randn(batch, length, heads, 32, device=device, generator=generator)
+    k = torch.randn(batch, length, heads, 32, device=device, generator=generator)
+    cos = torch.randn(batch, length, 32, device=device, generator=generator)
+    sin = torch.randn(batch, length, 32, device=device, generator=generator)
+    oq, ok = torch.empty_like(q), torch.empty_like(k)
+    qk_strides = api.Strides(length * heads * 32, 32, heads * 32)  # RotaryBenchmarks.cpp:55
+    table_strides = api.Strides(length * 32, 0, 32)                 # :56
+    stream = torch.cuda.current_stream(device)
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=device)
+
+    def step():
+        status = api.rotary_fp32(q, k, cos, sin, oq, ok, batch, heads, length, backward, qk_strides, qk_strides, table_strides,
+                                 table_strides, stream)
+        if status != 0:
+            raise api.HipError(status, "rotary_fp32")
+
+    inputs, outputs = [q, k, cos, sin], [oq, ok]
+    host_inputs = [t.cpu().pin_memory() for t in inputs]
+    host_outputs = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in outputs]
+
+    def step_e2e():
+        for device_tensor, host_tensor in zip(inputs, host_inputs):
+            device_tensor.copy_(host_tensor, non_blocking=True)
+        step()
+        for host_tensor, device_tensor in zip(host_outputs, outputs):
+            host_tensor.copy_(device_tensor, non_blocking=True)
+
+    def timed(fn, steps):
+        marks = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for i in range(steps):
+            flush.fill_(float(i))
+            marks[i][0].record(stream)
+            fn()
+            marks[i][1].record(stream)
+        torch.cuda.synchronize(device)
+        return sum(a.elapsed_time(b) for a, b in marks) / 1e3
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(device)
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    sampler = ClockSampler(visible.split(",")[int(os.environ.get("LOCAL_RANK", 0))].strip() if visible else str(rank))
+    if rank == 0:
+        sampler.start()
+        time.sleep(0.3)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    seconds = timed(step, args.steps)
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop() if rank == 0 else None
+    for _ in range(max(1, args.warmup // 2)):
+        step_e2e()
+    e2e_steps = max(1, min(args.steps, 50))
+    e2e_seconds = timed(step_e2e, e2e_steps)
+    times = torch.tensor([seconds, e2e_seconds], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    seconds, e2e_seconds = times.tolist()
+
+    moved = 4.0 * batch * heads * length * 32 * 4  # q, k read; oq, ok written (RotaryBenchmarks.cpp:68)
+    touched = moved + 2.0 * batch * length * 32 * 4  # plus the two tables
+    peaks, peak_source = measured_peaks()
+    achieved = touched / (seconds / args.steps) / 1e9
+    line = {
+        "metric": "rotary GB/s (4 x elements x 4 B per step: q, k read, oq, ok written; RotaryBenchmarks.cpp:68)",
+        "value": world * moved * args.steps / seconds / 1e9, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": seconds / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1) from a seeded torch generator",
+        "config": workload_config(args.workload, world),
+        "e2e": {"value": world * moved * e2e_steps / e2e_seconds / 1e9, "unit": "GB/s",
+                "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in host_inputs),
+                "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in host_outputs), "steps": e2e_steps},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": float(peaks["hbm_gbs"]), "unit": "GB/s",
+                     "frac": achieved / float(peaks["hbm_gbs"]), "traffic": traffic_from_profiles("rotary"),
+                     "peak_source": f"{peak_source} hbm_gbs", "kernel": f"rotary_kernel<{'backward' if backward else 'forward'}>",
+                     "bytes": "q, k, oq, ok and both tables once"},
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = rotary_cpu_baseline(spec)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def run_reference_generic(args, spec: dict) -> None:
@@ -347,8 +491,12 @@ def main() -> None:
             os.close(saved_stdout)
 
     spec = WORKLOADS[args.workload]
+    if spec.get("kind") == "rotary":
+        run_rotary(args, spec, device, world, rank, dist)
+        return
     heads, seq, dim, radius, with_backward = spec["heads"], spec["seq"], spec["dim"], spec["radius"], spec["backward"]
     generic = spec.get("generic")  # None, or the generic forward's storage type
+    rotary = spec.get("rotary", False)
     storage = torch.float16 if generic == "fp16" else torch.float32
     if with_backward:
         if spec["batch"] % world:
@@ -369,6 +517,14 @@ def main() -> None:
     out = torch.empty_like(q)
     lse = torch.empty(batch, heads, seq, 2, device=device)
     inputs, outputs = [q, k, v, mask], [out, lse]
+    if rotary:
+        angle = torch.rand(batch, seq, 16, device=device, generator=generator) * 6.0
+        cos = torch.cat([torch.cos(angle)] * 2, dim=-1).contiguous()
+        sin = torch.cat([torch.sin(angle)] * 2, dim=-1).contiguous()
+        table_strides = api.Strides(seq * 32, 0, 32)
+        rotated_q = torch.empty(batch, seq, heads, 32, device=device)
+        rotated_k = torch.empty_like(rotated_q)
+        inputs += [cos, sin]
     if with_backward:
         upstream = torch.randn(batch, heads, seq, dim, device=device, generator=generator)
         gq, gk, gv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
@@ -388,6 +544,12 @@ def main() -> None:
     launches_per_step = 1 + (2 if with_backward else 0)
 
     def forward():
+        if rotary:
+            status = api.attention_fp32_forward_flash_rotary(q, k, v, cos, sin, mask, out, lse, batch, heads, seq, seq, radius,
+                                                             qs, ks, vs, table_strides, table_strides, os_, stream)
+            if status != 0:
+                raise api.HipError(status, "attention_fp32_forward_flash_rotary")
+            return
         if generic:
             status = api.attention_generic_forward(q, k, v, mask, out, lse, batch, heads, seq, seq, dim, radius, qs, ks, vs, os_,
                                                    api.DType.Float16 if generic == "fp16" else api.DType.Float32, stream)
@@ -403,6 +565,17 @@ def main() -> None:
             raise api.HipError(status, backward_fn.__name__)
 
     phases = [forward, backward] if with_backward else [forward]
+
+    def unfused_rotary_forward():
+        """rotary_fp32 into token-major buffers, then the flash forward on them (the unfused sequence)."""
+        rs = api.Strides(seq * heads * 32, 32, heads * 32)
+        status = api.rotary_fp32(q, k, cos, sin, rotated_q, rotated_k, batch, heads, seq, 0, qs, ks, table_strides, table_strides,
+                                 stream)
+        if status == 0:
+            status = api.attention_fp32_forward_flash(rotated_q, rotated_k, v, mask, out, lse, batch, heads, seq, seq, radius, rs, rs,
+                                                      vs, os_, stream)
+        if status != 0:
+            raise api.HipError(status, "rotary_fp32 + attention_fp32_forward_flash")
 
     # Host-buffer leg: pinned inputs copied in and outputs copied out every step.
     host_inputs = [t.cpu().pin_memory() for t in inputs]
@@ -457,10 +630,16 @@ def main() -> None:
     e2e_steps = max(1, min(args.steps, 50))
     e2e_seconds, _ = timed([step_e2e], e2e_steps)
 
-    times = torch.tensor([device_seconds, e2e_seconds] + part_seconds, device=device, dtype=torch.float64)
+    unfused_seconds = 0.0
+    if rotary:
+        for _ in range(args.warmup):
+            unfused_rotary_forward()
+        unfused_seconds, _ = timed([unfused_rotary_forward], args.steps)
+
+    times = torch.tensor([device_seconds, e2e_seconds, unfused_seconds] + part_seconds, device=device, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    device_seconds, e2e_seconds, *part_seconds = times.tolist()
+    device_seconds, e2e_seconds, unfused_seconds, *part_seconds = times.tolist()
 
     value = world * flops_per_step * args.steps / device_seconds / 1e12
     e2e_value = world * flops_per_step * e2e_steps / e2e_seconds / 1e12
@@ -485,7 +664,7 @@ def main() -> None:
             path = api.generic_kernel_name(batch, heads, seq, seq, dim,
                                            api.DType.Float16 if generic == "fp16" else api.DType.Float32)
         else:
-            path = api.flash_kernel_name(batch, heads, seq, seq, dim)
+            path = api.flash_kernel_name(batch, heads, seq, seq, dim) + ("+rotary" if rotary else "")
         if path.startswith("tcgen05"):
             peak = float(peaks["bf16_tflops"])
             roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
@@ -510,7 +689,7 @@ def main() -> None:
         "ms_per_step": device_seconds / args.steps * 1e3,
         "higher_is_better": True,
         "scaling": "strong" if with_backward else "weak",
-        "vs_baseline": None if with_backward or generic else value / PUBLISHED_TFLOPS,
+        "vs_baseline": None if with_backward or generic or rotary else value / PUBLISHED_TFLOPS,
         "dtype": generic or "f32",
         "data": "synthetic N(0,1) from a seeded torch generator (rank-dependent seed)",
         "config": workload_config(args.workload, world),
@@ -526,6 +705,10 @@ def main() -> None:
         line["parts"] = {"forward_ms": part_seconds[0] / args.steps * 1e3, "backward_ms": part_seconds[1] / args.steps * 1e3,
                          "forward_effective_tflops": world * effective_forward * args.steps / part_seconds[0] / 1e12,
                          "backward_effective_tflops": world * effective_backward * args.steps / part_seconds[1] / 1e12}
+    if rotary:
+        line["unfused"] = {"ms_per_step": unfused_seconds / args.steps * 1e3,
+                           "sequence": "rotary_fp32 (token-major outputs) then attention_fp32_forward_flash",
+                           "tflops": world * flops_per_step * args.steps / unfused_seconds / 1e12}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(spec)
     if rank == 0:

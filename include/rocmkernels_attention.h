@@ -192,6 +192,29 @@ ROCMKERNELS_C_EXPORT int attention_generic_forward(const void *q, const void *k,
         RocmKernelsStrides qs, RocmKernelsStrides ks, RocmKernelsStrides vs, RocmKernelsStrides os,
         RocmKernelsDType dtype, RocmKernelsStream stream);
 
+/* Rotary embedding of q and k for 32-wide heads. Replaces rotary_fp32 (Positional/Rotary.hpp:9-11;
+ * Rotary.hip:44-56): q, k, cos and sin are read at their strides (the tables' head stride is
+ * not used: cos/sin hold 32 values per (batch, token)); oq and ok are written token-major,
+ * packed [batch][length][heads][32]. Feature c rotates with feature c + 16:
+ * forward lo' = lo cos_lo - hi sin_lo, hi' = hi cos_hi + lo sin_hi; backward != 0 applies the
+ * transposed rotation (the gradient). Returns 1 for null pointers or non-positive sizes (and,
+ * beyond the reference, for batch * heads * length above 2^29 rows). */
+ROCMKERNELS_C_EXPORT int rotary_fp32(const float *q, const float *k, const float *cos, const float *sin, float *oq,
+        float *ok, int batch, int heads, int length, int backward, RocmKernelsStrides qs, RocmKernelsStrides ks,
+        RocmKernelsStrides cs, RocmKernelsStrides ss, RocmKernelsStream stream);
+
+/* Flash forward with the rotary prologue fused in (no reference counterpart): the result of
+ * rotary_fp32 (forward) on q and k followed by attention_fp32_forward_flash on the rotated
+ * tensors, bit for bit, without writing or reading the rotated tensors. cos/sin are
+ * [batch][token][32] at cs/ss (batch and token strides; rows 0 .. max(queries, keys) - 1 are
+ * read: query i and key j use row i and row j). Validation as attention_fp32_forward_flash plus
+ * null tables (error 1). Tensor-core kernel when q, k, v are TMA-addressable and the tables
+ * 16-byte aligned with strides of 4 floats, else the exact SIMT kernel with the same prologue. */
+ROCMKERNELS_C_EXPORT int attention_fp32_forward_flash_rotary(const float *q, const float *k, const float *v,
+        const float *cos, const float *sin, const bool *mask, float *output, float *lse, int batch, int heads, int queries,
+        int keys, int radius, RocmKernelsStrides qs, RocmKernelsStrides ks, RocmKernelsStrides vs, RocmKernelsStrides cs,
+        RocmKernelsStrides ss, RocmKernelsStrides os, RocmKernelsStream stream);
+
 /* Library build identification: a static string naming the architecture the kernels were
  * compiled for ("sm_100a") and the kernel families present. No counterpart in the reference. */
 ROCMKERNELS_C_EXPORT const char *rocmkernels_attention_build_info(void);

@@ -13,6 +13,9 @@
  * reference tree (oracle/Makefile, target `ref`), and against the committed golden vectors in
  * tests/golden/.
  *
+ * It also restates the reference's CPU rotary embedding `ReferenceRotary`
+ * (ROCmKernels.Tests/PositionalTests.cpp:18-50), pinned bit-for-bit the same way.
+ *
  * It also restates the reference's input generator (ROCmKernels.Tests/TestSupport.hpp:11-21:
  * std::mt19937 + std::uniform_real_distribution<float>) and the libstdc++ normal distribution
  * used for the synthetic benchmark inputs, so Python code can reproduce the reference's inputs.
@@ -302,4 +305,42 @@ int oracle_attention(const float *q, const float *k, const float *v, const uint8
                      float *grad_q, float *grad_k, float *grad_v, int threads) {
     return oracle_attention_slices(q, k, v, mask, upstream, head_width, batch, heads, queries, keys, radius, output, lse,
                                    grad_q, grad_k, grad_v, 0, batch * heads, threads, 0, 0);
+}
+
+/* ------------------------------------------------------------------------------------------ */
+/* Reference rotary embedding (ROCmKernels.Tests/PositionalTests.cpp:18-50), 32-wide heads.     */
+/* ------------------------------------------------------------------------------------------ */
+
+/*
+ * input/output: token-major [batch][length][heads][32]; cosine/sine: [batch][length][32].
+ * Each head's low half (columns 0-15) and high half (16-31) rotate as pairs (column c with
+ * c + 16): forward lo' = lo*cos_lo - hi*sin_lo, hi' = hi*cos_hi + lo*sin_hi (:42-44); backward
+ * (the transposed rotation) lo' = lo*cos_lo + hi*sin_hi, hi' = hi*cos_hi - lo*sin_lo (:39-41).
+ */
+void oracle_rotary(const float *input, const float *cosine, const float *sine, float *output, int batch, int heads,
+                   int length, int backward) {
+    enum { kHeadWidth = 32 };
+    for (int b = 0; b < batch; ++b) {
+        for (int token = 0; token < length; ++token) {
+            const size_t bufferBase = ((size_t)b * length + token) * kHeadWidth; /* :24 */
+            for (int head = 0; head < heads; ++head) {
+                const size_t base = ((size_t)b * length + token) * heads * kHeadWidth + (size_t)head * kHeadWidth;
+                for (int column = 0; column < kHeadWidth / 2; ++column) { /* :31-46 */
+                    const float low = input[base + column];
+                    const float high = input[base + column + 16];
+                    const float cosineLow = cosine[bufferBase + column];
+                    const float cosineHigh = cosine[bufferBase + column + 16];
+                    const float sineLow = sine[bufferBase + column];
+                    const float sineHigh = sine[bufferBase + column + 16];
+                    if (backward) {
+                        output[base + column] = low * cosineLow + high * sineHigh;
+                        output[base + column + 16] = high * cosineHigh - low * sineLow;
+                    } else {
+                        output[base + column] = low * cosineLow - high * sineLow;
+                        output[base + column + 16] = high * cosineHigh + low * sineHigh;
+                    }
+                }
+            }
+        }
+    }
 }

@@ -1,13 +1,15 @@
 // A minimal, from-scratch stand-in for the part of Catch2 v3's <catch2/catch_test_macros.hpp>
-// that the reference's attention tests use (TEST_CASE, SECTION, REQUIRE, CHECK, INFO). Catch2 is
-// not available offline; this header lets ROCmKernels.Tests/AttentionTests.cpp compile unchanged.
+// that the reference's attention, generic-attention and positional tests use (TEST_CASE, SECTION,
+// REQUIRE, CHECK, INFO). Catch2 is not available offline; this header lets those test files
+// (ROCmKernels.Tests/AttentionTests.cpp, Generic/AttentionGenericTests.cpp, PositionalTests.cpp)
+// compile unchanged.
 // TEST INFRASTRUCTURE: built only into the oracle/_ref test binary.
 //
-// Semantics kept from Catch2: a TEST_CASE body is run once per leaf SECTION; each run enters, at
-// every nesting level, the first section that is not complete yet and skips its siblings (a
-// section is complete once it has run without discovering unfinished child sections). CHECK
-// records a failure and continues; REQUIRE records a failure and leaves the current run; INFO
-// messages in scope are printed with a failure. Command line: `-c <section>` runs only the
+// Semantics kept from Catch2: a TEST_CASE body is run once per leaf SECTION (once if it has
+// none); each run enters, at every nesting level, the first section that is not complete yet and
+// skips its siblings (a section is complete once it has run without discovering unfinished
+// child sections). CHECK records a failure and continues; REQUIRE records a failure and leaves
+// the current run; INFO messages in scope are printed with a failure. Command line: `-c <section>` runs only the
 // sections of that name (and everything inside them), `-s` also prints INFO messages of passing
 // checks, `--list` lists test names.
 #pragma once
@@ -148,9 +150,10 @@ inline int run(int argc, char **argv) {
                 ++s.failed_checks;
                 std::printf("FAILED: '%s' section '%s' threw: %s\n", test.name, s.current.c_str(), error.what());
             }
-            if (!s.current.empty()) {
+            if (!s.current.empty() || s.children[""].empty()) {  // a leaf section, or a test case without sections
                 ++sections_run;
-                std::printf("%s: %s / %s\n", s.failed_checks == failed_before ? "PASS" : "FAIL", test.name, s.current.c_str());
+                std::printf("%s: %s%s%s\n", s.failed_checks == failed_before ? "PASS" : "FAIL", test.name,
+                            s.current.empty() ? "" : " / ", s.current.c_str());
             }
             bool finished = true;  // every top-level section complete (or none exists)
             for (const std::string &child : s.children[""]) finished = finished && s.completed.count(child) > 0;

@@ -26,6 +26,9 @@ REFERENCE_LIBRARY = ORACLE_DIR / "_ref" / "libref_attention.so"
 REFERENCE_TESTS = ORACLE_DIR / "_ref" / "attention_tests"
 REFERENCE_BENCH = ORACLE_DIR / "_ref" / "attention_bench"
 REFERENCE_GENERIC_TESTS = ORACLE_DIR / "_ref" / "generic_tests"
+REFERENCE_POSITIONAL_LIBRARY = ORACLE_DIR / "_ref" / "libref_positional.so"
+REFERENCE_POSITIONAL_TESTS = ORACLE_DIR / "_ref" / "positional_tests"
+REFERENCE_ROTARY_BENCH = ORACLE_DIR / "_ref" / "rotary_bench"
 REFERENCE_GENERIC_BENCH = ORACLE_DIR / "_ref" / "generic_bench"
 
 _F32 = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
@@ -55,6 +58,8 @@ def _load_oracle() -> ctypes.CDLL:
         lib.oracle_normal_fill.argtypes = [_F32, ctypes.c_size_t, ctypes.c_uint32, ctypes.c_float, ctypes.c_float]
         lib.oracle_mt19937_raw.argtypes = [_U32, ctypes.c_size_t, ctypes.c_uint32]
         lib.oracle_lengths.argtypes = [_I32, ctypes.c_int, ctypes.c_uint32, ctypes.c_int32, ctypes.c_int32]
+        lib.oracle_rotary.argtypes = [_F32, _F32, _F32, _F32] + [ctypes.c_int] * 4
+        lib.oracle_rotary.restype = None
         _oracle = lib
     return _oracle
 
@@ -143,6 +148,42 @@ def reference_attention(q, k, v, mask, upstream, radius: int = -1) -> dict:
 def reference_random_values(count: int, seed: int, low: float = -1.0, high: float = 1.0) -> np.ndarray:
     out = np.empty(count, dtype=np.float32)
     _load_reference().ref_random_values(out, count, seed, low, high)
+    return out
+
+
+def rotary(x, cos, sin, backward: bool = False) -> np.ndarray:
+    """The reference's ReferenceRotary (PositionalTests.cpp:18-50) restated in attention_oracle.c:
+    x token-major [B, L, H, 32], cos/sin [B, L, 32] float32; returns the rotated [B, L, H, 32]."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    cos, sin = (np.ascontiguousarray(t, dtype=np.float32) for t in (cos, sin))
+    B, L, H, W = x.shape
+    if W != 32 or cos.shape != (B, L, 32) or sin.shape != (B, L, 32):
+        raise ValueError("rotary expects x [B, L, H, 32] and tables [B, L, 32]")
+    out = np.empty_like(x)
+    _load_oracle().oracle_rotary(x, cos, sin, out, B, H, L, int(backward))
+    return out
+
+
+_positional = None
+
+
+def reference_positional_available() -> bool:
+    return REFERENCE_POSITIONAL_LIBRARY.exists()
+
+
+def reference_rotary(x, cos, sin, backward: bool = False) -> np.ndarray:
+    """The reference's own ReferenceRotary, compiled from its source (same contract as rotary())."""
+    global _positional
+    if _positional is None:
+        lib = ctypes.CDLL(str(REFERENCE_POSITIONAL_LIBRARY))
+        lib.ref_rotary.argtypes = [_F32, _F32, _F32, _F32] + [ctypes.c_int] * 4
+        lib.ref_rotary.restype = None
+        _positional = lib
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    cos, sin = (np.ascontiguousarray(t, dtype=np.float32) for t in (cos, sin))
+    B, L, H, _ = x.shape
+    out = np.empty_like(x)
+    _positional.ref_rotary(x, cos, sin, out, B, H, L, int(backward))
     return out
 
 

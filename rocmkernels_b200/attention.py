@@ -2,8 +2,8 @@
 
 The reference's host API is C++: ``extern "C"`` launchers plus namespaced wrappers that throw
 ``ROCmKernels::HipError`` (ROCmKernels.Kernels/include/ROCmKernels/Kernels/Attention/Attention.hpp:44-108,
-Attention64.hpp:19-32, Generic/AttentionGeneric.hpp:15-25). This module exposes both layers under
-the same names:
+Attention64.hpp:19-32, Generic/AttentionGeneric.hpp:15-25, Positional/Rotary.hpp:13-22). This
+module exposes both layers under the same names:
 
 * ``lib()`` returns the loaded library whose ``attention_fp32_*`` / ``attention64_fp32_*``
   functions return the raw status code (0 = success, 1 = invalid value, else a CUDA error);
@@ -74,6 +74,7 @@ _SIGNATURES = {
     "attention_fp32_query_profile": _BACKWARD_SELECT_ARGS,
     "attention_fp32_statistics": [_POINTER] * 4 + [_INT] * 5 + [Strides] * 2 + [_POINTER],
     "attention_generic_forward": [_POINTER] * 6 + [_INT] * 6 + [Strides] * 4 + [ctypes.c_ubyte, _POINTER],
+    "rotary_fp32": [_POINTER] * 6 + [_INT] * 4 + [Strides] * 4 + [_POINTER],
 }
 ENTRY_POINTS = tuple(_SIGNATURES)
 
@@ -102,6 +103,8 @@ def lib() -> ctypes.CDLL:
         library.rocmkernels_attention_device_status.restype = ctypes.c_uint
         library.attention_fp32_backward_static_delta.argtypes = [_POINTER] * 10 + [_INT] * 5 + [Strides] * 5 + [_POINTER]
         library.attention_fp32_backward_static_delta.restype = ctypes.c_int
+        library.attention_fp32_forward_flash_rotary.argtypes = [_POINTER] * 8 + [_INT] * 5 + [Strides] * 6 + [_POINTER]
+        library.attention_fp32_forward_flash_rotary.restype = ctypes.c_int
         _lib = library
     return _lib
 
@@ -265,6 +268,20 @@ def attention_generic_forward(q, k, v, mask, output, lse, batch, heads, queries,
                  keys, head_width, radius, strides(qs), strides(ks), strides(vs), strides(os_), int(dtype), _stream(stream))
 
 
+def rotary_fp32(q, k, cos, sin, oq, ok, batch, heads, length, backward, qs, ks, cs, ss, stream=None):
+    return _call("rotary_fp32", ptr(q), ptr(k), ptr(cos), ptr(sin), ptr(oq), ptr(ok), batch, heads, length, int(bool(backward)),
+                 strides(qs), strides(ks), strides(cs), strides(ss), _stream(stream))
+
+
+def attention_fp32_forward_flash_rotary(q, k, v, cos, sin, mask, output, lse, batch, heads, queries, keys, radius, qs, ks, vs, cs,
+                                        ss, os_, stream=None):
+    """Flash forward with the rotary prologue (no reference counterpart): rotary_fp32 forward on q
+    and k, then attention_fp32_forward_flash, in one kernel."""
+    return _call("attention_fp32_forward_flash_rotary", ptr(q), ptr(k), ptr(v), ptr(cos), ptr(sin), ptr(mask), ptr(output),
+                 ptr(lse), batch, heads, queries, keys, radius, strides(qs), strides(ks), strides(vs), strides(cs), strides(ss),
+                 strides(os_), _stream(stream))
+
+
 def _check(status: int, function: str) -> None:
     if status != SUCCESS:
         raise HipError(status, function)
@@ -333,3 +350,7 @@ def AttentionGenericForward(q, k, v, mask, output, lse, batch, heads, queries, k
                             stream=None):
     _check(attention_generic_forward(q, k, v, mask, output, lse, batch, heads, queries, keys, head_width, radius, qs, ks, vs, os_,
                                      dtype, stream), "attention_generic_forward")
+
+
+def Rotary(q, k, cos, sin, oq, ok, batch, heads, length, backward, qs, ks, cs, ss, stream=None):
+    _check(rotary_fp32(q, k, cos, sin, oq, ok, batch, heads, length, backward, qs, ks, cs, ss, stream), "rotary_fp32")

@@ -26,6 +26,7 @@ SOURCES = [
     "csrc/attention_tc.cu",
     "csrc/attention_tc_backward.cu",
     "csrc/copy.cu",
+    "csrc/rotary.cu",
     "csrc/device.cpp",
 ]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -75,12 +75,12 @@ unsigned blocks_for(int tokens, int tile, int heads, int batch) {
     return static_cast<unsigned>((tokens + tile - 1) / tile) * static_cast<unsigned>(heads) * static_cast<unsigned>(batch);
 }
 
-template <int D, bool STATS_ONLY, class T = float>
+template <int D, bool STATS_ONLY, class T = float, bool kRotary = false>
 int launch_simt_forward(const AttentionParams &p, cudaStream_t stream) {
     constexpr int bytes = rk::simt::ForwardSmem<D, STATS_ONLY>::bytes;
-    cudaError_t status = rk::prepare_kernel<rk::simt::forward_kernel<D, STATS_ONLY, T>>(bytes);
+    cudaError_t status = rk::prepare_kernel<rk::simt::forward_kernel<D, STATS_ONLY, T, kRotary>>(bytes);
     if (status != cudaSuccess) return status;
-    rk::simt::forward_kernel<D, STATS_ONLY, T>
+    rk::simt::forward_kernel<D, STATS_ONLY, T, kRotary>
             <<<blocks_for(p.queries, rk::simt::kBlockQ, p.heads, p.batch), rk::simt::kThreads, bytes, stream>>>(p);
     return cudaGetLastError();
 }
@@ -406,6 +406,27 @@ const char *rocmkernels_attention_flash_kernel(int batch, int heads, int queries
     p.o = rk::OutTensor{nullptr, p.q.sb, p.q.sh, p.q.st};
     if (rk::tc::flash_supported(p)) return rk::tc::kernel_name(head_width);
     return head_width == 64 ? "simt-fp32-forward-d64" : "simt-fp32-forward-d32";
+}
+
+int attention_fp32_forward_flash_rotary(const float *q, const float *k, const float *v, const float *cos, const float *sin,
+                                        const bool *mask, float *output, float *lse, int batch, int heads, int queries,
+                                        int keys, int radius, RocmKernelsStrides qs, RocmKernelsStrides ks,
+                                        RocmKernelsStrides vs, RocmKernelsStrides cs, RocmKernelsStrides ss,
+                                        RocmKernelsStrides os, RocmKernelsStream stream) {
+    if (forward_args_bad(q, k, v, mask, output, lse, batch, heads, queries, keys) || !cos || !sin || radius < -1)
+        return cudaErrorInvalidValue;
+    AttentionParams p = forward_params(32, q, k, v, mask, output, lse, batch, heads, queries, keys, radius, qs, ks, vs, os);
+    p.rot_cos = cos;
+    p.rot_sin = sin;
+    p.rot_cb = cs.batch;
+    p.rot_ct = cs.token;
+    p.rot_sb = ss.batch;
+    p.rot_st = ss.token;
+    if (rk::tc::flash_supported(p)) {  // else (tensors or tables not 16-byte addressable) the exact SIMT kernel
+        const int status = rk::tc::launch_flash_forward_rotary(p, stream);
+        if (status != rk::tc::kNotEligible) return status;
+    }
+    return launch_simt_forward<32, false, float, true>(p, stream);
 }
 
 int attention_generic_forward(const void *q, const void *k, const void *v, const bool *mask, void *output, float *lse,

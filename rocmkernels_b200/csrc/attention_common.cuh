@@ -51,6 +51,12 @@ struct AttentionParams {
     int vec4;                   // every strided row starts 4-element aligned (float4 / 4 x FP16 loads)
     int zero_nan_rows;          // a row whose exponent sum is NaN gives O = 0 and {-inf, 0} (the generic
                                 // forward's epilogue, AttentionGeneric.hip:119-128) instead of NaN
+    // Rotary prologue (forward kernels built with it): q and k rows are rotated by the tables of
+    // their (batch, token) before use; tables [batch][token][32] at these element strides.
+    const float *rot_cos, *rot_sin;
+    long long rot_cb, rot_ct, rot_sb, rot_st;
+    __device__ __forceinline__ const float *cos_row(int b, int t) const { return rot_cos + b * rot_cb + t * rot_ct; }
+    __device__ __forceinline__ const float *sin_row(int b, int t) const { return rot_sin + b * rot_sb + t * rot_st; }
 };
 
 // Four consecutive elements widened to FP32: one 16-byte load for FP32, one 8-byte load for FP16.

@@ -17,6 +17,7 @@
 #pragma once
 
 #include "attention_common.cuh"
+#include "rotary.cuh"
 
 namespace rk {
 namespace simt {
@@ -117,6 +118,26 @@ __device__ __forceinline__ void tile_accumulate(float (&out)[4][Shape<D>::featur
     }
 }
 
+// Rotary prologue on a staged [64][pitch] tile of 32-wide rows (rows row0.. of batch b; rows at
+// or past `limit` are zero and stay zero): features f and f + 16 rotate by the tables of their
+// token (rotate_pair, the rotary_fp32 forward), then everything is multiplied by `scale`.
+template <int D>
+__device__ __forceinline__ void rotate_tile(float *tile, int b, int row0, int limit, const AttentionParams &p, float scale) {
+    static_assert(D == 32, "the rotary embedding is defined for 32-wide heads");
+    constexpr int pitch = Shape<D>::pitch;
+    for (int index = threadIdx.x; index < 64 * 16; index += kThreads) {
+        const int r = index >> 4, f = index & 15;
+        const int row = row0 + r;
+        if (row >= limit) continue;
+        const float *c = p.cos_row(b, row), *sn = p.sin_row(b, row);
+        float lo, hi;
+        rotate_pair<false>(tile[r * pitch + f], tile[r * pitch + f + 16], __ldg(c + f), __ldg(c + f + 16), __ldg(sn + f),
+                           __ldg(sn + f + 16), lo, hi);
+        tile[r * pitch + f] = lo * scale;
+        tile[r * pitch + f + 16] = hi * scale;
+    }
+}
+
 __device__ __forceinline__ float half_warp_max(float value) {
 #pragma unroll
     for (int offset = 8; offset; offset >>= 1) value = fmaxf(value, __shfl_xor_sync(0xffffffffu, value, offset));
@@ -142,7 +163,8 @@ __device__ __forceinline__ void decode_block(int block, int blocks_per_head, int
 // (AttentionTile32.h:12-217) and attention64_query<false> (Attention64.hip:34-129); with T =
 // __half or D = 16 it is the exact-FP32 path of the generic forward (attention_generic_query and
 // attention_generic_query_half, AttentionGeneric.hip:36-237): FP16 storage is widened on load,
-// every product and sum is FP32, O is rounded to the storage type on the store.
+// every product and sum is FP32, O is rounded to the storage type on the store. kRotary: q and
+// k rows are rotated (rotary_fp32's forward, Rotary.hip:37-40) as they are staged.
 // ------------------------------------------------------------------------------------------
 template <int D, bool STATS_ONLY>
 struct ForwardSmem {
@@ -150,7 +172,7 @@ struct ForwardSmem {
     static constexpr int bytes = floats * 4;
 };
 
-template <int D, bool STATS_ONLY, class T = float>
+template <int D, bool STATS_ONLY, class T = float, bool kRotary = false>
 __global__ void __launch_bounds__(kThreads) forward_kernel(AttentionParams p) {
     extern __shared__ float4 shared_raw[];
     float *Qs = reinterpret_cast<float *>(shared_raw);
@@ -167,7 +189,11 @@ __global__ void __launch_bounds__(kThreads) forward_kernel(AttentionParams p) {
     const int q0 = tile * kBlockQ;
     const unsigned char *mask = p.mask + (long long)b * p.keys;
 
-    load_rows<D, kBlockQ>(Qs, p.q.row_as<T>(b, h, 0), p.q.st, q0, p.queries, p.scale, p.vec4, nullptr);
+    load_rows<D, kBlockQ>(Qs, p.q.row_as<T>(b, h, 0), p.q.st, q0, p.queries, kRotary ? 1.f : p.scale, p.vec4, nullptr);
+    if constexpr (kRotary) {
+        __syncthreads();
+        rotate_tile<D>(Qs, b, q0, p.queries, p, p.scale);
+    }
 
     float m[4], l[4], o[4][F];
 #pragma unroll
@@ -192,6 +218,10 @@ __global__ void __launch_bounds__(kThreads) forward_kernel(AttentionParams p) {
         load_rows<D, kBlockK>(Ks, p.k.row_as<T>(b, h, 0), p.k.st, k0, last, 1.f, p.vec4, flags);
         if constexpr (!STATS_ONLY) load_rows<D, kBlockK>(Vs, p.v.row_as<T>(b, h, 0), p.v.st, k0, last, 1.f, p.vec4, flags);
         __syncthreads();
+        if constexpr (kRotary) {
+            rotate_tile<D>(Ks, b, k0, last, p, 1.f);
+            __syncthreads();
+        }
 
         float s[4][4] = {};
         tile_dot<D>(s, Qs, Ks, ty, tx);

@@ -51,7 +51,9 @@
 #include <cudaTypedefs.h>
 
 #include <mutex>
+#include <type_traits>
 
+#include "rotary.cuh"
 #include "tc_operands.cuh"
 
 namespace rk {
@@ -146,10 +148,19 @@ struct alignas(1024) SharedStorage {
     uint32_t tmem_base;
 };
 
+// The rotary prologue's extra operands: per stage, the cos and sin rows of the tile's 64 keys as
+// TMA lands them (64 rows x 32 FP32, 128B swizzle, the layout of one K box).
+template <int D>
+struct alignas(1024) RotaryStorage : SharedStorage<D, false> {
+    alignas(1024) float cos_raw[Forward<D, false>::kStages][kBoxFloats];
+    alignas(1024) float sin_raw[Forward<D, false>::kStages][kBoxFloats];
+};
+
 struct FlashArgs {
     AttentionParams p;
     int cta_per_head;  // ceil(queries / queries per CTA)
     int vec_out;       // output rows 16-byte addressable
+    int rot_batch;     // rotary tables: 1 = one table per sequence (batch coordinate b), 0 = one shared table
 };
 
 __device__ __forceinline__ uint32_t tmem_lane_address(uint32_t base, int warp) {
@@ -344,16 +355,37 @@ __device__ __forceinline__ void transpose_values(const float *v_raw, uint32_t *v
     }
 }
 
+// Rotary prologue of a 32-wide FP32 row held as 8 float4 (features 4c..4c+3 in x[c]): features f
+// and f + 16 rotate by the row's tables cs, sn (same layout; rotate_pair, the rotary_fp32 forward).
+__device__ __forceinline__ void rotate_row32(float4 (&x)[8], const float4 (&cs)[8], const float4 (&sn)[8]) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const float4 cl = cs[c], ch = cs[c + 4], sl = sn[c], sh = sn[c + 4];
+        float4 &lo = x[c], &hi = x[c + 4];
+        rotate_pair<false>(lo.x, hi.x, cl.x, ch.x, sl.x, sh.x, lo.x, hi.x);
+        rotate_pair<false>(lo.y, hi.y, cl.y, ch.y, sl.y, sh.y, lo.y, hi.y);
+        rotate_pair<false>(lo.z, hi.z, cl.z, ch.z, sl.z, sh.z, lo.z, hi.z);
+        rotate_pair<false>(lo.w, hi.w, cl.w, ch.w, sl.w, sh.w, lo.w, hi.w);
+    }
+}
+
 // kWidth: the tensors' head width when it is below the kernel's D (FP32 storage with 16 features
 // on the D = 32 kernel): the tensor maps are kWidth wide, so the TMA fills features kWidth..D-1
 // of K and V with zeros, Q rows are read and O rows written kWidth wide.
-template <int D, bool kHalf, int kWidth = D>
+// kRotary (D = 32, FP32): the rotary prologue — each Q row (softmax threads) and each K row (split
+// warps) is rotated by its token's tables before it is scaled and split, so the rotated tensors
+// never go through HBM; the result equals rotary_fp32 followed by this kernel bit for bit.
+// With kRotary the producer also lands the tile's cos and sin rows (tmap_cos, tmap_sin) in the
+// stage; the other instantiations ignore those two maps.
+template <int D, bool kHalf, int kWidth = D, bool kRotary = false>
 __global__ void __launch_bounds__(Forward<D, kHalf>::kThreads, 1)
         flash_forward_kernel(const FlashArgs args, const __grid_constant__ CUtensorMap tmap_k,
-                             const __grid_constant__ CUtensorMap tmap_v) {
+                             const __grid_constant__ CUtensorMap tmap_v, const __grid_constant__ CUtensorMap tmap_cos,
+                             const __grid_constant__ CUtensorMap tmap_sin) {
     static_assert(kWidth == D || (!kHalf && kWidth % 4 == 0 && kWidth < D), "narrow rows: FP32 storage only");
+    static_assert(!kRotary || (D == 32 && kWidth == 32 && !kHalf), "the rotary prologue is defined for 32-wide FP32 heads");
     using F = Forward<D, kHalf>;
-    using Storage = SharedStorage<D, kHalf>;
+    using Storage = std::conditional_t<kRotary, RotaryStorage<D>, SharedStorage<D, kHalf>>;
     constexpr int kStages = F::kStages;
     extern __shared__ uint8_t shared_raw[];
     Storage &s = *reinterpret_cast<Storage *>((reinterpret_cast<uintptr_t>(shared_raw) + 1023) & ~uintptr_t(1023));
@@ -370,6 +402,31 @@ __global__ void __launch_bounds__(Forward<D, kHalf>::kThreads, 1)
     int first, last;
     key_window(q0, min(q0 + F::kCtaQueries, p.queries), p.keys, p.radius, first, last);
     const int tiles = last > first ? (last - first + kKeyTile - 1) / kKeyTile : 0;
+
+    // The softmax threads issue the loads of their Q row (and, with the rotary prologue, of its
+    // table rows) before the set-up barrier, so their latency overlaps the TMEM allocation and
+    // the barrier initialisation.
+    constexpr int kQChunks = kHalf ? D / 8 : D / 4;  // 16-byte chunks of a Q row
+    uint4 q_chunks[kQChunks];
+    float4 q_cos[kRotary ? 8 : 1], q_sin[kRotary ? 8 : 1];
+    const int query = q0 + (warp >> 2) * kQTile + (threadIdx.x & (kQTile - 1));  // softmax threads' row
+    const bool row_valid = warp < F::kSoftmaxWarps && query < p.queries;
+    {
+        const uint4 *src = kHalf ? reinterpret_cast<const uint4 *>(p.q.row_as<__half>(b, h, row_valid ? query : 0))
+                                 : reinterpret_cast<const uint4 *>(p.q.row(b, h, row_valid ? query : 0));
+#pragma unroll
+        for (int c = 0; c < kQChunks; ++c)
+            q_chunks[c] = row_valid && (kHalf || c < kWidth / 4) ? __ldg(src + c) : make_uint4(0u, 0u, 0u, 0u);
+        if constexpr (kRotary) {
+            const float4 *c4 = reinterpret_cast<const float4 *>(p.cos_row(b, row_valid ? query : 0));
+            const float4 *s4 = reinterpret_cast<const float4 *>(p.sin_row(b, row_valid ? query : 0));
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                q_cos[c] = row_valid ? __ldg(c4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+                q_sin[c] = row_valid ? __ldg(s4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+    }
 
     if (warp == 0) {
         tmem_alloc(&s.tmem_base, F::kTmemColumns);
@@ -412,7 +469,12 @@ __global__ void __launch_bounds__(Forward<D, kHalf>::kThreads, 1)
                 if (j >= kStages) ok = mbar_wait(&s.kv_empty[stage], (use - 1) & 1);
                 if (!ok) break;
                 RK_TRACE(j, 12);
-                mbar_arrive_expect_tx(&s.kv_full[stage], 2 * F::kBoxes * kBoxBytes);
+                mbar_arrive_expect_tx(&s.kv_full[stage], (2 * F::kBoxes + (kRotary ? 2 : 0)) * kBoxBytes);
+                if constexpr (kRotary) {
+                    const int table = b * args.rot_batch;
+                    tma_load_4d(s.cos_raw[stage], &tmap_cos, &s.kv_full[stage], 0, first + j * kKeyTile, 0, table);
+                    tma_load_4d(s.sin_raw[stage], &tmap_sin, &s.kv_full[stage], 0, first + j * kKeyTile, 0, table);
+                }
 #pragma unroll
                 for (int box = 0; box < F::kBoxes; ++box) {
                     tma_load_4d(s.k_raw[stage] + box * kBoxFloats, &tmap_k, &s.kv_full[stage], 32 * box, first + j * kKeyTile, h, b);
@@ -519,8 +581,21 @@ __global__ void __launch_bounds__(Forward<D, kHalf>::kThreads, 1)
             for (int c = 0; c < D / 4; ++c) {
                 kx[c] = raw_chunk<D>(s.k_raw[stage], row, c);
                 if (!keep_row) kx[c] = make_float4(0.f, 0.f, 0.f, 0.f);
-                kmax = max3(kmax, fmaxf(fabsf(kx[c].x), fabsf(kx[c].y)), fmaxf(fabsf(kx[c].z), fabsf(kx[c].w)));
             }
+            if constexpr (kRotary) {
+                if (keep_row) {
+                    float4 cs[8], sn[8];
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        cs[c] = raw_chunk<32>(s.cos_raw[stage], row, c);
+                        sn[c] = raw_chunk<32>(s.sin_raw[stage], row, c);
+                    }
+                    rotate_row32(kx, cs, sn);
+                }
+            }
+#pragma unroll
+            for (int c = 0; c < D / 4; ++c)
+                kmax = max3(kmax, fmaxf(fabsf(kx[c].x), fabsf(kx[c].y)), fmaxf(fabsf(kx[c].z), fabsf(kx[c].w)));
 #pragma unroll
             for (int item = 0; item < D / 32; ++item) {
                 const int index = 64 * item + row;  // 0 .. 2D - 1
@@ -595,18 +670,16 @@ __global__ void __launch_bounds__(Forward<D, kHalf>::kThreads, 1)
         // ---------------------------------------------------------------- softmax / epilogue
         const int tile = warp >> 2;  // Q tile (0 = A, 1 = B)
         const int row_in_tile = threadIdx.x & (kQTile - 1);
-        const int query = q0 + tile * kQTile + row_in_tile;
-        const bool row_valid = query < p.queries;
+        // query and row_valid: this thread's row, computed with the Q prefetch above
         const uint32_t lane_base = tmem_lane_address(tmem, warp) + tile * F::kColTile;
         const bool tracer = row_in_tile == 0;
 
         int q_exponent = 0;
         if constexpr (kHalf) {  // Q row as FP16 pairs in TMEM, unscaled
-            const uint4 *q8 = reinterpret_cast<const uint4 *>(p.q.row_as<__half>(b, h, row_valid ? query : 0));
             float packed[D / 2];
 #pragma unroll
             for (int c = 0; c < D / 8; ++c) {
-                const uint4 v = row_valid ? __ldg(q8 + c) : make_uint4(0u, 0u, 0u, 0u);
+                const uint4 v = q_chunks[c];
                 packed[4 * c] = __uint_as_float(v.x);
                 packed[4 * c + 1] = __uint_as_float(v.y);
                 packed[4 * c + 2] = __uint_as_float(v.z);
@@ -624,15 +697,21 @@ __global__ void __launch_bounds__(Forward<D, kHalf>::kThreads, 1)
             mbar_arrive(&s.q_ready);
         } else {  // Q row -> scaled by 1/sqrt(D) and 2^q_exponent, split into FP16 q0/q1 pairs in TMEM
             float x[D];
-            const float4 *q4 = reinterpret_cast<const float4 *>(p.q.row(b, h, row_valid ? query : 0));
+            float4 raw[D / 4];
+#pragma unroll
+            for (int c = 0; c < D / 4; ++c)
+                raw[c] = make_float4(__uint_as_float(q_chunks[c].x), __uint_as_float(q_chunks[c].y),
+                                     __uint_as_float(q_chunks[c].z), __uint_as_float(q_chunks[c].w));
+            if constexpr (kRotary) {
+                if (row_valid) rotate_row32(raw, q_cos, q_sin);
+            }
             float qmax = 0.f;
 #pragma unroll
             for (int c = 0; c < D / 4; ++c) {
-                const float4 v = row_valid && c < kWidth / 4 ? __ldg(q4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-                x[4 * c] = v.x * p.scale;
-                x[4 * c + 1] = v.y * p.scale;
-                x[4 * c + 2] = v.z * p.scale;
-                x[4 * c + 3] = v.w * p.scale;
+                x[4 * c] = raw[c].x * p.scale;
+                x[4 * c + 1] = raw[c].y * p.scale;
+                x[4 * c + 2] = raw[c].z * p.scale;
+                x[4 * c + 3] = raw[c].w * p.scale;
 #pragma unroll
                 for (int e = 0; e < 4; ++e) qmax = fmaxf(qmax, fabsf(x[4 * c + e]));
             }
@@ -821,9 +900,12 @@ bool positive_tma_strides(const Tensor &t, int per16) {
            t.sh < limit && t.sb < limit && (reinterpret_cast<uintptr_t>(t.data) & 15u) == 0;
 }
 
-template <int D, bool kHalf>
+template <int D, bool kHalf, bool kRotary = false>
 constexpr int shared_bytes() {
-    return static_cast<int>(sizeof(SharedStorage<D, kHalf>)) + 1024;
+    if constexpr (kRotary)
+        return static_cast<int>(sizeof(RotaryStorage<D>)) + 1024;
+    else
+        return static_cast<int>(sizeof(SharedStorage<D, kHalf>)) + 1024;
 }
 template <int D, bool kHalf>
 constexpr bool layout_ok() {
@@ -837,24 +919,50 @@ constexpr bool layout_ok() {
 static_assert(layout_ok<32, false>() && layout_ok<64, false>() && layout_ok<16, true>() && layout_ok<32, true>() &&
                       layout_ok<64, true>(),
               "operand tiles, TMEM columns and shared memory budget");
+static_assert(shared_bytes<32, false, true>() <= 227 * 1024, "rotary tables fit beside the d = 32 stages");
 
-template <int D, bool kHalf, int kWidth = D>
+// Rotary table [batch][rows][32] FP32 (token stride st, batch stride sb, 0 = one table for every
+// sequence) as a 4-D map {32, rows, 1, batch} with the K boxes' shape: box = 32 features x 64 rows.
+bool make_table_map(CUtensorMap *map, const float *table, long long sb, long long st, int rows, int batch) {
+    auto encode = encode_function();
+    if (encode == nullptr || st <= 0 || sb < 0) return false;
+    const cuuint64_t dims[4] = {32, static_cast<cuuint64_t>(rows), 1, static_cast<cuuint64_t>(sb > 0 ? batch : 1)};
+    const cuuint64_t row_bytes = static_cast<cuuint64_t>(st) * 4;
+    const cuuint64_t strides[3] = {row_bytes, row_bytes * static_cast<cuuint64_t>(rows),
+                                   sb > 0 ? static_cast<cuuint64_t>(sb) * 4 : row_bytes * static_cast<cuuint64_t>(rows)};
+    const cuuint32_t box[4] = {32, static_cast<cuuint32_t>(kKeyTile), 1, 1};
+    const cuuint32_t element_strides[4] = {1, 1, 1, 1};
+    return encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float *>(table), dims, strides, box, element_strides,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int D, bool kHalf, int kWidth = D, bool kRotary = false>
 int launch(const AttentionParams &p, cudaStream_t stream) {
     using F = Forward<D, kHalf>;
     CUtensorMap tmap_k, tmap_v;
     if (!make_tensor_map(&tmap_k, p.k, kWidth, p.batch, p.heads, p.keys, kHalf) ||
         !make_tensor_map(&tmap_v, p.v, kWidth, p.batch, p.heads, p.keys, kHalf))
         return kNotEligible;
-    cudaError_t status = prepare_kernel<flash_forward_kernel<D, kHalf, kWidth>>(shared_bytes<D, kHalf>());
+    CUtensorMap tmap_cos = tmap_k, tmap_sin = tmap_k;
+    if constexpr (kRotary) {
+        const int rows = max(p.queries, p.keys);
+        if (!make_table_map(&tmap_cos, p.rot_cos, p.rot_cb, p.rot_ct, rows, p.batch) ||
+            !make_table_map(&tmap_sin, p.rot_sin, p.rot_sb, p.rot_st, rows, p.batch) || (p.rot_cb > 0) != (p.rot_sb > 0))
+            return kNotEligible;
+    }
+    constexpr int bytes = shared_bytes<D, kHalf, kRotary>();
+    cudaError_t status = prepare_kernel<flash_forward_kernel<D, kHalf, kWidth, kRotary>>(bytes);
     if (status != cudaSuccess) return status;
     constexpr int per16 = kHalf ? 8 : 4;
     FlashArgs args{};
     args.p = p;
+    args.rot_batch = p.rot_cb > 0 ? 1 : 0;
     args.cta_per_head = (p.queries + F::kCtaQueries - 1) / F::kCtaQueries;
     args.vec_out = (reinterpret_cast<uintptr_t>(p.o.data) & 15u) == 0 && p.o.sb % per16 == 0 && p.o.sh % per16 == 0 &&
                    p.o.st % per16 == 0;
     const unsigned blocks = static_cast<unsigned>(args.cta_per_head) * static_cast<unsigned>(p.heads) * static_cast<unsigned>(p.batch);
-    flash_forward_kernel<D, kHalf, kWidth><<<blocks, F::kThreads, shared_bytes<D, kHalf>(), stream>>>(args, tmap_k, tmap_v);
+    flash_forward_kernel<D, kHalf, kWidth, kRotary><<<blocks, F::kThreads, bytes, stream>>>(args, tmap_k, tmap_v, tmap_cos, tmap_sin);
     return cudaGetLastError();
 }
 
@@ -870,6 +978,14 @@ int launch_flash_forward(const AttentionParams &p, int head_width, cudaStream_t 
     if (head_width == 32) return launch<32, false>(p, stream);
     if (head_width == 64) return launch<64, false>(p, stream);
     return kNotEligible;
+}
+
+int launch_flash_forward_rotary(const AttentionParams &p, cudaStream_t stream) {
+    const auto aligned = [](const float *t, long long sb, long long st) {
+        return (reinterpret_cast<uintptr_t>(t) & 15u) == 0 && sb % 4 == 0 && st % 4 == 0;
+    };
+    if (!aligned(p.rot_cos, p.rot_cb, p.rot_ct) || !aligned(p.rot_sin, p.rot_sb, p.rot_st)) return kNotEligible;
+    return launch<32, false, 32, true>(p, stream);
 }
 
 bool half_flash_supported(const AttentionParams &p) {

@@ -16,6 +16,9 @@ bool flash_supported(const AttentionParams &p);
 // Launches the tensor-core flash forward for head width 32 or 64 (16: the 32-wide kernel over
 // zero-filled features 16-31); returns a cudaError_t value or kNotEligible.
 int launch_flash_forward(const AttentionParams &p, int head_width, cudaStream_t stream);
+// The flash forward for head width 32 with the rotary prologue (q and k rotated by the tables in
+// p.rot_*, which must be 16-byte aligned with strides of 4 floats); cudaError_t or kNotEligible.
+int launch_flash_forward_rotary(const AttentionParams &p, cudaStream_t stream);
 // True when the FP16-storage tensor-core forward accepts the tensors (TMA-addressable K and V,
 // 16-byte addressable Q rows).
 bool half_flash_supported(const AttentionParams &p);

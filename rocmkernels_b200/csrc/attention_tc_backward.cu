@@ -60,7 +60,6 @@ struct Geometry {
     static constexpr int kRawFloats = kBoxes * kBoxFloats;   // FP32 tile: kBoxes boxes of 64 x 32
     static constexpr int kRowWords = 64 * D;                // row layout: 64 rows x [x0 | x1] (2 D fp16 each)
     static constexpr int kTWords = 2 * D * 32;              // transposed: 2 D rows x 64 fp16
-    static constexpr int kKSteps = D / 16;                  // K=16 steps over the features
     // Row layout: D = 32 keeps [x0 | x1] in one 128-byte row; D = 64 uses an x0 tile and an x1
     // tile of 64 rows x 128 bytes each. Descriptor offset (16-byte units) of the x1 part.
     static constexpr uint64_t kDescX1 = row_x1_offset<D>();

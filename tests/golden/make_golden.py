@@ -12,6 +12,11 @@ sections of AttentionTests.cpp:272-286 (seeds 101-104, U(-1,1), mask[3] = 0). Th
 cases add what those sections do not cover: Q != K with a radius, a fully masked sequence, and
 a 64-wide masked radius case.
 
+The ``rotary_*`` cases pin the rotary oracle: inputs from ``RandomValues`` (q, k in [-2, 2),
+cos, sin in [-1, 1)) and outputs from the reference's ``ReferenceRotary``
+(ROCmKernels.Tests/PositionalTests.cpp:18-50, compiled in place into
+oracle/_ref/libref_positional.so); ``rotary_reference_*`` are that file's two test cases (:53-141).
+
 ``normal_pin.npz`` holds the first values of std::normal_distribution<float>(0, 1) over
 std::mt19937(seed). They come from a small C++ program compiled with g++, and pin the
 oracle's restatement of the libstdc++ normal distribution used for the benchmark inputs.
@@ -44,6 +49,14 @@ CASES = {
     "extra_radius_masked_d64": (64, 2, 2, 37, 29, 3, False, (1,)),
 }
 
+# name: (batch, heads, length, backward, seeds of q, k, cos, sin)
+ROTARY_CASES = {
+    "rotary_reference_forward": (2, 3, 4, False, (21, 22, 23, 24)),   # PositionalTests.cpp:53-96
+    "rotary_reference_backward": (1, 2, 3, True, (31, 32, 33, 34)),   # :98-141
+    "rotary_extra_forward": (3, 5, 37, False, (41, 42, 43, 44)),
+    "rotary_extra_backward": (2, 4, 29, True, (51, 52, 53, 54)),
+}
+
 NORMAL_SOURCE = r"""
 #include <cstdio>
 #include <cstdlib>
@@ -74,6 +87,16 @@ def make_case(head_width, batch, heads, queries, keys, radius, upstream_zero, ma
     return dict(q=q, k=k, v=v, upstream=upstream, mask=mask, radius=np.int32(radius), **expected)
 
 
+def make_rotary_case(batch, heads, length, backward, seeds):
+    elements, table = batch * heads * length * 32, batch * length * 32
+    q = oracle.reference_random_values(elements, seeds[0], -2.0, 2.0).reshape(batch, length, heads, 32)
+    k = oracle.reference_random_values(elements, seeds[1], -2.0, 2.0).reshape(batch, length, heads, 32)
+    cos = oracle.reference_random_values(table, seeds[2], -1.0, 1.0).reshape(batch, length, 32)
+    sin = oracle.reference_random_values(table, seeds[3], -1.0, 1.0).reshape(batch, length, 32)
+    return dict(q=q, k=k, cos=cos, sin=sin, backward=np.int32(backward), seeds=np.int32(seeds),
+                out_q=oracle.reference_rotary(q, cos, sin, backward), out_k=oracle.reference_rotary(k, cos, sin, backward))
+
+
 def normal_pin(seed: int, count: int) -> np.ndarray:
     with tempfile.TemporaryDirectory() as tmp:
         source = Path(tmp) / "normal.cpp"
@@ -92,6 +115,11 @@ def main() -> None:
         print("wrote", name)
     np.savez_compressed(HERE / "normal_pin.npz", seed101=normal_pin(101, 4096), seed105=normal_pin(105, 4096))
     print("wrote normal_pin")
+    if not oracle.reference_positional_available():
+        raise SystemExit("oracle/_ref/libref_positional.so is missing: run `make -C oracle ref` where the reference exists")
+    for name, spec in ROTARY_CASES.items():
+        np.savez_compressed(HERE / f"{name}.npz", **make_rotary_case(*spec))
+        print("wrote", name)
 
 
 if __name__ == "__main__":

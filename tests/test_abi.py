@@ -46,7 +46,7 @@ def test_reference_entry_points_all_declared():
         "attention_fp32_statistics", "attention_fp32_forward_tuned", "attention_fp32_forward_flash",
         "attention_fp32_forward_flash_tuned", "attention_fp32_backward_tuned", "attention64_fp32_forward",
         "attention64_fp32_backward", "attention_fp32_backward_profile", "attention_fp32_query_profile",
-        "attention_generic_forward",
+        "attention_generic_forward", "rotary_fp32",
     }
     assert reference_names <= set(declared_functions())
     assert reference_names == set(api.ENTRY_POINTS)
@@ -156,3 +156,29 @@ def test_generic_dispatch_names(head_width):
     assert api.generic_kernel_name(2, 8, 512, 512, head_width, api.DType.Float16) == f"tcgen05-f16-flash-d{head_width}"
     assert api.generic_kernel_name(2, 8, 512, 512, head_width, api.DType.Float32) == f"tcgen05-f16x2-flash-d{head_width}"
     assert api.generic_kernel_name(1, 1, 4, 4, 24, api.DType.Float16) == "unsupported"
+
+
+@pytest.mark.parametrize("null_index", range(6))
+def test_rotary_rejects_null_pointers(null_index):
+    # Rotary.hip:47-48: any null pointer, non-positive batch, heads or length
+    pointers = [1] * 6
+    pointers[null_index] = None
+    assert api.rotary_fp32(*pointers, 1, 1, 1, 0, S, S, S, S) == api.INVALID_VALUE
+
+
+@pytest.mark.parametrize("sizes", [(0, 1, 1), (1, 0, 1), (1, 1, 0), (-1, 2, 2)])
+def test_rotary_rejects_sizes(sizes):
+    assert api.rotary_fp32(1, 1, 1, 1, 1, 1, *sizes, 1, S, S, S, S) == api.INVALID_VALUE
+    with pytest.raises(api.HipError):
+        api.Rotary(1, 1, 1, 1, 1, 1, *sizes, True, S, S, S, S)
+
+
+@pytest.mark.parametrize("null_index", range(8))
+def test_fused_rotary_flash_rejects_null_pointers(null_index):
+    pointers = [1] * 8  # q, k, v, cos, sin, mask, output, lse
+    pointers[null_index] = None
+    assert api.attention_fp32_forward_flash_rotary(*pointers, 1, 1, 4, 4, -1, S, S, S, S, S, S) == api.INVALID_VALUE
+
+
+def test_fused_rotary_flash_rejects_radius():
+    assert api.attention_fp32_forward_flash_rotary(*[1] * 8, 1, 1, 4, 4, -2, S, S, S, S, S, S) == api.INVALID_VALUE

@@ -9,7 +9,8 @@ import pytest
 from oracle import oracle
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
-CASES = sorted(p.stem for p in GOLDEN.glob("*.npz") if p.stem != "normal_pin")
+CASES = sorted(p.stem for p in GOLDEN.glob("*.npz") if p.stem != "normal_pin" and not p.stem.startswith("rotary_"))
+ROTARY_CASES = sorted(p.stem for p in GOLDEN.glob("rotary_*.npz"))
 
 
 def bits(array):
@@ -104,3 +105,46 @@ def test_oracle_matches_compiled_reference(shape):
     theirs = oracle.reference_attention(q, k, v, mask, u, radius)
     for key in mine:
         assert np.array_equal(bits(mine[key]), bits(theirs[key])), key
+
+
+def test_rotary_golden_cases_present():
+    assert len(ROTARY_CASES) == 4
+
+
+@pytest.mark.parametrize("name", ROTARY_CASES)
+def test_rotary_oracle_matches_golden_bit_exact(name):
+    case = np.load(GOLDEN / f"{name}.npz")
+    backward = bool(case["backward"])
+    for x, expected in (("q", "out_q"), ("k", "out_k")):
+        got = oracle.rotary(case[x], case["cos"], case["sin"], backward)
+        assert np.array_equal(bits(got), bits(case[expected])), f"{name}: {x}"
+
+
+@pytest.mark.parametrize("name", ROTARY_CASES)
+def test_rotary_generator_reproduces_reference_inputs(name):
+    case = np.load(GOLDEN / f"{name}.npz")
+    seeds = [int(x) for x in case["seeds"]]
+    for key, seed, (low, high) in zip(("q", "k", "cos", "sin"), seeds, ((-2.0, 2.0), (-2.0, 2.0), (-1.0, 1.0), (-1.0, 1.0))):
+        expected = case[key].ravel()
+        assert np.array_equal(bits(oracle.uniform(expected.size, seed, low, high)), bits(expected)), key
+
+
+def test_rotary_backward_is_the_transpose():
+    """backward(forward(x)) = x (cos^2 + sin^2) per pair when cos_lo = cos_hi and sin_lo = sin_hi."""
+    x = oracle.uniform(2 * 7 * 3 * 32, 61, -2, 2).reshape(2, 7, 3, 32)
+    angle = oracle.uniform(2 * 7 * 16, 62, -3, 3).reshape(2, 7, 16).astype(np.float64)
+    cos = np.concatenate([np.cos(angle)] * 2, axis=-1).astype(np.float32)
+    sin = np.concatenate([np.sin(angle)] * 2, axis=-1).astype(np.float32)
+    back = oracle.rotary(oracle.rotary(x, cos, sin, False), cos, sin, True)
+    assert np.max(np.abs(back - x)) < 1e-5
+
+
+@pytest.mark.skipif(not oracle.reference_positional_available(), reason="reference not compiled here (oracle/_ref absent)")
+@pytest.mark.parametrize("shape", [(1, 1, 1), (2, 12, 64), (4, 3, 129)])
+@pytest.mark.parametrize("backward", [False, True])
+def test_rotary_oracle_matches_compiled_reference(shape, backward):
+    B, H, L = shape
+    x = oracle.uniform(B * L * H * 32, 71, -3, 3).reshape(B, L, H, 32)
+    cos = oracle.uniform(B * L * 32, 72).reshape(B, L, 32)
+    sin = oracle.uniform(B * L * 32, 73).reshape(B, L, 32)
+    assert np.array_equal(bits(oracle.rotary(x, cos, sin, backward)), bits(oracle.reference_rotary(x, cos, sin, backward)))

@@ -31,3 +31,14 @@ def test_reference_generic_tests_pass(cuda):
     print(result.stdout)
     assert result.returncode == 0, result.stdout + result.stderr
     assert result.stdout.count("PASS:") == 6
+
+
+@pytest.mark.skipif(not oracle.REFERENCE_POSITIONAL_TESTS.exists(),
+                    reason="reference positional test binary not built (needs the reference tree)")
+def test_reference_positional_tests_pass(cuda):
+    """ROCmKernels.Tests/PositionalTests.cpp, unchanged: the rotary forward and backward cases
+    against its ReferenceRotary with its 1e-6 max-abs bar."""
+    result = subprocess.run([str(oracle.REFERENCE_POSITIONAL_TESTS), "-s"], capture_output=True, text=True, timeout=300)
+    print(result.stdout)
+    assert result.returncode == 0, result.stdout + result.stderr
+    assert result.stdout.count("PASS:") == 2
