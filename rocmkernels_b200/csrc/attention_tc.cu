@@ -570,6 +570,7 @@ __global__ void __launch_bounds__(Forward<D, kHalf>::kThreads, 1)
             // Both split warps pass the named barrier below before either may give up, so a
             // failed wait can never leave one of them blocked in bar.sync.
             const bool landed = __all_sync(0xffffffffu, mbar_wait(&s.kv_full[stage], use & 1));
+            if (lane == 0) RK_TRACE(j, 13 + w);
             const int key = first + j * kKeyTile + row;
             const uint32_t bits = __ballot_sync(0xffffffffu, key < last && mask[key] != 0);
             const bool keep_row = (bits >> lane) & 1;
@@ -662,7 +663,7 @@ __global__ void __launch_bounds__(Forward<D, kHalf>::kThreads, 1)
                 }
             }
             fence_proxy_async_shared();
-            if (lane == 0 && w == 0) RK_TRACE(j, 3);
+            if (lane == 0) RK_TRACE(j, w == 0 ? 3 : 15);
             mbar_arrive(&s.kv_ready[stage]);
             }
         }
