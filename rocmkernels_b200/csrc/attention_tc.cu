@@ -432,6 +432,23 @@ __global__ void __launch_bounds__(Forward<D, kHalf>::kThreads, 1)
         tmem_alloc(&s.tmem_base, F::kTmemColumns);
         tmem_relinquish();
     }
+    // TMA loads of key tile j into its stage, completing on kv_full (producer thread only).
+    const auto issue_tile = [&](int j) {
+        const int stage = j % kStages;
+        RK_TRACE(j, 12);
+        mbar_arrive_expect_tx(&s.kv_full[stage], (2 * F::kBoxes + (kRotary ? 2 : 0)) * kBoxBytes);
+        if constexpr (kRotary) {
+            const int table = b * args.rot_batch;
+            tma_load_4d(s.cos_raw[stage], &tmap_cos, &s.kv_full[stage], 0, first + j * kKeyTile, 0, table);
+            tma_load_4d(s.sin_raw[stage], &tmap_sin, &s.kv_full[stage], 0, first + j * kKeyTile, 0, table);
+        }
+#pragma unroll
+        for (int box = 0; box < F::kBoxes; ++box) {
+            tma_load_4d(s.k_raw[stage] + box * kBoxFloats, &tmap_k, &s.kv_full[stage], 32 * box, first + j * kKeyTile, h, b);
+            tma_load_4d(s.v_raw[stage] + box * kBoxFloats, &tmap_v, &s.kv_full[stage], 32 * box, first + j * kKeyTile, h, b);
+        }
+    };
+    const int prefetched = min(tiles, kStages);  // issued before the set-up barrier
     if (threadIdx.x == F::kProducerWarp * 32) {
         for (int i = 0; i < kStages; ++i) {
             mbar_init(&s.kv_full[i], 1);
@@ -447,6 +464,9 @@ __global__ void __launch_bounds__(Forward<D, kHalf>::kThreads, 1)
         mbar_init(&s.q_ready, kQTile * F::kQTiles);
         mbar_init(&s.mma_done, 1);
         mbar_fence_init();
+        // The first stages are free: their loads overlap the TMEM allocation and the set-up
+        // barrier. Nothing else touches the raw K/V tiles or kv_full before that barrier.
+        for (int j = 0; j < prefetched; ++j) issue_tile(j);
     }
     // Rows 2D..2D+15 of every V operand tile are FP16 ones, so P.V also yields the row sums of P.
     if constexpr (!kHalf) {
@@ -462,24 +482,13 @@ __global__ void __launch_bounds__(Forward<D, kHalf>::kThreads, 1)
     if (warp == F::kProducerWarp) {
         // ---------------------------------------------------------------- TMA producer
         if (lane == 0) {
-            int issued = 0;
+            int issued = prefetched;
             bool ok = true;
-            for (int j = 0; j < tiles && ok; ++j) {
+            for (int j = prefetched; j < tiles && ok; ++j) {
                 const int stage = j % kStages, use = j / kStages;
-                if (j >= kStages) ok = mbar_wait(&s.kv_empty[stage], (use - 1) & 1);
+                ok = mbar_wait(&s.kv_empty[stage], (use - 1) & 1);  // j >= kStages here
                 if (!ok) break;
-                RK_TRACE(j, 12);
-                mbar_arrive_expect_tx(&s.kv_full[stage], (2 * F::kBoxes + (kRotary ? 2 : 0)) * kBoxBytes);
-                if constexpr (kRotary) {
-                    const int table = b * args.rot_batch;
-                    tma_load_4d(s.cos_raw[stage], &tmap_cos, &s.kv_full[stage], 0, first + j * kKeyTile, 0, table);
-                    tma_load_4d(s.sin_raw[stage], &tmap_sin, &s.kv_full[stage], 0, first + j * kKeyTile, 0, table);
-                }
-#pragma unroll
-                for (int box = 0; box < F::kBoxes; ++box) {
-                    tma_load_4d(s.k_raw[stage] + box * kBoxFloats, &tmap_k, &s.kv_full[stage], 32 * box, first + j * kKeyTile, h, b);
-                    tma_load_4d(s.v_raw[stage] + box * kBoxFloats, &tmap_v, &s.kv_full[stage], 32 * box, first + j * kKeyTile, h, b);
-                }
+                issue_tile(j);
                 ++issued;
             }
             if (!ok) {

@@ -81,8 +81,8 @@ struct alignas(1024) Storage {
     uint32_t b2[kStages][G::kRowWords];                    // raw2 rows (B of dP)
     uint32_t t1[kStages][G::kTWords];                      // raw1^T: rows 0..D-1 x0^T, D..2D-1 x1^T (B of X1)
     uint32_t t2[kKeyRows ? kStages : 1][G::kTWords];       // raw2^T (B of X2, key rows only)
-    float col_offset[kStages][kCols];                      // key rows: 14 - max log2e - log2(sum) per query
-    float col_delta[kStages][kCols];                       // key rows: delta per query
+    alignas(16) float col_offset[kStages][kCols];          // key rows: 14 - max log2e - log2(sum) per query
+    alignas(16) float col_delta[kStages][kCols];           // key rows: delta per query
     uint32_t col_mask[kStages][2];                         // visible columns
     int e1[kStages], e2[kStages];                          // tile scale exponents of raw1 (Q: of scale*Q) and raw2
     float col_delta_max[kStages];                          // key rows: max |delta| of the tile
@@ -546,11 +546,24 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
             for (int chunk = 0; chunk < 4; ++chunk) {  // rolled: keeps one chunk's values live
                 float sv[16], dv[16];  // scores, then P'; dP, then dS'
                 tmem_load16x2(lanes + G::kColS + 16 * chunk, sv, lanes + G::kColDP + 16 * chunk, dv);
+                // key rows, d = 32: the chunk's 16 query statistics with 16-byte loads (d = 64 keeps
+                // scalar loads: its key-rows kernel is at the register limit)
+                float col_offset[16], col_delta[16];
+                if constexpr (kKeyRows && D == 32) {
+                    const float4 *o4 = reinterpret_cast<const float4 *>(&s.col_offset[stage][16 * chunk]);
+                    const float4 *d4 = reinterpret_cast<const float4 *>(&s.col_delta[stage][16 * chunk]);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float4 o = o4[i], d = d4[i];
+                        col_offset[4 * i] = o.x, col_offset[4 * i + 1] = o.y, col_offset[4 * i + 2] = o.z, col_offset[4 * i + 3] = o.w;
+                        col_delta[4 * i] = d.x, col_delta[4 * i + 1] = d.y, col_delta[4 * i + 2] = d.z, col_delta[4 * i + 3] = d.w;
+                    }
+                }
 #pragma unroll
                 for (int c = 0; c < 16; ++c) {
                     const int col = 16 * chunk + c;
-                    const float offset = kKeyRows ? s.col_offset[stage][col] : row_offset;
-                    const float delta = kKeyRows ? s.col_delta[stage][col] : row_delta;
+                    const float offset = !kKeyRows ? row_offset : D == 32 ? col_offset[c] : s.col_offset[stage][col];
+                    const float delta = !kKeyRows ? row_delta : D == 32 ? col_delta[c] : s.col_delta[stage][col];
                     float pv = fast_exp2(fmaf(sv[c], slope, offset));
                     if (!all_active) pv = (active >> col) & 1 ? pv : 0.f;
                     sv[c] = pv;
