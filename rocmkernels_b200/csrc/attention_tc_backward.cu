@@ -42,6 +42,21 @@ namespace tc {
 
 namespace {
 
+// Optional pipeline timeline (build with -DRK_TC_TRACE; compiled out otherwise): clock64 stamps
+// of CTA 0 of each pass per column tile and role, read back with rocmkernels_attention_backward_trace().
+#ifdef RK_TC_TRACE
+constexpr int kTraceTiles = 64, kTraceEvents = 16;
+__device__ long long g_bwd_trace[2][kTraceTiles][kTraceEvents];
+#define RK_BTRACE(tile_index, event)                                                                              \
+    do {                                                                                                         \
+        if (blockIdx.x == 0 && (tile_index) < kTraceTiles) g_bwd_trace[kKeyRows][(tile_index)][(event)] = clock64(); \
+    } while (0)
+#else
+#define RK_BTRACE(tile_index, event) \
+    do {                            \
+    } while (0)
+#endif
+
 constexpr int kRows = 128;
 constexpr int kCols = 64;
 constexpr int kStages = 2;
@@ -357,6 +372,7 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
                 const int stage = j % kStages;
                 if (j >= kStages) ok = mbar_wait(&s.empty[stage], ((j / kStages) - 1) & 1);
                 if (!ok) break;
+                RK_BTRACE(j, 0);
                 mbar_arrive_expect_tx(&s.full[stage], 2 * G::kBoxes * kBoxBytes);
 #pragma unroll
                 for (int box = 0; box < G::kBoxes; ++box) {
@@ -384,8 +400,10 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
                 if (!ok) break;
                 tc_fence_after();
                 issue_product<D>(tmem + G::kColS, tmem + G::kColA1, b1_desc + row_stage * stage, nullptr);
+                if (lane == 0) RK_BTRACE(j, 4);
                 issue_product<D>(tmem + G::kColDP, tmem + G::kColA2, b2_desc + row_stage * stage, &s.s_full);
                 ok = mbar_wait_warp(&s.p_full, j & 1);
+                if (lane == 0) RK_BTRACE(j, 5);
                 if (!ok) break;
                 tc_fence_after();
                 if (kKeyRows) {
@@ -406,23 +424,39 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
         const int w = warp - kSplitWarp;
         const int row = 32 * w + lane;
         const float scale1 = kKeyRows ? p.scale : 1.f;  // Q enters the products as scale * Q
+        // This lane's column statistics (key rows: the query's saved {max, sum} and delta; query
+        // rows: whether the key exists and is visible), loaded one tile ahead so that their global
+        // load latency overlaps the previous tile's conversion.
+        float next_max = -INFINITY, next_total = 0.f, next_delta = 0.f;
+        bool next_flag = false;
+        const auto load_stats = [&](int jj) {
+            const int column = first + jj * kCols + row;
+            next_flag = jj < tiles && column < last;
+            if (kKeyRows) {
+                next_max = next_flag ? p.lse_in[(query_base + column) * 2] : -INFINITY;
+                next_total = next_flag ? p.lse_in[(query_base + column) * 2 + 1] : 0.f;
+                next_delta = next_flag ? p.delta[query_base + column] : 0.f;
+            } else {
+                next_flag = next_flag && mask[column] != 0;
+            }
+        };
+        load_stats(0);
         for (int j = 0; j < tiles; ++j) {
             const int stage = j % kStages, parity = j & 1;
+            const float maximum = next_max, total = next_total, delta = next_delta;
+            const bool flag = next_flag;
+            load_stats(j + 1);
             const bool landed = __all_sync(0xffffffffu, mbar_wait(&s.full[stage], (j / kStages) & 1));
-            const int column = first + j * kCols + row;
+            if (lane == 0) RK_BTRACE(j, 1 + w);
             bool visible;
             float delta_abs = 0.f;
             if (kKeyRows) {  // column = query: visible if it exists and has a finite row max
-                const bool exists = column < last;
-                const float maximum = exists ? p.lse_in[(query_base + column) * 2] : -INFINITY;
-                const float total = exists ? p.lse_in[(query_base + column) * 2 + 1] : 0.f;
-                const float delta = exists ? p.delta[query_base + column] : 0.f;
-                visible = exists && maximum != -INFINITY;
+                visible = flag && maximum != -INFINITY;
                 s.col_offset[stage][row] = visible ? 14.f - maximum * kLog2e - __log2f(total) : -INFINITY;
                 s.col_delta[stage][row] = delta;
                 delta_abs = visible ? fabsf(delta) : 0.f;
-            } else {  // column = key
-                visible = column < last && mask[column] != 0;
+            } else {  // column = key: visible if it exists and is not masked
+                visible = flag;
             }
             const uint32_t bits = __ballot_sync(0xffffffffu, visible);
             // Rows of masked key columns are zeroed (query rows only).
@@ -462,6 +496,7 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
             }
             convert_stage<D, kKeyRows>(s, stage, w, lane, keep_row, exp2_int(e1) * scale1, exp2_int(e2));
             fence_proxy_async_shared();
+            if (lane == 0) RK_BTRACE(j, 3 + w);
             mbar_arrive(&s.ready[stage]);
         }
     } else {
@@ -523,6 +558,7 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
         for (int j = 0; j < tiles && ok; ++j) {
             const int stage = j % kStages;
             ok = __all_sync(0xffffffffu, mbar_wait(&s.s_full, j & 1) && mbar_wait(&s.ready[stage], (j / kStages) & 1));
+            if (lane == 0 && (warp == 0 || warp == 3)) RK_BTRACE(j, warp == 0 ? 6 : 9);
             if (!ok) break;
             tc_fence_after();
             const int c0 = first + j * kCols;
@@ -572,6 +608,7 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
                 store_split_chunk(lanes + G::kColDP + 16 * chunk, dv);
                 if (kKeyRows) store_split_chunk(lanes + G::kColS + 16 * chunk, sv);
             }
+            if (lane == 0 && warp == 0) RK_BTRACE(j, 11);
             // Fold the previous tile's X before the P(j)/dS(j) arrival lets the MMA warp
             // overwrite it.
             if (j > 0) {
@@ -583,8 +620,10 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
                 tc_fence_after();
                 fold_x<D, kKeyRows>(acc1, acc2, lanes, pending_scale1, pending_scale2);
             }
+            if (lane == 0 && warp == 0) RK_BTRACE(j, 8);
             tmem_wait_store();
             tc_fence_before();
+            if (lane == 0 && (warp == 0 || warp == 3)) RK_BTRACE(j, warp == 0 ? 7 : 10);
             mbar_arrive(&s.p_full);
             // X1 = 2^(g + e1) * (dS . column operand 1); X2 = 2^(14 + e2) * (P . dO)
             pending_scale1 = exp2_int(-(g + e1));
@@ -713,6 +752,15 @@ int launch_backward(const AttentionParams &p, int head_width, cudaStream_t strea
     if (head_width == 64) return launch_both<64>(p, stream);
     return kNotEligible;
 }
+
+#ifdef RK_TC_TRACE
+extern "C" __attribute__((visibility("default"))) int rocmkernels_attention_backward_trace(long long *out, int capacity) {
+    const int count = 2 * kTraceTiles * kTraceEvents;
+    if (capacity < count) return -1;
+    if (cudaMemcpyFromSymbol(out, g_bwd_trace, sizeof(long long) * count) != cudaSuccess) return -2;
+    return count;
+}
+#endif
 
 unsigned int read_backward_status(bool clear) {
     unsigned int value = 0;
