@@ -59,7 +59,6 @@ __device__ long long g_bwd_trace[2][kTraceTiles][kTraceEvents];
 
 constexpr int kRows = 128;
 constexpr int kCols = 64;
-constexpr int kStages = 2;
 constexpr int kThreads = 256;
 constexpr int kProducerWarp = 4;
 constexpr int kMmaWarp = 5;
@@ -85,17 +84,31 @@ struct Geometry {
     static constexpr uint32_t kTmemColumns = D == 32 ? 256 : 512;
     static constexpr int kCtasPerSm = D == 32 ? 2 : 1;
     static constexpr uint32_t kIdescX = f16_instr_desc(128, D);
+    // Query rows: X1 = dS.[k0 | k1] with B = the row layout of K read MN-major (N = 2D)
+    static constexpr uint32_t kIdescXMn = f16_instr_desc_b_mn(128, 2 * D);
+    static constexpr uint32_t kMnChunkBytes = D == 32 ? 1024 : kBoxBytes;  // x1 part: the next 64-element chunk
 };
+
+// Transposed FP16 layouts, B of the key-rows X products (the query-rows X1 reads the row layout
+// MN-major and needs none).
+template <int D, bool kKeyRows, int kStages>
+struct alignas(1024) TransposedTiles {
+    uint32_t t1[kStages][Geometry<D>::kTWords];  // raw1^T: rows 0..D-1 x0^T, D..2D-1 x1^T (B of X1)
+    uint32_t t2[kStages][Geometry<D>::kTWords];  // raw2^T (B of X2)
+};
+template <int D, int kStages>
+struct TransposedTiles<D, false, kStages> {};
 
 template <int D, bool kKeyRows>
 struct alignas(1024) Storage {
     using G = Geometry<D>;
+    // Pipeline depth: the query-rows pass, without transposed tiles, has room for a third stage.
+    static constexpr int kStages = kKeyRows ? 2 : 3;
     float raw1[kStages][G::kRawFloats];                    // TMA tile: K (query rows) or Q (key rows), 128B swizzle
     float raw2[kStages][G::kRawFloats];                    // V or dO
     uint32_t b1[kStages][G::kRowWords];                    // raw1 rows as split FP16 (B of S), 128B swizzle
     uint32_t b2[kStages][G::kRowWords];                    // raw2 rows (B of dP)
-    uint32_t t1[kStages][G::kTWords];                      // raw1^T: rows 0..D-1 x0^T, D..2D-1 x1^T (B of X1)
-    uint32_t t2[kKeyRows ? kStages : 1][G::kTWords];       // raw2^T (B of X2, key rows only)
+    TransposedTiles<D, kKeyRows, kStages> t;               // key rows: B of X1 and X2
     alignas(16) float col_offset[kStages][kCols];          // key rows: 14 - max log2e - log2(sum) per query
     alignas(16) float col_delta[kStages][kCols];           // key rows: delta per query
     uint32_t col_mask[kStages][2];                         // visible columns
@@ -230,7 +243,24 @@ __device__ __forceinline__ void store_split_chunk(uint32_t chunk, const float (&
     tmem_store8x2_async(chunk, q0, chunk + 8, q1);
 }
 
-// acc1 += X1 * scale1 (and acc2 += X2 * scale2 for key rows), eight columns at a time.
+// X1 (N = 2D) = dS.[b0 | b1] for query rows: A chunks of 16 key columns at `chunks` + 16 kk
+// ([ds0 pairs 8 | ds1 pairs 8]), B = the row layout of K read MN-major (for each key a row of
+// [k0 | k1]; 16 keys = 2048 bytes), so the products with k0 land in columns 0..D-1 and those with
+// k1 in D..2D-1; no transposed copy of K is needed. Commits to `bar`. Warp-collective.
+template <int D>
+__device__ __forceinline__ void issue_x_mn(uint32_t d, uint32_t chunks, uint64_t b, uint64_t *bar) {
+    constexpr uint32_t idesc = Geometry<D>::kIdescXMn;
+    constexpr uint64_t step = 2048 / 16;
+    const uint32_t g1a[4] = {chunks, chunks + 8, chunks + 16, chunks + 24};
+    const uint64_t g1b[4] = {b, b, b + step, b + step};
+    mma4_f16_ts_warp(d, g1a, g1b, idesc, 1);
+    const uint32_t g2a[4] = {chunks + 32, chunks + 40, chunks + 48, chunks + 56};
+    const uint64_t g2b[4] = {b + 2 * step, b + 2 * step, b + 3 * step, b + 3 * step};
+    mma4_f16_ts_commit_warp(d, g2a, g2b, idesc, 0, bar);
+}
+
+// acc1 += X1 * scale1 (and acc2 += X2 * scale2 for key rows), eight columns at a time. Query rows:
+// X1 holds the k0 and k1 products in columns 0..D-1 and D..2D-1.
 template <int D, bool kKeyRows>
 __device__ __forceinline__ void fold_x(float (&acc1)[D], float (&acc2)[kKeyRows ? D : 1], uint32_t lanes, float scale1,
                                        float scale2) {
@@ -238,18 +268,22 @@ __device__ __forceinline__ void fold_x(float (&acc1)[D], float (&acc2)[kKeyRows 
 #pragma unroll
     for (int quarter = 0; quarter < D / 8; ++quarter) {
         float xa[8], xb[8];
-        tmem_load8x2(lanes + G::kColX1 + 8 * quarter, xa, lanes + (kKeyRows ? G::kColX2 : G::kColX1) + 8 * quarter, xb);
+        tmem_load8x2(lanes + G::kColX1 + 8 * quarter, xa, lanes + (kKeyRows ? G::kColX2 : G::kColX1 + D) + 8 * quarter, xb);
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-            acc1[8 * quarter + c] = fmaf(xa[c], scale1, acc1[8 * quarter + c]);
-            if constexpr (kKeyRows) acc2[8 * quarter + c] = fmaf(xb[c], scale2, acc2[8 * quarter + c]);
+            if constexpr (kKeyRows) {
+                acc1[8 * quarter + c] = fmaf(xa[c], scale1, acc1[8 * quarter + c]);
+                acc2[8 * quarter + c] = fmaf(xb[c], scale2, acc2[8 * quarter + c]);
+            } else {
+                acc1[8 * quarter + c] = fmaf(xa[c] + xb[c], scale1, acc1[8 * quarter + c]);
+            }
         }
     }
 }
 
 // Converts the two FP32 tiles of one stage (split warps, 64 threads): row layouts of both
-// (B of S and dP), transposed layouts of raw1 (and of raw2 for key rows), masked key rows zeroed
-// (query rows). Lane layout: row = 32 w + lane for the row layouts; (group of 8 rows, chunk of 4
+// (B of S and dP; for query rows also, read MN-major, the B of X1), and for key rows the
+// transposed layouts of raw1 and raw2 (B of X1 and X2); masked key rows zeroed (query rows). Lane layout: row = 32 w + lane for the row layouts; (group of 8 rows, chunk of 4
 // features) items for the transposed ones.
 template <int D, bool kKeyRows>
 __device__ __forceinline__ void convert_stage(Storage<D, kKeyRows> &s, int stage, int w, int lane, bool keep_row, float scale_1,
@@ -276,12 +310,13 @@ __device__ __forceinline__ void convert_stage(Storage<D, kKeyRows> &s, int stage
                                                        pack_half2(x1[4], x1[5]), pack_half2(x1[6], x1[7]));
         }
     }
-    // Transposed: feature rows f (x0) and D + f (x1); tile rows 8g..8g+7 are 16-byte chunk g
-    // (swizzled by f % 8). Item = (group g, feature chunk fc of 4 features).
+    // Transposed (key rows): feature rows f (x0) and D + f (x1); tile rows 8g..8g+7 are 16-byte
+    // chunk g (swizzled by f % 8). Item = (group g, feature chunk fc of 4 features).
+    if constexpr (kKeyRows) {
 #pragma unroll
-    for (int which = 0; which < (kKeyRows ? 2 : 1); ++which) {
+    for (int which = 0; which < 2; ++which) {
         const float *raw = which == 0 ? s.raw1[stage] : s.raw2[stage];
-        uint4 *dst = reinterpret_cast<uint4 *>(which == 0 ? s.t1[stage] : s.t2[kKeyRows ? stage : 0]);
+        uint4 *dst = reinterpret_cast<uint4 *>(which == 0 ? s.t.t1[stage] : s.t.t2[stage]);
         const float scale = which == 0 ? scale_1 : scale_2;
 #pragma unroll
         for (int item = 0; item < D / 32; ++item) {
@@ -312,6 +347,7 @@ __device__ __forceinline__ void convert_stage(Storage<D, kKeyRows> &s, int stage
             }
         }
     }
+    }
 }
 
 template <int D, bool kKeyRows>
@@ -320,6 +356,7 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
                         const __grid_constant__ CUtensorMap tmap2) {
     using G = Geometry<D>;
     using S = Storage<D, kKeyRows>;
+    constexpr int kStages = S::kStages;
     extern __shared__ uint8_t shared_raw[];
     S &s = *reinterpret_cast<S *>((reinterpret_cast<uintptr_t>(shared_raw) + 1023) & ~uintptr_t(1023));
     const AttentionParams &p = args.p;
@@ -388,11 +425,10 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
     } else if (warp == kMmaWarp) {
         // ---------------------------------------------------------------- MMA issuer
         if (tiles > 0) {
-            constexpr uint64_t row_stage = G::kRowWords * 4 / 16, t_stage = G::kTWords * 4 / 16;
+            constexpr uint64_t row_stage = G::kRowWords * 4 / 16;
             const uint64_t b1_desc = sw128_descriptor(smem_u32(s.b1[0]));
             const uint64_t b2_desc = sw128_descriptor(smem_u32(s.b2[0]));
-            const uint64_t t1_desc = sw128_descriptor(smem_u32(s.t1[0]));
-            const uint64_t t2_desc = sw128_descriptor(smem_u32(s.t2[0]));
+            const uint64_t b1_mn_desc = sw128_mn_descriptor(smem_u32(s.b1[0]), G::kMnChunkBytes);
             bool ok = mbar_wait_warp(&s.rows_ready, 0);
             for (int j = 0; j < tiles && ok; ++j) {
                 const int stage = j % kStages;
@@ -406,11 +442,13 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
                 if (lane == 0) RK_BTRACE(j, 5);
                 if (!ok) break;
                 tc_fence_after();
-                if (kKeyRows) {
-                    issue_x<D>(tmem + G::kColX1, tmem + G::kColDP, t1_desc + t_stage * stage, nullptr);
-                    issue_x<D>(tmem + G::kColX2, tmem + G::kColS, t2_desc + t_stage * stage, &s.x_done);
+                if constexpr (kKeyRows) {
+                    const uint64_t t1_desc = sw128_descriptor(smem_u32(s.t.t1[stage]));
+                    const uint64_t t2_desc = sw128_descriptor(smem_u32(s.t.t2[stage]));
+                    issue_x<D>(tmem + G::kColX1, tmem + G::kColDP, t1_desc, nullptr);
+                    issue_x<D>(tmem + G::kColX2, tmem + G::kColS, t2_desc, &s.x_done);
                 } else {
-                    issue_x<D>(tmem + G::kColX1, tmem + G::kColDP, t1_desc + t_stage * stage, &s.x_done);
+                    issue_x_mn<D>(tmem + G::kColX1, tmem + G::kColDP, b1_mn_desc + row_stage * stage, &s.x_done);
                 }
                 mma_commit_warp(&s.empty[stage]);
             }

@@ -251,6 +251,25 @@ __host__ __device__ constexpr uint32_t f16_instr_desc(int m, int n) {
     return (1u << 4) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
 }
 
+// The same with B MN-major (bit 16): B's N elements are contiguous for each K index.
+__host__ __device__ constexpr uint32_t f16_instr_desc_b_mn(int m, int n) { return f16_instr_desc(m, n) | (1u << 16); }
+
+// Shared-memory descriptor of an MN-major 128B-swizzled operand: for each K index a 128-byte row
+// of 64 consecutive MN elements, eight K rows per 1024-byte swizzle atom, the atoms of
+// consecutive K groups every 1024 bytes (stride byte offset) and further 64-element MN chunks
+// every `mn_chunk_bytes` (leading byte offset) -- the canonical layout
+// Swizzle<3,4,3> o ((8,n),(8,k)):((1,LBO),(8,SBO)) in 16-byte units. A K=16 step of FP16 is two
+// K groups: 2048 bytes.
+__device__ __forceinline__ uint64_t sw128_mn_descriptor(uint32_t smem_byte_address, uint32_t mn_chunk_bytes) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((smem_byte_address & 0x3FFFFu) >> 4);  // start address
+    d |= static_cast<uint64_t>(mn_chunk_bytes >> 4) << 16;             // leading byte offset: next MN chunk
+    d |= static_cast<uint64_t>(1024 >> 4) << 32;                       // stride byte offset: next 8 K rows
+    d |= static_cast<uint64_t>(1) << 46;                               // descriptor version (sm_100)
+    d |= static_cast<uint64_t>(2) << 61;                               // SWIZZLE_128B
+    return d;
+}
+
 // Warp-collective forms: the whole warp executes the call with warp-uniform operands and one
 // lane chosen by elect.sync issues the instructions. Issuing from a full warp keeps the operand
 // arithmetic on the uniform datapath; a single lane computing them itself needs several issue
