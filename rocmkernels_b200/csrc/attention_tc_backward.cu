@@ -14,19 +14,25 @@
 //   key rows   (pass 2): rows = keys, columns = query tiles.    S^T = K Q^T, dP^T = V dO^T,
 //                        X1 += dS^T Q (dK), X2 += P^T dO (dV).
 // Warps: 0-3 row warps (thread = row = TMEM lane), 4 TMA producer, 5 MMA issuer (whole warp,
-// elected issue), 6-7 split warps (FP16 conversion of each column tile). Two CTAs per SM
-// (256 TMEM columns each).
+// elected issue), 6-7 split warps (FP16 conversion of each column tile). d = 32: two CTAs per
+// SM (256 TMEM columns each); d = 64: one (512).
 //
 // Split FP16 operands as in the forward: every operand is scaled by a power of two so that its
 // largest magnitude lies in [2^14, 2^15) (row operands per row, column tiles per tile, P by
 // 2^14, dS per row and tile from the bound |dS| <= ||dO_i||_1 max|v| + |delta_i| (pass 1) or
 // ||v_j||_1 max|dO| + max|delta| (pass 2), which needs no extra pass over dS) and split into
-// x0 + x1: S = a0.b1 + a1.b0 + a0.b0 (6 MMAs N64), X = ds1.t0 + ds0.t0 + ds0.t1 per 16 columns
-// (12 MMAs N32). The per-tile products are folded into FP32 registers (the tensor core's
-// accumulation is not round-to-nearest), so the sums over column tiles are plain FP32.
+// x0 + x1: S = a0.b1 + a1.b0 + a0.b0 (6 MMAs N64 for d = 32). The X products read the column
+// tile's row layout [b0 | b1] as an MN-major B operand: one MMA of N = 2D per 16 columns and
+// term gives ds.b0 and ds.b1 side by side, X = (ds0 + ds1).[b0 | b1] (8 MMAs), and the fold adds
+// the two halves -- no transposed copy of any tile. The per-tile products are folded into FP32
+// registers (the tensor core's accumulation is not round-to-nearest), so the sums over column
+// tiles are plain FP32.
 //
-// TMEM (256 columns), per row:
-//   a1 [x0 16 | x1 16] 0-31 | a2 32-63 | S then P 64-127 | dP then dS 128-191 | X1 192-223 | X2 224-255
+// TMEM per row (d = 32; d = 64 doubles every width but the 64-column S and dP):
+//   query rows: a1 [x0 16 | x1 16] 0-31 | a2 32-63 | S 64-127 | dP then dS 128-191 | X1 [b0 | b1] 192-255
+//   key rows:   S then P 0-63 | dP then dS 64-127 | X1 [b0 | b1] 128-191 | X2 192-255, the row
+//               operands (K, V) in shared memory as the K-major A of S^T and dP^T (the d = 64
+//               key-rows pass keeps them in TMEM, 512 columns)
 // P and dS overwrite S and dP chunk by chunk: 16 columns [x0 pairs 8 | x1 pairs 8], which
 // occupy exactly the 16 columns of scores the chunk has just read.
 #include "attention_tc.cuh"
@@ -73,42 +79,47 @@ struct Geometry {
     static constexpr int kBoxes = D / 32;                   // TMA boxes per tile row
     static constexpr int kRawFloats = kBoxes * kBoxFloats;   // FP32 tile: kBoxes boxes of 64 x 32
     static constexpr int kRowWords = 64 * D;                // row layout: 64 rows x [x0 | x1] (2 D fp16 each)
-    static constexpr int kTWords = 2 * D * 32;              // transposed: 2 D rows x 64 fp16
     // Row layout: D = 32 keeps [x0 | x1] in one 128-byte row; D = 64 uses an x0 tile and an x1
     // tile of 64 rows x 128 bytes each. Descriptor offset (16-byte units) of the x1 part.
     static constexpr uint64_t kDescX1 = row_x1_offset<D>();
-    static constexpr uint64_t kDescUpper = D * 128 / 16;   // transposed: x1^T rows start
-    // TMEM columns
-    static constexpr uint32_t kColA1 = 0, kColA2 = D, kColS = 2 * D, kColDP = 2 * D + 64, kColX1 = 2 * D + 128,
-                              kColX2 = 3 * D + 128;
     static constexpr uint32_t kTmemColumns = D == 32 ? 256 : 512;
     static constexpr int kCtasPerSm = D == 32 ? 2 : 1;
-    static constexpr uint32_t kIdescX = f16_instr_desc(128, D);
-    // Query rows: X1 = dS.[k0 | k1] with B = the row layout of K read MN-major (N = 2D)
-    static constexpr uint32_t kIdescXMn = f16_instr_desc_b_mn(128, 2 * D);
-    static constexpr uint32_t kMnChunkBytes = D == 32 ? 1024 : kBoxBytes;  // x1 part: the next 64-element chunk
+    // X = dS.[b0 | b1]: B = the column tile's row layout read MN-major (N = 2D); for D = 64 the
+    // x1 part (MN elements 64..127) is the next 8 KB tile.
+    static constexpr uint32_t kIdescX = f16_instr_desc_b_mn(128, 2 * D);
+    static constexpr uint32_t kMnChunkBytes = D == 32 ? 1024 : kBoxBytes;
 };
 
-// Transposed FP16 layouts, B of the key-rows X products (the query-rows X1 reads the row layout
-// MN-major and needs none).
-template <int D, bool kKeyRows, int kStages>
-struct alignas(1024) TransposedTiles {
-    uint32_t t1[kStages][Geometry<D>::kTWords];  // raw1^T: rows 0..D-1 x0^T, D..2D-1 x1^T (B of X1)
-    uint32_t t2[kStages][Geometry<D>::kTWords];  // raw2^T (B of X2)
+// TMEM columns per row. The d = 32 key-rows pass keeps its row operands (K, V) in shared memory:
+// its 256 columns hold S, dP and the two 2D-wide X products.
+template <int D, bool kKeyRows>
+struct Columns {
+    static constexpr bool kRowOperandsInSmem = kKeyRows && D == 32;
+    static constexpr uint32_t kA1 = 0, kA2 = D;
+    static constexpr uint32_t kS = kRowOperandsInSmem ? 0 : 2 * D, kDP = kS + 64, kX1 = kS + 128, kX2 = kX1 + 2 * D;
+    static_assert((kKeyRows ? kX2 : kX1) + 2 * D <= Geometry<D>::kTmemColumns, "TMEM budget");
 };
-template <int D, int kStages>
-struct TransposedTiles<D, false, kStages> {};
+
+// Split FP16 row operands in shared memory (the d = 32 key-rows pass): K and V rows as
+// 128 x [x0 | x1] (128 bytes per row), 128B swizzle -- the K-major A of S^T and dP^T.
+template <int D, bool kInSmem>
+struct alignas(1024) RowOperandTiles {
+    uint32_t a1[kRows * D];  // K
+    uint32_t a2[kRows * D];  // V
+};
+template <int D>
+struct RowOperandTiles<D, false> {};
 
 template <int D, bool kKeyRows>
 struct alignas(1024) Storage {
     using G = Geometry<D>;
-    // Pipeline depth: the query-rows pass, without transposed tiles, has room for a third stage.
+    // Pipeline depth: the key-rows pass spends the room of a third stage on its row operands.
     static constexpr int kStages = kKeyRows ? 2 : 3;
     float raw1[kStages][G::kRawFloats];                    // TMA tile: K (query rows) or Q (key rows), 128B swizzle
     float raw2[kStages][G::kRawFloats];                    // V or dO
-    uint32_t b1[kStages][G::kRowWords];                    // raw1 rows as split FP16 (B of S), 128B swizzle
-    uint32_t b2[kStages][G::kRowWords];                    // raw2 rows (B of dP)
-    TransposedTiles<D, kKeyRows, kStages> t;               // key rows: B of X1 and X2
+    uint32_t b1[kStages][G::kRowWords];                    // raw1 rows as split FP16 (B of S; MN-major B of X1), 128B swizzle
+    uint32_t b2[kStages][G::kRowWords];                    // raw2 rows (B of dP; key rows: MN-major B of X2)
+    RowOperandTiles<D, Columns<D, kKeyRows>::kRowOperandsInSmem> a;  // d = 32 key rows: K, V
     alignas(16) float col_offset[kStages][kCols];          // key rows: 14 - max log2e - log2(sum) per query
     alignas(16) float col_delta[kStages][kCols];           // key rows: delta per query
     uint32_t col_mask[kStages][2];                         // visible columns
@@ -122,7 +133,7 @@ struct alignas(1024) Storage {
     uint64_t s_full;                                       // S and dP in TMEM (commit)
     uint64_t p_full;                                       // P / dS stored and the previous X folded (128 arrivals)
     uint64_t x_done;                                       // X1 (X2) of the tile in TMEM (commit)
-    uint64_t rows_ready;                                   // row operands in TMEM (128 arrivals)
+    uint64_t rows_ready;                                   // row operands stored (128 arrivals)
     uint64_t mma_done;                                     // every MMA finished (commit)
     uint32_t tmem_base;
 };
@@ -156,6 +167,20 @@ __device__ __forceinline__ void store_row_operand(const float (&x)[D], int expon
     }
 }
 
+// The same into a shared-memory row layout (row `row` of a 128-row tile, 128B swizzle).
+template <int D>
+__device__ __forceinline__ void store_row_operand_smem(const float (&x)[D], int exponent, uint32_t *tile, int row) {
+    const float scale = exp2_int(exponent);
+#pragma unroll
+    for (int m = 0; m < D / 8; ++m) {
+        float x0[8], x1[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) split_half(x[8 * m + e], scale, x0[e], x1[e]);
+        *row_chunk<D>(tile, row, 0, m) = pack_chunk(x0);
+        *row_chunk<D>(tile, row, 1, m) = pack_chunk(x1);
+    }
+}
+
 // Loads a D-float row (zeros when !valid), multiplied by `scale`.
 template <int D>
 __device__ __forceinline__ void load_row(const float *row, bool valid, float scale, float (&x)[D]) {
@@ -176,27 +201,6 @@ __device__ __forceinline__ float abs_max(const float (&x)[D]) {
 #pragma unroll
     for (int c = 0; c < D; c += 2) m = max3(m, fabsf(x[c]), fabsf(x[c + 1]));
     return m;
-}
-
-// X (N = D) = x1.t0 + x0.t0 + x0.t1 over the 64 columns: A chunks of 16 columns at
-// `chunks` + 16 kk ([x0 pairs 8 | x1 pairs 8]), B = t (rows 0..D-1 x0^T, D..2D-1 x1^T). Commits
-// to `bar` when given. Warp-collective.
-template <int D>
-__device__ __forceinline__ void issue_x(uint32_t d, uint32_t chunks, uint64_t t, uint64_t *bar) {
-    constexpr uint32_t idesc = Geometry<D>::kIdescX;
-    const uint64_t u = t + Geometry<D>::kDescUpper;
-    const uint32_t g1a[4] = {chunks, chunks + 8, chunks, chunks + 16};
-    const uint64_t g1b[4] = {t, t, u, t + kDescStep};
-    mma4_f16_ts_warp(d, g1a, g1b, idesc, 1);
-    const uint32_t g2a[4] = {chunks + 24, chunks + 16, chunks + 32, chunks + 40};
-    const uint64_t g2b[4] = {t + kDescStep, u + kDescStep, t + 2 * kDescStep, t + 2 * kDescStep};
-    mma4_f16_ts_warp(d, g2a, g2b, idesc, 0);
-    const uint32_t g3a[4] = {chunks + 32, chunks + 48, chunks + 56, chunks + 48};
-    const uint64_t g3b[4] = {u + 2 * kDescStep, t + 3 * kDescStep, t + 3 * kDescStep, u + 3 * kDescStep};
-    if (bar != nullptr)
-        mma4_f16_ts_commit_warp(d, g3a, g3b, idesc, 0, bar);
-    else
-        mma4_f16_ts_warp(d, g3a, g3b, idesc, 0);
 }
 
 // S (N = 64) = a0.b1 + a1.b0 + a0.b0 over the D features; a at TMEM `a` ([x0 D/2 | x1 D/2]),
@@ -229,6 +233,23 @@ __device__ __forceinline__ void issue_product(uint32_t d, uint32_t a, uint64_t b
     }
 }
 
+// The same with the row operand in shared memory (D = 32): `a` = descriptor of its row layout
+// ([x0 | x1] per 128-byte row, x1 at +64 bytes).
+template <int D>
+__device__ __forceinline__ void issue_product_smem(uint32_t d, uint64_t a, uint64_t b, uint64_t *bar) {
+    static_assert(D == 32, "shared-memory row operands: d = 32 only");
+    constexpr uint64_t x1 = Geometry<D>::kDescX1;
+    const uint64_t ga[4] = {a, a + kDescStep, a + x1, a + x1 + kDescStep};  // a0 . b1, a1 . b0
+    const uint64_t gb[4] = {b + x1, b + x1 + kDescStep, b, b + kDescStep};
+    mma4_f16_ss_warp(d, ga, gb, kIdescS, 1);
+    const uint64_t ha[2] = {a, a + kDescStep};  // a0 . b0
+    const uint64_t hb[2] = {b, b + kDescStep};
+    if (bar != nullptr)
+        mma2_f16_ss_commit_warp(d, ha, hb, kIdescS, bar);
+    else
+        mma2_f16_ss_warp(d, ha, hb, kIdescS);
+}
+
 // Splits 16 values (columns of a chunk) into FP16 pairs and stores them, without waiting, as
 // [x0 pairs 8 | x1 pairs 8] at TMEM `chunk` (the A layout of one K=16 step).
 __device__ __forceinline__ void store_split_chunk(uint32_t chunk, const float (&v)[16]) {
@@ -243,54 +264,53 @@ __device__ __forceinline__ void store_split_chunk(uint32_t chunk, const float (&
     tmem_store8x2_async(chunk, q0, chunk + 8, q1);
 }
 
-// X1 (N = 2D) = dS.[b0 | b1] for query rows: A chunks of 16 key columns at `chunks` + 16 kk
-// ([ds0 pairs 8 | ds1 pairs 8]), B = the row layout of K read MN-major (for each key a row of
-// [k0 | k1]; 16 keys = 2048 bytes), so the products with k0 land in columns 0..D-1 and those with
-// k1 in D..2D-1; no transposed copy of K is needed. Commits to `bar`. Warp-collective.
+// X (N = 2D) = (x0 + x1).[b0 | b1] over the 64 columns: A chunks of 16 columns at
+// `chunks` + 16 kk ([x0 pairs 8 | x1 pairs 8]), B = the column tile's row layout read MN-major
+// (for each column a row of [b0 | b1]; 16 columns = 2048 bytes), so the products with b0 land
+// in accumulator columns 0..D-1 and those with b1 in D..2D-1. Commits to `bar` when given.
+// Warp-collective.
 template <int D>
-__device__ __forceinline__ void issue_x_mn(uint32_t d, uint32_t chunks, uint64_t b, uint64_t *bar) {
-    constexpr uint32_t idesc = Geometry<D>::kIdescXMn;
+__device__ __forceinline__ void issue_x(uint32_t d, uint32_t chunks, uint64_t b, uint64_t *bar) {
+    constexpr uint32_t idesc = Geometry<D>::kIdescX;
     constexpr uint64_t step = 2048 / 16;
     const uint32_t g1a[4] = {chunks, chunks + 8, chunks + 16, chunks + 24};
     const uint64_t g1b[4] = {b, b, b + step, b + step};
     mma4_f16_ts_warp(d, g1a, g1b, idesc, 1);
     const uint32_t g2a[4] = {chunks + 32, chunks + 40, chunks + 48, chunks + 56};
     const uint64_t g2b[4] = {b + 2 * step, b + 2 * step, b + 3 * step, b + 3 * step};
-    mma4_f16_ts_commit_warp(d, g2a, g2b, idesc, 0, bar);
+    if (bar != nullptr)
+        mma4_f16_ts_commit_warp(d, g2a, g2b, idesc, 0, bar);
+    else
+        mma4_f16_ts_warp(d, g2a, g2b, idesc, 0);
 }
 
-// acc1 += X1 * scale1 (and acc2 += X2 * scale2 for key rows), eight columns at a time. Query rows:
-// X1 holds the k0 and k1 products in columns 0..D-1 and D..2D-1.
+// acc1 += X1 * scale1 (and acc2 += X2 * scale2 for key rows), eight columns at a time; each X
+// holds the b0 and b1 products in columns 0..D-1 and D..2D-1.
 template <int D, bool kKeyRows>
 __device__ __forceinline__ void fold_x(float (&acc1)[D], float (&acc2)[kKeyRows ? D : 1], uint32_t lanes, float scale1,
                                        float scale2) {
-    using G = Geometry<D>;
+    using C = Columns<D, kKeyRows>;
 #pragma unroll
     for (int quarter = 0; quarter < D / 8; ++quarter) {
         float xa[8], xb[8];
-        tmem_load8x2(lanes + G::kColX1 + 8 * quarter, xa, lanes + (kKeyRows ? G::kColX2 : G::kColX1 + D) + 8 * quarter, xb);
+        tmem_load8x2(lanes + C::kX1 + 8 * quarter, xa, lanes + C::kX1 + D + 8 * quarter, xb);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-            if constexpr (kKeyRows) {
-                acc1[8 * quarter + c] = fmaf(xa[c], scale1, acc1[8 * quarter + c]);
-                acc2[8 * quarter + c] = fmaf(xb[c], scale2, acc2[8 * quarter + c]);
-            } else {
-                acc1[8 * quarter + c] = fmaf(xa[c] + xb[c], scale1, acc1[8 * quarter + c]);
-            }
+        for (int c = 0; c < 8; ++c) acc1[8 * quarter + c] = fmaf(xa[c] + xb[c], scale1, acc1[8 * quarter + c]);
+        if constexpr (kKeyRows) {
+            tmem_load8x2(lanes + C::kX2 + 8 * quarter, xa, lanes + C::kX2 + D + 8 * quarter, xb);
+#pragma unroll
+            for (int c = 0; c < 8; ++c) acc2[8 * quarter + c] = fmaf(xa[c] + xb[c], scale2, acc2[8 * quarter + c]);
         }
     }
 }
 
-// Converts the two FP32 tiles of one stage (split warps, 64 threads): row layouts of both
-// (B of S and dP; for query rows also, read MN-major, the B of X1), and for key rows the
-// transposed layouts of raw1 and raw2 (B of X1 and X2); masked key rows zeroed (query rows). Lane layout: row = 32 w + lane for the row layouts; (group of 8 rows, chunk of 4
-// features) items for the transposed ones.
+// Converts the two FP32 tiles of one stage (split warps, 64 threads, row = 32 w + lane) to their
+// row layouts: the B of S and dP, and read MN-major the B of X1 (and X2 for key rows); masked
+// key rows zeroed (query rows).
 template <int D, bool kKeyRows>
 __device__ __forceinline__ void convert_stage(Storage<D, kKeyRows> &s, int stage, int w, int lane, bool keep_row, float scale_1,
                                               float scale_2) {
-    using G = Geometry<D>;
     const int row = 32 * w + lane;
-    const uint32_t bits0 = s.col_mask[stage][0], bits1 = s.col_mask[stage][1];
 #pragma unroll
     for (int which = 0; which < 2; ++which) {
         const float *raw = which == 0 ? s.raw1[stage] : s.raw2[stage];
@@ -304,49 +324,9 @@ __device__ __forceinline__ void convert_stage(Storage<D, kKeyRows> &s, int stage
             float x0[8], x1[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) split_half(x[e], scale, x0[e], x1[e]);
-            *row_chunk<D>(dst, row, 0, m) = make_uint4(pack_half2(x0[0], x0[1]), pack_half2(x0[2], x0[3]),
-                                                       pack_half2(x0[4], x0[5]), pack_half2(x0[6], x0[7]));
-            *row_chunk<D>(dst, row, 1, m) = make_uint4(pack_half2(x1[0], x1[1]), pack_half2(x1[2], x1[3]),
-                                                       pack_half2(x1[4], x1[5]), pack_half2(x1[6], x1[7]));
+            *row_chunk<D>(dst, row, 0, m) = pack_chunk(x0);
+            *row_chunk<D>(dst, row, 1, m) = pack_chunk(x1);
         }
-    }
-    // Transposed (key rows): feature rows f (x0) and D + f (x1); tile rows 8g..8g+7 are 16-byte
-    // chunk g (swizzled by f % 8). Item = (group g, feature chunk fc of 4 features).
-    if constexpr (kKeyRows) {
-#pragma unroll
-    for (int which = 0; which < 2; ++which) {
-        const float *raw = which == 0 ? s.raw1[stage] : s.raw2[stage];
-        uint4 *dst = reinterpret_cast<uint4 *>(which == 0 ? s.t.t1[stage] : s.t.t2[stage]);
-        const float scale = which == 0 ? scale_1 : scale_2;
-#pragma unroll
-        for (int item = 0; item < D / 32; ++item) {
-            const int index = 64 * item + 32 * w + lane;  // 0 .. 2D - 1
-            const int group = index >> 3 & 7;
-            const int fchunk = (index & 7) + 8 * (index >> 6);
-            float4 values[8];
-#pragma unroll
-            for (int r = 0; r < 8; ++r) {
-                const int trow = 8 * group + r;
-                values[r] = raw_chunk<D>(raw, trow, fchunk);
-                const uint32_t word = trow < 32 ? bits0 : bits1;
-                if (!kKeyRows && !((word >> (trow & 31)) & 1)) values[r] = make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int f = 4 * fchunk + e;
-                float x0[8], x1[8];
-#pragma unroll
-                for (int r = 0; r < 8; ++r) {
-                    const float value = e == 0 ? values[r].x : e == 1 ? values[r].y : e == 2 ? values[r].z : values[r].w;
-                    split_half(value, scale, x0[r], x1[r]);
-                }
-                dst[f * 8 + (group ^ (f & 7))] = make_uint4(pack_half2(x0[0], x0[1]), pack_half2(x0[2], x0[3]),
-                                                            pack_half2(x0[4], x0[5]), pack_half2(x0[6], x0[7]));
-                dst[(D + f) * 8 + (group ^ (f & 7))] = make_uint4(pack_half2(x1[0], x1[1]), pack_half2(x1[2], x1[3]),
-                                                                  pack_half2(x1[4], x1[5]), pack_half2(x1[6], x1[7]));
-            }
-        }
-    }
     }
 }
 
@@ -355,6 +335,7 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
         backward_kernel(const BackwardArgs args, const __grid_constant__ CUtensorMap tmap1,
                         const __grid_constant__ CUtensorMap tmap2) {
     using G = Geometry<D>;
+    using C = Columns<D, kKeyRows>;
     using S = Storage<D, kKeyRows>;
     constexpr int kStages = S::kStages;
     extern __shared__ uint8_t shared_raw[];
@@ -429,26 +410,31 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
             const uint64_t b1_desc = sw128_descriptor(smem_u32(s.b1[0]));
             const uint64_t b2_desc = sw128_descriptor(smem_u32(s.b2[0]));
             const uint64_t b1_mn_desc = sw128_mn_descriptor(smem_u32(s.b1[0]), G::kMnChunkBytes);
+            const uint64_t b2_mn_desc = sw128_mn_descriptor(smem_u32(s.b2[0]), G::kMnChunkBytes);
             bool ok = mbar_wait_warp(&s.rows_ready, 0);
             for (int j = 0; j < tiles && ok; ++j) {
                 const int stage = j % kStages;
                 ok = mbar_wait_warp(&s.ready[stage], (j / kStages) & 1);
                 if (!ok) break;
                 tc_fence_after();
-                issue_product<D>(tmem + G::kColS, tmem + G::kColA1, b1_desc + row_stage * stage, nullptr);
-                if (lane == 0) RK_BTRACE(j, 4);
-                issue_product<D>(tmem + G::kColDP, tmem + G::kColA2, b2_desc + row_stage * stage, &s.s_full);
+                if constexpr (C::kRowOperandsInSmem) {
+                    issue_product_smem<D>(tmem + C::kS, sw128_descriptor(smem_u32(s.a.a1)), b1_desc + row_stage * stage, nullptr);
+                    if (lane == 0) RK_BTRACE(j, 4);
+                    issue_product_smem<D>(tmem + C::kDP, sw128_descriptor(smem_u32(s.a.a2)), b2_desc + row_stage * stage, &s.s_full);
+                } else {
+                    issue_product<D>(tmem + C::kS, tmem + C::kA1, b1_desc + row_stage * stage, nullptr);
+                    if (lane == 0) RK_BTRACE(j, 4);
+                    issue_product<D>(tmem + C::kDP, tmem + C::kA2, b2_desc + row_stage * stage, &s.s_full);
+                }
                 ok = mbar_wait_warp(&s.p_full, j & 1);
                 if (lane == 0) RK_BTRACE(j, 5);
                 if (!ok) break;
                 tc_fence_after();
                 if constexpr (kKeyRows) {
-                    const uint64_t t1_desc = sw128_descriptor(smem_u32(s.t.t1[stage]));
-                    const uint64_t t2_desc = sw128_descriptor(smem_u32(s.t.t2[stage]));
-                    issue_x<D>(tmem + G::kColX1, tmem + G::kColDP, t1_desc, nullptr);
-                    issue_x<D>(tmem + G::kColX2, tmem + G::kColS, t2_desc, &s.x_done);
+                    issue_x<D>(tmem + C::kX1, tmem + C::kDP, b1_mn_desc + row_stage * stage, nullptr);
+                    issue_x<D>(tmem + C::kX2, tmem + C::kS, b2_mn_desc + row_stage * stage, &s.x_done);
                 } else {
-                    issue_x_mn<D>(tmem + G::kColX1, tmem + G::kColDP, b1_mn_desc + row_stage * stage, &s.x_done);
+                    issue_x<D>(tmem + C::kX1, tmem + C::kDP, b1_mn_desc + row_stage * stage, &s.x_done);
                 }
                 mma_commit_warp(&s.empty[stage]);
             }
@@ -554,7 +540,10 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
 #pragma unroll
                 for (int c = 0; c < D; ++c) row_l1 += fabsf(x[c]);
                 ea2 = fp16_scale_exponent(abs_max<D>(x));
-                store_row_operand<D>(x, ea2, lanes + G::kColA2);
+                if constexpr (C::kRowOperandsInSmem)
+                    store_row_operand_smem<D>(x, ea2, s.a.a2, r);
+                else
+                    store_row_operand<D>(x, ea2, lanes + C::kA2);
                 load_row<D>(p.k.row(b, h, row_valid ? row : 0), row_active, 1.f, x);
             } else {
                 const float maximum = row_valid ? p.lse_in[(query_base + row) * 2] : -INFINITY;
@@ -577,11 +566,16 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
                 row_delta = delta;
                 if (row_valid) p.delta[query_base + row] = delta;
                 ea2 = fp16_scale_exponent(abs_max<D>(x));
-                store_row_operand<D>(x, ea2, lanes + G::kColA2);
+                store_row_operand<D>(x, ea2, lanes + C::kA2);
                 load_row<D>(p.q.row(b, h, row_valid ? row : 0), row_valid, p.scale, x);
             }
             ea1 = fp16_scale_exponent(abs_max<D>(x));
-            store_row_operand<D>(x, ea1, lanes + G::kColA1);
+            if constexpr (C::kRowOperandsInSmem) {
+                store_row_operand_smem<D>(x, ea1, s.a.a1, r);
+                fence_proxy_async_shared();  // the stores, visible to the MMAs' shared-memory reads
+            } else {
+                store_row_operand<D>(x, ea1, lanes + C::kA1);
+            }
             tc_fence_before();
             mbar_arrive(&s.rows_ready);
         }
@@ -619,7 +613,7 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
 #pragma unroll 1
             for (int chunk = 0; chunk < 4; ++chunk) {  // rolled: keeps one chunk's values live
                 float sv[16], dv[16];  // scores, then P'; dP, then dS'
-                tmem_load16x2(lanes + G::kColS + 16 * chunk, sv, lanes + G::kColDP + 16 * chunk, dv);
+                tmem_load16x2(lanes + C::kS + 16 * chunk, sv, lanes + C::kDP + 16 * chunk, dv);
                 // key rows, d = 32: the chunk's 16 query statistics with 16-byte loads (d = 64 keeps
                 // scalar loads: its key-rows kernel is at the register limit)
                 float col_offset[16], col_delta[16];
@@ -643,8 +637,8 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
                     sv[c] = pv;
                     dv[c] = pv * fmaf(dv[c], w_scale, -delta * to_ds);
                 }
-                store_split_chunk(lanes + G::kColDP + 16 * chunk, dv);
-                if (kKeyRows) store_split_chunk(lanes + G::kColS + 16 * chunk, sv);
+                store_split_chunk(lanes + C::kDP + 16 * chunk, dv);
+                if (kKeyRows) store_split_chunk(lanes + C::kS + 16 * chunk, sv);
             }
             if (lane == 0 && warp == 0) RK_BTRACE(j, 11);
             // Fold the previous tile's X before the P(j)/dS(j) arrival lets the MMA warp

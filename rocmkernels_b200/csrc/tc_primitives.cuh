@@ -377,6 +377,51 @@ __device__ __forceinline__ void mma2_f16_ts_warp(uint32_t d, uint32_t a0, uint32
             : "memory");
 }
 
+// Warp-collective: four kind::f16 MMAs with A from shared memory (descriptors `a`) into one
+// accumulator, the first overwriting it when `overwrite` is set (no commit).
+__device__ __forceinline__ void mma4_f16_ss_warp(uint32_t d, const uint64_t (&a)[4], const uint64_t (&b)[4], uint32_t idesc,
+                                                 uint32_t overwrite) {
+    asm volatile(
+            "{\n\t.reg .pred e, first, rest;\n\t"
+            "elect.sync _|e, 0xffffffff;\n\t"
+            "setp.eq.b32 first, %10, 0;\n\t"
+            "setp.eq.b32 rest, %10, %10;\n\t"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %5, %9, first;\n\t"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %2, %6, %9, rest;\n\t"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %3, %7, %9, rest;\n\t"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %4, %8, %9, rest;\n\t}" ::"r"(d),
+            "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "r"(idesc),
+            "r"(overwrite)
+            : "memory");
+}
+
+// Warp-collective: two accumulating kind::f16 MMAs with A from shared memory (no commit).
+__device__ __forceinline__ void mma2_f16_ss_warp(uint32_t d, const uint64_t (&a)[2], const uint64_t (&b)[2], uint32_t idesc) {
+    asm volatile(
+            "{\n\t.reg .pred e, rest;\n\t"
+            "elect.sync _|e, 0xffffffff;\n\t"
+            "setp.eq.b32 rest, %5, %5;\n\t"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %3, %5, rest;\n\t"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %2, %4, %5, rest;\n\t}" ::"r"(d),
+            "l"(a[0]), "l"(a[1]), "l"(b[0]), "l"(b[1]), "r"(idesc)
+            : "memory");
+}
+
+// Warp-collective: two accumulating kind::f16 MMAs with A from shared memory and a commit to
+// `bar`, one elected sequence.
+__device__ __forceinline__ void mma2_f16_ss_commit_warp(uint32_t d, const uint64_t (&a)[2], const uint64_t (&b)[2], uint32_t idesc,
+                                                        uint64_t *bar) {
+    asm volatile(
+            "{\n\t.reg .pred e, rest;\n\t"
+            "elect.sync _|e, 0xffffffff;\n\t"
+            "setp.eq.b32 rest, %5, %5;\n\t"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %3, %5, rest;\n\t"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %2, %4, %5, rest;\n\t"
+            "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%6];\n\t}" ::"r"(d),
+            "l"(a[0]), "l"(a[1]), "l"(b[0]), "l"(b[1]), "r"(idesc), "r"(smem_u32(bar))
+            : "memory");
+}
+
 // Bounded wait by every lane of a warp; true only if every lane saw the phase complete.
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity) {
     return __all_sync(0xffffffffu, mbar_wait(bar, parity));
