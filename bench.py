@@ -31,7 +31,10 @@ taken with an all-reduce. FLOPs follow the reference's convention (4*B*H*Q*K*d f
 8*B*H*Q*K*d backward, AttentionBenchmarks.cpp:141-142).
 
 Also reported: ``e2e`` (the same step through the public C entry points with pinned host
-buffers: H2D of the inputs and D2H of the outputs inside the timed region), ``roofline`` of the
+buffers: every step copies all its inputs in and all its outputs back inside the timed region,
+pipelined as a serving loop runs it -- step i's H2D copies, kernels and D2H copies on a copy-in,
+a compute and a copy-out stream, overlapping the neighbouring steps, with two device buffer sets
+alternating; the time runs from the first H2D to the last D2H), ``roofline`` of the
 dominant kernel, ``cpu_baseline`` (rank 0, N=1: the CPU oracle timed on this box's host cores),
 ``clocks`` sampled with nvidia-smi during the timed region, and ``gpu_launches``.
 
@@ -342,22 +345,24 @@ def run_rotary(args, spec: dict, device, world: int, rank: int, dist) -> None:
     stream = torch.cuda.current_stream(device)
     flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=device)
 
-    def step():
-        status = api.rotary_fp32(q, k, cos, sin, oq, ok, batch, heads, length, backward, qk_strides, qk_strides, table_strides,
-                                 table_strides, stream)
+    def run(tensors, st):
+        tq, tk, tcos, tsin, toq, tok = tensors
+        status = api.rotary_fp32(tq, tk, tcos, tsin, toq, tok, batch, heads, length, backward, qk_strides, qk_strides,
+                                 table_strides, table_strides, st)
         if status != 0:
             raise api.HipError(status, "rotary_fp32")
+
+    def step():
+        run((q, k, cos, sin, oq, ok), stream)
 
     inputs, outputs = [q, k, cos, sin], [oq, ok]
     host_inputs = [t.cpu().pin_memory() for t in inputs]
     host_outputs = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in outputs]
+    e2e_sets = [(inputs, outputs), ([torch.empty_like(t) for t in inputs], [torch.empty_like(t) for t in outputs])]
 
-    def step_e2e():
-        for device_tensor, host_tensor in zip(inputs, host_inputs):
-            device_tensor.copy_(host_tensor, non_blocking=True)
-        step()
-        for host_tensor, device_tensor in zip(host_outputs, outputs):
-            host_tensor.copy_(device_tensor, non_blocking=True)
+    def launch_set(index, st):
+        set_inputs, set_outputs = e2e_sets[index]
+        run((*set_inputs, *set_outputs), st)
 
     def timed(fn, steps):
         marks = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
@@ -384,10 +389,9 @@ def run_rotary(args, spec: dict, device, world: int, rank: int, dist) -> None:
     if world > 1:
         dist.barrier()
     clocks = sampler.stop() if rank == 0 else None
-    for _ in range(max(1, args.warmup // 2)):
-        step_e2e()
+    pipelined_e2e(device, e2e_sets, host_inputs, host_outputs, launch_set, 2)
     e2e_steps = max(1, min(args.steps, 50))
-    e2e_seconds = timed(step_e2e, e2e_steps)
+    e2e_seconds = pipelined_e2e(device, e2e_sets, host_inputs, host_outputs, launch_set, e2e_steps)
     times = torch.tensor([seconds, e2e_seconds], device=device, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
@@ -436,6 +440,44 @@ def run_reference_generic(args, spec: dict) -> None:
             "cpu_baseline": base,
             "e2e": {"value": base["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def pipelined_e2e(device, sets, host_inputs, host_outputs, launch, steps: int) -> float:
+    """Seconds for `steps` end-to-end steps: step i copies `host_inputs` (pinned) into the device
+    inputs of buffer set i % 2 (copy-in stream), runs `launch(set, stream)` on the compute stream
+    and copies the set's outputs back into `host_outputs` (pinned, copy-out stream). A set's inputs
+    are refilled only after the kernels that read them finished, and its outputs rewritten only
+    after their read-back, so step i's copies overlap steps i - 1 and i + 1. Timed with events
+    from the first H2D to the last D2H."""
+    import torch
+
+    copy_in, compute, copy_out = (torch.cuda.Stream(device=device) for _ in range(3))
+    loaded, computed, unloaded = ([torch.cuda.Event() for _ in sets] for _ in range(3))
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(device)
+    start.record(copy_in)
+    for i in range(steps):
+        s = i % len(sets)
+        device_inputs, device_outputs = sets[s]
+        if i >= len(sets):
+            copy_in.wait_event(computed[s])
+        with torch.cuda.stream(copy_in):
+            for device_tensor, host_tensor in zip(device_inputs, host_inputs):
+                device_tensor.copy_(host_tensor, non_blocking=True)
+        loaded[s].record(copy_in)
+        compute.wait_event(loaded[s])
+        if i >= len(sets):
+            compute.wait_event(unloaded[s])
+        launch(s, compute)
+        computed[s].record(compute)
+        copy_out.wait_event(computed[s])
+        with torch.cuda.stream(copy_out):
+            for host_tensor, device_tensor in zip(host_outputs, device_outputs):
+                host_tensor.copy_(device_tensor, non_blocking=True)
+        unloaded[s].record(copy_out)
+    end.record(copy_out)
+    torch.cuda.synchronize(device)
+    return start.elapsed_time(end) / 1e3
 
 
 def traffic_from_profiles(kernel_tag: str):
@@ -543,28 +585,42 @@ def main() -> None:
     effective_per_step = effective_forward + (effective_backward if with_backward else 0.0)
     launches_per_step = 1 + (2 if with_backward else 0)
 
-    def forward():
-        if rotary:
-            status = api.attention_fp32_forward_flash_rotary(q, k, v, cos, sin, mask, out, lse, batch, heads, seq, seq, radius,
-                                                             qs, ks, vs, table_strides, table_strides, os_, stream)
+    # The step's device tensors by name (one set for the device-timed steps; the e2e leg uses two).
+    tensors = dict(q=q, k=k, v=v, mask=mask, out=out, lse=lse)
+    if rotary:
+        tensors.update(cos=cos, sin=sin)
+    if with_backward:
+        tensors.update(upstream=upstream, gq=gq, gk=gk, gv=gv, delta=delta)
+
+    def make_phases(t, st):
+        """The step's kernel calls on tensor set `t`, launched on stream `st`."""
+        def forward():
+            if rotary:
+                status = api.attention_fp32_forward_flash_rotary(t["q"], t["k"], t["v"], t["cos"], t["sin"], t["mask"], t["out"],
+                                                                 t["lse"], batch, heads, seq, seq, radius, qs, ks, vs, table_strides,
+                                                                 table_strides, os_, st)
+                if status != 0:
+                    raise api.HipError(status, "attention_fp32_forward_flash_rotary")
+                return
+            if generic:
+                status = api.attention_generic_forward(t["q"], t["k"], t["v"], t["mask"], t["out"], t["lse"], batch, heads, seq, seq,
+                                                       dim, radius, qs, ks, vs, os_,
+                                                       api.DType.Float16 if generic == "fp16" else api.DType.Float32, st)
+            else:
+                status = forward_fn(t["q"], t["k"], t["v"], t["mask"], t["out"], t["lse"], batch, heads, seq, seq, radius, qs, ks, vs,
+                                    os_, st)
             if status != 0:
-                raise api.HipError(status, "attention_fp32_forward_flash_rotary")
-            return
-        if generic:
-            status = api.attention_generic_forward(q, k, v, mask, out, lse, batch, heads, seq, seq, dim, radius, qs, ks, vs, os_,
-                                                   api.DType.Float16 if generic == "fp16" else api.DType.Float32, stream)
-        else:
-            status = forward_fn(q, k, v, mask, out, lse, batch, heads, seq, seq, radius, qs, ks, vs, os_, stream)
-        if status != 0:
-            raise api.HipError(status, "attention_generic_forward" if generic else forward_fn.__name__)
+                raise api.HipError(status, "attention_generic_forward" if generic else forward_fn.__name__)
 
-    def backward():
-        status = backward_fn(q, k, v, mask, out, lse, upstream, gq, gk, gv, delta, batch, heads, seq, seq, radius, qs, ks, vs, os_,
-                             api.strides_of(upstream), stream)
-        if status != 0:
-            raise api.HipError(status, backward_fn.__name__)
+        def backward():
+            status = backward_fn(t["q"], t["k"], t["v"], t["mask"], t["out"], t["lse"], t["upstream"], t["gq"], t["gk"], t["gv"],
+                                 t["delta"], batch, heads, seq, seq, radius, qs, ks, vs, os_, api.strides_of(t["upstream"]), st)
+            if status != 0:
+                raise api.HipError(status, backward_fn.__name__)
 
-    phases = [forward, backward] if with_backward else [forward]
+        return [forward, backward] if with_backward else [forward]
+
+    phases = make_phases(tensors, stream)
 
     def unfused_rotary_forward():
         """rotary_fp32 into token-major buffers, then the flash forward on them (the unfused sequence)."""
@@ -577,19 +633,19 @@ def main() -> None:
         if status != 0:
             raise api.HipError(status, "rotary_fp32 + attention_fp32_forward_flash")
 
-    # Host-buffer leg: pinned inputs copied in and outputs copied out every step.
+    # Host-buffer leg: pinned inputs copied in and outputs copied out every step, two device sets.
     host_inputs = [t.cpu().pin_memory() for t in inputs]
     host_outputs = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in outputs]
     h2d_bytes = sum(t.numel() * t.element_size() for t in host_inputs)
     d2h_bytes = sum(t.numel() * t.element_size() for t in host_outputs)
+    second = {name: torch.empty_like(t) for name, t in tensors.items()}
+    by_id = {id(t): name for name, t in tensors.items()}
+    e2e_tensors = [tensors, second]
+    e2e_sets = [([t[by_id[id(x)]] for x in inputs], [t[by_id[id(x)]] for x in outputs]) for t in e2e_tensors]
 
-    def step_e2e():
-        for device_tensor, host_tensor in zip(inputs, host_inputs):
-            device_tensor.copy_(host_tensor, non_blocking=True)
-        for phase in phases:
+    def launch_set(index, st):
+        for phase in make_phases(e2e_tensors[index], st):
             phase()
-        for host_tensor, device_tensor in zip(host_outputs, outputs):
-            host_tensor.copy_(device_tensor, non_blocking=True)
 
     def timed(fns, steps):
         """Seconds summed over `steps`: in total and per callable of `fns` (events between them)."""
@@ -624,11 +680,9 @@ def main() -> None:
         dist.barrier()
     clocks = sampler.stop() if rank == 0 else None
 
-    for _ in range(max(1, args.warmup // 2)):
-        step_e2e()
-    torch.cuda.synchronize(device)
+    pipelined_e2e(device, e2e_sets, host_inputs, host_outputs, launch_set, 2)
     e2e_steps = max(1, min(args.steps, 50))
-    e2e_seconds, _ = timed([step_e2e], e2e_steps)
+    e2e_seconds = pipelined_e2e(device, e2e_sets, host_inputs, host_outputs, launch_set, e2e_steps)
 
     unfused_seconds = 0.0
     if rotary:
