@@ -107,6 +107,12 @@ struct Forward {
     static constexpr int kProducerWarp = kSoftmaxWarps, kMmaWarp = kSoftmaxWarps + 1, kSplitWarp = kSoftmaxWarps + 2;
     static constexpr int kThreads = 32 * (kSoftmaxWarps + 4);
     static constexpr int kSplitThreads = 64;
+    // d = 64: the raw K/V stage is refilled as soon as the split warps have read it into registers
+    // (their conversion then waits for the MMAs to release the converted stage). Measured on B200:
+    // d = 64 171 -> 164 us (B8 H6 S1024); d = 32 slower (36.9 -> 39.9 us at B8 H3 S1024, 608 -> 674
+    // at B4 H12 S4096: the two d = 32 split warps then run inside the softmax warps' busy phase on
+    // the two sub-partitions they share), so d = 32 refills a stage after its MMAs finished.
+    static constexpr bool kEarlyRawRefill = !kHalf && D == 64;
     static constexpr int kBoxes = kHalf ? 1 : D / 32;        // TMA boxes of 64 rows x 128 bytes per raw tile
     static constexpr int kRawFloats = kBoxes * kBoxFloats;  // raw tile of 64 keys in 32-bit words
     static constexpr int kKWords = kHalf ? 0 : 64 * D;       // row layout [k0 | k1] of 64 keys (FP16: the raw tile)
@@ -138,6 +144,7 @@ struct alignas(1024) SharedStorage {
     float split_max[2][2];                     // per split warp: max |K|, max |V| of its rows
     int split_ok[2];                           // per split warp: its kv_full wait succeeded
     uint64_t kv_full[F::kStages];              // TMA bytes landed
+    uint64_t raw_free[F::kStages];             // kEarlyRawRefill: the raw tiles read by the split warps (64 arrivals)
     uint64_t kv_ready[F::kStages];             // conversion done (64 arrivals)
     uint64_t kv_empty[F::kStages];             // MMAs reading the stage finished (commit)
     uint64_t s_full[F::kQTiles][2];            // S of a buffer is in TMEM (commit)
@@ -452,6 +459,7 @@ __global__ void __launch_bounds__(Forward<D, kHalf>::kThreads, 1)
     if (threadIdx.x == F::kProducerWarp * 32) {
         for (int i = 0; i < kStages; ++i) {
             mbar_init(&s.kv_full[i], 1);
+            mbar_init(&s.raw_free[i], F::kSplitThreads);
             mbar_init(&s.kv_ready[i], F::kSplitThreads);
             mbar_init(&s.kv_empty[i], 1);
         }
@@ -486,7 +494,10 @@ __global__ void __launch_bounds__(Forward<D, kHalf>::kThreads, 1)
             bool ok = true;
             for (int j = prefetched; j < tiles && ok; ++j) {
                 const int stage = j % kStages, use = j / kStages;
-                ok = mbar_wait(&s.kv_empty[stage], (use - 1) & 1);  // j >= kStages here
+                // j >= kStages here. kEarlyRawRefill: the raw stage is free once the split warps
+                // have read tile j - kStages into registers (the MMAs read only the converted
+                // tiles); otherwise once the MMAs reading the stage finished.
+                ok = mbar_wait(F::kEarlyRawRefill ? &s.raw_free[stage] : &s.kv_empty[stage], (use - 1) & 1);
                 if (!ok) break;
                 issue_tile(j);
                 ++issued;
@@ -619,15 +630,21 @@ __global__ void __launch_bounds__(Forward<D, kHalf>::kThreads, 1)
                                 fmaxf(fabsf(vx[item][r].z), fabsf(vx[item][r].w)));
                 }
             }
+            // Everything of the raw stage is in registers now: the producer may refill it.
+            if constexpr (F::kEarlyRawRefill) mbar_arrive(&s.raw_free[stage]);
 #pragma unroll
             for (int offset = 16; offset; offset >>= 1) {
                 kmax = fmaxf(kmax, __shfl_xor_sync(0xffffffffu, kmax, offset));
                 vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, offset));
             }
+            // The converted stage (and the stage's mask and exponents, which the softmax threads
+            // read for tile j - kStages) is rewritten only after the MMAs of that tile finished.
+            const bool stage_free = !F::kEarlyRawRefill || j < kStages ||
+                                    __all_sync(0xffffffffu, mbar_wait(&s.kv_empty[stage], ((j / kStages) - 1) & 1));
             if (lane == 0) {
                 s.split_max[w][0] = kmax;
                 s.split_max[w][1] = vmax;
-                s.split_ok[w] = landed;
+                s.split_ok[w] = landed && stage_free;
                 s.key_mask[stage][w] = bits;
             }
             asm volatile("bar.sync 1, 64;" ::: "memory");
