@@ -128,6 +128,7 @@ struct alignas(1024) Storage {
     float split_max[2][2][3];                              // [tile parity][split warp]: max|raw1|, max|raw2|, max|delta|
     int split_ok[2][2];                                    // [tile parity][split warp]: its TMA wait succeeded
     uint64_t full[kStages];                                // TMA bytes landed
+    uint64_t raw_free[kStages];                            // raw tiles converted: TMA may refill (64 arrivals)
     uint64_t ready[kStages];                               // conversion done (64 arrivals)
     uint64_t empty[kStages];                               // MMAs reading the stage finished (commit)
     uint64_t s_full;                                       // S and dP in TMEM (commit)
@@ -366,6 +367,7 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
     if (threadIdx.x == kProducerWarp * 32) {
         for (int i = 0; i < kStages; ++i) {
             mbar_init(&s.full[i], 1);
+            mbar_init(&s.raw_free[i], kSplitThreads);
             mbar_init(&s.ready[i], kSplitThreads);
             mbar_init(&s.empty[i], 1);
         }
@@ -388,7 +390,9 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
             bool ok = true;
             for (int j = 0; j < tiles && ok; ++j) {
                 const int stage = j % kStages;
-                if (j >= kStages) ok = mbar_wait(&s.empty[stage], ((j / kStages) - 1) & 1);
+                // The raw stage is refilled as soon as the split warps have converted it (the MMAs
+                // read only the converted layouts).
+                if (j >= kStages) ok = mbar_wait(&s.raw_free[stage], ((j / kStages) - 1) & 1);
                 if (!ok) break;
                 RK_BTRACE(j, 0);
                 mbar_arrive_expect_tx(&s.full[stage], 2 * G::kBoxes * kBoxBytes);
@@ -473,11 +477,10 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
             const bool landed = __all_sync(0xffffffffu, mbar_wait(&s.full[stage], (j / kStages) & 1));
             if (lane == 0) RK_BTRACE(j, 1 + w);
             bool visible;
-            float delta_abs = 0.f;
+            float delta_abs = 0.f, col_offset = -INFINITY;
             if (kKeyRows) {  // column = query: visible if it exists and has a finite row max
                 visible = flag && maximum != -INFINITY;
-                s.col_offset[stage][row] = visible ? 14.f - maximum * kLog2e - __log2f(total) : -INFINITY;
-                s.col_delta[stage][row] = delta;
+                col_offset = visible ? 14.f - maximum * kLog2e - __log2f(total) : -INFINITY;
                 delta_abs = visible ? fabsf(delta) : 0.f;
             } else {  // column = key: visible if it exists and is not masked
                 visible = flag;
@@ -501,11 +504,18 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
                 max2 = fmaxf(max2, __shfl_xor_sync(0xffffffffu, max2, offset));
                 delta_abs = fmaxf(delta_abs, __shfl_xor_sync(0xffffffffu, delta_abs, offset));
             }
+            // The stage's statistics and converted layouts (read by the row warps and the MMAs
+            // for tile j - kStages) are rewritten only after those MMAs finished.
+            const bool stage_free = j < kStages || __all_sync(0xffffffffu, mbar_wait(&s.empty[stage], ((j / kStages) - 1) & 1));
+            if (kKeyRows) {
+                s.col_offset[stage][row] = col_offset;
+                s.col_delta[stage][row] = delta;
+            }
             if (lane == 0) {
                 s.split_max[parity][w][0] = max1;
                 s.split_max[parity][w][1] = max2;
                 s.split_max[parity][w][2] = delta_abs;
-                s.split_ok[parity][w] = landed;
+                s.split_ok[parity][w] = landed && stage_free;
                 s.col_mask[stage][w] = bits;
             }
             // One barrier per tile: the maxima are double-buffered by tile parity.
@@ -519,6 +529,7 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
                 s.col_delta_max[stage] = fmaxf(s.split_max[parity][0][2], s.split_max[parity][1][2]);
             }
             convert_stage<D, kKeyRows>(s, stage, w, lane, keep_row, exp2_int(e1) * scale1, exp2_int(e2));
+            mbar_arrive(&s.raw_free[stage]);
             fence_proxy_async_shared();
             if (lane == 0) RK_BTRACE(j, 3 + w);
             mbar_arrive(&s.ready[stage]);
