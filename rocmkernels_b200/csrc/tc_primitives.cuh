@@ -449,6 +449,45 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
     return packed;
 }
 
+// Packed FP32 pairs (sm_100 f32x2 instructions: one issue for two lanes of work, IEEE results
+// identical to the scalar forms).
+__device__ __forceinline__ float2 fma_f32x2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n\t.reg .b64 x, y, z, w;\n\t"
+        "mov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\tmov.b64 z, {%6, %7};\n\t"
+        "fma.rn.f32x2 w, x, y, z;\n\tmov.b64 {%0, %1}, w;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+__device__ __forceinline__ float2 add_f32x2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 x, y, w;\n\t"
+        "mov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\t"
+        "add.rn.f32x2 w, x, y;\n\tmov.b64 {%0, %1}, w;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+__device__ __forceinline__ float2 mul_f32x2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 x, y, w;\n\t"
+        "mov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\t"
+        "mul.rn.f32x2 w, x, y;\n\tmov.b64 {%0, %1}, w;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+__device__ __forceinline__ float2 sub_f32x2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 x, y, w;\n\t"
+        "mov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\t"
+        "sub.rn.f32x2 w, x, y;\n\tmov.b64 {%0, %1}, w;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+
 // max(a, b, c) in one instruction (sm_100 three-input max; NaN operands are ignored like fmaxf).
 __device__ __forceinline__ float max3(float a, float b, float c) {
     float r;
