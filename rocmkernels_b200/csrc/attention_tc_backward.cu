@@ -259,8 +259,9 @@ __device__ __forceinline__ void store_split_chunk(uint32_t chunk, const float (&
     for (int c = 0; c < 8; ++c) {
         const float x0 = __uint_as_float(__float_as_uint(v[2 * c]) & 0xFFFFE000u);
         const float y0 = __uint_as_float(__float_as_uint(v[2 * c + 1]) & 0xFFFFE000u);
+        const float2 residual = sub_f32x2(make_float2(v[2 * c], v[2 * c + 1]), make_float2(x0, y0));
         q0[c] = __uint_as_float(pack_half2(x0, y0));
-        q1[c] = __uint_as_float(pack_half2(v[2 * c] - x0, v[2 * c + 1] - y0));
+        q1[c] = __uint_as_float(pack_half2(residual.x, residual.y));
     }
     tmem_store8x2_async(chunk, q0, chunk + 8, q1);
 }
@@ -294,13 +295,24 @@ __device__ __forceinline__ void fold_x(float (&acc1)[D], float (&acc2)[kKeyRows 
 #pragma unroll
     for (int quarter = 0; quarter < D / 8; ++quarter) {
         float xa[8], xb[8];
+        const float2 s1 = make_float2(scale1, scale1), s2 = make_float2(scale2, scale2);
         tmem_load8x2(lanes + C::kX1 + 8 * quarter, xa, lanes + C::kX1 + D + 8 * quarter, xb);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) acc1[8 * quarter + c] = fmaf(xa[c] + xb[c], scale1, acc1[8 * quarter + c]);
+        for (int c = 0; c < 8; c += 2) {
+            float *a = &acc1[8 * quarter + c];
+            const float2 r = fma_f32x2(add_f32x2(make_float2(xa[c], xa[c + 1]), make_float2(xb[c], xb[c + 1])), s1, make_float2(a[0], a[1]));
+            a[0] = r.x;
+            a[1] = r.y;
+        }
         if constexpr (kKeyRows) {
             tmem_load8x2(lanes + C::kX2 + 8 * quarter, xa, lanes + C::kX2 + D + 8 * quarter, xb);
 #pragma unroll
-            for (int c = 0; c < 8; ++c) acc2[8 * quarter + c] = fmaf(xa[c] + xb[c], scale2, acc2[8 * quarter + c]);
+            for (int c = 0; c < 8; c += 2) {
+                float *a = &acc2[8 * quarter + c];
+                const float2 r = fma_f32x2(add_f32x2(make_float2(xa[c], xa[c + 1]), make_float2(xb[c], xb[c + 1])), s2, make_float2(a[0], a[1]));
+                a[0] = r.x;
+                a[1] = r.y;
+            }
         }
     }
 }
@@ -638,15 +650,49 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
                         col_delta[4 * i] = d.x, col_delta[4 * i + 1] = d.y, col_delta[4 * i + 2] = d.z, col_delta[4 * i + 3] = d.w;
                     }
                 }
+                // Column pairs as packed FP32 pairs (fma/mul .f32x2), except in the d = 32
+                // key-rows kernel, whose 128 registers a thread cannot hold the pairs.
+                if constexpr (kKeyRows && D == 32) {
 #pragma unroll
-                for (int c = 0; c < 16; ++c) {
-                    const int col = 16 * chunk + c;
-                    const float offset = !kKeyRows ? row_offset : D == 32 ? col_offset[c] : s.col_offset[stage][col];
-                    const float delta = !kKeyRows ? row_delta : D == 32 ? col_delta[c] : s.col_delta[stage][col];
-                    float pv = fast_exp2(fmaf(sv[c], slope, offset));
-                    if (!all_active) pv = (active >> col) & 1 ? pv : 0.f;
-                    sv[c] = pv;
-                    dv[c] = pv * fmaf(dv[c], w_scale, -delta * to_ds);
+                    for (int c = 0; c < 16; ++c) {
+                        const int col = 16 * chunk + c;
+                        const float offset = !kKeyRows ? row_offset : D == 32 ? col_offset[c] : s.col_offset[stage][col];
+                        const float delta = !kKeyRows ? row_delta : D == 32 ? col_delta[c] : s.col_delta[stage][col];
+                        float pv = fast_exp2(fmaf(sv[c], slope, offset));
+                        if (!all_active) pv = (active >> col) & 1 ? pv : 0.f;
+                        sv[c] = pv;
+                        dv[c] = pv * fmaf(dv[c], w_scale, -delta * to_ds);
+                    }
+                } else {
+#pragma unroll
+                    for (int c = 0; c < 16; c += 2) {  // column pairs as packed FP32 pairs
+                        const int col = 16 * chunk + c;
+                        float2 offset, delta;
+                        if constexpr (!kKeyRows) {
+                            offset = make_float2(row_offset, row_offset);
+                            delta = make_float2(row_delta, row_delta);
+                        } else if constexpr (D == 32) {
+                            offset = make_float2(col_offset[c], col_offset[c + 1]);
+                            delta = make_float2(col_delta[c], col_delta[c + 1]);
+                        } else {
+                            offset = make_float2(s.col_offset[stage][col], s.col_offset[stage][col + 1]);
+                            delta = make_float2(s.col_delta[stage][col], s.col_delta[stage][col + 1]);
+                        }
+                        const float2 arg = fma_f32x2(make_float2(sv[c], sv[c + 1]), make_float2(slope, slope), offset);
+                        float pa = fast_exp2(arg.x), pb = fast_exp2(arg.y);
+                        if (!all_active) {
+                            pa = (active >> col) & 1 ? pa : 0.f;
+                            pb = (active >> (col + 1)) & 1 ? pb : 0.f;
+                        }
+                        sv[c] = pa;
+                        sv[c + 1] = pb;
+                        // dS' = P' (dP w - delta to_ds)
+                        const float2 shifted = fma_f32x2(make_float2(dv[c], dv[c + 1]), make_float2(w_scale, w_scale),
+                                                         mul_f32x2(delta, make_float2(-to_ds, -to_ds)));
+                        const float2 ds = mul_f32x2(make_float2(pa, pb), shifted);
+                        dv[c] = ds.x;
+                        dv[c + 1] = ds.y;
+                    }
                 }
                 store_split_chunk(lanes + C::kDP + 16 * chunk, dv);
                 if (kKeyRows) store_split_chunk(lanes + C::kS + 16 * chunk, sv);
