@@ -5,9 +5,11 @@
 //   (128 bytes per row, 128B swizzle: 16-byte chunk c of row r at r * 8 + (c ^ (r % 8))).
 //   Row layout (K-major B operand over the features): row r holds x0 (D FP16) and x1 (D FP16);
 //   for D = 32 both halves share one 128-byte row ([x0 | x1]), for D = 64 x0 and x1 are separate
-//   64 x 128-byte tiles. 128B swizzle.
-//   Transposed layout (K-major B operand over the 64 rows): feature rows f (x0) and D + f (x1),
-//   each 64 FP16 (128 bytes), rows 8g..8g+7 of the source tile in 16-byte chunk g. 128B swizzle.
+//   64 x 128-byte tiles. 128B swizzle. Read MN-major it is also the B operand over the 64 rows
+//   (each row one K index, [x0 | x1] its 2D MN elements): the backward's X products.
+//   Transposed layout (K-major B operand over the 64 rows, the forward's V): feature rows f (x0)
+//   and D + f (x1), each 64 FP16 (128 bytes), rows 8g..8g+7 of the source tile in 16-byte chunk
+//   g. 128B swizzle.
 #pragma once
 
 #include "tc_primitives.cuh"
