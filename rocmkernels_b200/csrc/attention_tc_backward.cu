@@ -98,6 +98,7 @@ struct Columns {
     static constexpr uint32_t kA1 = 0, kA2 = D;
     static constexpr uint32_t kS = kRowOperandsInSmem ? 0 : 2 * D, kDP = kS + 64, kX1 = kS + 128, kX2 = kX1 + 2 * D;
     static_assert((kKeyRows ? kX2 : kX1) + 2 * D <= Geometry<D>::kTmemColumns, "TMEM budget");
+    static_assert(kRowOperandsInSmem || (kA1 + D <= kA2 && kA2 + D <= kS), "row operands below S");
 };
 
 // Split FP16 row operands in shared memory (the d = 32 key-rows pass): K and V rows as
