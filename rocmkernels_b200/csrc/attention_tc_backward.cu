@@ -336,8 +336,7 @@ __device__ __forceinline__ void convert_stage(Storage<D, kKeyRows> &s, int stage
             if (!keep_row) lo = hi = make_float4(0.f, 0.f, 0.f, 0.f);
             const float x[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
             float x0[8], x1[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) split_half(x[e], scale, x0[e], x1[e]);
+            split_half8(x, scale, x0, x1);
             *row_chunk<D>(dst, row, 0, m) = pack_chunk(x0);
             *row_chunk<D>(dst, row, 1, m) = pack_chunk(x1);
         }

@@ -29,6 +29,21 @@ __device__ __forceinline__ void split_half(float x, float scale, float &x0, floa
     x1 = scaled - x0;
 }
 
+// split_half of eight values, the multiplications and subtractions as packed FP32 pairs (the same
+// results, half the issue slots).
+__device__ __forceinline__ void split_half8(const float (&x)[8], float scale, float (&x0)[8], float (&x1)[8]) {
+    const float2 scale2 = make_float2(scale, scale);
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+        const float2 scaled = mul_f32x2(make_float2(x[e], x[e + 1]), scale2);
+        x0[e] = round_tf32(scaled.x);
+        x0[e + 1] = round_tf32(scaled.y);
+        const float2 residual = sub_f32x2(scaled, make_float2(x0[e], x0[e + 1]));
+        x1[e] = residual.x;
+        x1[e + 1] = residual.y;
+    }
+}
+
 // 16-byte chunk `chunk` (features 4 chunk .. 4 chunk + 3) of row `row` of an FP32 tile.
 template <int D>
 __device__ __forceinline__ float4 raw_chunk(const float *tile, int row, int chunk) {
