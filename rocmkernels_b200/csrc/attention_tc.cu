@@ -151,6 +151,8 @@ struct alignas(1024) SharedStorage {
     uint64_t p_full[F::kQTiles];               // P of the current tile is in TMEM (128 arrivals)
     uint64_t pv_done[F::kQTiles];              // Ot of the current tile is in TMEM (commit)
     uint64_t q_ready;                          // q0/q1 of every Q tile in TMEM (128 arrivals per tile)
+    uint64_t range_ready;                      // tile_count written (1 arrival)
+    int tile_count;                            // key tiles up to the last visible key of the window
     uint64_t mma_done;                         // every MMA of the CTA finished (commit)
     uint32_t tmem_base;
 };
@@ -436,7 +438,9 @@ __global__ void __launch_bounds__(Forward<D, kHalf>::kThreads, 1)
     const int q0 = cta_tile * F::kCtaQueries;
     int first, last;
     key_window(q0, min(q0 + F::kCtaQueries, p.queries), p.keys, p.radius, first, last);
-    const int tiles = last > first ? (last - first + kKeyTile - 1) / kKeyTile : 0;
+    // Key tiles of the window; trailing tiles whose keys are all masked are dropped after the
+    // set-up barrier (visible_tiles below), so that key-padded sequences skip their padding.
+    const int window_tiles = last > first ? (last - first + kKeyTile - 1) / kKeyTile : 0;
 
     // The softmax threads issue the loads of their Q row (and, with the rotary prologue, of its
     // table rows) before the set-up barrier, so their latency overlaps the TMEM allocation and
@@ -483,7 +487,7 @@ __global__ void __launch_bounds__(Forward<D, kHalf>::kThreads, 1)
             tma_load_4d(s.v_raw[stage] + box * kBoxFloats, &tmap_v, &s.kv_full[stage], 32 * box, first + j * kKeyTile, h, b);
         }
     };
-    const int prefetched = min(tiles, kStages);  // issued before the set-up barrier
+    const int prefetched = min(window_tiles, kStages);  // issued before the set-up barrier
     if (threadIdx.x == F::kProducerWarp * 32) {
         for (int i = 0; i < kStages; ++i) {
             mbar_init(&s.kv_full[i], 1);
@@ -498,6 +502,7 @@ __global__ void __launch_bounds__(Forward<D, kHalf>::kThreads, 1)
             mbar_init(&s.pv_done[t], 1);
         }
         mbar_init(&s.q_ready, kQTile * F::kQTiles);
+        mbar_init(&s.range_ready, 1);
         mbar_init(&s.mma_done, 1);
         mbar_fence_init();
         // The first stages are free: their loads overlap the TMEM allocation and the set-up
@@ -514,10 +519,18 @@ __global__ void __launch_bounds__(Forward<D, kHalf>::kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = s.tmem_base;
+    // The window's tiles up to its last visible key (published by the producer warp).
+    const auto visible_tiles = [&]() { return mbar_wait(&s.range_ready, 0) ? s.tile_count : 0; };
 
     if (warp == F::kProducerWarp) {
         // ---------------------------------------------------------------- TMA producer
+        // The last visible key of the window: the mask read backwards 128 keys at a time (one
+        // step when the window's last keys are visible), while the first tiles' loads are in
+        // flight.
+        const int tiles = visible_tiles_of(p.mask + static_cast<long long>(b) * p.keys, first, last, lane);
         if (lane == 0) {
+            s.tile_count = tiles;
+            mbar_arrive(&s.range_ready);
             int issued = prefetched;
             bool ok = true;
             for (int j = prefetched; j < tiles && ok; ++j) {
@@ -535,6 +548,8 @@ __global__ void __launch_bounds__(Forward<D, kHalf>::kThreads, 1)
                 for (int j = max(0, issued - kStages); j < issued; ++j)
                     mbar_wait(&s.kv_full[j % kStages], (j / kStages) & 1);
             }
+            // Prefetched tiles past the last visible key are never converted: wait for them.
+            for (int j = tiles; j < prefetched; ++j) mbar_wait(&s.kv_full[j], 0);
         }
     } else if (warp == F::kMmaWarp) {
         // ---------------------------------------------------------------- MMA issuer
@@ -542,6 +557,7 @@ __global__ void __launch_bounds__(Forward<D, kHalf>::kThreads, 1)
         // first gets P(j).V and S(j + 2) (into the buffer P(j) occupied) issued first; the K/V
         // stage of tile j is released once every P.V product is issued. The whole warp runs
         // the loop (uniform control flow and descriptors); elected lanes issue the tcgen05 ops.
+        const int tiles = __shfl_sync(0xffffffffu, visible_tiles(), 0);
         if (tiles > 0) {
             const uint64_t k_desc0 = sw128_descriptor(smem_u32(kHalf ? static_cast<const void *>(s.k_raw[0]) : s.k16[0]));
             const uint64_t v_desc0 = sw128_descriptor(smem_u32(s.vt16[0]));
@@ -602,7 +618,17 @@ __global__ void __launch_bounds__(Forward<D, kHalf>::kThreads, 1)
         const int w = warp - F::kSplitWarp;
         const unsigned char *mask = p.mask + static_cast<long long>(b) * p.keys;
         const int row = 32 * w + lane;  // K row of this lane
-        for (int j = 0; j < tiles; ++j) {
+        // The prefetched tiles are converted without waiting for the visible-tile count (which
+        // comes from a mask read); tiles of them past the last visible key are converted for
+        // nothing and never consumed.
+        int tiles = prefetched;
+        bool counted = false;
+        for (int j = 0; j < tiles || !counted; ++j) {
+            if (!counted && j >= prefetched) {
+                tiles = __shfl_sync(0xffffffffu, visible_tiles(), 0);
+                counted = true;
+                if (j >= tiles) break;
+            }
             const int stage = j % kStages, use = j / kStages;
             if constexpr (kHalf) {
                 // FP16 storage: the MMAs read K from the TMA tile; V is transposed, masked rows zeroed.
@@ -797,6 +823,7 @@ __global__ void __launch_bounds__(Forward<D, kHalf>::kThreads, 1)
         float pending_weight = 0.f;  // exp(m_(j-2) - m_(j-1)), applied when tile j-1 is folded
         int pending_exponent = 0;    // c_(j-1): the V exponent of tile j-1
         bool ok = true;
+        const int tiles = __shfl_sync(0xffffffffu, visible_tiles(), 0);
         for (int j = 0; j < tiles && ok; ++j) {
             const int stage = j % kStages, use = j / kStages, buffer = j & 1;
             const uint32_t pbuf = lane_base + F::kColBuffer + buffer * F::kBufferColumns;

@@ -137,7 +137,9 @@ struct alignas(1024) Storage {
     uint64_t x_done;                                       // X1 (X2) of the tile in TMEM (commit)
     uint64_t rows_ready;                                   // row operands stored (128 arrivals)
     uint64_t mma_done;                                     // every MMA finished (commit)
+    uint64_t range_ready;                                  // tile_count written (1 arrival)
     uint32_t tmem_base;
+    int tile_count;                                        // column tiles visited
 };
 
 struct BackwardArgs {
@@ -367,7 +369,7 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
     const int column_count = kKeyRows ? p.queries : p.keys;
     int first, last;  // columns that can see (or be seen by) the row tile
     key_window(r0, min(r0 + kRows, row_count), column_count, p.radius, first, last);
-    const int tiles = last > first ? (last - first + kCols - 1) / kCols : 0;
+    const int window_tiles = last > first ? (last - first + kCols - 1) / kCols : 0;
     const long long query_base = (static_cast<long long>(b) * p.heads + h) * p.queries;
     const long long key_base = (static_cast<long long>(b) * p.heads + h) * p.keys;
     const unsigned char *mask = p.mask + static_cast<long long>(b) * p.keys;
@@ -387,6 +389,7 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
         mbar_init(&s.p_full, kRows);
         mbar_init(&s.x_done, 1);
         mbar_init(&s.rows_ready, kRows);
+        mbar_init(&s.range_ready, 1);
         mbar_init(&s.mma_done, 1);
         mbar_fence_init();
     }
@@ -394,33 +397,61 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = s.tmem_base;
+    // Column tiles actually visited (published by the producer warp after its first loads).
+    // Query rows: the key window up to its last visible key (trailing key padding is skipped).
+    // Key rows: none when every key of the tile is masked (dK = dV = 0); else the query window.
+    const int prefetched = min(window_tiles, kStages);
+    const auto visible_tiles = [&]() { return mbar_wait(&s.range_ready, 0) ? s.tile_count : 0; };
 
     if (warp == kProducerWarp) {
         // ---------------------------------------------------------------- TMA producer
-        if (lane == 0) {
-            int issued = 0;
-            bool ok = true;
-            for (int j = 0; j < tiles && ok; ++j) {
-                const int stage = j % kStages;
-                // The raw stage is refilled as soon as the split warps have converted it (the MMAs
-                // read only the converted layouts).
-                if (j >= kStages) ok = mbar_wait(&s.raw_free[stage], ((j / kStages) - 1) & 1);
-                if (!ok) break;
-                RK_BTRACE(j, 0);
-                mbar_arrive_expect_tx(&s.full[stage], 2 * G::kBoxes * kBoxBytes);
+        const auto issue = [&](int j) {
+            const int stage = j % kStages;
+            RK_BTRACE(j, 0);
+            mbar_arrive_expect_tx(&s.full[stage], 2 * G::kBoxes * kBoxBytes);
 #pragma unroll
-                for (int box = 0; box < G::kBoxes; ++box) {
-                    tma_load_4d(s.raw1[stage] + box * kBoxFloats, &tmap1, &s.full[stage], 32 * box, first + j * kCols, h, b);
-                    tma_load_4d(s.raw2[stage] + box * kBoxFloats, &tmap2, &s.full[stage], 32 * box, first + j * kCols, h, b);
-                }
+            for (int box = 0; box < G::kBoxes; ++box) {
+                tma_load_4d(s.raw1[stage] + box * kBoxFloats, &tmap1, &s.full[stage], 32 * box, first + j * kCols, h, b);
+                tma_load_4d(s.raw2[stage] + box * kBoxFloats, &tmap2, &s.full[stage], 32 * box, first + j * kCols, h, b);
+            }
+        };
+        // The first stages go out before the mask is read.
+        if (lane == 0)
+            for (int j = 0; j < prefetched; ++j) issue(j);
+        int tiles = window_tiles;
+        if constexpr (kKeyRows) {
+            bool visible = false;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int key = r0 + 4 * lane + e;
+                visible = visible || (key < row_count && mask[key] != 0);
+            }
+            if (!__any_sync(0xffffffffu, visible)) tiles = 0;
+        } else {
+            tiles = visible_tiles_of(mask, first, last, lane);
+        }
+        if (lane == 0) {
+            s.tile_count = tiles;
+            mbar_arrive(&s.range_ready);
+            int issued = prefetched;
+            bool ok = true;
+            for (int j = prefetched; j < tiles && ok; ++j) {
+                // The raw stage is refilled as soon as the split warps have converted it (the MMAs
+                // read only the converted layouts); j >= kStages here.
+                ok = mbar_wait(&s.raw_free[j % kStages], ((j / kStages) - 1) & 1);
+                if (!ok) break;
+                issue(j);
                 ++issued;
             }
             if (!ok) {
                 for (int j = max(0, issued - kStages); j < issued; ++j) mbar_wait(&s.full[j % kStages], (j / kStages) & 1);
             }
+            // Prefetched tiles past the visited ones: converted for nothing; wait for their loads.
+            for (int j = tiles; j < prefetched; ++j) mbar_wait(&s.full[j], 0);
         }
     } else if (warp == kMmaWarp) {
         // ---------------------------------------------------------------- MMA issuer
+        const int tiles = __shfl_sync(0xffffffffu, visible_tiles(), 0);
         if (tiles > 0) {
             constexpr uint64_t row_stage = G::kRowWords * 4 / 16;
             const uint64_t b1_desc = sw128_descriptor(smem_u32(s.b1[0]));
@@ -471,7 +502,7 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
         bool next_flag = false;
         const auto load_stats = [&](int jj) {
             const int column = first + jj * kCols + row;
-            next_flag = jj < tiles && column < last;
+            next_flag = jj < window_tiles && column < last;
             if (kKeyRows) {
                 next_max = next_flag ? p.lse_in[(query_base + column) * 2] : -INFINITY;
                 next_total = next_flag ? p.lse_in[(query_base + column) * 2 + 1] : 0.f;
@@ -481,7 +512,17 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
             }
         };
         load_stats(0);
-        for (int j = 0; j < tiles; ++j) {
+        // Query rows: the prefetched tiles are converted without waiting for the visited-tile
+        // count (which comes from a mask read); those past it are converted for nothing and never
+        // consumed. Key rows (count 0 or the whole window) wait for it.
+        int tiles = kKeyRows ? __shfl_sync(0xffffffffu, visible_tiles(), 0) : prefetched;
+        bool counted = kKeyRows;
+        for (int j = 0; j < tiles || !counted; ++j) {
+            if (!counted && j >= prefetched) {
+                tiles = __shfl_sync(0xffffffffu, visible_tiles(), 0);
+                counted = true;
+                if (j >= tiles) break;
+            }
             const int stage = j % kStages, parity = j & 1;
             const float maximum = next_max, total = next_total, delta = next_delta;
             const bool flag = next_flag;
@@ -610,6 +651,7 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
         for (int c = 0; c < (kKeyRows ? D : 1); ++c) acc2[c] = 0.f;
         float pending_scale1 = 0.f, pending_scale2 = 0.f;  // 2^-(scales) of the last tile's X1, X2
         bool ok = true;
+        const int tiles = __shfl_sync(0xffffffffu, visible_tiles(), 0);
         for (int j = 0; j < tiles && ok; ++j) {
             const int stage = j % kStages;
             ok = __all_sync(0xffffffffu, mbar_wait(&s.s_full, j & 1) && mbar_wait(&s.ready[stage], (j / kStages) & 1));

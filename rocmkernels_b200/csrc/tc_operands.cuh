@@ -72,5 +72,28 @@ __device__ __forceinline__ uint4 pack_chunk(const float (&x)[8]) {
     return make_uint4(pack_half2(x[0], x[1]), pack_half2(x[2], x[3]), pack_half2(x[4], x[5]), pack_half2(x[6], x[7]));
 }
 
+// Key tiles (of 64 keys) of the window [first, last) up to its last visible key (mask[key] != 0), 0 when every
+// key is masked: the warp reads the mask backwards from `last`, 128 keys (4 per lane) at a time.
+// Warp-collective; every lane returns the count.
+__device__ __forceinline__ int visible_tiles_of(const unsigned char *mask, int first, int last, int lane) {
+    int end = last;
+    while (end > first) {
+        const int lo = max(first, end - 128);
+        int top = -1;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int key = end - 1 - 4 * lane - e;
+            if (key >= lo && mask[key] != 0) top = max(top, key);
+        }
+        top = __reduce_max_sync(0xffffffffu, top);
+        if (top >= 0) {
+            end = top + 1;
+            break;
+        }
+        end = lo;
+    }
+    return end > first ? (end - first + kBoxRows - 1) / kBoxRows : 0;
+}
+
 }  // namespace tc
 }  // namespace rk
