@@ -94,13 +94,16 @@ constexpr uint32_t kIdescS = f16_instr_desc(128, 64);  // S: 64 keys
 constexpr uint64_t kDescStep = 2;                      // one K=16 step of FP16 = 32 bytes
 
 // Configuration per storage mode and head width. Split FP32 (kHalf false): d = 32 has two Q tiles
-// of 128 queries per CTA sharing each K/V tile (12 warps, 4 stages), d = 64 one Q tile per CTA
-// (8 warps, 3 stages) with operands twice as wide. FP16 storage (kHalf true, d = 16, 32 or 64):
-// one Q tile, 3 stages, one FP16 term per operand.
-template <int D, bool kHalf>
+// of 128 queries per CTA sharing each K/V tile (12 warps, 4 stages), or one Q tile (8 warps) when
+// that grid fits in one wave of CTAs (launch below); d = 64 one Q tile per CTA (8 warps,
+// 3 stages) with operands twice as wide. FP16 storage (kHalf true, d = 16, 32 or 64): one Q tile,
+// 3 stages, one FP16 term per operand. The TMEM column layout of a Q tile is the same for one or
+// two Q tiles.
+template <int D, bool kHalf, int kTiles = !kHalf && D == 32 ? 2 : 1>
 struct Forward {
+    static_assert(kTiles == 1 || (kTiles == 2 && !kHalf && D == 32), "two Q tiles per CTA: split FP32, d = 32");
     static constexpr int kTerms = kHalf ? 1 : 2;  // FP16 terms per operand
-    static constexpr int kQTiles = !kHalf && D == 32 ? 2 : 1;
+    static constexpr int kQTiles = kTiles;
     static constexpr int kCtaQueries = kQTile * kQTiles;
     static constexpr int kStages = !kHalf && D == 32 ? 4 : 3;
     static constexpr int kSoftmaxWarps = 4 * kQTiles;
@@ -124,14 +127,13 @@ struct Forward {
                               kColO = kColBuffer + 128, kColSum = kColO + kTerms * D,
                               kColTile = kHalf || D == 32 ? 256 : 512;
     static constexpr uint32_t kTmemColumns = kHalf ? 256 : 512;
-    static constexpr uint32_t kIdescPV = f16_instr_desc(128, kVRows);
     static constexpr uint64_t kDescStageK = (kHalf ? kRawFloats : kKWords) * 4 / 16, kDescStageV = kVWords * 4 / 16;
 };
 
 // Operand tiles are rows of 128 bytes in 1024-byte aligned 8-row atoms (the 128B swizzle).
-template <int D, bool kHalf>
+template <int D, bool kHalf, int kTiles = Forward<D, kHalf>::kQTiles>
 struct alignas(1024) SharedStorage {
-    using F = Forward<D, kHalf>;
+    using F = Forward<D, kHalf, kTiles>;
     float k_raw[F::kStages][F::kRawFloats];    // K tile as TMA lands it (FP32: swizzled boxes of 64 x 32; FP16: 64 x 64)
     float v_raw[F::kStages][F::kRawFloats];    // V tile
     uint32_t k16[F::kStages][F::kKWords > 0 ? F::kKWords : 1];  // 64 key rows as [k0 | k1] FP16 (row layout),
@@ -159,8 +161,8 @@ struct alignas(1024) SharedStorage {
 
 // The rotary prologue's extra operands: per stage, the cos and sin rows of the tile's 64 keys as
 // TMA lands them (64 rows x 32 FP32, 128B swizzle, the layout of one K box).
-template <int D>
-struct alignas(1024) RotaryStorage : SharedStorage<D, false> {
+template <int D, int kTiles>
+struct alignas(1024) RotaryStorage : SharedStorage<D, false, kTiles> {
     alignas(1024) float cos_raw[Forward<D, false>::kStages][kBoxFloats];
     alignas(1024) float sin_raw[Forward<D, false>::kStages][kBoxFloats];
 };
@@ -222,13 +224,14 @@ __device__ __forceinline__ void issue_values(uint32_t tmem, uint64_t v_desc, int
     using F = Forward<D, kHalf>;
     const uint32_t t = tmem + tile * F::kColTile;
     const uint32_t pbuf = t + F::kColBuffer + buffer * F::kBufferColumns;
+    constexpr uint32_t kIdescPV = f16_instr_desc(128, F::kVRows);
     const uint64_t bv[4] = {v_desc, v_desc + kDescStep, v_desc + 2 * kDescStep, v_desc + 3 * kDescStep};
     const uint32_t a0[4] = {pbuf, pbuf + 8, pbuf + 16, pbuf + 24};
     if constexpr (!kHalf) {
         const uint32_t a1[4] = {pbuf + 32, pbuf + 40, pbuf + 48, pbuf + 56};
-        mma4_f16_ts_warp(t + F::kColO, a1, bv, F::kIdescPV, 1);
+        mma4_f16_ts_warp(t + F::kColO, a1, bv, kIdescPV, 1);
     }
-    mma4_f16_ts_commit_warp(t + F::kColO, a0, bv, F::kIdescPV, kHalf ? 1 : 0, bar);
+    mma4_f16_ts_commit_warp(t + F::kColO, a0, bv, kIdescPV, kHalf ? 1 : 0, bar);
 }
 
 // Folds the last finished key tile into the running output and row sum. In TMEM, Oa + Ob is the
@@ -414,15 +417,15 @@ __device__ __forceinline__ void rotate_row32(float4 (&x)[8], const float4 (&cs)[
 // never go through HBM; the result equals rotary_fp32 followed by this kernel bit for bit.
 // With kRotary the producer also lands the tile's cos and sin rows (tmap_cos, tmap_sin) in the
 // stage; the other instantiations ignore those two maps.
-template <int D, bool kHalf, int kWidth = D, bool kRotary = false>
-__global__ void __launch_bounds__(Forward<D, kHalf>::kThreads, 1)
+template <int D, bool kHalf, int kWidth = D, bool kRotary = false, int kTiles = Forward<D, kHalf>::kQTiles>
+__global__ void __launch_bounds__(Forward<D, kHalf, kTiles>::kThreads, 1)
         flash_forward_kernel(const FlashArgs args, const __grid_constant__ CUtensorMap tmap_k,
                              const __grid_constant__ CUtensorMap tmap_v, const __grid_constant__ CUtensorMap tmap_cos,
                              const __grid_constant__ CUtensorMap tmap_sin) {
     static_assert(kWidth == D || (!kHalf && kWidth % 4 == 0 && kWidth < D), "narrow rows: FP32 storage only");
     static_assert(!kRotary || (D == 32 && kWidth == 32 && !kHalf), "the rotary prologue is defined for 32-wide FP32 heads");
-    using F = Forward<D, kHalf>;
-    using Storage = std::conditional_t<kRotary, RotaryStorage<D>, SharedStorage<D, kHalf>>;
+    using F = Forward<D, kHalf, kTiles>;
+    using Storage = std::conditional_t<kRotary, RotaryStorage<D, kTiles>, SharedStorage<D, kHalf, kTiles>>;
     constexpr int kStages = F::kStages;
     extern __shared__ uint8_t shared_raw[];
     Storage &s = *reinterpret_cast<Storage *>((reinterpret_cast<uintptr_t>(shared_raw) + 1023) & ~uintptr_t(1023));
@@ -982,26 +985,27 @@ bool positive_tma_strides(const Tensor &t, int per16) {
            t.sh < limit && t.sb < limit && (reinterpret_cast<uintptr_t>(t.data) & 15u) == 0;
 }
 
-template <int D, bool kHalf, bool kRotary = false>
+template <int D, bool kHalf, bool kRotary = false, int kTiles = Forward<D, kHalf>::kQTiles>
 constexpr int shared_bytes() {
     if constexpr (kRotary)
-        return static_cast<int>(sizeof(RotaryStorage<D>)) + 1024;
+        return static_cast<int>(sizeof(RotaryStorage<D, kTiles>)) + 1024;
     else
-        return static_cast<int>(sizeof(SharedStorage<D, kHalf>)) + 1024;
+        return static_cast<int>(sizeof(SharedStorage<D, kHalf, kTiles>)) + 1024;
 }
-template <int D, bool kHalf>
+template <int D, bool kHalf, int kTiles = Forward<D, kHalf>::kQTiles>
 constexpr bool layout_ok() {
-    using F = Forward<D, kHalf>;
-    using S = SharedStorage<D, kHalf>;
+    using F = Forward<D, kHalf, kTiles>;
+    using S = SharedStorage<D, kHalf, kTiles>;
     return (kHalf || sizeof(S::k16[0]) == 64 * 2 * D * 2) && sizeof(S::vt16[0]) == F::kVRows * 128 &&
            sizeof(S::vt16[0]) % 1024 == 0 && sizeof(S::k_raw[0]) % 1024 == 0 &&
            F::kColSum + (kHalf ? 0 : 16) <= (F::kQTiles == 2 ? F::kColTile : F::kTmemColumns) &&
-           shared_bytes<D, kHalf>() <= 227 * 1024;
+           shared_bytes<D, kHalf, false, kTiles>() <= 227 * 1024;
 }
-static_assert(layout_ok<32, false>() && layout_ok<64, false>() && layout_ok<16, true>() && layout_ok<32, true>() &&
-                      layout_ok<64, true>(),
+static_assert(layout_ok<32, false>() && layout_ok<32, false, 1>() && layout_ok<64, false>() && layout_ok<16, true>() &&
+                      layout_ok<32, true>() && layout_ok<64, true>(),
               "operand tiles, TMEM columns and shared memory budget");
-static_assert(shared_bytes<32, false, true>() <= 227 * 1024, "rotary tables fit beside the d = 32 stages");
+static_assert(shared_bytes<32, false, true>() <= 227 * 1024 && shared_bytes<32, false, true, 1>() <= 227 * 1024,
+              "rotary tables fit beside the d = 32 stages");
 
 // Rotary table [batch][rows][32] FP32 (token stride st, batch stride sb, 0 = one table for every
 // sequence) as a 4-D map {32, rows, 1, batch} with the K boxes' shape: box = 32 features x 64 rows.
@@ -1019,9 +1023,9 @@ bool make_table_map(CUtensorMap *map, const float *table, long long sb, long lon
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int D, bool kHalf, int kWidth = D, bool kRotary = false>
-int launch(const AttentionParams &p, cudaStream_t stream) {
-    using F = Forward<D, kHalf>;
+template <int D, bool kHalf, int kWidth = D, bool kRotary = false, int kTiles = Forward<D, kHalf>::kQTiles>
+int launch_tiles(const AttentionParams &p, cudaStream_t stream) {
+    using F = Forward<D, kHalf, kTiles>;
     CUtensorMap tmap_k, tmap_v;
     if (!make_tensor_map(&tmap_k, p.k, kWidth, p.batch, p.heads, p.keys, kHalf) ||
         !make_tensor_map(&tmap_v, p.v, kWidth, p.batch, p.heads, p.keys, kHalf))
@@ -1033,8 +1037,8 @@ int launch(const AttentionParams &p, cudaStream_t stream) {
             !make_table_map(&tmap_sin, p.rot_sin, p.rot_sb, p.rot_st, rows, p.batch) || (p.rot_cb > 0) != (p.rot_sb > 0))
             return kNotEligible;
     }
-    constexpr int bytes = shared_bytes<D, kHalf, kRotary>();
-    cudaError_t status = prepare_kernel<flash_forward_kernel<D, kHalf, kWidth, kRotary>>(bytes);
+    constexpr int bytes = shared_bytes<D, kHalf, kRotary, kTiles>();
+    cudaError_t status = prepare_kernel<flash_forward_kernel<D, kHalf, kWidth, kRotary, kTiles>>(bytes);
     if (status != cudaSuccess) return status;
     constexpr int per16 = kHalf ? 8 : 4;
     FlashArgs args{};
@@ -1044,8 +1048,26 @@ int launch(const AttentionParams &p, cudaStream_t stream) {
     args.vec_out = (reinterpret_cast<uintptr_t>(p.o.data) & 15u) == 0 && p.o.sb % per16 == 0 && p.o.sh % per16 == 0 &&
                    p.o.st % per16 == 0;
     const unsigned blocks = static_cast<unsigned>(args.cta_per_head) * static_cast<unsigned>(p.heads) * static_cast<unsigned>(p.batch);
-    flash_forward_kernel<D, kHalf, kWidth, kRotary><<<blocks, F::kThreads, bytes, stream>>>(args, tmap_k, tmap_v, tmap_cos, tmap_sin);
+    flash_forward_kernel<D, kHalf, kWidth, kRotary, kTiles>
+            <<<blocks, F::kThreads, bytes, stream>>>(args, tmap_k, tmap_v, tmap_cos, tmap_sin);
     return cudaGetLastError();
+}
+
+// d = 32 split FP32: two Q tiles per CTA share each K/V tile's conversion, but a grid of 128-query
+// CTAs that fits in one wave (at most one CTA per SM) finishes sooner than half as many CTAs of
+// two Q tiles. Measured on B200 (us): B2 H8 S512 23.5 -> 19.4 with one Q tile (64 CTAs);
+// B8 H3 S1024 (192 one-tile CTAs, two waves) 35.8 -> 56.3, so two tiles stay there.
+template <int D, bool kHalf, int kWidth = D, bool kRotary = false>
+int launch(const AttentionParams &p, cudaStream_t stream) {
+    if constexpr (Forward<D, kHalf>::kQTiles == 2) {
+        int device = 0, sms = 0;
+        cudaError_t status = cudaGetDevice(&device);
+        if (status == cudaSuccess) status = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+        if (status != cudaSuccess) return status;
+        const long long one_tile_ctas = static_cast<long long>((p.queries + kQTile - 1) / kQTile) * p.heads * p.batch;
+        if (one_tile_ctas <= sms) return launch_tiles<D, kHalf, kWidth, kRotary, 1>(p, stream);
+    }
+    return launch_tiles<D, kHalf, kWidth, kRotary>(p, stream);
 }
 
 }  // namespace
