@@ -411,7 +411,7 @@ def run_rotary(args, spec: dict, device, world: int, rank: int, dist) -> None:
                 "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in host_inputs),
                 "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in host_outputs), "steps": e2e_steps},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": float(peaks["hbm_gbs"]), "unit": "GB/s",
-                     "frac": achieved / float(peaks["hbm_gbs"]), "traffic": traffic_from_profiles("rotary"),
+                     "frac": achieved / float(peaks["hbm_gbs"]), "traffic": traffic_from_profiles("rotary", args.workload),
                      "peak_source": f"{peak_source} hbm_gbs", "kernel": f"rotary_kernel<{'backward' if backward else 'forward'}>",
                      "bytes": "q, k, oq, ok and both tables once"},
         "gpu_launches": args.steps,
@@ -480,13 +480,16 @@ def pipelined_e2e(device, sets, host_inputs, host_outputs, launch, steps: int) -
     return start.elapsed_time(end) / 1e3
 
 
-def traffic_from_profiles(kernel_tag: str):
+def traffic_from_profiles(kernel_tag: str, workload: str):
+    """DRAM bytes per launch of `kernel_tag` from the committed ncu summaries, only when they were
+    captured on this same workload (another shape moves other bytes); else None."""
     path = REPO / "profiles" / "traffic.json"
     if not path.exists():
         return None
-    data = json.loads(path.read_text())
-    entry = data.get(kernel_tag)
-    return None if entry is None else entry.get("dram_bytes_per_launch")
+    entry = json.loads(path.read_text()).get(kernel_tag)
+    if entry is None or entry.get("workload") != workload:
+        return None
+    return entry.get("dram_bytes_per_launch")
 
 
 def main() -> None:
@@ -707,7 +710,7 @@ def main() -> None:
         achieved = effective_backward / (part_seconds[1] / args.steps) / 1e12
         peak = float(peaks["bf16_tflops"])
         roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                    "traffic": traffic_from_profiles(f"tcgen05-backward-d{dim}"),
+                    "traffic": traffic_from_profiles(f"tcgen05-backward-d{dim}", args.workload),
                     "peak_source": f"{peak_source} bf16_tflops (burst); the TF32 dense rate is half of it",
                     "frac_of_tf32_dense": achieved / (peak / 2), "frac_of_fp32_fma": achieved / fma_peak,
                     "kernel": f"tcgen05 split-FP16 backward d{dim} (query-major delta+dQ, key-major dK/dV)",
@@ -722,7 +725,7 @@ def main() -> None:
         if path.startswith("tcgen05"):
             peak = float(peaks["bf16_tflops"])
             roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                        "traffic": traffic_from_profiles(path), "kernel": path}
+                        "traffic": traffic_from_profiles(path, args.workload), "kernel": path}
             if path.startswith("tcgen05-f16x2"):  # FP32 storage: compare with the TF32 dense rate as well
                 roofline["peak_source"] = f"{peak_source} bf16_tflops (burst); the TF32 dense rate is half of it"
                 roofline["frac_of_tf32_dense"] = achieved / (peak / 2)
@@ -730,7 +733,7 @@ def main() -> None:
                 roofline["peak_source"] = f"{peak_source} bf16_tflops (burst), the FP16 dense rate"
         else:
             roofline = {"bound": "fp32-fma", "achieved": achieved, "peak": fma_peak, "unit": "TFLOP/s", "frac": achieved / fma_peak,
-                        "traffic": traffic_from_profiles(path),
+                        "traffic": traffic_from_profiles(path, args.workload),
                         "peak_source": "148 SMs x 128 FP32 lanes x 2 FLOP x median SM clock under load", "kernel": path}
 
     line = {
