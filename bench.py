@@ -90,7 +90,7 @@ for _width in (16, 32, 64):
                 description=f"AttentionGeneric{_width} {_storage} b2 h8 l512 (AttentionGenericBenchmarks.cpp:79-110), "
                             f"attention_generic_forward")
 DEFAULT_WORKLOAD = "flash_fwd_b8h3s1024d32"
-PUBLISHED_TFLOPS = 3.36  # flash fwd d32, same FLOPs (B2 H12 L1024), RX 6700 (README.md:63)
+PUBLISHED_TFLOPS = 3.36  # the reference's published flash fwd d32 figure, same FLOPs (B2 H12 L1024), RX 6700 (README.md:63)
 METRIC = "FP32 attention TFLOP/s (repo FLOP convention: 4*B*H*Q*K*d forward, 8*B*H*Q*K*d backward)"
 
 
