@@ -586,6 +586,17 @@ def main() -> None:
     effective_forward, effective_backward = 4.0 * pairs * dim, 8.0 * pairs * dim
     flops_per_step = flops_forward + (flops_backward if with_backward else 0.0)
     effective_per_step = effective_forward + (effective_backward if with_backward else 0.0)
+    # Whole-job totals over all ranks: under strong scaling the ranks hold different sequences
+    # (key-padded lengths differ), so the job's active pairs are summed over the global batch;
+    # under weak scaling every rank runs the same shape.
+    if with_backward:
+        job_pairs = sum(active_pairs(seq, radius, length) for length in key_lengths(spec)) * heads
+        job_flops_per_step = (4.0 + 8.0) * spec["batch"] * heads * seq * seq * dim
+        job_effective_forward, job_effective_backward = 4.0 * job_pairs * dim, 8.0 * job_pairs * dim
+    else:
+        job_flops_per_step = world * flops_per_step
+        job_effective_forward, job_effective_backward = world * effective_forward, 0.0
+    job_effective_per_step = job_effective_forward + job_effective_backward
     launches_per_step = 1 + (2 if with_backward else 0)
 
     # The step's device tensors by name (one set for the device-timed steps; the e2e leg uses two).
@@ -698,8 +709,8 @@ def main() -> None:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
     device_seconds, e2e_seconds, unfused_seconds, *part_seconds = times.tolist()
 
-    value = world * flops_per_step * args.steps / device_seconds / 1e12
-    e2e_value = world * flops_per_step * e2e_steps / e2e_seconds / 1e12
+    value = job_flops_per_step * args.steps / device_seconds / 1e12
+    e2e_value = job_flops_per_step * e2e_steps / e2e_seconds / 1e12
     peaks, peak_source = measured_peaks()
     sm_mhz = (clocks or {}).get("sm_mhz") or float(peaks.get("sm_max_mhz", 1965.0))
     fma_peak = 148 * 128 * 2 * sm_mhz * 1e6 / 1e12
@@ -757,15 +768,15 @@ def main() -> None:
         "clocks": clocks,
     }
     if with_backward:
-        line["effective"] = {"value": world * effective_per_step * args.steps / device_seconds / 1e12, "unit": "TFLOP/s",
+        line["effective"] = {"value": job_effective_per_step * args.steps / device_seconds / 1e12, "unit": "TFLOP/s",
                              "flops": "12*d per active (query, key) pair"}
         line["parts"] = {"forward_ms": part_seconds[0] / args.steps * 1e3, "backward_ms": part_seconds[1] / args.steps * 1e3,
-                         "forward_effective_tflops": world * effective_forward * args.steps / part_seconds[0] / 1e12,
-                         "backward_effective_tflops": world * effective_backward * args.steps / part_seconds[1] / 1e12}
+                         "forward_effective_tflops": job_effective_forward * args.steps / part_seconds[0] / 1e12,
+                         "backward_effective_tflops": job_effective_backward * args.steps / part_seconds[1] / 1e12}
     if rotary:
         line["unfused"] = {"ms_per_step": unfused_seconds / args.steps * 1e3,
                            "sequence": "rotary_fp32 (token-major outputs) then attention_fp32_forward_flash",
-                           "tflops": world * flops_per_step * args.steps / unfused_seconds / 1e12}
+                           "tflops": job_flops_per_step * args.steps / unfused_seconds / 1e12}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(spec)
     if rank == 0:
