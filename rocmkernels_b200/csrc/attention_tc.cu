@@ -315,8 +315,9 @@ __device__ __forceinline__ void fold_output(float (&o)[D], float &row_sum, int &
 // without any visible key yet has an infinite offset). kHalf: P' rounded to FP16 once, pairs in
 // columns 0-31, and the FP32 sum of the unrounded P' returned (0 otherwise).
 // kPacked: the exponent arguments and residuals as packed FP32 pairs (fma/sub .f32x2: one issue
-// for two values). Used where registers allow: the split d = 32 kernel (168 registers a thread)
-// spills with it and is faster without (36.9 against 36.2 us at B8 H3 S1024); d = 64 gains 8 %.
+// for two values). Used where registers allow: the split d = 32 kernel with two Q tiles (168
+// registers a thread) spills with it and is faster without (36.9 against 36.2 us at B8 H3 S1024);
+// d = 64 gains 8 %, the one-Q-tile d = 32 kernel 6-7 %.
 template <bool kPlain, bool kHalf, bool kPacked>
 __device__ __forceinline__ float exp_split_store(const float (&sc)[64], float slope, float offset, uint32_t pbuf) {
     float sum[4] = {0.f, 0.f, 0.f, 0.f};
@@ -870,9 +871,10 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles>::kThreads, 1)
             // the MMA warp start P(j).V, which overwrites Ot. The TMEM stores inside are
             // warp-collective, so the branch is taken by the whole warp (the explicit path is
             // exact for finite rows too).
+            constexpr bool kPackedSplit = kHalf || D == 64 || F::kQTiles == 1;
             const float tile_sum = __all_sync(0xffffffffu, isfinite(offset) && slope > 0.f)
-                                           ? exp_split_store<true, kHalf, kHalf || D == 64>(sc, slope, offset, pbuf)
-                                           : exp_split_store<false, kHalf, kHalf || D == 64>(sc, slope, offset, pbuf);
+                                           ? exp_split_store<true, kHalf, kPackedSplit>(sc, slope, offset, pbuf)
+                                           : exp_split_store<false, kHalf, kPackedSplit>(sc, slope, offset, pbuf);
             if constexpr (kHalf) row_sum = fmaf(row_sum, old_weight, tile_sum);  // kept in units of the new max
             RK_WARP_TRACE(j, 2);
             if (j > 0) {  // fold tile j-1 before P(j).V overwrites its Ot
