@@ -486,10 +486,11 @@ def traffic_from_profiles(kernel_tag: str, workload: str):
     path = REPO / "profiles" / "traffic.json"
     if not path.exists():
         return None
-    entry = json.loads(path.read_text()).get(kernel_tag)
-    if entry is None or entry.get("workload") != workload:
-        return None
-    return entry.get("dram_bytes_per_launch")
+    entries = json.loads(path.read_text()).get(kernel_tag, [])
+    for entry in entries if isinstance(entries, list) else [entries]:
+        if entry.get("workload") == workload:
+            return entry.get("dram_bytes_per_launch")
+    return None
 
 
 def main() -> None:
