@@ -269,6 +269,10 @@ int attention_fp32_statistics(const float *q, const float *k, const bool *mask, 
         return cudaErrorInvalidValue;
     const AttentionParams p =
             forward_params(32, q, k, nullptr, mask, nullptr, lse, batch, heads, queries, keys, radius, qs, ks, ks, ks);
+    if (rk::tc::statistics_supported(p)) {
+        const int status = rk::tc::launch_statistics(p, stream);
+        if (status != rk::tc::kNotEligible) return status;
+    }
     return launch_simt_forward<32, true>(p, stream);
 }
 

@@ -418,13 +418,15 @@ __device__ __forceinline__ void rotate_row32(float4 (&x)[8], const float4 (&cs)[
 // never go through HBM; the result equals rotary_fp32 followed by this kernel bit for bit.
 // With kRotary the producer also lands the tile's cos and sin rows (tmap_cos, tmap_sin) in the
 // stage; the other instantiations ignore those two maps.
-template <int D, bool kHalf, int kWidth = D, bool kRotary = false, int kTiles = Forward<D, kHalf>::kQTiles>
+template <int D, bool kHalf, int kWidth = D, bool kRotary = false, int kTiles = Forward<D, kHalf>::kQTiles,
+          bool kStats = false>
 __global__ void __launch_bounds__(Forward<D, kHalf, kTiles>::kThreads, 1)
         flash_forward_kernel(const FlashArgs args, const __grid_constant__ CUtensorMap tmap_k,
                              const __grid_constant__ CUtensorMap tmap_v, const __grid_constant__ CUtensorMap tmap_cos,
                              const __grid_constant__ CUtensorMap tmap_sin) {
     static_assert(kWidth == D || (!kHalf && kWidth % 4 == 0 && kWidth < D), "narrow rows: FP32 storage only");
     static_assert(!kRotary || (D == 32 && kWidth == 32 && !kHalf), "the rotary prologue is defined for 32-wide FP32 heads");
+    static_assert(!kStats || (D == 32 && kWidth == 32 && !kHalf && !kRotary), "statistics: 32-wide FP32 heads");
     using F = Forward<D, kHalf, kTiles>;
     using Storage = std::conditional_t<kRotary, RotaryStorage<D, kTiles>, SharedStorage<D, kHalf, kTiles>>;
     constexpr int kStages = F::kStages;
@@ -479,7 +481,7 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles>::kThreads, 1)
     const auto issue_tile = [&](int j) {
         const int stage = j % kStages;
         RK_TRACE(j, 12);
-        mbar_arrive_expect_tx(&s.kv_full[stage], (2 * F::kBoxes + (kRotary ? 2 : 0)) * kBoxBytes);
+        mbar_arrive_expect_tx(&s.kv_full[stage], ((kStats ? 1 : 2) * F::kBoxes + (kRotary ? 2 : 0)) * kBoxBytes);
         if constexpr (kRotary) {
             const int table = b * args.rot_batch;
             tma_load_4d(s.cos_raw[stage], &tmap_cos, &s.kv_full[stage], 0, first + j * kKeyTile, 0, table);
@@ -488,7 +490,8 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles>::kThreads, 1)
 #pragma unroll
         for (int box = 0; box < F::kBoxes; ++box) {
             tma_load_4d(s.k_raw[stage] + box * kBoxFloats, &tmap_k, &s.kv_full[stage], 32 * box, first + j * kKeyTile, h, b);
-            tma_load_4d(s.v_raw[stage] + box * kBoxFloats, &tmap_v, &s.kv_full[stage], 32 * box, first + j * kKeyTile, h, b);
+            if constexpr (!kStats)
+                tma_load_4d(s.v_raw[stage] + box * kBoxFloats, &tmap_v, &s.kv_full[stage], 32 * box, first + j * kKeyTile, h, b);
         }
     };
     const int prefetched = min(window_tiles, kStages);  // issued before the set-up barrier
@@ -588,7 +591,8 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles>::kThreads, 1)
                         if (!ok || served[t] || !mbar_test_wait_warp(&s.p_full[t], j & 1)) continue;
                         if (lane == 0) RK_TRACE(j, t);
                         tc_fence_after();
-                        issue_values<D, kHalf>(tmem, v_desc0 + F::kDescStageV * stage, t, buffer, &s.pv_done[t]);
+                        if constexpr (!kStats)
+                            issue_values<D, kHalf>(tmem, v_desc0 + F::kDescStageV * stage, t, buffer, &s.pv_done[t]);
                         if (more) {
                             if (!next_ready) {
                                 next_ready = mbar_wait_warp(&s.kv_ready[next_stage], ((j + 2) / kStages) & 1);
@@ -676,7 +680,7 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles>::kThreads, 1)
             for (int c = 0; c < D / 4; ++c)
                 kmax = max3(kmax, fmaxf(fabsf(kx[c].x), fabsf(kx[c].y)), fmaxf(fabsf(kx[c].z), fabsf(kx[c].w)));
 #pragma unroll
-            for (int item = 0; item < D / 32; ++item) {
+            for (int item = 0; item < (kStats ? 0 : D / 32); ++item) {  // statistics: no V
                 const int index = 64 * item + row;  // 0 .. 2D - 1
                 const int group = index >> 3 & 7, fchunk = (index & 7) + 8 * (index >> 6);
 #pragma unroll
@@ -729,7 +733,7 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles>::kThreads, 1)
             // V^T rows f (v0) and D + f (v1), keys 8g..8g+7 = 16-byte chunk g (swizzled by f % 8)
             uint4 *vt16 = reinterpret_cast<uint4 *>(s.vt16[stage]);
 #pragma unroll
-            for (int item = 0; item < D / 32; ++item) {
+            for (int item = 0; item < (kStats ? 0 : D / 32); ++item) {
                 const int index = 64 * item + row;
                 const int group = index >> 3 & 7, fchunk = (index & 7) + 8 * (index >> 6);
 #pragma unroll
@@ -851,6 +855,18 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles>::kThreads, 1)
             // TMEM S -> scaled score (FP16 storage: S is the plain dot product)
             const float s_scale = kHalf ? p.scale : exp2_int(-(q_exponent + s.k_exponent[stage]));
             const int v_exponent = kHalf ? 0 : s.v_exponent[stage];
+            if constexpr (kStats) {
+                // S and the stage's mask and exponent are in registers: S(j + 2) may overwrite the
+                // buffer and the stage may be refilled. The MMA warp must have seen this tile's
+                // release of buffer j - 1 before this arrival (two arrivals it has not seen would
+                // complete two phases of p_full, which its parity wait cannot tell from none); it
+                // issues S(j + 1) only after seeing that release, so wait for S(j + 1) first.
+                if (j + 1 < tiles)
+                    ok = __all_sync(0xffffffffu, mbar_wait(&s.s_full[tile][buffer ^ 1], ((j + 1) >> 1) & 1));
+                if (!ok) break;
+                tc_fence_before();
+                mbar_arrive(&s.p_full[tile]);
+            }
             // Row max (four independent three-input max chains).
             if (active != ~0ull) {
 #pragma unroll
@@ -867,6 +883,16 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles>::kThreads, 1)
             const float old_weight = isfinite(row_max) ? fast_exp2((row_max - next) * kLog2e) : 0.f;
             const float slope = s_scale * kLog2e;
             const float offset = fmaf(-next, kLog2e, 14.f);  // P' = 2^14 exp(S - max) = exp2(S * slope + offset)
+            if constexpr (kStats) {
+                // Statistics only: the row sum of P' in FP32, no P, no output.
+                float partial[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int c = 0; c < 64; ++c)
+                    partial[c & 3] += sc[c] == -INFINITY ? 0.f : fast_exp2(fmaf(sc[c], slope, offset));
+                row_sum = fmaf(row_sum, old_weight, (partial[0] + partial[1]) + (partial[2] + partial[3]));
+                row_max = next;
+                continue;
+            }
             // P(j) may be written before Ot(j - 1) is folded: only the p_full arrival below lets
             // the MMA warp start P(j).V, which overwrites Ot. The TMEM stores inside are
             // warp-collective, so the branch is taken by the whole warp (the explicit path is
@@ -898,7 +924,7 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles>::kThreads, 1)
         }
 
         // Epilogue (AttentionFlash32.h:157-169): O / total; fully masked rows give 0 and {-inf, 0}.
-        if (tiles > 0 && ok) {
+        if (!kStats && tiles > 0 && ok) {
             ok = __all_sync(0xffffffffu, mbar_wait(&s.pv_done[tile], (tiles - 1) & 1));
             tc_fence_after();
             if (ok) fold_output<D, kHalf>(o, row_sum, o_exp, lane_base, pending_weight, pending_exponent);
@@ -921,7 +947,7 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles>::kThreads, 1)
 #pragma unroll
                     for (int c = 0; c < D; ++c) out[c] = __float2half_rn(o[c]);
                 }
-            } else {
+            } else if constexpr (!kStats) {  // statistics: no output rows
                 float *out = p.o.row(b, h, query);
                 if (args.vec_out) {
 #pragma unroll
@@ -1025,12 +1051,15 @@ bool make_table_map(CUtensorMap *map, const float *table, long long sb, long lon
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int D, bool kHalf, int kWidth = D, bool kRotary = false, int kTiles = Forward<D, kHalf>::kQTiles>
+template <int D, bool kHalf, int kWidth = D, bool kRotary = false, int kTiles = Forward<D, kHalf>::kQTiles,
+          bool kStats = false>
 int launch_tiles(const AttentionParams &p, cudaStream_t stream) {
     using F = Forward<D, kHalf, kTiles>;
     CUtensorMap tmap_k, tmap_v;
-    if (!make_tensor_map(&tmap_k, p.k, kWidth, p.batch, p.heads, p.keys, kHalf) ||
-        !make_tensor_map(&tmap_v, p.v, kWidth, p.batch, p.heads, p.keys, kHalf))
+    if (!make_tensor_map(&tmap_k, p.k, kWidth, p.batch, p.heads, p.keys, kHalf)) return kNotEligible;
+    if constexpr (kStats)
+        tmap_v = tmap_k;  // statistics: no V (the map is never used)
+    else if (!make_tensor_map(&tmap_v, p.v, kWidth, p.batch, p.heads, p.keys, kHalf))
         return kNotEligible;
     CUtensorMap tmap_cos = tmap_k, tmap_sin = tmap_k;
     if constexpr (kRotary) {
@@ -1040,7 +1069,7 @@ int launch_tiles(const AttentionParams &p, cudaStream_t stream) {
             return kNotEligible;
     }
     constexpr int bytes = shared_bytes<D, kHalf, kRotary, kTiles>();
-    cudaError_t status = prepare_kernel<flash_forward_kernel<D, kHalf, kWidth, kRotary, kTiles>>(bytes);
+    cudaError_t status = prepare_kernel<flash_forward_kernel<D, kHalf, kWidth, kRotary, kTiles, kStats>>(bytes);
     if (status != cudaSuccess) return status;
     constexpr int per16 = kHalf ? 8 : 4;
     FlashArgs args{};
@@ -1050,7 +1079,7 @@ int launch_tiles(const AttentionParams &p, cudaStream_t stream) {
     args.vec_out = (reinterpret_cast<uintptr_t>(p.o.data) & 15u) == 0 && p.o.sb % per16 == 0 && p.o.sh % per16 == 0 &&
                    p.o.st % per16 == 0;
     const unsigned blocks = static_cast<unsigned>(args.cta_per_head) * static_cast<unsigned>(p.heads) * static_cast<unsigned>(p.batch);
-    flash_forward_kernel<D, kHalf, kWidth, kRotary, kTiles>
+    flash_forward_kernel<D, kHalf, kWidth, kRotary, kTiles, kStats>
             <<<blocks, F::kThreads, bytes, stream>>>(args, tmap_k, tmap_v, tmap_cos, tmap_sin);
     return cudaGetLastError();
 }
@@ -1059,7 +1088,7 @@ int launch_tiles(const AttentionParams &p, cudaStream_t stream) {
 // CTAs that fits in one wave (at most one CTA per SM) finishes sooner than half as many CTAs of
 // two Q tiles. Measured on B200 (us): B2 H8 S512 23.5 -> 19.4 with one Q tile (64 CTAs);
 // B8 H3 S1024 (192 one-tile CTAs, two waves) 35.8 -> 56.3, so two tiles stay there.
-template <int D, bool kHalf, int kWidth = D, bool kRotary = false>
+template <int D, bool kHalf, int kWidth = D, bool kRotary = false, bool kStats = false>
 int launch(const AttentionParams &p, cudaStream_t stream) {
     if constexpr (Forward<D, kHalf>::kQTiles == 2) {
         int device = 0, sms = 0;
@@ -1067,9 +1096,9 @@ int launch(const AttentionParams &p, cudaStream_t stream) {
         if (status == cudaSuccess) status = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
         if (status != cudaSuccess) return status;
         const long long one_tile_ctas = static_cast<long long>((p.queries + kQTile - 1) / kQTile) * p.heads * p.batch;
-        if (one_tile_ctas <= sms) return launch_tiles<D, kHalf, kWidth, kRotary, 1>(p, stream);
+        if (one_tile_ctas <= sms) return launch_tiles<D, kHalf, kWidth, kRotary, 1, kStats>(p, stream);
     }
-    return launch_tiles<D, kHalf, kWidth, kRotary>(p, stream);
+    return launch_tiles<D, kHalf, kWidth, kRotary, Forward<D, kHalf>::kQTiles, kStats>(p, stream);
 }
 
 }  // namespace
@@ -1085,6 +1114,12 @@ int launch_flash_forward(const AttentionParams &p, int head_width, cudaStream_t 
     if (head_width == 64) return launch<64, false>(p, stream);
     return kNotEligible;
 }
+
+bool statistics_supported(const AttentionParams &p) {
+    return p.vec4 && positive_tma_strides(p.k, 4) && (p.q.st % 4 == 0) && (reinterpret_cast<uintptr_t>(p.q.data) & 15u) == 0;
+}
+
+int launch_statistics(const AttentionParams &p, cudaStream_t stream) { return launch<32, false, 32, false, true>(p, stream); }
 
 int launch_flash_forward_rotary(const AttentionParams &p, cudaStream_t stream) {
     const auto aligned = [](const float *t, long long sb, long long st) {

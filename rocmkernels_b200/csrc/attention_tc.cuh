@@ -19,6 +19,12 @@ int launch_flash_forward(const AttentionParams &p, int head_width, cudaStream_t 
 // The flash forward for head width 32 with the rotary prologue (q and k rotated by the tables in
 // p.rot_*, which must be 16-byte aligned with strides of 4 floats); cudaError_t or kNotEligible.
 int launch_flash_forward_rotary(const AttentionParams &p, cudaStream_t stream);
+
+// Statistics only ({row max, sum} per query, no V and no output): the split-FP16 flash forward
+// without the P.V products; the row sums are taken in FP32 by the softmax threads. Eligible when
+// K is TMA-addressable and Q rows 16-byte addressable; cudaError_t or kNotEligible.
+bool statistics_supported(const AttentionParams &p);
+int launch_statistics(const AttentionParams &p, cudaStream_t stream);
 // True when the FP16-storage tensor-core forward accepts the tensors (TMA-addressable K and V,
 // 16-byte addressable Q rows).
 bool half_flash_supported(const AttentionParams &p);
