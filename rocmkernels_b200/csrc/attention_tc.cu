@@ -1179,7 +1179,8 @@ extern "C" __attribute__((visibility("default"))) int rocmkernels_attention_trac
 
 const char *build_info() {
     return "sm_100a; tcgen05-f16x2-flash-d16/d32/d64 forward (TMA + TMEM, split FP16 operands, double-buffered S, tensor-core row "
-           "sums); tcgen05-f16-flash-d16/d32/d64 generic forward for FP16 storage; tcgen05 split-FP16 backward d32/d64 "
+           "sums; one or two Q tiles per CTA by grid size; a statistics-only mode for d32); tcgen05-f16-flash-d16/d32/d64 generic "
+           "forward for FP16 storage; tcgen05 split-FP16 backward d32/d64 "
            "(query-major delta+dQ, key-major dK/dV); simt-fp32 d16/d32/d64 forward (FP32 or FP16 storage), d32/d64 backward";
 }
 
