@@ -193,22 +193,28 @@ bool known_group(int group) {
 constexpr long long kStaticDeltaRows = 1ll << 22;  // batch * heads * queries <= 4,194,304 (16 MiB)
 static __device__ __align__(256) float g_static_delta[kStaticDeltaRows];
 
-// Device address of g_static_delta on the current device, looked up once per device (with that
-// device current) by its first call.
+// Device address of g_static_delta on the current device, looked up (with that device current)
+// by the first call in each context. The address belongs to the context: cudaDeviceReset
+// (ROCmKernels::ResetDevice, or anyone else in the process) unloads the module that holds the
+// array, and the context the runtime creates next may place it elsewhere, so each entry records
+// the context key it was taken in and is looked up again when another context is current.
 cudaError_t static_delta_address(float **address) {
     constexpr int kDevices = 64;
     static std::mutex lock;
     static float *addresses[kDevices] = {};
+    static unsigned long long keys[kDevices] = {};
     int device = 0;
     cudaError_t status = cudaGetDevice(&device);
     if (status != cudaSuccess) return status;
     if (device < 0 || device >= kDevices) return cudaErrorInvalidDevice;
     std::lock_guard<std::mutex> guard(lock);
-    if (addresses[device] == nullptr) {
+    const unsigned long long key = rk::context_key();
+    if (key == 0 || keys[device] != key || addresses[device] == nullptr) {
         void *pointer = nullptr;
-        status = cudaGetSymbolAddress(&pointer, g_static_delta);
+        status = cudaGetSymbolAddress(&pointer, g_static_delta);  // creates the context if needed
         if (status != cudaSuccess) return status;
         addresses[device] = static_cast<float *>(pointer);
+        keys[device] = rk::context_key();
     }
     *address = addresses[device];
     return cudaSuccess;

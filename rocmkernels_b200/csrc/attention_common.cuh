@@ -7,6 +7,8 @@
 
 #include <atomic>
 
+#include "context.h"
+
 namespace rk {
 
 constexpr float kLog2e = 1.4426950408889634f;
@@ -91,17 +93,21 @@ __host__ __device__ __forceinline__ void key_window(int q0, int q1, int keys, in
     last = radius < 0 ? keys : min(keys, q1 + radius);
 }
 
-// Configures the dynamic shared memory limit of a kernel once per device.
+// Configures the dynamic shared memory limit of a kernel once per device and context: the
+// attribute belongs to the context, so a device reset (which destroys it) makes the next launch
+// set it again (context.h).
 template <auto KernelFn>
 inline cudaError_t prepare_kernel(int shared_bytes) {
-    static std::atomic<unsigned long long> configured{0};
+    constexpr int kDevices = 64;
+    static std::atomic<unsigned long long> configured[kDevices] = {};
     int device = 0;
     cudaError_t status = cudaGetDevice(&device);
     if (status != cudaSuccess) return status;
-    const unsigned long long bit = 1ull << (device & 63);
-    if (configured.load(std::memory_order_acquire) & bit) return cudaSuccess;
+    const int slot = device & (kDevices - 1);
+    const unsigned long long key = context_key();
+    if (key != 0 && configured[slot].load(std::memory_order_acquire) == key) return cudaSuccess;
     status = cudaFuncSetAttribute(KernelFn, cudaFuncAttributeMaxDynamicSharedMemorySize, shared_bytes);
-    if (status == cudaSuccess) configured.fetch_or(bit, std::memory_order_acq_rel);
+    if (status == cudaSuccess) configured[slot].store(context_key(), std::memory_order_release);
     return status;
 }
 

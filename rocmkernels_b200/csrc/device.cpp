@@ -2,6 +2,8 @@
 #include <ROCmKernels/Common/Device.hpp>
 #include <ROCmKernels/Common/Error.hpp>
 
+#include "context.h"
+
 // The harness links these C++ symbols from the shared library.
 #pragma GCC visibility push(default)
 namespace ROCmKernels {
@@ -36,6 +38,9 @@ void SynchronizeDevice(const int deviceIndex) {
 
 void ResetDevice(const int deviceIndex) {
     ROCMKERNELS_HIP_CHECK(hipSetDevice(deviceIndex));
+    // Per-context caches (kernel attributes, the static delta array's address) are dropped even
+    // if the driver were to hand the next context the same id.
+    rk::invalidate_context_caches();
     ROCMKERNELS_HIP_CHECK(hipDeviceReset());
 }
 

@@ -182,3 +182,29 @@ def test_fused_rotary_flash_rejects_null_pointers(null_index):
 
 def test_fused_rotary_flash_rejects_radius():
     assert api.attention_fp32_forward_flash_rotary(*[1] * 8, 1, 1, 4, 4, -2, S, S, S, S, S, S) == api.INVALID_VALUE
+
+
+def _cuda_device_visible() -> bool:
+    try:
+        import torch
+
+        return torch.cuda.is_available()
+    except Exception:  # pragma: no cover
+        return False
+
+
+@pytest.mark.skipif(_cuda_device_visible(), reason="boundary probe needs a machine without a CUDA device: the accepted "
+                                                   "case would otherwise launch on stand-in pointers")
+def test_static_delta_row_limit_boundary():
+    """attention_fp32_backward_static_delta holds delta for at most 4,194,304 (batch, head, query)
+    rows. Exactly that many pass the size check (the call then stops at the device lookup, which
+    fails without a driver: an error other than 1); one more row is rejected with error 1 before
+    any CUDA call."""
+    limit = 1 << 22
+    for (batch, heads, queries) in [(2, 16, 131072), (1, 1, limit), (4, 8, limit // 32)]:
+        assert batch * heads * queries == limit
+        status = api.attention_fp32_backward_static_delta(1, 1, 1, 1, 1, 1, 1, 1, 1, 1, batch, heads, queries, 64, -1, S, S, S, S, S)
+        assert status not in (0, api.INVALID_VALUE), (batch, heads, queries, status)
+    for (batch, heads, queries) in [(2, 16, 131073), (1, 1, limit + 1), (4097, 1024, 1)]:
+        status = api.attention_fp32_backward_static_delta(1, 1, 1, 1, 1, 1, 1, 1, 1, 1, batch, heads, queries, 64, -1, S, S, S, S, S)
+        assert status == api.INVALID_VALUE, (batch, heads, queries, status)
