@@ -6,7 +6,8 @@
 // ROCmKernels.Tests/AttentionTests.cpp where it lies. Its ReferenceAttention (:28-125) and
 // TestSupport.hpp's RandomValues (:11-21) live in this translation unit, so the extern "C"
 // functions below can call them. The file's TEST_CASE references the library's entry points,
-// which is why this object links librocmkernels_attention.so; nothing here calls them.
+// which oracle/ref_link_stubs.cpp defines as local stand-ins: nothing here calls them, and the
+// shim loads neither the product library nor a CUDA runtime.
 #include <cstddef>
 #include <cstdint>
 #include <vector>

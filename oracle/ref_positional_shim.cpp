@@ -5,7 +5,8 @@
 // The reference file is included, not copied: ROCMKERNELS_REFERENCE_POSITIONAL names
 // ROCmKernels.Tests/PositionalTests.cpp where it lies, so its ReferenceRotary (:18-50) lives in
 // this translation unit. The file's TEST_CASEs reference the library's rotary entry point,
-// which is why this object links librocmkernels_attention.so; nothing here calls it.
+// which oracle/ref_link_stubs.cpp defines as a local stand-in: nothing here calls it, and the
+// shim loads neither the product library nor a CUDA runtime.
 #include <cstddef>
 #include <vector>
 
