@@ -86,6 +86,12 @@ __device__ long long g_warp_trace[8][8];
     } while (0)
 #endif
 
+#ifdef RK_WAIT_TEST
+// Wait-test build only: the key tile whose TMA loads CTA 0's producer never issues (-1: none), so
+// that every wait on it runs out (set by rocmkernels_attention_test_withhold_tile).
+__device__ int g_withheld_tile = -1;
+#endif
+
 constexpr int kQTile = 128;
 constexpr int kKeyTile = 64;
 constexpr float kPScale = 16384.f;  // P is split as P * 2^14
@@ -480,6 +486,9 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles>::kThreads, 1)
     // TMA loads of key tile j into its stage, completing on kv_full (producer thread only).
     const auto issue_tile = [&](int j) {
         const int stage = j % kStages;
+#ifdef RK_WAIT_TEST
+        if (blockIdx.x == 0 && j == g_withheld_tile) return;  // its kv_full phase never completes
+#endif
         RK_TRACE(j, 12);
         mbar_arrive_expect_tx(&s.kv_full[stage], ((kStats ? 1 : 2) * F::kBoxes + (kRotary ? 2 : 0)) * kBoxBytes);
         if constexpr (kRotary) {
@@ -550,11 +559,12 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles>::kThreads, 1)
                 issue_tile(j);
                 ++issued;
             }
-            if (!ok) {
-                // Do not leave copies in flight into shared memory of a finishing CTA.
-                for (int j = max(0, issued - kStages); j < issued; ++j)
-                    mbar_wait(&s.kv_full[j % kStages], (j / kStages) & 1);
-            }
+            // No copy may still be in flight into the shared memory of a finishing CTA. The last
+            // use of each stage is waited for even when every wait above succeeded: if the split
+            // warps gave up, the MMA warp still releases the stages it had, and the tiles issued
+            // into them are consumed by nobody. On the normal path these phases completed long
+            // ago (the split warps waited for them), so each wait is one test.
+            for (int j = max(0, issued - kStages); j < issued; ++j) mbar_wait(&s.kv_full[j % kStages], (j / kStages) & 1);
             // Prefetched tiles past the last visible key are never converted: wait for them.
             for (int j = tiles; j < prefetched; ++j) mbar_wait(&s.kv_full[j], 0);
         }
@@ -1166,6 +1176,14 @@ unsigned int read_device_status(bool clear) {
 const char *kernel_name(int head_width) {
     return head_width == 64 ? "tcgen05-f16x2-flash-d64" : head_width == 16 ? "tcgen05-f16x2-flash-d16" : "tcgen05-f16x2-flash-d32";
 }
+
+#ifdef RK_WAIT_TEST
+// Wait-test build only: makes CTA 0 of the next flash forwards withhold key tile `tile` (-1 to
+// stop). Returns the cudaMemcpyToSymbol status.
+extern "C" __attribute__((visibility("default"))) int rocmkernels_attention_test_withhold_tile(int tile) {
+    return cudaMemcpyToSymbol(g_withheld_tile, &tile, sizeof(tile));
+}
+#endif
 
 #ifdef RK_TC_TRACE
 extern "C" __attribute__((visibility("default"))) int rocmkernels_attention_trace(long long *out, int capacity) {

@@ -20,7 +20,14 @@ static __device__ unsigned int g_device_status = 0;
 constexpr unsigned int kStatusWaitTimeout = 1u;
 
 // ~1 s at 2 GHz: a healthy wait is microseconds; a wait this long means a protocol bug.
+// The wait-test build of the library (RK_WAIT_TEST, librocmkernels_attention_waittest.so, used
+// only by tests/test_wait_timeout_gpu.py) gives up after ~0.5 ms instead, so that a test can make
+// a wait run out quickly.
+#ifdef RK_WAIT_TEST
+constexpr long long kWaitTimeoutCycles = 1ll << 20;
+#else
 constexpr long long kWaitTimeoutCycles = 1ll << 31;
+#endif
 
 __device__ __forceinline__ uint32_t smem_u32(const void *pointer) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(pointer));
