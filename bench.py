@@ -72,6 +72,10 @@ WORKLOADS = {
                                                       "lengths U[1024,2048]"),
     "c5_fwd_bwd_b64h12s4096d32": dict(batch=64, heads=12, seq=4096, dim=32, radius=-1, lengths=None, backward=True,
                                       description="BASELINE configs[4]: forward+backward B64 H12 S4096 d32, full attention"),
+    "simt_fwd_b8h3s1024d32": dict(batch=8, heads=3, seq=1024, dim=32, radius=-1, lengths=None, backward=False,
+                                  entry="attention_fp32_forward",
+                                  description="the headline shape through attention_fp32_forward: the exact-FP32 SIMT kernel "
+                                              "(for the tensor-core vs SIMT comparison)"),
     "fwd_bwd_b4h12s4096d32": dict(batch=4, heads=12, seq=4096, dim=32, radius=-1, lengths=None, backward=True,
                                   description="profiling case: C5's shape at B=4 (inputs above L2, a few hundred MB)"),
 }
@@ -95,7 +99,9 @@ METRIC = "FP32 attention TFLOP/s (repo FLOP convention: 4*B*H*Q*K*d forward, 8*B
 
 
 def key_lengths(spec: dict) -> list[int]:
-    """Visible keys per sequence of the global batch (keys [0, length) visible)."""
+    """Visible keys per sequence of the global batch (keys [0, length) visible): BASELINE's
+    lengths U[lo, hi] drawn from MT19937 seed 105 (oracle.lengths, the same draws the parity tests
+    use); without the oracle library, numpy's generator (other values) stands in."""
     import numpy as np
 
     batch, seq, lengths = spec["batch"], spec["seq"], spec["lengths"]
@@ -104,7 +110,12 @@ def key_lengths(spec: dict) -> list[int]:
     if lengths == "c1":
         return [seq if b != 1 else seq - 16 for b in range(batch)]
     low, high = lengths
-    return [int(x) for x in np.random.default_rng(105).integers(low, high + 1, size=batch)]
+    try:
+        from oracle import oracle
+
+        return [int(x) for x in oracle.lengths(batch, 105, low, high)]
+    except (ImportError, OSError, subprocess.CalledProcessError):
+        return [int(x) for x in np.random.default_rng(105).integers(low, high + 1, size=batch)]
 
 
 def active_pairs(seq: int, radius: int, length: int) -> int:
@@ -237,9 +248,19 @@ def cpu_baseline(spec: dict) -> dict:
 
 
 def run_reference(args, rank: int) -> None:
-    """--impl reference: the reference's CPU attention on rank 0; other ranks exit without work."""
+    """--impl reference: the reference's CPU attention on rank 0; other ranks exit without work.
+
+    The reference's own ReferenceAttention (AttentionTests.cpp:28-125), compiled from its source
+    into oracle/_ref/libref_attention.so (a self-contained library: it maps neither this
+    repository's CUDA library nor a CUDA runtime), else the oracle's restatement of it. A step is
+    the workload's own (batch, head) slices on its seeded inputs -- all of them for the forward
+    workloads (the headline: B8 H3 S1024, 24 slices), a bounded sample of one slice per host
+    thread for the forward + backward configs -- spread over every host thread. The function always
+    computes forward and backward, so its FLOPs are counted as 12*S*S*d per slice."""
     if rank != 0:
         return
+    import concurrent.futures
+
     import numpy as np
     from oracle import oracle
 
@@ -257,29 +278,36 @@ def run_reference(args, rank: int) -> None:
                           "e2e": {"value": base["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
               flush=True)
         return
-    seq, dim, radius = spec["seq"], spec["dim"], spec["radius"]
-    length = key_lengths(spec)[0]
+    seq, dim, radius, heads = spec["seq"], spec["dim"], spec["radius"], spec["heads"]
     threads = oracle.cpu_count()
     use_ref = oracle.reference_available()
-    q = oracle.normal(threads * seq * dim, 101).reshape(threads, 1, seq, dim)
-    k = oracle.normal(threads * seq * dim, 102).reshape(threads, 1, seq, dim)
-    v = oracle.normal(threads * seq * dim, 103).reshape(threads, 1, seq, dim)
-    u = oracle.normal(threads * seq * dim, 104).reshape(threads, 1, seq, dim)
-    mask = np.zeros((1, seq), np.uint8)
-    mask[:, :length] = 1
+    lengths = key_lengths(spec)
+    if spec["backward"]:  # a bounded sample: one slice per thread, spread over the global batch
+        batch = min(spec["batch"], threads)
+        slice_list = [(b, b % heads) for b in range(batch)]
+        what = f"a sample of {batch} of the workload's {spec['batch'] * heads} (batch, head) slices"
+    else:
+        batch = spec["batch"]
+        slice_list = [(b, h) for b in range(batch) for h in range(heads)]
+        what = f"all {batch * heads} (batch, head) slices of the workload (B{batch} H{heads})"
+    count = batch * heads * seq * dim
+    q, k, v, u = (oracle.normal(count, seed).reshape(batch, heads, seq, dim) for seed in (101, 102, 103, 104))
+    mask = np.zeros((batch, seq), np.uint8)
+    for b in range(batch):
+        mask[b, :lengths[b]] = 1
 
-    def one_slice(i):
+    def one_slice(bh):
+        b, h = bh
+        cut = lambda x: np.ascontiguousarray(x[b:b + 1, h:h + 1])  # noqa: E731
         if use_ref:
-            oracle.reference_attention(q[i:i + 1], k[i:i + 1], v[i:i + 1], mask, u[i:i + 1], radius)
+            oracle.reference_attention(cut(q), cut(k), cut(v), mask[b:b + 1], cut(u), radius)
         else:
-            oracle.attention(q[i:i + 1], k[i:i + 1], v[i:i + 1], mask, u[i:i + 1], radius, threads=1)
+            oracle.attention(cut(q), cut(k), cut(v), mask[b:b + 1], cut(u), radius, threads=1)
+
+    pool = concurrent.futures.ThreadPoolExecutor(threads)  # the library calls release the GIL
 
     def step():
-        workers = [threading.Thread(target=one_slice, args=(i,)) for i in range(threads)]
-        for w in workers:
-            w.start()
-        for w in workers:
-            w.join()
+        list(pool.map(one_slice, slice_list))
 
     for _ in range(args.warmup):
         step()
@@ -287,17 +315,18 @@ def run_reference(args, rank: int) -> None:
     for _ in range(args.steps):
         step()
     elapsed = time.perf_counter() - start
-    flops = 12.0 * threads * seq * seq * dim * args.steps  # forward (4) + backward (8) per pair: it computes both
+    pool.shutdown()
+    flops = 12.0 * len(slice_list) * seq * seq * dim * args.steps  # forward (4) + backward (8): it computes both
     value = flops / elapsed / 1e12
     kind = "reference" if use_ref else "port"
     sample = (f"{'ReferenceAttention (AttentionTests.cpp:28-125, compiled from the reference source)' if use_ref else 'oracle port'}"
-              f" forward+backward of {threads} (batch, head) slices S={seq} d={dim} ({length} visible keys, radius {radius})"
-              f" per step, one slice per thread; FLOPs counted as 12*S*S*d per slice (the function always computes"
-              f" forward and backward)")
+              f" forward+backward of {what} per step, S={seq} d={dim}, radius {radius}, on {threads} threads;"
+              f" FLOPs counted as 12*S*S*d per slice (the function always computes forward and backward)")
     line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3, "higher_is_better": True,
             "scaling": "weak" if not spec["backward"] else "strong", "vs_baseline": None,
-            "dtype": "f64-accumulate/f32-storage", "data": "synthetic N(0,1), seeded",
+            "dtype": "f64-accumulate/f32-storage",
+            "data": "synthetic N(0,1), seeds 101-104 (std::mt19937 + libstdc++ normal_distribution, the reference's generator)",
             "config": workload_config(args.workload, args.gpus), "impl": "reference",
             "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": kind, "sample": sample},
             "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -493,6 +522,167 @@ def traffic_from_profiles(kernel_tag: str, workload: str):
     return None
 
 
+def seeded_problem(batch: int, heads: int, seq: int, dim: int, lengths: list[int], upstream: bool):
+    """The workload's inputs: Q, K, V (and dO) ~ N(0, 1) from seeds 101..104 drawn with the
+    reference's generator (std::mt19937 + libstdc++ normal_distribution, restated in
+    oracle/attention_oracle.c; the parity tests draw the same tensors), and the [batch, seq] mask
+    with keys [0, length) visible. Returns (arrays, description), or (None, reason) when that
+    generator's library is not available (the caller then draws from torch and reports no parity)."""
+    import concurrent.futures
+
+    import numpy as np
+
+    try:
+        from oracle import oracle
+
+        oracle._load_oracle()
+    except Exception as error:  # noqa: BLE001 - any failure to load the generator
+        return None, f"seeded generator unavailable ({type(error).__name__})"
+    count = batch * heads * seq * dim
+    seeds = (101, 102, 103, 104) if upstream else (101, 102, 103)
+    with concurrent.futures.ThreadPoolExecutor(len(seeds)) as pool:  # the generator releases the GIL
+        drawn = list(pool.map(lambda seed: oracle.normal(count, seed).reshape(batch, heads, seq, dim), seeds))
+    mask = np.zeros((batch, seq), np.uint8)
+    for b, length in enumerate(lengths):
+        mask[b, :length] = 1
+    arrays = {"q": drawn[0], "k": drawn[1], "v": drawn[2], "mask": mask}
+    if upstream:
+        arrays["upstream"] = drawn[3]
+    return arrays, ("synthetic N(0,1), seeds 101-104 (Q, K, V, dO) from std::mt19937 + libstdc++ normal_distribution, "
+                    "the reference's generator")
+
+
+def _normwise(actual, expected) -> float:
+    """max|actual - expected| / max|expected| over finite entries; inf if the non-finite patterns differ."""
+    import numpy as np
+
+    a, e = np.asarray(actual, np.float64), np.asarray(expected, np.float64)
+    finite = np.isfinite(e)
+    if not np.array_equal(finite, np.isfinite(a)) or not np.array_equal(np.isnan(a), np.isnan(e)):
+        return float("inf")
+    if not finite.any():
+        return 0.0
+    scale = float(np.max(np.abs(e[finite])))
+    diff = float(np.max(np.abs(a[finite] - e[finite])))
+    return diff / scale if scale > 0 else diff
+
+
+def parity_check(arrays: dict, results: dict, slices: list, radius: int, backward: bool) -> dict:
+    """The CPU oracle (checker only) on the listed (batch, head) slices of the workload's own inputs,
+    compared with the device's results for those slices (`results`: name -> [B, H, ...] arrays).
+    Bars: O and lse normwise <= 1e-5, gradients <= 1e-4 (the parity tests' bars)."""
+    import concurrent.futures
+
+    import numpy as np
+    from oracle import oracle
+
+    def one(bh):
+        b, h = bh
+        cut = lambda x: np.ascontiguousarray(x[b:b + 1, h:h + 1])  # noqa: E731
+        return oracle.attention(cut(arrays["q"]), cut(arrays["k"]), cut(arrays["v"]), arrays["mask"][b:b + 1],
+                                cut(arrays["upstream"]) if backward else None, radius, forward_only=not backward)
+
+    with concurrent.futures.ThreadPoolExecutor(max(1, min(len(slices), oracle.cpu_count()))) as pool:
+        expected = list(pool.map(one, slices))
+    names = [("O", "out", "output", None), ("lse_max", "lse", "lse", 0), ("lse_sum", "lse", "lse", 1)]
+    if backward:
+        names += [(n, n, n, None) for n in ("grad_q", "grad_k", "grad_v")]
+    errors = {}
+    for label, ours, theirs, column in names:
+        worst = 0.0
+        for (b, h), exp in zip(slices, expected):
+            got = results[ours][b:b + 1, h:h + 1]
+            want = exp[theirs]
+            if column is not None:
+                got, want = got[..., column], want[..., column]
+            worst = max(worst, _normwise(got, want))
+        errors[label] = worst
+    ok = all(v <= (1e-4 if k.startswith("grad") else 1e-5) for k, v in errors.items())
+    return {"ok": bool(ok), "slices": len(slices), **{f"max_rel_{k}": v for k, v in errors.items()},
+            "bars": "normwise max|x-ref|/max|ref|: O, lse <= 1e-5; gradients <= 1e-4",
+            "checker": "oracle/attention_oracle.c (ReferenceAttention restated, pinned bit-exact to the reference)"}
+
+
+def c5_strong(args, device, world: int, rank: int, dist, api) -> dict:
+    """BASELINE configs[4] (B64 H12 S4096 d32, forward + backward, full attention) strong-scaled:
+    the global problem is split over the ranks by rocmkernels_b200.sharding (contiguous batch
+    ranges), every rank making its calls through the library's entry points, no collective on the
+    data path. Inputs are larger than L2 (1.6 GB), so no flush between steps. Rank 0 checks the
+    (0, 0) slice, which it computes itself, against the oracle."""
+    import torch
+
+    from rocmkernels_b200.sharding import run_backward, run_forward, shard_plan
+
+    spec = WORKLOADS["c5_fwd_bwd_b64h12s4096d32"]
+    B, H, S, D = spec["batch"], spec["heads"], spec["seq"], spec["dim"]
+    arrays, data = seeded_problem(B, H, S, D, [S] * B, True)
+    generator = torch.Generator(device=device)
+    generator.manual_seed(101)
+    t = {}
+    for name in ("q", "k", "v", "upstream"):
+        t[name] = (torch.from_numpy(arrays[name]).to(device) if arrays is not None
+                   else torch.randn(B, H, S, D, device=device, generator=generator))
+    t["mask"] = torch.ones(B, S, dtype=torch.uint8, device=device)
+    t["out"] = torch.empty_like(t["q"])
+    t["lse"] = torch.empty(B, H, S, 2, device=device)
+    for name in ("grad_q", "grad_k", "grad_v"):
+        t[name] = torch.empty_like(t["q"])
+    t["delta"] = torch.empty(B, H, S, device=device)
+    st = api.strides_of(t["q"])
+    strides = {r: st for r in ("q", "k", "v", "out", "upstream")}
+    plan = shard_plan(B, H, world, rank)
+    geometry = dict(heads=H, queries=S, keys=S, width=D, radius=-1, strides=strides)
+    stream = torch.cuda.current_stream(device)
+    fwd_t = {r: t[r] for r in ("q", "k", "v", "mask", "out", "lse")}
+
+    def forward():
+        status = run_forward(api.attention_fp32_forward_flash, fwd_t, plan, stream=stream, **geometry)
+        if status != 0:
+            raise api.HipError(status, "attention_fp32_forward_flash")
+
+    def backward():
+        status = run_backward(api.attention_fp32_backward, t, plan, stream=stream, **geometry)
+        if status != 0:
+            raise api.HipError(status, "attention_fp32_backward")
+
+    for _ in range(2):
+        forward()
+        backward()
+    steps = max(3, min(args.steps, 10))
+    marks = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    for i in range(steps):
+        marks[i][0].record(stream)
+        forward()
+        marks[i][1].record(stream)
+        backward()
+        marks[i][2].record(stream)
+    torch.cuda.synchronize(device)
+    own = [sum(m[0].elapsed_time(m[1]) for m in marks) / steps, sum(m[1].elapsed_time(m[2]) for m in marks) / steps]
+    times = torch.tensor([own[0] + own[1]] + own, device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    step_ms, forward_ms, backward_ms = times.tolist()
+    slices = [c.batch * c.heads for c in plan]
+    record = {"workload": "c5_fwd_bwd_b64h12s4096d32", "description": spec["description"], "scaling": "strong",
+              "ranks": world, "steps": steps, "ms_per_step": step_ms, "forward_ms": forward_ms, "backward_ms": backward_ms,
+              "tflops": 12.0 * B * H * S * S * D / (step_ms * 1e-3) / 1e12,
+              "rank0_slices": sum(slices), "rank0_active_pairs": sum(slices) * S * S,
+              "partition": "rocmkernels_b200.sharding.shard_plan: contiguous batch ranges, no collective on the data path",
+              "gpu_launches_per_rank": steps * 3 * len(plan), "data": data,
+              "time": "CUDA events per rank around each step's calls, mean over steps, max over ranks; inputs > L2"}
+    if rank == 0 and arrays is not None:
+        results = {n: t[n][0:1, 0:1].cpu().numpy() for n in ("out", "lse", "grad_q", "grad_k", "grad_v")}
+        record["parity"] = parity_check(arrays, results, [(0, 0)], -1, True)
+    if world > 1:
+        dist.barrier()
+    del t, fwd_t
+    torch.cuda.empty_cache()
+    return record
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--gpus", type=int, default=1)
@@ -501,6 +691,7 @@ def main() -> None:
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
     parser.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
     parser.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU oracle leg")
+    parser.add_argument("--no-c5", action="store_true", help="skip the C5 strong-scaling record of the default workload")
     args = parser.parse_args()
 
     rank = env_int("RANK", 0)
@@ -514,6 +705,7 @@ def main() -> None:
     import torch.distributed as dist
 
     import rocmkernels_b200.attention as api
+    from rocmkernels_b200.sharding import ShardCall, run_backward, run_forward, shard_plan
 
     if not torch.cuda.is_available():
         raise SystemExit("bench.py needs a CUDA device")
@@ -544,19 +736,26 @@ def main() -> None:
     generic = spec.get("generic")  # None, or the generic forward's storage type
     rotary = spec.get("rotary", False)
     storage = torch.float16 if generic == "fp16" else torch.float32
+    batch = spec["batch"]
     if with_backward:
-        if spec["batch"] % world:
-            raise SystemExit(f"the global batch {spec['batch']} must be divisible by the {world} ranks")
-        batch = spec["batch"] // world
-        lengths = key_lengths(spec)[rank * batch:(rank + 1) * batch]
+        # Strong scaling: every rank holds the global problem and computes its shard of (batch,
+        # head) slices through the library's calls (rocmkernels_b200.sharding).
+        lengths = key_lengths(spec)
+        plan = shard_plan(batch, heads, world, rank)
     else:
-        batch = spec["batch"]
+        # Weak scaling: every rank runs the whole per-GPU problem (the same seeded inputs).
         lengths = [seq] * batch
+        plan = [ShardCall(0, batch, 0, heads)]
+    arrays, data = seeded_problem(batch, heads, seq, dim, lengths, with_backward)
     generator = torch.Generator(device=device)
-    generator.manual_seed(101 + rank)
-    q = torch.randn(batch, heads, seq, dim, device=device, generator=generator).to(storage)
-    k = torch.randn(batch, heads, seq, dim, device=device, generator=generator).to(storage)
-    v = torch.randn(batch, heads, seq, dim, device=device, generator=generator).to(storage)
+    generator.manual_seed(101)
+
+    def device_input(name):
+        if arrays is not None:
+            return torch.from_numpy(arrays[name]).to(device).to(storage)
+        return torch.randn(batch, heads, seq, dim, device=device, generator=generator).to(storage)
+
+    q, k, v = device_input("q"), device_input("k"), device_input("v")
     mask = torch.zeros(batch, seq, dtype=torch.uint8, device=device)
     for i, length in enumerate(lengths):
         mask[i, :length] = 1
@@ -572,7 +771,7 @@ def main() -> None:
         rotated_k = torch.empty_like(rotated_q)
         inputs += [cos, sin]
     if with_backward:
-        upstream = torch.randn(batch, heads, seq, dim, device=device, generator=generator)
+        upstream = device_input("upstream").float()
         gq, gk, gv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
         delta = torch.empty(batch, heads, seq, device=device)
         inputs.append(upstream)
@@ -580,62 +779,68 @@ def main() -> None:
     flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=device)
     stream = torch.cuda.current_stream(device)
     qs, ks, vs, os_ = (api.strides_of(t) for t in (q, k, v, out))
-    forward_fn = api.attention_fp32_forward_flash if dim == 32 else api.attention64_fp32_forward
+    forward_fn = (getattr(api, spec["entry"]) if spec.get("entry") else
+                  api.attention_fp32_forward_flash if dim == 32 else api.attention64_fp32_forward)
     backward_fn = api.attention_fp32_backward if dim == 32 else api.attention64_fp32_backward
-    pairs = sum(active_pairs(seq, radius, length) for length in lengths) * heads
-    flops_forward, flops_backward = 4.0 * batch * heads * seq * seq * dim, 8.0 * batch * heads * seq * seq * dim
-    effective_forward, effective_backward = 4.0 * pairs * dim, 8.0 * pairs * dim
-    flops_per_step = flops_forward + (flops_backward if with_backward else 0.0)
-    effective_per_step = effective_forward + (effective_backward if with_backward else 0.0)
+    # This rank's work: the (batch, head) slices of its plan.
+    rank_pairs = sum(active_pairs(seq, radius, lengths[b]) * (c.h1 - c.h0) for c in plan for b in range(c.b0, c.b1))
+    rank_slices = sum(c.batch * c.heads for c in plan)
+    flops_forward, flops_backward = 4.0 * rank_slices * seq * seq * dim, 8.0 * rank_slices * seq * seq * dim
+    effective_forward, effective_backward = 4.0 * rank_pairs * dim, 8.0 * rank_pairs * dim
     # Whole-job totals over all ranks: under strong scaling the ranks hold different sequences
     # (key-padded lengths differ), so the job's active pairs are summed over the global batch;
     # under weak scaling every rank runs the same shape.
     if with_backward:
-        job_pairs = sum(active_pairs(seq, radius, length) for length in key_lengths(spec)) * heads
-        job_flops_per_step = (4.0 + 8.0) * spec["batch"] * heads * seq * seq * dim
+        job_pairs = sum(active_pairs(seq, radius, length) for length in lengths) * heads
+        job_flops_per_step = (4.0 + 8.0) * batch * heads * seq * seq * dim
         job_effective_forward, job_effective_backward = 4.0 * job_pairs * dim, 8.0 * job_pairs * dim
     else:
-        job_flops_per_step = world * flops_per_step
+        job_flops_per_step = world * flops_forward
         job_effective_forward, job_effective_backward = world * effective_forward, 0.0
     job_effective_per_step = job_effective_forward + job_effective_backward
-    launches_per_step = 1 + (2 if with_backward else 0)
+    launches_per_step = len(plan) * (1 + (2 if with_backward else 0))
 
-    # The step's device tensors by name (one set for the device-timed steps; the e2e leg uses two).
+    # The step's device tensors by role (one set for the device-timed steps; the e2e leg uses two).
     tensors = dict(q=q, k=k, v=v, mask=mask, out=out, lse=lse)
     if rotary:
         tensors.update(cos=cos, sin=sin)
     if with_backward:
-        tensors.update(upstream=upstream, gq=gq, gk=gk, gv=gv, delta=delta)
+        tensors.update(upstream=upstream, grad_q=gq, grad_k=gk, grad_v=gv, delta=delta)
+    strides = {"q": qs, "k": ks, "v": vs, "out": os_}
+    if with_backward:
+        strides["upstream"] = api.strides_of(upstream)
 
-    def make_phases(t, st):
-        """The step's kernel calls on tensor set `t`, launched on stream `st`."""
+    def make_phases(t, st, calls, problem_batch):
+        """The step's kernel calls on tensor set `t` (a problem of `problem_batch` sequences),
+        making the calls of `calls`, launched on stream `st`."""
+        geometry = dict(heads=heads, queries=seq, keys=seq, width=dim, radius=radius, strides=strides)
+
         def forward():
             if rotary:
                 status = api.attention_fp32_forward_flash_rotary(t["q"], t["k"], t["v"], t["cos"], t["sin"], t["mask"], t["out"],
-                                                                 t["lse"], batch, heads, seq, seq, radius, qs, ks, vs, table_strides,
-                                                                 table_strides, os_, st)
+                                                                 t["lse"], problem_batch, heads, seq, seq, radius, qs, ks, vs,
+                                                                 table_strides, table_strides, os_, st)
                 if status != 0:
                     raise api.HipError(status, "attention_fp32_forward_flash_rotary")
                 return
             if generic:
-                status = api.attention_generic_forward(t["q"], t["k"], t["v"], t["mask"], t["out"], t["lse"], batch, heads, seq, seq,
-                                                       dim, radius, qs, ks, vs, os_,
+                status = api.attention_generic_forward(t["q"], t["k"], t["v"], t["mask"], t["out"], t["lse"], problem_batch, heads,
+                                                       seq, seq, dim, radius, qs, ks, vs, os_,
                                                        api.DType.Float16 if generic == "fp16" else api.DType.Float32, st)
             else:
-                status = forward_fn(t["q"], t["k"], t["v"], t["mask"], t["out"], t["lse"], batch, heads, seq, seq, radius, qs, ks, vs,
-                                    os_, st)
+                status = run_forward(forward_fn, {r: t[r] for r in ("q", "k", "v", "mask", "out", "lse")}, calls, stream=st,
+                                     **geometry)
             if status != 0:
                 raise api.HipError(status, "attention_generic_forward" if generic else forward_fn.__name__)
 
         def backward():
-            status = backward_fn(t["q"], t["k"], t["v"], t["mask"], t["out"], t["lse"], t["upstream"], t["gq"], t["gk"], t["gv"],
-                                 t["delta"], batch, heads, seq, seq, radius, qs, ks, vs, os_, api.strides_of(t["upstream"]), st)
+            status = run_backward(backward_fn, t, calls, stream=st, **geometry)
             if status != 0:
                 raise api.HipError(status, backward_fn.__name__)
 
         return [forward, backward] if with_backward else [forward]
 
-    phases = make_phases(tensors, stream)
+    phases = make_phases(tensors, stream, plan, batch)
 
     def unfused_rotary_forward():
         """rotary_fp32 into token-major buffers, then the flash forward on them (the unfused sequence)."""
@@ -648,18 +853,24 @@ def main() -> None:
         if status != 0:
             raise api.HipError(status, "rotary_fp32 + attention_fp32_forward_flash")
 
-    # Host-buffer leg: pinned inputs copied in and outputs copied out every step, two device sets.
-    host_inputs = [t.cpu().pin_memory() for t in inputs]
-    host_outputs = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in outputs]
-    h2d_bytes = sum(t.numel() * t.element_size() for t in host_inputs)
-    d2h_bytes = sum(t.numel() * t.element_size() for t in host_outputs)
-    second = {name: torch.empty_like(t) for name, t in tensors.items()}
-    by_id = {id(t): name for name, t in tensors.items()}
-    e2e_tensors = [tensors, second]
+    # Host-buffer leg: pinned inputs copied in and outputs copied out every step, two device sets of
+    # this rank's sequences [base, end) (its whole problem under weak scaling).
+    base, end = min(c.b0 for c in plan), max(c.b1 for c in plan)
+    local_plan = [ShardCall(c.b0 - base, c.b1 - base, c.h0, c.h1) for c in plan]
+    local = {name: x[base:end] for name, x in tensors.items() if name not in ("cos", "sin")}
+    if rotary:
+        local.update(cos=cos, sin=sin)
+    by_id = {id(x): name for name, x in tensors.items()}
+    host_inputs = [local[by_id[id(x)]].cpu().pin_memory() for x in inputs]
+    host_outputs = [torch.empty(local[by_id[id(x)]].shape, dtype=x.dtype).pin_memory() for x in outputs]
+    h2d_bytes = sum(x.numel() * x.element_size() for x in host_inputs)
+    d2h_bytes = sum(x.numel() * x.element_size() for x in host_outputs)
+    second = {name: torch.empty_like(x) for name, x in local.items()}
+    e2e_tensors = [local, second]
     e2e_sets = [([t[by_id[id(x)]] for x in inputs], [t[by_id[id(x)]] for x in outputs]) for t in e2e_tensors]
 
     def launch_set(index, st):
-        for phase in make_phases(e2e_tensors[index], st):
+        for phase in make_phases(e2e_tensors[index], st, local_plan, end - base):
             phase()
 
     def timed(fns, steps):
@@ -694,6 +905,17 @@ def main() -> None:
     if world > 1:
         dist.barrier()
     clocks = sampler.stop() if rank == 0 else None
+
+    # The results of the last timed step, for the parity check below (the outputs of the e2e leg
+    # are other buffers).
+    parity_results = None
+    if rank == 0 and arrays is not None and not rotary and not generic:
+        chosen = sorted({(b, h) for c in plan for b in range(c.b0, c.b1) for h in range(c.h0, c.h1)})
+        if len(chosen) > 24:  # a bounded, declared subset: the first, middle and last slice of the rank
+            chosen = [chosen[0], chosen[len(chosen) // 2], chosen[-1]]
+        names = ["out", "lse"] + (["grad_q", "grad_k", "grad_v"] if with_backward else [])
+        parity_slices = chosen
+        parity_results = {n: tensors[n].cpu().numpy() for n in names}
 
     pipelined_e2e(device, e2e_sets, host_inputs, host_outputs, launch_set, 2)
     e2e_steps = max(1, min(args.steps, 50))
@@ -732,6 +954,8 @@ def main() -> None:
         if generic:
             path = api.generic_kernel_name(batch, heads, seq, seq, dim,
                                            api.DType.Float16 if generic == "fp16" else api.DType.Float32)
+        elif spec.get("entry") == "attention_fp32_forward":
+            path = f"simt-fp32-forward-d{dim}"
         else:
             path = api.flash_kernel_name(batch, heads, seq, seq, dim) + ("+rotary" if rotary else "")
         if path.startswith("tcgen05"):
@@ -760,7 +984,7 @@ def main() -> None:
         "scaling": "strong" if with_backward else "weak",
         "vs_baseline": None if with_backward or generic or rotary else value / PUBLISHED_TFLOPS,
         "dtype": generic or "f32",
-        "data": "synthetic N(0,1) from a seeded torch generator (rank-dependent seed)",
+        "data": data if arrays is not None else f"synthetic N(0,1) from a seeded torch generator ({data})",
         "config": workload_config(args.workload, world),
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": d2h_bytes,
                 "steps": e2e_steps},
@@ -768,6 +992,8 @@ def main() -> None:
         "gpu_launches": args.steps * launches_per_step,
         "clocks": clocks,
     }
+    if generic == "fp16" and arrays is not None:
+        line["data"] += ", rounded to FP16 storage"
     if with_backward:
         line["effective"] = {"value": job_effective_per_step * args.steps / device_seconds / 1e12, "unit": "TFLOP/s",
                              "flops": "12*d per active (query, key) pair"}
@@ -778,6 +1004,10 @@ def main() -> None:
         line["unfused"] = {"ms_per_step": unfused_seconds / args.steps * 1e3,
                            "sequence": "rotary_fp32 (token-major outputs) then attention_fp32_forward_flash",
                            "tflops": job_flops_per_step * args.steps / unfused_seconds / 1e12}
+    if args.workload == DEFAULT_WORKLOAD and not args.no_c5:
+        line["c5_strong"] = c5_strong(args, device, world, rank, dist, api)
+    if parity_results is not None:
+        line["parity"] = parity_check(arrays, parity_results, parity_slices, radius, with_backward)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(spec)
     if rank == 0:

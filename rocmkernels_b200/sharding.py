@@ -9,6 +9,12 @@ delta and gradients by (b*heads + h) rows.
 ``shard_plan`` returns the calls one rank makes: contiguous batch ranges when there are at
 least as many sequences as ranks, otherwise one call per sequence over a contiguous head range
 (a single sequence's heads are contiguous in every packed output).
+
+``shard_offsets`` turns one call into the element offset of every tensor argument, and
+``run_forward`` / ``run_backward`` make a rank's calls through the library's entry points
+(``rocmkernels_b200.attention``) with those offsets applied to the full tensors' device
+addresses. The offsets are plain integers, so the same function drives the CPU check in
+tests/test_sharding.py.
 """
 from __future__ import annotations
 
@@ -61,3 +67,64 @@ def shard_plan(batch: int, heads: int, world: int, rank: int) -> list[ShardCall]
         if hi > lo:
             calls.append(ShardCall(b, b + 1, lo - b * heads, hi - b * heads))
     return calls
+
+
+# Tensor arguments by role: strided [batch][heads][tokens][D] inputs/outputs, the [batch][keys]
+# mask, and the packed outputs (their row counts per (batch, head) slice and row width).
+STRIDED = ("q", "k", "v", "out", "upstream")
+
+
+def shard_offsets(call: ShardCall, *, heads: int, queries: int, keys: int, width: int, strides: dict) -> dict:
+    """Element offsets of every tensor argument for `call` into the full problem's tensors.
+
+    `strides` maps the strided roles present (q, k, v, out, upstream) to (batch, head, token)
+    element strides. Packed outputs: lse [B][H][Q][2], delta [B][H][Q], grad_q [B][H][Q][D],
+    grad_k and grad_v [B][H][K][D]."""
+    first_row = call.b0 * heads + call.h0  # flattened (batch, head) slice of the call's first row block
+    offsets = {"mask": call.b0 * keys, "lse": first_row * queries * 2, "delta": first_row * queries,
+               "grad_q": first_row * queries * width, "grad_k": first_row * keys * width,
+               "grad_v": first_row * keys * width}
+    for role, s in strides.items():
+        sb, sh = (s.batch, s.head) if hasattr(s, "batch") else (s[0], s[1])
+        offsets[role] = call.b0 * sb + call.h0 * sh
+    return offsets
+
+
+def _address(tensor) -> int:
+    return tensor if isinstance(tensor, int) else int(tensor.data_ptr())
+
+
+def _shifted(tensors: dict, offsets: dict, element_bytes: dict) -> dict:
+    return {role: _address(t) + offsets[role] * element_bytes.get(role, 4) for role, t in tensors.items()}
+
+
+def run_forward(entry, tensors: dict, plan: list[ShardCall], *, heads: int, queries: int, keys: int, width: int, radius: int,
+                strides: dict, stream=None) -> int:
+    """One rank's forward calls: `entry` is a forward entry point of rocmkernels_b200.attention
+    (same argument order as attention_fp32_forward_flash); `tensors` holds the full problem's q,
+    k, v, mask, out, lse (torch tensors or device addresses). Returns the first non-zero status."""
+    for call in plan:
+        offsets = shard_offsets(call, heads=heads, queries=queries, keys=keys, width=width,
+                                strides={r: strides[r] for r in ("q", "k", "v", "out")})
+        p = _shifted(tensors, offsets, {"mask": 1})
+        status = entry(p["q"], p["k"], p["v"], p["mask"], p["out"], p["lse"], call.batch, call.heads, queries, keys, radius,
+                       strides["q"], strides["k"], strides["v"], strides["out"], stream)
+        if status != 0:
+            return status
+    return 0
+
+
+def run_backward(entry, tensors: dict, plan: list[ShardCall], *, heads: int, queries: int, keys: int, width: int, radius: int,
+                 strides: dict, stream=None) -> int:
+    """One rank's backward calls (argument order of attention_fp32_backward); `tensors` holds the
+    full problem's q, k, v, mask, out, lse, upstream, grad_q, grad_k, grad_v, delta."""
+    for call in plan:
+        offsets = shard_offsets(call, heads=heads, queries=queries, keys=keys, width=width,
+                                strides={r: strides[r] for r in STRIDED})
+        p = _shifted(tensors, offsets, {"mask": 1})
+        status = entry(p["q"], p["k"], p["v"], p["mask"], p["out"], p["lse"], p["upstream"], p["grad_q"], p["grad_k"],
+                       p["grad_v"], p["delta"], call.batch, call.heads, queries, keys, radius, strides["q"], strides["k"],
+                       strides["v"], strides["out"], strides["upstream"], stream)
+        if status != 0:
+            return status
+    return 0
