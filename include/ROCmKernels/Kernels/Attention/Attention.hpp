@@ -59,7 +59,7 @@ namespace ROCmKernels::Kernels {
                 attention_fp32_forward_tuned(q, k, v, mask, output, lse, batch, heads, queries, keys, radius, group, qs, ks, vs, os, stream));
     }
 
-    /// Flash forward: tcgen05/TMEM kernel with 3xTF32 compensation on sm_100a.
+    /// Flash forward: tcgen05/TMEM kernel with split-FP16 operands (kind::f16, ~22-bit products) on sm_100a.
     inline void AttentionForwardFlash(const float *q, const float *k, const float *v, const bool *mask, float *output, float *lse,
             const int batch, const int heads, const int queries, const int keys, const int radius, const Strides &qs, const Strides &ks,
             const Strides &vs, const Strides &os, hipStream_t stream = nullptr) {

@@ -108,8 +108,9 @@ ROCMKERNELS_C_EXPORT int attention_fp32_forward_tuned(const float *q, const floa
         RocmKernelsStrides qs, RocmKernelsStrides ks, RocmKernelsStrides vs, RocmKernelsStrides os,
         RocmKernelsStream stream);
 
-/* Flash forward, the headline entry: tcgen05/TMEM 3xTF32 kernel on sm_100a; radius < -1 is
- * invalid. Replaces attention_fp32_forward_flash (Attention.hpp:28-30; Attention.hip:372-390). */
+/* Flash forward, the headline entry: tcgen05/TMEM kernel on sm_100a with split-FP16 operands
+ * (kind::f16; each FP32 operand as two FP16 terms, three products) when the tensors are
+ * TMA-addressable, else the exact FP32 SIMT kernel; radius < -1 is invalid. Replaces attention_fp32_forward_flash (Attention.hpp:28-30; Attention.hip:372-390). */
 ROCMKERNELS_C_EXPORT int attention_fp32_forward_flash(const float *q, const float *k, const float *v, const bool *mask,
         float *output, float *lse, int batch, int heads, int queries, int keys, int radius, RocmKernelsStrides qs,
         RocmKernelsStrides ks, RocmKernelsStrides vs, RocmKernelsStrides os, RocmKernelsStream stream);

@@ -6,7 +6,7 @@ Parity bars (written here once, used by every test):
   * gradients and delta: normwise <= GRADIENT_TOL;
   * key selection: bit-exact (non-finite lse entries must match exactly, masked keys give
     dK = dV = 0.0 exactly).
-The tensor-core (3xTF32) flash path is held to the same bars as the SIMT path.
+The tensor-core (split-FP16, kind::f16) paths are held to the same bars as the SIMT path.
 """
 from __future__ import annotations
 
