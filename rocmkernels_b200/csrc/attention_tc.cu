@@ -17,8 +17,9 @@
 //
 // Split FP16 operands. Every FP32 operand x is scaled by a power of two 2^e (Q: per row; K, V:
 // per tile; P: 2^14) so that its largest magnitude lies in [2^14, 2^15), then split
-// x' = x0 + x1 with x0 = x' cut to 11 significant bits (exactly representable in FP16) and
-// x1 = FP16(x' - x0). Products keep ~22 bits:
+// x' = x0 + x1: for Q, K and V x0 = FP16(x') (cvt.rn: 11 significant bits) and x1 = FP16(x' - x0),
+// the residual taken from x0 widened back (tc_operands.cuh, split_pack2); for P x0 = P' with its
+// low 13 mantissa bits cleared (also exact in FP16) and x1 = FP16(P' - x0). Products keep ~22 bits:
 //   S            = q0.k1 + q1.k0 + q0.k0               (M128 N64 K16 x 6; scaled by 2^(a_i + b_j))
 //   [Oa|Ob|sums] = p1.[v0 ; v1 ; 1] + p0.[v0 ; v1 ; 1] (M128 N80 K16 x 8), Ot = Oa + Ob
 //   (P keeps its 2^14 in Ot and in the row sums, so it cancels in O = sum Ot / sum P; the 16
@@ -734,11 +735,10 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles>::kThreads, 1)
             for (int m = 0; m < D / 8; ++m) {
                 const float x[8] = {kx[2 * m].x, kx[2 * m].y, kx[2 * m].z, kx[2 * m].w,
                                     kx[2 * m + 1].x, kx[2 * m + 1].y, kx[2 * m + 1].z, kx[2 * m + 1].w};
-                float x0[8], x1[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) split_half(x[e], k_scale, x0[e], x1[e]);
-                *row_chunk<D>(s.k16[stage], row, 0, m) = pack_chunk(x0);
-                *row_chunk<D>(s.k16[stage], row, 1, m) = pack_chunk(x1);
+                uint4 c0, c1;
+                split_pack8<false>(x, k_scale, c0, c1);
+                *row_chunk<D>(s.k16[stage], row, 0, m) = c0;
+                *row_chunk<D>(s.k16[stage], row, 1, m) = c1;
             }
             // V^T rows f (v0) and D + f (v1), keys 8g..8g+7 = 16-byte chunk g (swizzled by f % 8)
             uint4 *vt16 = reinterpret_cast<uint4 *>(s.vt16[stage]);
@@ -749,15 +749,16 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles>::kThreads, 1)
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                     const int f = 4 * fchunk + e;
-                    float v0[8], v1[8];
+                    float column[8];
 #pragma unroll
                     for (int r = 0; r < 8; ++r) {
                         const float4 &x = vx[item][r];
-                        const float value = e == 0 ? x.x : e == 1 ? x.y : e == 2 ? x.z : x.w;
-                        split_half(value, v_scale, v0[r], v1[r]);
+                        column[r] = e == 0 ? x.x : e == 1 ? x.y : e == 2 ? x.z : x.w;
                     }
-                    vt16[f * 8 + (group ^ (f & 7))] = pack_chunk(v0);
-                    vt16[(D + f) * 8 + (group ^ (f & 7))] = pack_chunk(v1);
+                    uint4 c0, c1;
+                    split_pack8<false>(column, v_scale, c0, c1);
+                    vt16[f * 8 + (group ^ (f & 7))] = c0;
+                    vt16[(D + f) * 8 + (group ^ (f & 7))] = c1;
                 }
             }
             fence_proxy_async_shared();
@@ -821,11 +822,10 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles>::kThreads, 1)
                 float packed0[16], packed1[16];
 #pragma unroll
                 for (int c = 0; c < 16; ++c) {
-                    float a0, a1, b0, b1;
-                    split_half(x[32 * half + 2 * c], q_scale, a0, a1);
-                    split_half(x[32 * half + 2 * c + 1], q_scale, b0, b1);
-                    packed0[c] = __uint_as_float(pack_half2(a0, b0));
-                    packed1[c] = __uint_as_float(pack_half2(a1, b1));
+                    uint32_t p0, p1;
+                    split_pack2<false>(x[32 * half + 2 * c], x[32 * half + 2 * c + 1], q_scale, p0, p1);
+                    packed0[c] = __uint_as_float(p0);
+                    packed1[c] = __uint_as_float(p1);
                 }
                 tmem_store16x2(lane_base + F::kColQ0 + 16 * half, packed0, lane_base + F::kColQ1 + 16 * half, packed1);
             }

@@ -161,11 +161,10 @@ __device__ __forceinline__ void store_row_operand(const float (&x)[D], int expon
         float a[16], b[16];
 #pragma unroll
         for (int c = 0; c < 16; ++c) {
-            float a0, a1, b0, b1;
-            split_half(x[32 * half + 2 * c], scale, a0, a1);
-            split_half(x[32 * half + 2 * c + 1], scale, b0, b1);
-            a[c] = __uint_as_float(pack_half2(a0, b0));
-            b[c] = __uint_as_float(pack_half2(a1, b1));
+            uint32_t p0, p1;
+            split_pack2<false>(x[32 * half + 2 * c], x[32 * half + 2 * c + 1], scale, p0, p1);
+            a[c] = __uint_as_float(p0);
+            b[c] = __uint_as_float(p1);
         }
         tmem_store16x2(column + 16 * half, a, column + D / 2 + 16 * half, b);
     }
@@ -177,11 +176,12 @@ __device__ __forceinline__ void store_row_operand_smem(const float (&x)[D], int 
     const float scale = exp2_int(exponent);
 #pragma unroll
     for (int m = 0; m < D / 8; ++m) {
-        float x0[8], x1[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) split_half(x[8 * m + e], scale, x0[e], x1[e]);
-        *row_chunk<D>(tile, row, 0, m) = pack_chunk(x0);
-        *row_chunk<D>(tile, row, 1, m) = pack_chunk(x1);
+        const float chunk[8] = {x[8 * m], x[8 * m + 1], x[8 * m + 2], x[8 * m + 3],
+                                x[8 * m + 4], x[8 * m + 5], x[8 * m + 6], x[8 * m + 7]};
+        uint4 c0, c1;
+        split_pack8<false>(chunk, scale, c0, c1);
+        *row_chunk<D>(tile, row, 0, m) = c0;
+        *row_chunk<D>(tile, row, 1, m) = c1;
     }
 }
 
@@ -337,10 +337,10 @@ __device__ __forceinline__ void convert_stage(Storage<D, kKeyRows> &s, int stage
             float4 lo = raw_chunk<D>(raw, row, 2 * m), hi = raw_chunk<D>(raw, row, 2 * m + 1);
             if (!keep_row) lo = hi = make_float4(0.f, 0.f, 0.f, 0.f);
             const float x[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
-            float x0[8], x1[8];
-            split_half8(x, scale, x0, x1);
-            *row_chunk<D>(dst, row, 0, m) = pack_chunk(x0);
-            *row_chunk<D>(dst, row, 1, m) = pack_chunk(x1);
+            uint4 c0, c1;
+            split_pack8<true>(x, scale, c0, c1);
+            *row_chunk<D>(dst, row, 0, m) = c0;
+            *row_chunk<D>(dst, row, 1, m) = c1;
         }
     }
 }

@@ -21,27 +21,33 @@ constexpr int kBoxRows = 64;
 constexpr int kBoxFloats = kBoxRows * 32;  // one TMA box: 64 rows x 32 FP32 (8 KB)
 constexpr int kBoxBytes = kBoxFloats * 4;
 
-// x' = x * scale split into x0 (11 significant bits, exact in FP16) and x1 = x' - x0 (rounded to
-// FP16 when packed).
-__device__ __forceinline__ void split_half(float x, float scale, float &x0, float &x1) {
-    const float scaled = x * scale;
-    x0 = round_tf32(scaled);
-    x1 = scaled - x0;
+// x' = (a, b) * scale split into FP16 pairs: p0 = FP16(x') rounded to nearest (11 significant
+// bits), p1 = FP16(x' - p0), the residual taken from p0 widened back, so it is exact in FP32 before
+// its own rounding. Low halves hold a. kPairs: the multiply and subtract as packed FP32 pairs (three
+// issue slots per value instead of four; needs register pairs, which the d = 32 forward's split
+// warps cannot spare without spilling).
+template <bool kPairs>
+__device__ __forceinline__ void split_pack2(float a, float b, float scale, uint32_t &p0, uint32_t &p1) {
+    if constexpr (kPairs) {
+        const float2 scaled = mul_f32x2(make_float2(a, b), make_float2(scale, scale));
+        p0 = pack_half2(scaled.x, scaled.y);
+        const float2 residual = sub_f32x2(scaled, unpack_half2(p0));
+        p1 = pack_half2(residual.x, residual.y);
+    } else {
+        const float sa = a * scale, sb = b * scale;
+        p0 = pack_half2(sa, sb);
+        const float2 widened = unpack_half2(p0);
+        p1 = pack_half2(sa - widened.x, sb - widened.y);
+    }
 }
 
-// split_half of eight values, the multiplications and subtractions as packed FP32 pairs (the same
-// results, half the issue slots).
-__device__ __forceinline__ void split_half8(const float (&x)[8], float scale, float (&x0)[8], float (&x1)[8]) {
-    const float2 scale2 = make_float2(scale, scale);
-#pragma unroll
-    for (int e = 0; e < 8; e += 2) {
-        const float2 scaled = mul_f32x2(make_float2(x[e], x[e + 1]), scale2);
-        x0[e] = round_tf32(scaled.x);
-        x0[e + 1] = round_tf32(scaled.y);
-        const float2 residual = sub_f32x2(scaled, make_float2(x0[e], x0[e + 1]));
-        x1[e] = residual.x;
-        x1[e + 1] = residual.y;
-    }
+// Eight values (scaled) as the 16-byte FP16 chunks of x0 and x1 (split_pack2 per pair).
+template <bool kPairs>
+__device__ __forceinline__ void split_pack8(const float (&x)[8], float scale, uint4 &x0, uint4 &x1) {
+    split_pack2<kPairs>(x[0], x[1], scale, x0.x, x1.x);
+    split_pack2<kPairs>(x[2], x[3], scale, x0.y, x1.y);
+    split_pack2<kPairs>(x[4], x[5], scale, x0.z, x1.z);
+    split_pack2<kPairs>(x[6], x[7], scale, x0.w, x1.w);
 }
 
 // 16-byte chunk `chunk` (features 4 chunk .. 4 chunk + 3) of row `row` of an FP32 tile.
@@ -65,11 +71,6 @@ __device__ __forceinline__ uint4 *row_chunk(uint32_t *tile, int row, int part, i
 template <int D>
 constexpr uint64_t row_x1_offset() {
     return D == 32 ? 4 : kBoxBytes / 16;
-}
-
-// Packs eight FP32 values into one 16-byte FP16 chunk (element i at byte 2 i).
-__device__ __forceinline__ uint4 pack_chunk(const float (&x)[8]) {
-    return make_uint4(pack_half2(x[0], x[1]), pack_half2(x[2], x[3]), pack_half2(x[4], x[5]), pack_half2(x[6], x[7]));
 }
 
 // Key tiles (of 64 keys) of the window [first, last) up to its last visible key (mask[key] != 0), 0 when every

@@ -429,6 +429,21 @@ __device__ __forceinline__ void mma2_f16_ss_commit_warp(uint32_t d, const uint64
             : "memory");
 }
 
+// One potentially blocking test of the phase with the given parity: the thread may be suspended
+// until the phase completes or about `hint_ns` nanoseconds pass (no issue slots are used while it
+// is suspended). True if the phase completed.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t done;
+    asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+            : "memory");
+    return done != 0;
+}
+
 // Bounded wait by every lane of a warp; true only if every lane saw the phase complete.
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity) {
     return __all_sync(0xffffffffu, mbar_wait(bar, parity));
@@ -439,21 +454,21 @@ __device__ __forceinline__ bool mbar_test_wait_warp(uint64_t *bar, uint32_t pari
     return __all_sync(0xffffffffu, mbar_test_wait(bar, parity));
 }
 
-// Round to the nearest TF32 value (10 explicit mantissa bits, ties away from zero) with two
-// integer operations: add half an ulp of the 13 dropped bits to the magnitude, clear them. The
-// carry propagates into the exponent when needed; the sign bit is untouched; infinities stay
-// infinite. The result is exactly representable in TF32, so the tensor core's own operand
-// conversion leaves it unchanged whatever its rounding mode.
-__device__ __forceinline__ float round_tf32(float x) {
-    return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
-}
-
 // Packs two FP32 values as FP16 (round to nearest): a in the low half, b in the high half (the
 // order a K-major fp16 operand stores consecutive elements in one 32-bit word).
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
     uint32_t packed;
     asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(packed) : "f"(b), "f"(a));
     return packed;
+}
+
+// The two FP16 halves of a packed pair as FP32 (low half in .x), exact.
+__device__ __forceinline__ float2 unpack_half2(uint32_t packed) {
+    float2 r;
+    asm("{\n\t.reg .f16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\tcvt.f32.f16 %0, lo;\n\tcvt.f32.f16 %1, hi;\n\t}"
+        : "=f"(r.x), "=f"(r.y)
+        : "r"(packed));
+    return r;
 }
 
 // Packed FP32 pairs (sm_100 f32x2 instructions: one issue for two lanes of work, IEEE results
