@@ -595,7 +595,13 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles>::kThreads, 1)
                 bool next_ready = !more;
                 bool served[F::kQTiles] = {};
                 const long long start_clock = clock64();
-                int remaining = F::kQTiles;
+                // Statistics: p_full(j) only tells that buffer j may take S(j + 2); for the last two
+                // tiles there is nothing to issue, so they are not waited for. (Waiting would be wrong:
+                // a softmax warp releases tile j after S(j + 1) is issued -- which keeps it at most one
+                // phase ahead -- but the last tile has no S(j + 1), so its release may complete a second
+                // p_full phase before this warp has seen the first, and a parity wait cannot tell two
+                // completed phases from none.)
+                int remaining = kStats && !more ? 0 : F::kQTiles;
                 while (remaining > 0 && ok) {
 #pragma unroll
                     for (int t = 0; t < F::kQTiles; ++t) {

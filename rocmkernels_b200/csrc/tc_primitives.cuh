@@ -429,21 +429,6 @@ __device__ __forceinline__ void mma2_f16_ss_commit_warp(uint32_t d, const uint64
             : "memory");
 }
 
-// One potentially blocking test of the phase with the given parity: the thread may be suspended
-// until the phase completes or about `hint_ns` nanoseconds pass (no issue slots are used while it
-// is suspended). True if the phase completed.
-__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {
-    uint32_t done;
-    asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t}"
-            : "=r"(done)
-            : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
-            : "memory");
-    return done != 0;
-}
-
 // Bounded wait by every lane of a warp; true only if every lane saw the phase complete.
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity) {
     return __all_sync(0xffffffffu, mbar_wait(bar, parity));
