@@ -102,3 +102,21 @@ def test_statistics_ignore_masked_key_rows(cuda):
     status, lse = run_statistics(cuda, q, k_garbage, mask, -1)
     assert status == 0
     check(lse, expected, "masked rows hold NaN")
+
+
+@pytest.mark.parametrize("side", ["one_wave", "two_waves"])
+@pytest.mark.parametrize("key_tiles", [1, 2, 3, 4, 5])
+def test_statistics_short_windows_repeated(cuda, side, key_tiles):
+    """Windows of one to five key tiles, called repeatedly: the MMA warp's handling of the last
+    two tiles (their releases are not waited for in statistics mode) must never leave a pipeline
+    wait to run out, whatever the timing between the softmax and MMA warps."""
+    H, Q = 2, 129
+    K = 64 * key_tiles - 7  # a ragged last tile
+    B = batch_for(cuda, side, H, Q)
+    q, k, v, _, _ = make_inputs(B, H, Q, K, 32, seed=741 + key_tiles, dist="normal", mask3=False)
+    mask = padded_mask(B, K, 743 + key_tiles)
+    expected = oracle.attention(q, k, v, mask, None, -1, forward_only=True, threads=oracle.cpu_count())
+    for _ in range(8):  # run_statistics asserts the device status word after every call
+        status, lse = run_statistics(cuda, q, k, mask, -1)
+        assert status == 0
+    check(lse, expected, f"B{B} {side} {key_tiles} tiles")
