@@ -95,6 +95,19 @@ ROCMKERNELS_C_EXPORT int attention_fp32_backward_tiled(const float *q, const flo
         RocmKernelsStrides ks, RocmKernelsStrides vs, RocmKernelsStrides os, RocmKernelsStrides us,
         RocmKernelsStream stream);
 
+/* 32-wide backward in one key-major pass (the single-pass form of attention_fp32_backward, same
+ * arguments and outputs): a pre-pass writes delta and zeroes gradient_q, then one kernel computes
+ * dK and dV per key and adds each key tile's share of dQ with FP32 atomics, so dQ's summation
+ * order over key tiles is not fixed (results may differ in the last bits from run to run; the
+ * reference's two-kernel split, attention_fp32_backward, is deterministic). Tensors the tensor-core
+ * kernels cannot address take the two-pass path. No counterpart in the reference (its backward is
+ * the two-pass Attention.hip:205-223). */
+ROCMKERNELS_C_EXPORT int attention_fp32_backward_fused(const float *q, const float *k, const float *v, const bool *mask,
+        const float *output, const float *lse, const float *upstream, float *gradient_q, float *gradient_k,
+        float *gradient_v, float *delta, int batch, int heads, int queries, int keys, int radius, RocmKernelsStrides qs,
+        RocmKernelsStrides ks, RocmKernelsStrides vs, RocmKernelsStrides os, RocmKernelsStrides us,
+        RocmKernelsStream stream);
+
 /* Softmax statistics only ({max, sum} per row; no V read, no O write); radius < -1 is invalid.
  * Replaces attention_fp32_statistics (Attention.hpp:23-24; Attention.hip:252-261). */
 ROCMKERNELS_C_EXPORT int attention_fp32_statistics(const float *q, const float *k, const bool *mask, float *lse,

@@ -103,6 +103,8 @@ def lib() -> ctypes.CDLL:
         library.rocmkernels_attention_device_status.restype = ctypes.c_uint
         library.attention_fp32_backward_static_delta.argtypes = [_POINTER] * 10 + [_INT] * 5 + [Strides] * 5 + [_POINTER]
         library.attention_fp32_backward_static_delta.restype = ctypes.c_int
+        library.attention_fp32_backward_fused.argtypes = _BACKWARD_ARGS
+        library.attention_fp32_backward_fused.restype = ctypes.c_int
         library.attention_fp32_forward_flash_rotary.argtypes = [_POINTER] * 8 + [_INT] * 5 + [Strides] * 6 + [_POINTER]
         library.attention_fp32_forward_flash_rotary.restype = ctypes.c_int
         _lib = library
@@ -230,6 +232,14 @@ def attention_fp32_backward_static_delta(q, k, v, mask, output, lse, upstream, g
     return _call("attention_fp32_backward_static_delta", ptr(q), ptr(k), ptr(v), ptr(mask), ptr(output), ptr(lse),
                  ptr(upstream), ptr(gq), ptr(gk), ptr(gv), batch, heads, queries, keys, radius, strides(qs), strides(ks),
                  strides(vs), strides(os_), strides(us), _stream(stream))
+
+
+def attention_fp32_backward_fused(q, k, v, mask, output, lse, upstream, gq, gk, gv, delta, batch, heads, queries, keys, radius, qs, ks,
+                                  vs, os_, us, stream=None):
+    """attention_fp32_backward in one key-major pass (dQ added with FP32 atomics: its summation
+    order over key tiles is not fixed)."""
+    return _backward("attention_fp32_backward_fused", q, k, v, mask, output, lse, upstream, gq, gk, gv, delta, batch, heads, queries,
+                     keys, radius, qs, ks, vs, os_, us, stream)
 
 
 def attention_fp32_backward_tiled(q, k, v, mask, output, lse, upstream, gq, gk, gv, delta, batch, heads, queries, keys, radius, qs, ks,

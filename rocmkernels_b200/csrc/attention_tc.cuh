@@ -50,6 +50,10 @@ bool backward_supported(const AttentionParams &p);
 // Launches the tensor-core backward for head width 32 or 64: delta and dQ (query-major), then
 // dK and dV (key-major), ordered on `stream`; returns a cudaError_t value or kNotEligible.
 int launch_backward(const AttentionParams &p, int head_width, cudaStream_t stream);
+// Launches the fused single-pass backward for head width 32 (a pre-pass writing delta and zeroing
+// dQ, then one key-major kernel: dK and dV per key row, dQ added per query tile with FP32
+// atomics); returns a cudaError_t value or kNotEligible. Same tensors as launch_backward.
+int launch_fused_backward(const AttentionParams &p, cudaStream_t stream);
 // Device status word of the backward kernels (as read_device_status).
 unsigned int read_backward_status(bool clear);
 

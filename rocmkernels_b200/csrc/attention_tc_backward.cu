@@ -323,9 +323,8 @@ __device__ __forceinline__ void fold_x(float (&acc1)[D], float (&acc2)[kKeyRows 
 // Converts the two FP32 tiles of one stage (split warps, 64 threads, row = 32 w + lane) to their
 // row layouts: the B of S and dP, and read MN-major the B of X1 (and X2 for key rows); masked
 // key rows zeroed (query rows).
-template <int D, bool kKeyRows>
-__device__ __forceinline__ void convert_stage(Storage<D, kKeyRows> &s, int stage, int w, int lane, bool keep_row, float scale_1,
-                                              float scale_2) {
+template <int D, class St>
+__device__ __forceinline__ void convert_stage(St &s, int stage, int w, int lane, bool keep_row, float scale_1, float scale_2) {
     const int row = 32 * w + lane;
 #pragma unroll
     for (int which = 0; which < 2; ++which) {
@@ -345,6 +344,207 @@ __device__ __forceinline__ void convert_stage(Storage<D, kKeyRows> &s, int stage
     }
 }
 
+// The column tiles a CTA walks: its row tile [r0, r0 + 128) of row_count rows, the window
+// [first, last) of columns that can see (or be seen by) it, window_tiles = 64-column tiles of the
+// window, prefetched = those loaded before the mask is read.
+struct TileWindow {
+    int r0, row_count, first, last, window_tiles, prefetched, h, b;
+    long long query_base;
+    const unsigned char *mask;
+};
+
+// The CTA's row tile (blockIdx.x enumerates (batch, head, row tile), row tiles fastest) and its
+// column window.
+template <int kStages>
+__device__ __forceinline__ TileWindow tile_window(const AttentionParams &p, bool key_rows, int blocks_per_head) {
+    TileWindow t;
+    int block = blockIdx.x;
+    const int row_tile = block % blocks_per_head;
+    block /= blocks_per_head;
+    t.h = block % p.heads;
+    t.b = block / p.heads;
+    t.r0 = row_tile * kRows;
+    t.row_count = key_rows ? p.keys : p.queries;
+    const int column_count = key_rows ? p.queries : p.keys;
+    key_window(t.r0, min(t.r0 + kRows, t.row_count), column_count, p.radius, t.first, t.last);
+    t.window_tiles = t.last > t.first ? (t.last - t.first + kCols - 1) / kCols : 0;
+    t.prefetched = min(t.window_tiles, kStages);
+    t.query_base = (static_cast<long long>(t.b) * p.heads + t.h) * p.queries;
+    t.mask = p.mask + static_cast<long long>(t.b) * p.keys;
+    return t;
+}
+
+// Column tiles actually visited (published by the producer warp after its first loads).
+// Query rows: the key window up to its last visible key (trailing key padding is skipped).
+// Key rows: none when every key of the tile is masked (dK = dV = 0); else the query window.
+template <class St>
+__device__ __forceinline__ int visited_tiles(St &s) {
+    return mbar_wait(&s.range_ready, 0) ? s.tile_count : 0;
+}
+
+// TMA producer warp (lane 0 issues): the raw FP32 column tiles into the stage ring, the visited
+// tile count published on range_ready.
+template <int D, bool kKeyRows, class St>
+__device__ __forceinline__ void producer_role(St &s, const TileWindow &t, const CUtensorMap &tmap1, const CUtensorMap &tmap2,
+                                              int lane) {
+    using G = Geometry<D>;
+    constexpr int kStages = St::kStages;
+    const int first = t.first, last = t.last, window_tiles = t.window_tiles, prefetched = t.prefetched;
+    const int r0 = t.r0, row_count = t.row_count, h = t.h, b = t.b;
+    const unsigned char *mask = t.mask;
+    const auto issue = [&](int j) {
+        const int stage = j % kStages;
+        RK_BTRACE(j, 0);
+        mbar_arrive_expect_tx(&s.full[stage], 2 * G::kBoxes * kBoxBytes);
+#pragma unroll
+        for (int box = 0; box < G::kBoxes; ++box) {
+            tma_load_4d(s.raw1[stage] + box * kBoxFloats, &tmap1, &s.full[stage], 32 * box, first + j * kCols, h, b);
+            tma_load_4d(s.raw2[stage] + box * kBoxFloats, &tmap2, &s.full[stage], 32 * box, first + j * kCols, h, b);
+        }
+    };
+    // The first stages go out before the mask is read.
+    if (lane == 0)
+        for (int j = 0; j < prefetched; ++j) issue(j);
+    int tiles = window_tiles;
+    if constexpr (kKeyRows) {
+        bool visible = false;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int key = r0 + 4 * lane + e;
+            visible = visible || (key < row_count && mask[key] != 0);
+        }
+        if (!__any_sync(0xffffffffu, visible)) tiles = 0;
+    } else {
+        tiles = visible_tiles_of(mask, first, last, lane);
+    }
+    if (lane == 0) {
+        s.tile_count = tiles;
+        mbar_arrive(&s.range_ready);
+        int issued = prefetched;
+        bool ok = true;
+        for (int j = prefetched; j < tiles && ok; ++j) {
+            // The raw stage is refilled as soon as the split warps have converted it (the MMAs
+            // read only the converted layouts); j >= kStages here.
+            ok = mbar_wait(&s.raw_free[j % kStages], ((j / kStages) - 1) & 1);
+            if (!ok) break;
+            issue(j);
+            ++issued;
+        }
+        if (!ok) {
+            for (int j = max(0, issued - kStages); j < issued; ++j) mbar_wait(&s.full[j % kStages], (j / kStages) & 1);
+        }
+        // Prefetched tiles past the visited ones: converted for nothing; wait for their loads.
+        for (int j = tiles; j < prefetched; ++j) mbar_wait(&s.full[j], 0);
+    }
+}
+
+// Split warps (two, 64 threads; w = 0 or 1): FP16 conversion of each column tile and its column
+// statistics.
+template <int D, bool kKeyRows, class St>
+__device__ __forceinline__ void split_role(St &s, const AttentionParams &p, const TileWindow &t, int w, int lane) {
+    constexpr int kStages = St::kStages;
+    const int first = t.first, last = t.last, window_tiles = t.window_tiles, prefetched = t.prefetched;
+    const long long query_base = t.query_base;
+    const unsigned char *mask = t.mask;
+    const auto visible_tiles = [&]() { return visited_tiles(s); };
+    // Split warp w owns rows [32w, 32w + 32) of each column tile for the maxima, the masks and
+    // the column statistics; convert_stage writes the operand layouts.
+    const int row = 32 * w + lane;
+    const float scale1 = kKeyRows ? p.scale : 1.f;  // Q enters the products as scale * Q
+    // This lane's column statistics (key rows: the query's saved {max, sum} and delta; query
+    // rows: whether the key exists and is visible), loaded one tile ahead so that their global
+    // load latency overlaps the previous tile's conversion.
+    float next_max = -INFINITY, next_total = 0.f, next_delta = 0.f;
+    bool next_flag = false;
+    const auto load_stats = [&](int jj) {
+        const int column = first + jj * kCols + row;
+        next_flag = jj < window_tiles && column < last;
+        if (kKeyRows) {
+            next_max = next_flag ? p.lse_in[(query_base + column) * 2] : -INFINITY;
+            next_total = next_flag ? p.lse_in[(query_base + column) * 2 + 1] : 0.f;
+            next_delta = next_flag ? p.delta[query_base + column] : 0.f;
+        } else {
+            next_flag = next_flag && mask[column] != 0;
+        }
+    };
+    load_stats(0);
+    // Query rows: the prefetched tiles are converted without waiting for the visited-tile
+    // count (which comes from a mask read); those past it are converted for nothing and never
+    // consumed. Key rows (count 0 or the whole window) wait for it.
+    int tiles = kKeyRows ? __shfl_sync(0xffffffffu, visible_tiles(), 0) : prefetched;
+    bool counted = kKeyRows;
+    for (int j = 0; j < tiles || !counted; ++j) {
+        if (!counted && j >= prefetched) {
+            tiles = __shfl_sync(0xffffffffu, visible_tiles(), 0);
+            counted = true;
+            if (j >= tiles) break;
+        }
+        const int stage = j % kStages, parity = j & 1;
+        const float maximum = next_max, total = next_total, delta = next_delta;
+        const bool flag = next_flag;
+        load_stats(j + 1);
+        const bool landed = __all_sync(0xffffffffu, mbar_wait(&s.full[stage], (j / kStages) & 1));
+        if (lane == 0) RK_BTRACE(j, 1 + w);
+        bool visible;
+        float delta_abs = 0.f, col_offset = -INFINITY;
+        if (kKeyRows) {  // column = query: visible if it exists and has a finite row max
+            visible = flag && maximum != -INFINITY;
+            col_offset = visible ? 14.f - maximum * kLog2e - __log2f(total) : -INFINITY;
+            delta_abs = visible ? fabsf(delta) : 0.f;
+        } else {  // column = key: visible if it exists and is not masked
+            visible = flag;
+        }
+        const uint32_t bits = __ballot_sync(0xffffffffu, visible);
+        // Rows of masked key columns are zeroed (query rows only).
+        const bool keep_row = kKeyRows || ((bits >> lane) & 1);
+        float max1 = 0.f, max2 = 0.f;
+#pragma unroll
+        for (int c = 0; c < D / 4; ++c) {
+            const float4 x = raw_chunk<D>(s.raw1[stage], row, c);
+            const float4 y = raw_chunk<D>(s.raw2[stage], row, c);
+            if (keep_row) {
+                max1 = max3(max1, fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
+                max2 = max3(max2, fmaxf(fabsf(y.x), fabsf(y.y)), fmaxf(fabsf(y.z), fabsf(y.w)));
+            }
+        }
+#pragma unroll
+        for (int offset = 16; offset; offset >>= 1) {
+            max1 = fmaxf(max1, __shfl_xor_sync(0xffffffffu, max1, offset));
+            max2 = fmaxf(max2, __shfl_xor_sync(0xffffffffu, max2, offset));
+            delta_abs = fmaxf(delta_abs, __shfl_xor_sync(0xffffffffu, delta_abs, offset));
+        }
+        // The stage's statistics and converted layouts (read by the row warps and the MMAs
+        // for tile j - kStages) are rewritten only after those MMAs finished.
+        const bool stage_free = j < kStages || __all_sync(0xffffffffu, mbar_wait(&s.empty[stage], ((j / kStages) - 1) & 1));
+        if (kKeyRows) {
+            s.col_offset[stage][row] = col_offset;
+            s.col_delta[stage][row] = delta;
+        }
+        if (lane == 0) {
+            s.split_max[parity][w][0] = max1;
+            s.split_max[parity][w][1] = max2;
+            s.split_max[parity][w][2] = delta_abs;
+            s.split_ok[parity][w] = landed && stage_free;
+            s.col_mask[stage][w] = bits;
+        }
+        // One barrier per tile: the maxima are double-buffered by tile parity.
+        asm volatile("bar.sync 1, 64;" ::: "memory");
+        if (!(s.split_ok[parity][0] && s.split_ok[parity][1])) break;
+        const int e1 = fp16_scale_exponent(fmaxf(s.split_max[parity][0][0], s.split_max[parity][1][0]) * scale1);
+        const int e2 = fp16_scale_exponent(fmaxf(s.split_max[parity][0][1], s.split_max[parity][1][1]));
+        if (w == 0 && lane == 0) {
+            s.e1[stage] = e1;
+            s.e2[stage] = e2;
+            s.col_delta_max[stage] = fmaxf(s.split_max[parity][0][2], s.split_max[parity][1][2]);
+        }
+        convert_stage<D>(s, stage, w, lane, keep_row, exp2_int(e1) * scale1, exp2_int(e2));
+        mbar_arrive(&s.raw_free[stage]);
+        fence_proxy_async_shared();
+        if (lane == 0) RK_BTRACE(j, 3 + w);
+        mbar_arrive(&s.ready[stage]);
+    }
+}
+
 template <int D, bool kKeyRows>
 __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
         backward_kernel(const BackwardArgs args, const __grid_constant__ CUtensorMap tmap1,
@@ -359,20 +559,11 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
-    int block = blockIdx.x;
-    const int row_tile = block % args.blocks_per_head;
-    block /= args.blocks_per_head;
-    const int h = block % p.heads;
-    const int b = block / p.heads;
-    const int r0 = row_tile * kRows;
-    const int row_count = kKeyRows ? p.keys : p.queries;
-    const int column_count = kKeyRows ? p.queries : p.keys;
-    int first, last;  // columns that can see (or be seen by) the row tile
-    key_window(r0, min(r0 + kRows, row_count), column_count, p.radius, first, last);
-    const int window_tiles = last > first ? (last - first + kCols - 1) / kCols : 0;
-    const long long query_base = (static_cast<long long>(b) * p.heads + h) * p.queries;
+    const TileWindow window = tile_window<kStages>(p, kKeyRows, args.blocks_per_head);
+    const int h = window.h, b = window.b, r0 = window.r0, row_count = window.row_count, first = window.first;
+    const long long query_base = window.query_base;
     const long long key_base = (static_cast<long long>(b) * p.heads + h) * p.keys;
-    const unsigned char *mask = p.mask + static_cast<long long>(b) * p.keys;
+    const unsigned char *mask = window.mask;
 
     if (warp == 0) {
         tmem_alloc(&s.tmem_base, G::kTmemColumns);
@@ -397,61 +588,13 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = s.tmem_base;
-    // Column tiles actually visited (published by the producer warp after its first loads).
-    // Query rows: the key window up to its last visible key (trailing key padding is skipped).
-    // Key rows: none when every key of the tile is masked (dK = dV = 0); else the query window.
-    const int prefetched = min(window_tiles, kStages);
-    const auto visible_tiles = [&]() { return mbar_wait(&s.range_ready, 0) ? s.tile_count : 0; };
 
     if (warp == kProducerWarp) {
         // ---------------------------------------------------------------- TMA producer
-        const auto issue = [&](int j) {
-            const int stage = j % kStages;
-            RK_BTRACE(j, 0);
-            mbar_arrive_expect_tx(&s.full[stage], 2 * G::kBoxes * kBoxBytes);
-#pragma unroll
-            for (int box = 0; box < G::kBoxes; ++box) {
-                tma_load_4d(s.raw1[stage] + box * kBoxFloats, &tmap1, &s.full[stage], 32 * box, first + j * kCols, h, b);
-                tma_load_4d(s.raw2[stage] + box * kBoxFloats, &tmap2, &s.full[stage], 32 * box, first + j * kCols, h, b);
-            }
-        };
-        // The first stages go out before the mask is read.
-        if (lane == 0)
-            for (int j = 0; j < prefetched; ++j) issue(j);
-        int tiles = window_tiles;
-        if constexpr (kKeyRows) {
-            bool visible = false;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int key = r0 + 4 * lane + e;
-                visible = visible || (key < row_count && mask[key] != 0);
-            }
-            if (!__any_sync(0xffffffffu, visible)) tiles = 0;
-        } else {
-            tiles = visible_tiles_of(mask, first, last, lane);
-        }
-        if (lane == 0) {
-            s.tile_count = tiles;
-            mbar_arrive(&s.range_ready);
-            int issued = prefetched;
-            bool ok = true;
-            for (int j = prefetched; j < tiles && ok; ++j) {
-                // The raw stage is refilled as soon as the split warps have converted it (the MMAs
-                // read only the converted layouts); j >= kStages here.
-                ok = mbar_wait(&s.raw_free[j % kStages], ((j / kStages) - 1) & 1);
-                if (!ok) break;
-                issue(j);
-                ++issued;
-            }
-            if (!ok) {
-                for (int j = max(0, issued - kStages); j < issued; ++j) mbar_wait(&s.full[j % kStages], (j / kStages) & 1);
-            }
-            // Prefetched tiles past the visited ones: converted for nothing; wait for their loads.
-            for (int j = tiles; j < prefetched; ++j) mbar_wait(&s.full[j], 0);
-        }
+        producer_role<D, kKeyRows>(s, window, tmap1, tmap2, lane);
     } else if (warp == kMmaWarp) {
         // ---------------------------------------------------------------- MMA issuer
-        const int tiles = __shfl_sync(0xffffffffu, visible_tiles(), 0);
+        const int tiles = __shfl_sync(0xffffffffu, visited_tiles(s), 0);
         if (tiles > 0) {
             constexpr uint64_t row_stage = G::kRowWords * 4 / 16;
             const uint64_t b1_desc = sw128_descriptor(smem_u32(s.b1[0]));
@@ -490,103 +633,7 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
         }
     } else if (warp >= kSplitWarp) {
         // ---------------------------------------------------------------- FP16 split
-        // Split warp w owns rows [32w, 32w + 32) of each column tile for the maxima, the masks and
-        // the column statistics; convert_stage writes the operand layouts.
-        const int w = warp - kSplitWarp;
-        const int row = 32 * w + lane;
-        const float scale1 = kKeyRows ? p.scale : 1.f;  // Q enters the products as scale * Q
-        // This lane's column statistics (key rows: the query's saved {max, sum} and delta; query
-        // rows: whether the key exists and is visible), loaded one tile ahead so that their global
-        // load latency overlaps the previous tile's conversion.
-        float next_max = -INFINITY, next_total = 0.f, next_delta = 0.f;
-        bool next_flag = false;
-        const auto load_stats = [&](int jj) {
-            const int column = first + jj * kCols + row;
-            next_flag = jj < window_tiles && column < last;
-            if (kKeyRows) {
-                next_max = next_flag ? p.lse_in[(query_base + column) * 2] : -INFINITY;
-                next_total = next_flag ? p.lse_in[(query_base + column) * 2 + 1] : 0.f;
-                next_delta = next_flag ? p.delta[query_base + column] : 0.f;
-            } else {
-                next_flag = next_flag && mask[column] != 0;
-            }
-        };
-        load_stats(0);
-        // Query rows: the prefetched tiles are converted without waiting for the visited-tile
-        // count (which comes from a mask read); those past it are converted for nothing and never
-        // consumed. Key rows (count 0 or the whole window) wait for it.
-        int tiles = kKeyRows ? __shfl_sync(0xffffffffu, visible_tiles(), 0) : prefetched;
-        bool counted = kKeyRows;
-        for (int j = 0; j < tiles || !counted; ++j) {
-            if (!counted && j >= prefetched) {
-                tiles = __shfl_sync(0xffffffffu, visible_tiles(), 0);
-                counted = true;
-                if (j >= tiles) break;
-            }
-            const int stage = j % kStages, parity = j & 1;
-            const float maximum = next_max, total = next_total, delta = next_delta;
-            const bool flag = next_flag;
-            load_stats(j + 1);
-            const bool landed = __all_sync(0xffffffffu, mbar_wait(&s.full[stage], (j / kStages) & 1));
-            if (lane == 0) RK_BTRACE(j, 1 + w);
-            bool visible;
-            float delta_abs = 0.f, col_offset = -INFINITY;
-            if (kKeyRows) {  // column = query: visible if it exists and has a finite row max
-                visible = flag && maximum != -INFINITY;
-                col_offset = visible ? 14.f - maximum * kLog2e - __log2f(total) : -INFINITY;
-                delta_abs = visible ? fabsf(delta) : 0.f;
-            } else {  // column = key: visible if it exists and is not masked
-                visible = flag;
-            }
-            const uint32_t bits = __ballot_sync(0xffffffffu, visible);
-            // Rows of masked key columns are zeroed (query rows only).
-            const bool keep_row = kKeyRows || ((bits >> lane) & 1);
-            float max1 = 0.f, max2 = 0.f;
-#pragma unroll
-            for (int c = 0; c < D / 4; ++c) {
-                const float4 x = raw_chunk<D>(s.raw1[stage], row, c);
-                const float4 y = raw_chunk<D>(s.raw2[stage], row, c);
-                if (keep_row) {
-                    max1 = max3(max1, fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
-                    max2 = max3(max2, fmaxf(fabsf(y.x), fabsf(y.y)), fmaxf(fabsf(y.z), fabsf(y.w)));
-                }
-            }
-#pragma unroll
-            for (int offset = 16; offset; offset >>= 1) {
-                max1 = fmaxf(max1, __shfl_xor_sync(0xffffffffu, max1, offset));
-                max2 = fmaxf(max2, __shfl_xor_sync(0xffffffffu, max2, offset));
-                delta_abs = fmaxf(delta_abs, __shfl_xor_sync(0xffffffffu, delta_abs, offset));
-            }
-            // The stage's statistics and converted layouts (read by the row warps and the MMAs
-            // for tile j - kStages) are rewritten only after those MMAs finished.
-            const bool stage_free = j < kStages || __all_sync(0xffffffffu, mbar_wait(&s.empty[stage], ((j / kStages) - 1) & 1));
-            if (kKeyRows) {
-                s.col_offset[stage][row] = col_offset;
-                s.col_delta[stage][row] = delta;
-            }
-            if (lane == 0) {
-                s.split_max[parity][w][0] = max1;
-                s.split_max[parity][w][1] = max2;
-                s.split_max[parity][w][2] = delta_abs;
-                s.split_ok[parity][w] = landed && stage_free;
-                s.col_mask[stage][w] = bits;
-            }
-            // One barrier per tile: the maxima are double-buffered by tile parity.
-            asm volatile("bar.sync 1, 64;" ::: "memory");
-            if (!(s.split_ok[parity][0] && s.split_ok[parity][1])) break;
-            const int e1 = fp16_scale_exponent(fmaxf(s.split_max[parity][0][0], s.split_max[parity][1][0]) * scale1);
-            const int e2 = fp16_scale_exponent(fmaxf(s.split_max[parity][0][1], s.split_max[parity][1][1]));
-            if (threadIdx.x == kSplitWarp * 32) {
-                s.e1[stage] = e1;
-                s.e2[stage] = e2;
-                s.col_delta_max[stage] = fmaxf(s.split_max[parity][0][2], s.split_max[parity][1][2]);
-            }
-            convert_stage<D, kKeyRows>(s, stage, w, lane, keep_row, exp2_int(e1) * scale1, exp2_int(e2));
-            mbar_arrive(&s.raw_free[stage]);
-            fence_proxy_async_shared();
-            if (lane == 0) RK_BTRACE(j, 3 + w);
-            mbar_arrive(&s.ready[stage]);
-        }
+        split_role<D, kKeyRows>(s, p, window, warp - kSplitWarp, lane);
     } else {
         // ---------------------------------------------------------------- row warps
         const int r = threadIdx.x;  // row within the tile = TMEM lane
@@ -651,7 +698,7 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
         for (int c = 0; c < (kKeyRows ? D : 1); ++c) acc2[c] = 0.f;
         float pending_scale1 = 0.f, pending_scale2 = 0.f;  // 2^-(scales) of the last tile's X1, X2
         bool ok = true;
-        const int tiles = __shfl_sync(0xffffffffu, visible_tiles(), 0);
+        const int tiles = __shfl_sync(0xffffffffu, visited_tiles(s), 0);
         for (int j = 0; j < tiles && ok; ++j) {
             const int stage = j % kStages;
             ok = __all_sync(0xffffffffu, mbar_wait(&s.s_full, j & 1) && mbar_wait(&s.ready[stage], (j / kStages) & 1));
@@ -798,6 +845,403 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
     }
 }
 
+// ---- fused single-pass backward (d = 32) ---------------------------------------------------------
+// One key-major pass computes dK, dV and dQ: the key-rows kernel's S^T, dP^T, P and dS^T, plus
+// dQ = scale dS K per 64-query tile as a tensor-core product whose A is dS^T from shared memory
+// (MN-major: each key row's 64 query values are one 128-byte row) and whose B is the CTA's K rows
+// read MN-major ([k0 | k1], N = 64). The per-tile dQ rows are added into the gradient with FP32
+// atomics (the summation order over key tiles is not fixed), after a pre-pass that writes delta
+// and zeroes dQ. K and dS enter that product with one exponent for all 128 keys of the CTA
+// (the key-rows pass scales them per key). One CTA per SM (512 TMEM columns): warps 0-7 are two
+// row warpgroups -- warpgroup g handles columns [32 g, 32 g + 32) of every tile and features
+// [16 g, 16 g + 16) of the outputs -- warp 8 the TMA producer, warp 9 the MMA issuer, warps
+// 10-11 the split warps. S and dP are double-buffered so that the next tile's products run while
+// the row warps work on this one.
+namespace fused {
+constexpr int kThreads = 384;
+constexpr int kRowThreads = 256;
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int kSplitWarp = 10;
+// TMEM columns: S / P and dP / dS of tile parity i at 128 i and 128 i + 64; X1 (dK) and X2 (dV)
+// as [b0 | b1] products; dQ (M = 64: query m at lane (m % 16) + 32 (m / 16)) as [k0 | k1].
+constexpr uint32_t kScores = 0, kX1 = 256, kX2 = 320, kDQ = 384;
+constexpr uint32_t kTmemColumns = 512;
+// dQ: M = 64, N = 64, A and B both MN-major.
+constexpr uint32_t kIdescDQ = f16_instr_desc(64, 64) | (1u << 15) | (1u << 16);
+
+struct alignas(1024) Storage {
+    using G = Geometry<32>;
+    static constexpr int kStages = 3;
+    float raw1[kStages][G::kRawFloats];      // TMA tile of Q, 128B swizzle
+    float raw2[kStages][G::kRawFloats];      // dO
+    uint32_t b1[kStages][G::kRowWords];      // scale Q rows as split FP16 [q0 | q1] (B of S^T; MN-major B of dK)
+    uint32_t b2[kStages][G::kRowWords];      // dO rows (B of dP^T; MN-major B of dV)
+    uint32_t a1[kRows * 32];                 // K rows [k0 | k1] (A of S^T; MN-major B of dQ)
+    uint32_t a2[kRows * 32];                 // V rows (A of dP^T)
+    uint32_t ds[2][2][kRows * 32];           // [tile parity][term]: dS^T rows, 64 FP16 queries per key (A of dQ)
+    alignas(16) float col_offset[kStages][kCols];
+    alignas(16) float col_delta[kStages][kCols];
+    uint32_t col_mask[kStages][2];
+    int e1[kStages], e2[kStages];
+    float col_delta_max[kStages];
+    float split_max[2][2][3];
+    int split_ok[2][2];
+    float row_max[4][2];                     // per row warp of warpgroup 0: max |K|, max ||V row||_1
+    uint64_t full[kStages];
+    uint64_t raw_free[kStages];
+    uint64_t ready[kStages];
+    uint64_t empty[kStages];
+    uint64_t s_full[2];                      // S and dP of the tile parity in TMEM (commit)
+    uint64_t p_full;                         // P / dS stored, the previous products folded (256 arrivals)
+    uint64_t x_done;                         // dK, dV and dQ products of the tile in TMEM (commit)
+    uint64_t rows_ready;                     // K and V rows stored (256 arrivals)
+    uint64_t mma_done;
+    uint64_t range_ready;
+    uint32_t tmem_base;
+    int tile_count;
+};
+
+constexpr int shared_bytes() { return static_cast<int>(sizeof(Storage)) + 1024; }
+static_assert(shared_bytes() <= 227 * 1024, "fused backward: shared memory");
+
+// store_split_chunk, also writing the two FP16 terms into the dS^T tiles of key row `row`
+// (queries 16 chunk .. 16 chunk + 15 = 16-byte chunks 2 chunk and 2 chunk + 1, 128B swizzle).
+__device__ __forceinline__ void store_split_chunk_dual(uint32_t column, const float (&v)[16], uint32_t *tile0, uint32_t *tile1,
+                                                       int row, int chunk) {
+    uint32_t q0[8], q1[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        const float x0 = __uint_as_float(__float_as_uint(v[2 * c]) & 0xFFFFE000u);
+        const float y0 = __uint_as_float(__float_as_uint(v[2 * c + 1]) & 0xFFFFE000u);
+        const float2 residual = sub_f32x2(make_float2(v[2 * c], v[2 * c + 1]), make_float2(x0, y0));
+        q0[c] = pack_half2(x0, y0);
+        q1[c] = pack_half2(residual.x, residual.y);
+    }
+    tmem_store8x2_async(column, reinterpret_cast<const float *>(q0), column + 8, reinterpret_cast<const float *>(q1));
+    uint4 *t0 = reinterpret_cast<uint4 *>(tile0) + row * 8;
+    uint4 *t1 = reinterpret_cast<uint4 *>(tile1) + row * 8;
+    const int swizzle = row & 7;
+    t0[(2 * chunk) ^ swizzle] = make_uint4(q0[0], q0[1], q0[2], q0[3]);
+    t0[(2 * chunk + 1) ^ swizzle] = make_uint4(q0[4], q0[5], q0[6], q0[7]);
+    t1[(2 * chunk) ^ swizzle] = make_uint4(q1[0], q1[1], q1[2], q1[3]);
+    t1[(2 * chunk + 1) ^ swizzle] = make_uint4(q1[4], q1[5], q1[6], q1[7]);
+}
+
+// acc1 += X1 * scale1, acc2 += X2 * scale2 for features [16 g, 16 g + 16) (warpgroup g).
+__device__ __forceinline__ void fold_x_half(float (&acc1)[16], float (&acc2)[16], uint32_t lanes, int g, float scale1, float scale2) {
+#pragma unroll
+    for (int which = 0; which < 2; ++which) {
+        float xa[16], xb[16];
+        const uint32_t x = lanes + (which == 0 ? kX1 : kX2) + 16 * g;
+        tmem_load16x2(x, xa, x + 32, xb);
+        float *acc = which == 0 ? acc1 : acc2;
+        const float s = which == 0 ? scale1 : scale2;
+#pragma unroll
+        for (int c = 0; c < 16; c += 2) {
+            const float2 r = fma_f32x2(add_f32x2(make_float2(xa[c], xa[c + 1]), make_float2(xb[c], xb[c + 1])), make_float2(s, s),
+                                       make_float2(acc[c], acc[c + 1]));
+            acc[c] = r.x;
+            acc[c + 1] = r.y;
+        }
+    }
+}
+
+// Adds the dQ rows of a finished tile into the gradient: lanes 0-15 of warp w hold queries
+// 16 (w % 4) + lane; warpgroup g adds features [16 g, 16 g + 16). `tile` = the gradient row of the
+// tile's first query, `valid` = queries of the tile inside the window.
+__device__ __forceinline__ void fold_dq(float *tile, int valid, uint32_t lanes, int g, int warp, int lane, float scale) {
+    float xa[16], xb[16];
+    tmem_load16x2(lanes + kDQ + 16 * g, xa, lanes + kDQ + 32 + 16 * g, xb);
+    const int m = 16 * (warp & 3) + lane;
+    if (lane < 16 && m < valid) {
+        float4 *dst = reinterpret_cast<float4 *>(tile + m * 32 + 16 * g);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            atomicAdd(dst + i, make_float4((xa[4 * i] + xb[4 * i]) * scale, (xa[4 * i + 1] + xb[4 * i + 1]) * scale,
+                                           (xa[4 * i + 2] + xb[4 * i + 2]) * scale, (xa[4 * i + 3] + xb[4 * i + 3]) * scale));
+    }
+}
+
+// delta_i = sum_c dO_ic O_ic and dQ_i = 0 for every query row (eight threads per row, one float4
+// of each).
+__global__ void __launch_bounds__(256) prepass_kernel(const AttentionParams p, long long rows) {
+    const long long t = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const long long row = t >> 3;
+    const int part = static_cast<int>(t & 7);
+    float d = 0.f;
+    if (row < rows) {
+        const int q = static_cast<int>(row % p.queries);
+        const long long bh = row / p.queries;
+        const int h = static_cast<int>(bh % p.heads), b = static_cast<int>(bh / p.heads);
+        const float4 u = __ldg(reinterpret_cast<const float4 *>(p.dout.row(b, h, q)) + part);
+        const float4 o = __ldg(reinterpret_cast<const float4 *>(p.o_in.row(b, h, q)) + part);
+        d = fmaf(u.w, o.w, fmaf(u.z, o.z, fmaf(u.y, o.y, u.x * o.x)));
+        reinterpret_cast<float4 *>(p.dq + row * 32)[part] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    d += __shfl_xor_sync(0xffffffffu, d, 1);
+    d += __shfl_xor_sync(0xffffffffu, d, 2);
+    d += __shfl_xor_sync(0xffffffffu, d, 4);
+    if (row < rows && part == 0) p.delta[row] = d;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+        backward_kernel(const BackwardArgs args, const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_dout) {
+    using S = Storage;
+    constexpr int kStages = S::kStages;
+    extern __shared__ uint8_t shared_raw[];
+    S &s = *reinterpret_cast<S *>((reinterpret_cast<uintptr_t>(shared_raw) + 1023) & ~uintptr_t(1023));
+    const AttentionParams &p = args.p;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const TileWindow window = tile_window<kStages>(p, true, args.blocks_per_head);
+    const int h = window.h, b = window.b;
+
+    if (warp == 0) {
+        tmem_alloc(&s.tmem_base, kTmemColumns);
+        tmem_relinquish();
+    }
+    if (threadIdx.x == kProducerWarp * 32) {
+        for (int i = 0; i < kStages; ++i) {
+            mbar_init(&s.full[i], 1);
+            mbar_init(&s.raw_free[i], kSplitThreads);
+            mbar_init(&s.ready[i], kSplitThreads);
+            mbar_init(&s.empty[i], 1);
+        }
+        mbar_init(&s.s_full[0], 1);
+        mbar_init(&s.s_full[1], 1);
+        mbar_init(&s.p_full, kRowThreads);
+        mbar_init(&s.x_done, 1);
+        mbar_init(&s.rows_ready, kRowThreads);
+        mbar_init(&s.range_ready, 1);
+        mbar_init(&s.mma_done, 1);
+        mbar_fence_init();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s.tmem_base;
+
+    if (warp == kProducerWarp) {
+        producer_role<32, true>(s, window, tmap_q, tmap_dout, lane);
+    } else if (warp >= kSplitWarp) {
+        split_role<32, true>(s, p, window, warp - kSplitWarp, lane);
+    } else if (warp == kMmaWarp) {
+        // ---------------------------------------------------------------- MMA issuer
+        // Per tile j: S(j + 1) and dP(j + 1) go out before waiting for P(j) / dS(j); then dK, dV
+        // and dQ of tile j. The MMAs run in issue order, so S(j + 2) overwrites the buffers of
+        // tile j only after the products that read them.
+        const int tiles = __shfl_sync(0xffffffffu, visited_tiles(s), 0);
+        if (tiles > 0) {
+            using G = Geometry<32>;
+            constexpr uint64_t row_stage = G::kRowWords * 4 / 16;
+            constexpr uint64_t k_step = 2048 / 16;  // 16 K rows of an MN-major operand
+            const uint64_t b1_desc = sw128_descriptor(smem_u32(s.b1[0]));
+            const uint64_t b2_desc = sw128_descriptor(smem_u32(s.b2[0]));
+            const uint64_t b1_mn_desc = sw128_mn_descriptor(smem_u32(s.b1[0]), G::kMnChunkBytes);
+            const uint64_t b2_mn_desc = sw128_mn_descriptor(smem_u32(s.b2[0]), G::kMnChunkBytes);
+            const uint64_t k_desc = sw128_descriptor(smem_u32(s.a1));
+            const uint64_t v_desc = sw128_descriptor(smem_u32(s.a2));
+            const uint64_t k_mn_desc = sw128_mn_descriptor(smem_u32(s.a1), G::kMnChunkBytes);
+            const auto issue_scores = [&](int j) -> bool {
+                const int stage = j % kStages;
+                if (!mbar_wait_warp(&s.ready[stage], (j / kStages) & 1)) return false;
+                tc_fence_after();
+                const uint32_t scores = tmem + kScores + 128 * (j & 1);
+                issue_product_smem<32>(scores, k_desc, b1_desc + row_stage * stage, nullptr);
+                issue_product_smem<32>(scores + 64, v_desc, b2_desc + row_stage * stage, &s.s_full[j & 1]);
+                return true;
+            };
+            bool ok = mbar_wait_warp(&s.rows_ready, 0) && issue_scores(0);
+            for (int j = 0; j < tiles && ok; ++j) {
+                const int stage = j % kStages;
+                if (j + 1 < tiles && !issue_scores(j + 1)) {
+                    ok = false;
+                    break;
+                }
+                ok = mbar_wait_warp(&s.p_full, j & 1);
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t scores = tmem + kScores + 128 * (j & 1);
+                issue_x<32>(tmem + kX1, scores + 64, b1_mn_desc + row_stage * stage, nullptr);
+                issue_x<32>(tmem + kX2, scores, b2_mn_desc + row_stage * stage, nullptr);
+#pragma unroll
+                for (int term = 0; term < 2; ++term) {
+                    const uint64_t ds_desc = sw128_mn_descriptor(smem_u32(s.ds[j & 1][term]), G::kMnChunkBytes);
+#pragma unroll
+                    for (int half = 0; half < 2; ++half) {
+                        const uint64_t a[4] = {ds_desc + (4 * half) * k_step, ds_desc + (4 * half + 1) * k_step,
+                                               ds_desc + (4 * half + 2) * k_step, ds_desc + (4 * half + 3) * k_step};
+                        const uint64_t bk[4] = {k_mn_desc + (4 * half) * k_step, k_mn_desc + (4 * half + 1) * k_step,
+                                                k_mn_desc + (4 * half + 2) * k_step, k_mn_desc + (4 * half + 3) * k_step};
+                        mma4_f16_ss_warp(tmem + kDQ, a, bk, kIdescDQ, term == 0 && half == 0);
+                    }
+                }
+                mma_commit_warp(&s.x_done);
+                mma_commit_warp(&s.empty[stage]);
+            }
+            mma_commit_warp(&s.mma_done);
+            mbar_wait_warp(&s.mma_done, 0);
+        }
+    } else {
+        // ---------------------------------------------------------------- row warps
+        const int g = warp >> 2;               // warpgroup: column half of each tile, feature half of the outputs
+        const int r = threadIdx.x & (kRows - 1);  // key row within the tile = TMEM lane
+        const int row = window.r0 + r;
+        const bool row_valid = row < p.keys;
+        const bool row_active = row_valid && window.mask[row] != 0;
+        const uint32_t lanes = lane_address(tmem, warp);
+        float l1_max;  // max over the CTA's keys of ||v_j||_1
+        int ea1, ea2;  // exponents of K (one for the CTA) and of this key's V row
+        {
+            float x[32];
+            load_row<32>(p.v.row(b, h, row_valid ? row : 0), row_active, 1.f, x);
+            float l1 = 0.f;
+#pragma unroll
+            for (int c = 0; c < 32; ++c) l1 += fabsf(x[c]);
+            ea2 = fp16_scale_exponent(abs_max<32>(x));
+            if (g == 0) store_row_operand_smem<32>(x, ea2, s.a2, r);
+            load_row<32>(p.k.row(b, h, row_valid ? row : 0), row_active, 1.f, x);
+            float k_max = abs_max<32>(x);
+#pragma unroll
+            for (int offset = 16; offset; offset >>= 1) {
+                k_max = fmaxf(k_max, __shfl_xor_sync(0xffffffffu, k_max, offset));
+                l1 = fmaxf(l1, __shfl_xor_sync(0xffffffffu, l1, offset));
+            }
+            if (g == 0 && lane == 0) {
+                s.row_max[warp][0] = k_max;
+                s.row_max[warp][1] = l1;
+            }
+            asm volatile("bar.sync 2, 256;" ::: "memory");
+            k_max = max3(max3(s.row_max[0][0], s.row_max[1][0], s.row_max[2][0]), s.row_max[3][0], 0.f);
+            l1_max = max3(max3(s.row_max[0][1], s.row_max[1][1], s.row_max[2][1]), s.row_max[3][1], 0.f);
+            ea1 = fp16_scale_exponent(k_max);
+            if (g == 1) store_row_operand_smem<32>(x, ea1, s.a1, r);
+            fence_proxy_async_shared();  // the stores, visible to the MMAs' shared-memory reads
+            mbar_arrive(&s.rows_ready);
+        }
+
+        float acc1[16], acc2[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) acc1[c] = acc2[c] = 0.f;
+        float pending1 = 0.f, pending2 = 0.f, pending_dq = 0.f;  // scales of the last tile's products
+        int pending_c0 = 0;
+        bool ok = true;
+        const int tiles = __shfl_sync(0xffffffffu, visited_tiles(s), 0);
+        for (int j = 0; j < tiles && ok; ++j) {
+            const int stage = j % kStages;
+            const uint32_t scores = lanes + kScores + 128 * (j & 1);
+            ok = __all_sync(0xffffffffu, mbar_wait(&s.s_full[j & 1], (j >> 1) & 1) && mbar_wait(&s.ready[stage], (j / kStages) & 1));
+            if (!ok) break;
+            tc_fence_after();
+            const int c0 = window.first + j * kCols;
+            const int e1 = s.e1[stage], e2 = s.e2[stage];
+            const float slope = kLog2e * exp2_int(-(ea1 + e1));  // TMEM S -> log2e * score
+            const float dp_scale = exp2_int(-(ea2 + e2));        // TMEM dP -> dP
+            // One dS exponent for the CTA: |dS| <= max_j ||v_j||_1 max|dO| + max|delta| (P <= 1)
+            const int gs = fp16_scale_exponent(l1_max * exp2_int(15 - e2) + s.col_delta_max[stage]);
+            const float to_ds = exp2_int(gs - 14);  // P' (= 2^14 P) * (dP - delta) * to_ds = 2^gs dS
+            const float w_scale = dp_scale * to_ds;
+            uint64_t active = row_active ? (static_cast<uint64_t>(s.col_mask[stage][0]) | (static_cast<uint64_t>(s.col_mask[stage][1]) << 32))
+                                         : 0ull;
+            if (p.radius >= 0) {
+                const int lo_col = max(0, row - p.radius - c0), hi_col = min(kCols - 1, row + p.radius - c0);
+                active &= lo_col > hi_col ? 0ull : ((~0ull) >> (63 - (hi_col - lo_col))) << lo_col;
+            }
+            const bool all_active = __all_sync(0xffffffffu, static_cast<uint32_t>(active >> (32 * g)) == ~0u);
+#pragma unroll
+            for (int cc = 0; cc < 2; ++cc) {
+                const int chunk = 2 * g + cc;
+                float sv[16], dv[16];  // scores, then P'; dP, then dS'
+                tmem_load16x2(scores + 16 * chunk, sv, scores + 64 + 16 * chunk, dv);
+                float col_offset[16], col_delta[16];
+                const float4 *o4 = reinterpret_cast<const float4 *>(&s.col_offset[stage][16 * chunk]);
+                const float4 *d4 = reinterpret_cast<const float4 *>(&s.col_delta[stage][16 * chunk]);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float4 o = o4[i], d = d4[i];
+                    col_offset[4 * i] = o.x, col_offset[4 * i + 1] = o.y, col_offset[4 * i + 2] = o.z, col_offset[4 * i + 3] = o.w;
+                    col_delta[4 * i] = d.x, col_delta[4 * i + 1] = d.y, col_delta[4 * i + 2] = d.z, col_delta[4 * i + 3] = d.w;
+                }
+#pragma unroll
+                for (int c = 0; c < 16; c += 2) {
+                    const int col = 16 * chunk + c;
+                    const float2 arg = fma_f32x2(make_float2(sv[c], sv[c + 1]), make_float2(slope, slope),
+                                                 make_float2(col_offset[c], col_offset[c + 1]));
+                    float pa = fast_exp2(arg.x), pb = fast_exp2(arg.y);
+                    if (!all_active) {
+                        pa = (active >> col) & 1 ? pa : 0.f;
+                        pb = (active >> (col + 1)) & 1 ? pb : 0.f;
+                    }
+                    sv[c] = pa;
+                    sv[c + 1] = pb;
+                    // dS' = P' (dP w - delta to_ds)
+                    const float2 shifted = fma_f32x2(make_float2(dv[c], dv[c + 1]), make_float2(w_scale, w_scale),
+                                                     mul_f32x2(make_float2(col_delta[c], col_delta[c + 1]), make_float2(-to_ds, -to_ds)));
+                    const float2 ds = mul_f32x2(make_float2(pa, pb), shifted);
+                    dv[c] = ds.x;
+                    dv[c + 1] = ds.y;
+                }
+                store_split_chunk_dual(scores + 64 + 16 * chunk, dv, s.ds[j & 1][0], s.ds[j & 1][1], r, chunk);
+                store_split_chunk(scores + 16 * chunk, sv);
+            }
+            // Fold the previous tile's products before the P(j)/dS(j) arrival lets the MMA warp
+            // overwrite them.
+            if (j > 0) {
+                ok = __all_sync(0xffffffffu, mbar_wait(&s.x_done, (j - 1) & 1));
+                if (!ok) {
+                    tmem_wait_store();
+                    break;
+                }
+                tc_fence_after();
+                fold_x_half(acc1, acc2, lanes, g, pending1, pending2);
+                fold_dq(p.dq + (window.query_base + pending_c0) * 32, window.last - pending_c0, lanes, g, warp, lane, pending_dq);
+            }
+            tmem_wait_store();
+            fence_proxy_async_shared();  // the dS^T stores, visible to the dQ MMAs
+            tc_fence_before();
+            mbar_arrive(&s.p_full);
+            // dK = 2^-(gs + e1) X1; dV = 2^-(14 + e2) X2; dQ = scale 2^-(gs + ea1) (dS' . K')
+            pending1 = exp2_int(-(gs + e1));
+            pending2 = exp2_int(-(14 + e2));
+            pending_dq = p.scale * exp2_int(-(gs + ea1));
+            pending_c0 = c0;
+        }
+        if (tiles > 0 && ok) {
+            ok = __all_sync(0xffffffffu, mbar_wait(&s.x_done, (tiles - 1) & 1));
+            tc_fence_after();
+            if (ok) {
+                fold_x_half(acc1, acc2, lanes, g, pending1, pending2);
+                fold_dq(p.dq + (window.query_base + pending_c0) * 32, window.last - pending_c0, lanes, g, warp, lane, pending_dq);
+            }
+        }
+        // dK, dV (packed [batch][heads][keys][32]), features [16 g, 16 g + 16); a failed wait leaves NaN.
+        if (row_valid) {
+            const float bad = ok ? 1.f : NAN;
+            const long long key_row = (static_cast<long long>(b) * p.heads + h) * p.keys + row;
+            float4 *dk = reinterpret_cast<float4 *>(p.dk + key_row * 32 + 16 * g);
+            float4 *dv = reinterpret_cast<float4 *>(p.dv + key_row * 32 + 16 * g);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                if (row_active) {
+                    dk[c] = make_float4(acc1[4 * c] * bad, acc1[4 * c + 1] * bad, acc1[4 * c + 2] * bad, acc1[4 * c + 3] * bad);
+                    dv[c] = make_float4(acc2[4 * c] * bad, acc2[4 * c + 1] * bad, acc2[4 * c + 2] * bad, acc2[4 * c + 3] * bad);
+                } else {
+                    dk[c] = dv[c] = make_float4(0.f, 0.f, 0.f, 0.f);  // masked key: exactly zero
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemColumns);
+    }
+}
+}  // namespace fused
+
 // ---- host side ----------------------------------------------------------------------------------
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_function() {
@@ -870,6 +1314,26 @@ int launch_both(const AttentionParams &p, cudaStream_t stream) {
     return launch_pass<D, true>(p, map_q, map_dout, stream);  // dK, dV (reads delta)
 }
 
+// The fused backward: the delta / dQ-zeroing pre-pass, then the key-major pass, ordered on `stream`.
+int launch_fused(const AttentionParams &p, cudaStream_t stream) {
+    CUtensorMap map_q, map_dout;
+    if (!make_tensor_map(&map_q, p.q, 32, p.batch, p.heads, p.queries) ||
+        !make_tensor_map(&map_dout, p.dout, 32, p.batch, p.heads, p.queries))
+        return kNotEligible;
+    cudaError_t status = prepare_kernel<fused::backward_kernel>(fused::shared_bytes());
+    if (status != cudaSuccess) return status;
+    const long long rows = static_cast<long long>(p.batch) * p.heads * p.queries;
+    fused::prepass_kernel<<<static_cast<unsigned>((rows * 8 + 255) / 256), 256, 0, stream>>>(p, rows);
+    status = cudaGetLastError();
+    if (status != cudaSuccess) return status;
+    BackwardArgs args{};
+    args.p = p;
+    args.blocks_per_head = (p.keys + kRows - 1) / kRows;
+    const unsigned blocks = static_cast<unsigned>(args.blocks_per_head) * static_cast<unsigned>(p.heads) * static_cast<unsigned>(p.batch);
+    fused::backward_kernel<<<blocks, fused::kThreads, fused::shared_bytes(), stream>>>(args, map_q, map_dout);
+    return cudaGetLastError();
+}
+
 }  // namespace
 
 bool backward_supported(const AttentionParams &p) {
@@ -883,6 +1347,8 @@ int launch_backward(const AttentionParams &p, int head_width, cudaStream_t strea
     if (head_width == 64) return launch_both<64>(p, stream);
     return kNotEligible;
 }
+
+int launch_fused_backward(const AttentionParams &p, cudaStream_t stream) { return launch_fused(p, stream); }
 
 #ifdef RK_TC_TRACE
 extern "C" __attribute__((visibility("default"))) int rocmkernels_attention_backward_trace(long long *out, int capacity) {

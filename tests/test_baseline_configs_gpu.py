@@ -83,7 +83,8 @@ C1 = dict(batch=2, heads=12, seq=128, dim=32)
 C1_FORWARD = ([("attention_fp32_forward", None), ("attention_fp32_forward_tiled", None), ("attention_fp32_forward_flash", None)]
               + [("attention_fp32_forward_flash_tuned", v) for v in range(19)]
               + [("attention_fp32_forward_tuned", g) for g in (2, 4, 8, 84, 164, 1164, 1264)])
-C1_BACKWARD = ([("attention_fp32_backward", None), ("attention_fp32_backward_tiled", None)]
+C1_BACKWARD = ([("attention_fp32_backward", None), ("attention_fp32_backward_tiled", None),
+                ("attention_fp32_backward_fused", None)]
                + [("attention_fp32_backward_tuned", g) for g in (2, 4, 8, 84, 164, 1164, 1264)])
 
 
@@ -151,18 +152,19 @@ def _forward_backward_config(dev, label, batch, heads, seq, dim, radius, low, hi
     q, k, v, u, mask = config_inputs(batch, heads, seq, dim, lengths)
     expected = oracle.attention(q, k, v, mask, u, radius, threads=oracle.cpu_count())
     forward = "attention_fp32_forward_flash" if dim == 32 else "attention64_fp32_forward"
-    backward = "attention_fp32_backward" if dim == 32 else "attention64_fp32_backward"
+    backwards = ["attention_fp32_backward", "attention_fp32_backward_fused"] if dim == 32 else ["attention64_fp32_backward"]
     status, out, lse = dev.forward(forward, q, k, v, mask, radius)
     assert status == 0
     assert_forward_close(out, lse, expected, label)
-    status, grads = dev.backward(backward, q, k, v, mask, u, out, lse, radius)
-    assert status == 0
-    assert_gradients_close(grads, expected, label)
-    for b, length in enumerate(lengths):  # masked keys: exact zeros
-        assert np.all(grads["grad_k"][b][:, length:] == 0.0) and np.all(grads["grad_v"][b][:, length:] == 0.0)
     report(label, O=normwise(out, expected["output"]), lse_max=normwise(lse[..., 0], expected["lse"][..., 0]),
-           lse_sum=normwise(lse[..., 1], expected["lse"][..., 1]),
-           **{n: normwise(grads[n], expected[n]) for n in ("grad_q", "grad_k", "grad_v")})
+           lse_sum=normwise(lse[..., 1], expected["lse"][..., 1]))
+    for backward in backwards:
+        status, grads = dev.backward(backward, q, k, v, mask, u, out, lse, radius)
+        assert status == 0
+        assert_gradients_close(grads, expected, f"{label} {backward}")
+        for b, length in enumerate(lengths):  # masked keys: exact zeros
+            assert np.all(grads["grad_k"][b][:, length:] == 0.0) and np.all(grads["grad_v"][b][:, length:] == 0.0)
+        report(f"{label}/{backward}", **{n: normwise(grads[n], expected[n]) for n in ("grad_q", "grad_k", "grad_v")})
     status, out0, lse0 = dev.forward(forward, np.zeros_like(q), k, v, mask, radius)
     assert status == 0
     assert_selection_exact(lse0, out0, visible_counts(mask, radius), f"{label} selection")
@@ -194,9 +196,14 @@ def test_c5_declared_slices(dev):
     st = api.strides_of(dq)
     assert api.attention_fp32_forward_flash(dq, dk, dv, dmask, out, lse, B, H, S, S, -1, st, st, st, st) == 0
     assert api.attention_fp32_backward(dq, dk, dv, dmask, out, lse, du, gq, gk, gv, delta, B, H, S, S, -1, st, st, st, st, st) == 0
+    fq, fk, fv = (torch.full_like(dq, float("nan")) for _ in range(3))  # the fused single-pass backward
+    fdelta = torch.full((B, H, S), float("nan"), device=device)
+    assert api.attention_fp32_backward_fused(dq, dk, dv, dmask, out, lse, du, fq, fk, fv, fdelta, B, H, S, S, -1,
+                                             st, st, st, st, st) == 0
     torch.cuda.synchronize()
     assert api.device_status() == 0
     assert bool(torch.isfinite(out).all()) and bool(torch.isfinite(gq).all()) and bool(torch.isfinite(gk).all())
+    assert bool(torch.isfinite(fq).all()) and bool(torch.isfinite(fk).all()) and bool(torch.isfinite(fv).all())
 
     def slice_check(bh):
         b, h = bh
@@ -215,10 +222,13 @@ def test_c5_declared_slices(dev):
         report(label, O=normwise(got_out, exp["output"]), lse_max=normwise(got_lse[..., 0], exp["lse"][..., 0]),
                lse_sum=normwise(got_lse[..., 1], exp["lse"][..., 1]),
                **{n: normwise(grads[n], exp[n]) for n in ("grad_q", "grad_k", "grad_v")})
+        fused = {n: t[b:b + 1, h:h + 1].cpu().numpy() for n, t in (("grad_q", fq), ("grad_k", fk), ("grad_v", fv))}
+        assert_gradients_close(fused, exp, f"{label} fused")
+        report(f"{label} fused", **{n: normwise(fused[n], exp[n]) for n in ("grad_q", "grad_k", "grad_v")})
     # Selection on the whole problem: Q = 0 gives max 0 and sum 4096 in every row.
     dq.zero_()
     assert api.attention_fp32_forward_flash(dq, dk, dv, dmask, out, lse, B, H, S, S, -1, st, st, st, st) == 0
     torch.cuda.synchronize()
     assert bool((lse[..., 0] == 0).all()) and bool((lse[..., 1] == float(S)).all())
-    del dq, dk, dv, du, out, lse, gq, gk, gv, delta
+    del dq, dk, dv, du, out, lse, gq, gk, gv, delta, fq, fk, fv, fdelta
     torch.cuda.empty_cache()

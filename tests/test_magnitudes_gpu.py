@@ -52,10 +52,12 @@ def test_scaled_inputs_forward_backward(dev, width, scales):
     assert normwise(out, expected["output"]) <= FORWARD_TOL, label
     assert normwise(lse[..., 0], expected["lse"][..., 0]) <= FORWARD_TOL, label
     assert normwise(lse[..., 1], expected["lse"][..., 1]) <= FORWARD_TOL, label
-    status, grads = dev.backward(backward, q, k, v, mask, upstream, out, lse)
-    assert status == 0
-    for name in ("grad_q", "grad_k", "grad_v"):
-        assert normwise(grads[name], expected[name]) <= GRADIENT_TOL, f"{label} {name}"
+    # d = 32 also through the fused single-pass backward (one K and dS exponent per 128-key tile)
+    for entry in [backward] + (["attention_fp32_backward_fused"] if width == 32 else []):
+        status, grads = dev.backward(entry, q, k, v, mask, upstream, out, lse)
+        assert status == 0
+        for name in ("grad_q", "grad_k", "grad_v"):
+            assert normwise(grads[name], expected[name]) <= GRADIENT_TOL, f"{label} {entry} {name}"
 
 
 @pytest.mark.parametrize("scales", SCALES[:2], ids=lambda s: "q{:g}_k{:g}".format(*s[:2]))

@@ -37,6 +37,7 @@ FORWARD_32 = [
 BACKWARD_32 = [
     ("attention_fp32_backward", None),
     ("attention_fp32_backward_tiled", None),
+    ("attention_fp32_backward_fused", None),
     ("attention_fp32_backward_tuned", 4),
     ("attention_fp32_backward_tuned", 1264),
 ]
@@ -148,12 +149,13 @@ def test_statistics_entry_matches_forward_lse(dev):
     assert normwise(got[..., 1], expected["lse"][..., 1]) <= 1e-5
 
 
-def test_masked_keys_get_zero_gradients_bitwise(dev):
+@pytest.mark.parametrize("entry", ["attention_fp32_backward", "attention_fp32_backward_fused"])
+def test_masked_keys_get_zero_gradients_bitwise(dev, entry):
     q, k, v, upstream, mask = make_inputs(2, 2, 90, 110, 32, dist="normal", mask_fraction=0.4)
     k[0][:, mask[0] == 0] = np.nan  # garbage in masked rows must not leak (the reference zeroes them)
     v[0][:, mask[0] == 0] = np.inf
     _, out, lse = dev.forward("attention_fp32_forward", q, k, v, mask)
-    status, grads = dev.backward("attention_fp32_backward", q, k, v, mask, upstream, out, lse)
+    status, grads = dev.backward(entry, q, k, v, mask, upstream, out, lse)
     assert status == 0
     for b in range(2):
         hidden = mask[b] == 0
