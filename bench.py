@@ -78,6 +78,13 @@ WORKLOADS = {
                                               "(for the tensor-core vs SIMT comparison)"),
     "fwd_bwd_b4h12s4096d32": dict(batch=4, heads=12, seq=4096, dim=32, radius=-1, lengths=None, backward=True,
                                   description="profiling case: C5's shape at B=4 (inputs above L2, a few hundred MB)"),
+    "c5_fused_fwd_bwd_b64h12s4096d32": dict(batch=64, heads=12, seq=4096, dim=32, radius=-1, lengths=None, backward=True,
+                                            backward_entry="attention_fp32_backward_fused",
+                                            description="BASELINE configs[4] with the fused single-pass backward "
+                                                        "(attention_fp32_backward_fused)"),
+    "fused_fwd_bwd_b4h12s4096d32": dict(batch=4, heads=12, seq=4096, dim=32, radius=-1, lengths=None, backward=True,
+                                        backward_entry="attention_fp32_backward_fused",
+                                        description="profiling case of the fused single-pass backward: C5's shape at B=4"),
 }
 WORKLOADS["flash_rotary_fwd_b8h3s1024d32"] = dict(
         batch=8, heads=3, seq=1024, dim=32, radius=-1, lengths=None, backward=False, rotary=True,
@@ -611,7 +618,7 @@ def c5_strong(args, device, world: int, rank: int, dist, api) -> dict:
     (0, 0) slice, which it computes itself, against the oracle."""
     import torch
 
-    from rocmkernels_b200.sharding import run_backward, run_forward, shard_plan
+    from rocmkernels_b200.sharding import run_backward, run_forward, shard_plan, workspace_bytes
 
     spec = WORKLOADS["c5_fwd_bwd_b64h12s4096d32"]
     B, H, S, D = spec["batch"], spec["heads"], spec["seq"], spec["dim"]
@@ -640,16 +647,22 @@ def c5_strong(args, device, world: int, rank: int, dist, api) -> dict:
         if status != 0:
             raise api.HipError(status, "attention_fp32_forward_flash")
 
-    def backward():
-        status = run_backward(api.attention_fp32_backward, t, plan, stream=stream, **geometry)
+    two_pass, fused = "attention_fp32_backward", "attention_fp32_backward_fused"
+    workspace = torch.empty(max(1, workspace_bytes(api.attention_fp32_backward_fused_workspace_size, plan, S)), dtype=torch.uint8,
+                            device=device)
+
+    def backward(entry):
+        status = run_backward(getattr(api, entry), t, plan, stream=stream, workspace=workspace if entry == fused else None,
+                              **geometry)
         if status != 0:
-            raise api.HipError(status, "attention_fp32_backward")
+            raise api.HipError(status, entry)
 
     for _ in range(2):
         forward()
-        backward()
+        backward(two_pass)
+        backward(fused)
     steps = max(3, min(args.steps, 10))
-    marks = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+    marks = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
     torch.cuda.synchronize(device)
     if world > 1:
         dist.barrier()
@@ -657,28 +670,39 @@ def c5_strong(args, device, world: int, rank: int, dist, api) -> dict:
         marks[i][0].record(stream)
         forward()
         marks[i][1].record(stream)
-        backward()
+        backward(two_pass)
         marks[i][2].record(stream)
+        backward(fused)
+        marks[i][3].record(stream)
     torch.cuda.synchronize(device)
-    own = [sum(m[0].elapsed_time(m[1]) for m in marks) / steps, sum(m[1].elapsed_time(m[2]) for m in marks) / steps]
-    times = torch.tensor([own[0] + own[1]] + own, device=device, dtype=torch.float64)
+    own = [sum(m[e].elapsed_time(m[e + 1]) for m in marks) / steps for e in range(3)]
+    times = torch.tensor([own[0] + own[2], own[0] + own[1]] + own, device=device, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    step_ms, forward_ms, backward_ms = times.tolist()
+    step_ms, step_two_pass_ms, forward_ms, backward_ms, backward_fused_ms = times.tolist()
     slices = [c.batch * c.heads for c in plan]
+    flops = 12.0 * B * H * S * S * D
     record = {"workload": "c5_fwd_bwd_b64h12s4096d32", "description": spec["description"], "scaling": "strong",
-              "ranks": world, "steps": steps, "ms_per_step": step_ms, "forward_ms": forward_ms, "backward_ms": backward_ms,
-              "tflops": 12.0 * B * H * S * S * D / (step_ms * 1e-3) / 1e12,
+              "ranks": world, "steps": steps,
+              "ms_per_step": step_ms, "tflops": flops / (step_ms * 1e-3) / 1e12,
+              "step": "attention_fp32_forward_flash + attention_fp32_backward_fused (the single-pass backward)",
+              "ms_per_step_two_pass": step_two_pass_ms, "tflops_two_pass": flops / (step_two_pass_ms * 1e-3) / 1e12,
+              "forward_ms": forward_ms, "backward_two_pass_ms": backward_ms, "backward_fused_ms": backward_fused_ms,
               "rank0_slices": sum(slices), "rank0_active_pairs": sum(slices) * S * S,
               "partition": "rocmkernels_b200.sharding.shard_plan: contiguous batch ranges, no collective on the data path",
-              "gpu_launches_per_rank": steps * 3 * len(plan), "data": data,
-              "time": "CUDA events per rank around each step's calls, mean over steps, max over ranks; inputs > L2"}
+              "gpu_launches_per_rank": steps * 5 * len(plan), "data": data,
+              "time": "CUDA events per rank around each call, mean over steps, max over ranks; inputs > L2; both "
+                      "backward forms run every step on the same forward output"}
     if rank == 0 and arrays is not None:
         results = {n: t[n][0:1, 0:1].cpu().numpy() for n in ("out", "lse", "grad_q", "grad_k", "grad_v")}
         record["parity"] = parity_check(arrays, results, [(0, 0)], -1, True)
+        backward(two_pass)  # the (0, 0) slice through the two-pass backward as well
+        torch.cuda.synchronize(device)
+        results = {n: t[n][0:1, 0:1].cpu().numpy() for n in ("out", "lse", "grad_q", "grad_k", "grad_v")}
+        record["parity_two_pass"] = parity_check(arrays, results, [(0, 0)], -1, True)
     if world > 1:
         dist.barrier()
-    del t, fwd_t
+    del t, fwd_t, workspace
     torch.cuda.empty_cache()
     return record
 
@@ -705,7 +729,7 @@ def main() -> None:
     import torch.distributed as dist
 
     import rocmkernels_b200.attention as api
-    from rocmkernels_b200.sharding import ShardCall, run_backward, run_forward, shard_plan
+    from rocmkernels_b200.sharding import ShardCall, run_backward, run_forward, shard_plan, workspace_bytes
 
     if not torch.cuda.is_available():
         raise SystemExit("bench.py needs a CUDA device")
@@ -781,7 +805,8 @@ def main() -> None:
     qs, ks, vs, os_ = (api.strides_of(t) for t in (q, k, v, out))
     forward_fn = (getattr(api, spec["entry"]) if spec.get("entry") else
                   api.attention_fp32_forward_flash if dim == 32 else api.attention64_fp32_forward)
-    backward_fn = api.attention_fp32_backward if dim == 32 else api.attention64_fp32_backward
+    backward_fn = (getattr(api, spec["backward_entry"]) if spec.get("backward_entry") else
+                   api.attention_fp32_backward if dim == 32 else api.attention64_fp32_backward)
     # This rank's work: the (batch, head) slices of its plan.
     rank_pairs = sum(active_pairs(seq, radius, lengths[b]) * (c.h1 - c.h0) for c in plan for b in range(c.b0, c.b1))
     rank_slices = sum(c.batch * c.heads for c in plan)
@@ -810,10 +835,22 @@ def main() -> None:
     if with_backward:
         strides["upstream"] = api.strides_of(upstream)
 
+    fused_backward = with_backward and spec.get("backward_entry") == "attention_fp32_backward_fused"
+    workspaces = {}  # the fused backward's workspace by size; every call using one is ordered on one stream
+
+    def workspace_for(calls):
+        if not fused_backward:
+            return None
+        size = workspace_bytes(api.attention_fp32_backward_fused_workspace_size, calls, seq)
+        if size not in workspaces:
+            workspaces[size] = torch.empty(max(size, 1), dtype=torch.uint8, device=device)
+        return workspaces[size]
+
     def make_phases(t, st, calls, problem_batch):
         """The step's kernel calls on tensor set `t` (a problem of `problem_batch` sequences),
         making the calls of `calls`, launched on stream `st`."""
         geometry = dict(heads=heads, queries=seq, keys=seq, width=dim, radius=radius, strides=strides)
+        workspace = workspace_for(calls)
 
         def forward():
             if rotary:
@@ -834,7 +871,7 @@ def main() -> None:
                 raise api.HipError(status, "attention_generic_forward" if generic else forward_fn.__name__)
 
         def backward():
-            status = run_backward(backward_fn, t, calls, stream=st, **geometry)
+            status = run_backward(backward_fn, t, calls, stream=st, workspace=workspace, **geometry)
             if status != 0:
                 raise api.HipError(status, backward_fn.__name__)
 
@@ -947,7 +984,9 @@ def main() -> None:
                     "traffic": traffic_from_profiles(f"tcgen05-backward-d{dim}", args.workload),
                     "peak_source": f"{peak_source} bf16_tflops (burst); the TF32 dense rate is half of it",
                     "frac_of_tf32_dense": achieved / (peak / 2), "frac_of_fp32_fma": achieved / fma_peak,
-                    "kernel": f"tcgen05 split-FP16 backward d{dim} (query-major delta+dQ, key-major dK/dV)",
+                    "kernel": (f"tcgen05 split-FP16 fused single-pass backward d{dim} (column pre-pass, key-major dK/dV/dQ)"
+                               if fused_backward else
+                               f"tcgen05 split-FP16 backward d{dim} (query-major delta+dQ, key-major dK/dV)"),
                     "flops": "effective: 8*d per active (query, key) pair"}
     else:
         achieved = effective_forward / (part_seconds[0] / args.steps) / 1e12

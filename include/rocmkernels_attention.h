@@ -96,17 +96,26 @@ ROCMKERNELS_C_EXPORT int attention_fp32_backward_tiled(const float *q, const flo
         RocmKernelsStream stream);
 
 /* 32-wide backward in one key-major pass (the single-pass form of attention_fp32_backward, same
- * arguments and outputs): a pre-pass writes delta and zeroes gradient_q, then one kernel computes
- * dK and dV per key and adds each key tile's share of dQ with FP32 atomics, so dQ's summation
- * order over key tiles is not fixed (results may differ in the last bits from run to run; the
- * reference's two-kernel split, attention_fp32_backward, is deterministic). Tensors the tensor-core
- * kernels cannot address take the two-pass path. No counterpart in the reference (its backward is
+ * arguments and outputs plus a workspace): a column pre-pass writes delta, zeroes gradient_q and
+ * stores in `workspace` the split-FP16 copies of scaled Q and of upstream and per-64-query
+ * statistics; then one kernel computes dK and dV per key and adds each key tile's share of dQ with
+ * FP32 atomics, so dQ's summation order over key tiles is not fixed (results may differ in the
+ * last bits from run to run; dK, dV and delta are repeatable; the reference's two-kernel split,
+ * attention_fp32_backward, is deterministic). `workspace` is device memory of at least
+ * attention_fp32_backward_fused_workspace_size(batch, heads, queries) bytes, 128-byte aligned
+ * for the single-pass kernels (a null or smaller workspace returns 1; an unaligned one, or
+ * tensors the tensor-core kernels cannot address, take the two-pass path); it may be reused
+ * between calls that are ordered on one stream. No counterpart in the reference (its backward is
  * the two-pass Attention.hip:205-223). */
 ROCMKERNELS_C_EXPORT int attention_fp32_backward_fused(const float *q, const float *k, const float *v, const bool *mask,
         const float *output, const float *lse, const float *upstream, float *gradient_q, float *gradient_k,
-        float *gradient_v, float *delta, int batch, int heads, int queries, int keys, int radius, RocmKernelsStrides qs,
-        RocmKernelsStrides ks, RocmKernelsStrides vs, RocmKernelsStrides os, RocmKernelsStrides us,
-        RocmKernelsStream stream);
+        float *gradient_v, float *delta, void *workspace, unsigned long long workspace_bytes, int batch, int heads,
+        int queries, int keys, int radius, RocmKernelsStrides qs, RocmKernelsStrides ks, RocmKernelsStrides vs,
+        RocmKernelsStrides os, RocmKernelsStrides us, RocmKernelsStream stream);
+
+/* Workspace bytes attention_fp32_backward_fused needs: 256 bytes per query (rounded up to 64
+ * queries per (batch, head)) plus 528 bytes per 64 queries; 0 for non-positive sizes. */
+ROCMKERNELS_C_EXPORT unsigned long long attention_fp32_backward_fused_workspace_size(int batch, int heads, int queries);
 
 /* Softmax statistics only ({max, sum} per row; no V read, no O write); radius < -1 is invalid.
  * Replaces attention_fp32_statistics (Attention.hpp:23-24; Attention.hip:252-261). */

@@ -103,8 +103,11 @@ def lib() -> ctypes.CDLL:
         library.rocmkernels_attention_device_status.restype = ctypes.c_uint
         library.attention_fp32_backward_static_delta.argtypes = [_POINTER] * 10 + [_INT] * 5 + [Strides] * 5 + [_POINTER]
         library.attention_fp32_backward_static_delta.restype = ctypes.c_int
-        library.attention_fp32_backward_fused.argtypes = _BACKWARD_ARGS
+        library.attention_fp32_backward_fused.argtypes = ([_POINTER] * 12 + [ctypes.c_ulonglong] + [_INT] * 5 + [Strides] * 5
+                                                          + [_POINTER])
         library.attention_fp32_backward_fused.restype = ctypes.c_int
+        library.attention_fp32_backward_fused_workspace_size.argtypes = [_INT] * 3
+        library.attention_fp32_backward_fused_workspace_size.restype = ctypes.c_ulonglong
         library.attention_fp32_forward_flash_rotary.argtypes = [_POINTER] * 8 + [_INT] * 5 + [Strides] * 6 + [_POINTER]
         library.attention_fp32_forward_flash_rotary.restype = ctypes.c_int
         _lib = library
@@ -234,12 +237,26 @@ def attention_fp32_backward_static_delta(q, k, v, mask, output, lse, upstream, g
                  strides(vs), strides(os_), strides(us), _stream(stream))
 
 
+def attention_fp32_backward_fused_workspace_size(batch, heads, queries) -> int:
+    """Bytes of device workspace attention_fp32_backward_fused needs for these sizes."""
+    return int(lib().attention_fp32_backward_fused_workspace_size(batch, heads, queries))
+
+
 def attention_fp32_backward_fused(q, k, v, mask, output, lse, upstream, gq, gk, gv, delta, batch, heads, queries, keys, radius, qs, ks,
-                                  vs, os_, us, stream=None):
+                                  vs, os_, us, stream=None, workspace=None):
     """attention_fp32_backward in one key-major pass (dQ added with FP32 atomics: its summation
-    order over key tiles is not fixed)."""
-    return _backward("attention_fp32_backward_fused", q, k, v, mask, output, lse, upstream, gq, gk, gv, delta, batch, heads, queries,
-                     keys, radius, qs, ks, vs, os_, us, stream)
+    order over key tiles is not fixed). `workspace`: a device buffer (a torch tensor or a pointer)
+    of attention_fp32_backward_fused_workspace_size bytes; None allocates one with torch on q's
+    device (the caching allocator reuses it across calls)."""
+    size = attention_fp32_backward_fused_workspace_size(batch, heads, queries)
+    if workspace is None:
+        import torch
+
+        workspace = torch.empty(max(size, 1), dtype=torch.uint8, device=q.device)
+    capacity = workspace.numel() * workspace.element_size() if hasattr(workspace, "numel") else size
+    return _call("attention_fp32_backward_fused", ptr(q), ptr(k), ptr(v), ptr(mask), ptr(output), ptr(lse), ptr(upstream), ptr(gq),
+                 ptr(gk), ptr(gv), ptr(delta), ptr(workspace), capacity, batch, heads, queries, keys, radius, strides(qs), strides(ks),
+                 strides(vs), strides(os_), strides(us), _stream(stream))
 
 
 def attention_fp32_backward_tiled(q, k, v, mask, output, lse, upstream, gq, gk, gv, delta, batch, heads, queries, keys, radius, qs, ks,

@@ -258,20 +258,28 @@ int attention_fp32_backward(const float *q, const float *k, const float *v, cons
     return launch_backward<32>(p, stream, false);
 }
 
+unsigned long long attention_fp32_backward_fused_workspace_size(int batch, int heads, int queries) {
+    if (batch <= 0 || heads <= 0 || queries <= 0) return 0;
+    return static_cast<unsigned long long>(
+            rk::tc::fused_backward_workspace_bytes(static_cast<long long>(batch) * heads, queries));
+}
+
 int attention_fp32_backward_fused(const float *q, const float *k, const float *v, const bool *mask, const float *output,
                                   const float *lse, const float *upstream, float *gradient_q, float *gradient_k,
-                                  float *gradient_v, float *delta, int batch, int heads, int queries, int keys, int radius,
-                                  RocmKernelsStrides qs, RocmKernelsStrides ks, RocmKernelsStrides vs, RocmKernelsStrides os,
-                                  RocmKernelsStrides us, RocmKernelsStream stream) {
+                                  float *gradient_v, float *delta, void *workspace, unsigned long long workspace_bytes,
+                                  int batch, int heads, int queries, int keys, int radius, RocmKernelsStrides qs,
+                                  RocmKernelsStrides ks, RocmKernelsStrides vs, RocmKernelsStrides os, RocmKernelsStrides us,
+                                  RocmKernelsStream stream) {
     if (backward_args_bad(q, k, v, mask, output, lse, upstream, gradient_q, gradient_k, gradient_v, delta, batch, heads,
-                          queries, keys))
+                          queries, keys) ||
+        !workspace || workspace_bytes < attention_fp32_backward_fused_workspace_size(batch, heads, queries))
         return cudaErrorInvalidValue;
     const AttentionParams p = backward_params(32, q, k, v, mask, output, lse, upstream, gradient_q, gradient_k, gradient_v,
                                               delta, batch, heads, queries, keys, radius, qs, ks, vs, os, us);
-    // Tensors the tensor maps cannot describe take the two-pass backward (same results up to the
-    // order of dQ's sums).
+    // Tensors the tensor maps cannot describe (or a workspace that is not 128-byte aligned) take
+    // the two-pass backward: the same results up to the order of dQ's sums.
     if (rk::tc::backward_supported(p)) {
-        const int status = rk::tc::launch_fused_backward(p, stream);
+        const int status = rk::tc::launch_fused_backward(p, workspace, stream);
         if (status != rk::tc::kNotEligible) return status;
     }
     return attention_fp32_backward(q, k, v, mask, output, lse, upstream, gradient_q, gradient_k, gradient_v, delta, batch,

@@ -50,10 +50,16 @@ bool backward_supported(const AttentionParams &p);
 // Launches the tensor-core backward for head width 32 or 64: delta and dQ (query-major), then
 // dK and dV (key-major), ordered on `stream`; returns a cudaError_t value or kNotEligible.
 int launch_backward(const AttentionParams &p, int head_width, cudaStream_t stream);
-// Launches the fused single-pass backward for head width 32 (a pre-pass writing delta and zeroing
-// dQ, then one key-major kernel: dK and dV per key row, dQ added per query tile with FP32
-// atomics); returns a cudaError_t value or kNotEligible. Same tensors as launch_backward.
-int launch_fused_backward(const AttentionParams &p, cudaStream_t stream);
+// Workspace bytes of the fused backward for batch * heads heads of `queries` queries: the split
+// scale Q and dO rows (128 bytes per query, queries padded to 64 per head) and one 528-byte record
+// per 64-query tile.
+long long fused_backward_workspace_bytes(long long batch_heads, long long queries);
+// Launches the fused single-pass backward for head width 32 (a column pre-pass writing delta,
+// zeroing dQ and filling the workspace, then one key-major kernel: dK and dV per key row, dQ added
+// per query tile with FP32 atomics); returns a cudaError_t value or kNotEligible (also for a
+// workspace that is not 128-byte aligned). Same tensors as launch_backward; `workspace` holds
+// fused_backward_workspace_bytes bytes.
+int launch_fused_backward(const AttentionParams &p, void *workspace, cudaStream_t stream);
 // Device status word of the backward kernels (as read_device_status).
 unsigned int read_backward_status(bool clear);
 

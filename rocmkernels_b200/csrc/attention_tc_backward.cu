@@ -57,8 +57,15 @@ __device__ long long g_bwd_trace[2][kTraceTiles][kTraceEvents];
     do {                                                                                                         \
         if (blockIdx.x == 0 && (tile_index) < kTraceTiles) g_bwd_trace[kKeyRows][(tile_index)][(event)] = clock64(); \
     } while (0)
+#define RK_FTRACE(tile_index, event)                                                                    \
+    do {                                                                                               \
+        if (blockIdx.x == 0 && (tile_index) < kTraceTiles) g_bwd_trace[0][(tile_index)][(event)] = clock64(); \
+    } while (0)
 #else
 #define RK_BTRACE(tile_index, event) \
+    do {                            \
+    } while (0)
+#define RK_FTRACE(tile_index, event) \
     do {                            \
     } while (0)
 #endif
@@ -850,19 +857,25 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
 // dQ = scale dS K per 64-query tile as a tensor-core product whose A is dS^T from shared memory
 // (MN-major: each key row's 64 query values are one 128-byte row) and whose B is the CTA's K rows
 // read MN-major ([k0 | k1], N = 64). The per-tile dQ rows are added into the gradient with FP32
-// atomics (the summation order over key tiles is not fixed), after a pre-pass that writes delta
-// and zeroes dQ. K and dS enter that product with one exponent for all 128 keys of the CTA
-// (the key-rows pass scales them per key). One CTA per SM (512 TMEM columns): warps 0-7 are two
-// row warpgroups -- warpgroup g handles columns [32 g, 32 g + 32) of every tile and features
-// [16 g, 16 g + 16) of the outputs -- warp 8 the TMA producer, warp 9 the MMA issuer, warps
-// 10-11 the split warps. S and dP are double-buffered so that the next tile's products run while
-// the row warps work on this one.
+// atomics (the summation order over key tiles is not fixed). K and dS enter that product with one
+// exponent for all 128 keys of the CTA (the key-rows pass scales them per key).
+//
+// A column pre-pass runs first, once per 64-query tile: it writes delta, zeroes dQ, and stores in
+// the caller's workspace the tile's operands already split -- scale Q and dO as FP16 rows
+// [x0 | x1] (128 bytes per query, the row layout the key-rows pass builds in its split warps for
+// every key tile again) -- and a record of the tile's column statistics (exponents, softmax
+// offsets, delta). The main kernel TMA-loads those tiles straight into the operand layout (a 128B-
+// swizzled box of 64 FP16 x 64 rows) and has no split warps: one CTA per SM (512 TMEM columns),
+// warps 0-7 two row warpgroups -- warpgroup g handles columns [32 g, 32 g + 32) of every tile and
+// features [16 g, 16 g + 16) of the outputs -- warp 8 the TMA producer, warp 9 the MMA issuer.
+// S and dP are double-buffered so that the next tile's products run while the row warps work on
+// this one. Query tiles are 64-aligned (the window's first tile starts at a multiple of 64; the
+// radius test zeroes the columns outside the window).
 namespace fused {
-constexpr int kThreads = 384;
+constexpr int kThreads = 320;
 constexpr int kRowThreads = 256;
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
-constexpr int kSplitWarp = 10;
 // TMEM columns: S / P and dP / dS of tile parity i at 128 i and 128 i + 64; X1 (dK) and X2 (dV)
 // as [b0 | b1] products; dQ (M = 64: query m at lane (m % 16) + 32 (m / 16)) as [k0 | k1].
 constexpr uint32_t kScores = 0, kX1 = 256, kX2 = 320, kDQ = 384;
@@ -870,28 +883,45 @@ constexpr uint32_t kTmemColumns = 512;
 // dQ: M = 64, N = 64, A and B both MN-major.
 constexpr uint32_t kIdescDQ = f16_instr_desc(64, 64) | (1u << 15) | (1u << 16);
 
+// Column statistics of one 64-query tile, written by the pre-pass.
+struct alignas(16) TileRecord {
+    float col_offset[kCols];  // 14 - max log2e - log2(sum) per query; -inf if it sees no key (or does not exist)
+    float col_delta[kCols];   // delta per visible query, else 0
+    int e1, e2;               // exponents of the tile's scale Q and dO splits
+    float delta_max;          // max |col_delta|
+    int unused;
+};
+constexpr uint32_t kRecordBytes = sizeof(TileRecord);
+static_assert(kRecordBytes % 16 == 0, "bulk copies move multiples of 16 bytes");
+constexpr uint32_t kTileBytes = kCols * 128;  // one split tile: 64 rows x [x0 | x1] FP16
+
+// Workspace carve-up for B*H*Q queries: split Q rows, split dO rows (each padded to 64 queries per
+// (batch, head)), then the tile records. Offsets in bytes, all 16-byte aligned.
+struct Workspace {
+    long long tiles_per_head, rows, q_offset, dout_offset, record_offset, bytes;
+};
+__host__ __device__ inline Workspace workspace_layout(long long batch_heads, long long queries) {
+    Workspace w;
+    w.tiles_per_head = (queries + kCols - 1) / kCols;
+    w.rows = batch_heads * w.tiles_per_head * kCols;
+    w.q_offset = 0;
+    w.dout_offset = w.rows * 128;
+    w.record_offset = 2 * w.rows * 128;
+    w.bytes = w.record_offset + batch_heads * w.tiles_per_head * kRecordBytes;
+    return w;
+}
+
 struct alignas(1024) Storage {
-    using G = Geometry<32>;
-    static constexpr int kStages = 3;
-    float raw1[kStages][G::kRawFloats];      // TMA tile of Q, 128B swizzle
-    float raw2[kStages][G::kRawFloats];      // dO
-    uint32_t b1[kStages][G::kRowWords];      // scale Q rows as split FP16 [q0 | q1] (B of S^T; MN-major B of dK)
-    uint32_t b2[kStages][G::kRowWords];      // dO rows (B of dP^T; MN-major B of dV)
+    static constexpr int kStages = 4;
+    uint32_t b1[kStages][kCols * 32];        // scale Q rows as split FP16 [q0 | q1] (B of S^T; MN-major B of dK), 128B swizzle
+    uint32_t b2[kStages][kCols * 32];        // dO rows (B of dP^T; MN-major B of dV)
     uint32_t a1[kRows * 32];                 // K rows [k0 | k1] (A of S^T; MN-major B of dQ)
     uint32_t a2[kRows * 32];                 // V rows (A of dP^T)
     uint32_t ds[2][2][kRows * 32];           // [tile parity][term]: dS^T rows, 64 FP16 queries per key (A of dQ)
-    alignas(16) float col_offset[kStages][kCols];
-    alignas(16) float col_delta[kStages][kCols];
-    uint32_t col_mask[kStages][2];
-    int e1[kStages], e2[kStages];
-    float col_delta_max[kStages];
-    float split_max[2][2][3];
-    int split_ok[2][2];
+    TileRecord record[kStages];
     float row_max[4][2];                     // per row warp of warpgroup 0: max |K|, max ||V row||_1
-    uint64_t full[kStages];
-    uint64_t raw_free[kStages];
-    uint64_t ready[kStages];
-    uint64_t empty[kStages];
+    uint64_t full[kStages];                  // the stage's tiles and record landed (TMA bytes)
+    uint64_t empty[kStages];                 // MMAs reading the stage finished (commit)
     uint64_t s_full[2];                      // S and dP of the tile parity in TMEM (commit)
     uint64_t p_full;                         // P / dS stored, the previous products folded (256 arrivals)
     uint64_t x_done;                         // dK, dV and dQ products of the tile in TMEM (commit)
@@ -904,6 +934,13 @@ struct alignas(1024) Storage {
 
 constexpr int shared_bytes() { return static_cast<int>(sizeof(Storage)) + 1024; }
 static_assert(shared_bytes() <= 227 * 1024, "fused backward: shared memory");
+
+struct Args {
+    AttentionParams p;
+    int blocks_per_head;  // key tiles per (batch, head)
+    long long tiles_per_head;  // 64-query tiles per (batch, head) in the workspace
+    const TileRecord *records;
+};
 
 // store_split_chunk, also writing the two FP16 terms into the dS^T tiles of key row `row`
 // (queries 16 chunk .. 16 chunk + 15 = 16-byte chunks 2 chunk and 2 chunk + 1, 128B swizzle).
@@ -949,7 +986,7 @@ __device__ __forceinline__ void fold_x_half(float (&acc1)[16], float (&acc2)[16]
 
 // Adds the dQ rows of a finished tile into the gradient: lanes 0-15 of warp w hold queries
 // 16 (w % 4) + lane; warpgroup g adds features [16 g, 16 g + 16). `tile` = the gradient row of the
-// tile's first query, `valid` = queries of the tile inside the window.
+// tile's first query, `valid` = queries of the tile that exist.
 __device__ __forceinline__ void fold_dq(float *tile, int valid, uint32_t lanes, int g, int warp, int lane, float scale) {
     float xa[16], xb[16];
     tmem_load16x2(lanes + kDQ + 16 * g, xa, lanes + kDQ + 32 + 16 * g, xb);
@@ -963,30 +1000,93 @@ __device__ __forceinline__ void fold_dq(float *tile, int valid, uint32_t lanes, 
     }
 }
 
-// delta_i = sum_c dO_ic O_ic and dQ_i = 0 for every query row (eight threads per row, one float4
-// of each).
-__global__ void __launch_bounds__(256) prepass_kernel(const AttentionParams p, long long rows) {
-    const long long t = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-    const long long row = t >> 3;
-    const int part = static_cast<int>(t & 7);
-    float d = 0.f;
-    if (row < rows) {
-        const int q = static_cast<int>(row % p.queries);
-        const long long bh = row / p.queries;
-        const int h = static_cast<int>(bh % p.heads), b = static_cast<int>(bh / p.heads);
-        const float4 u = __ldg(reinterpret_cast<const float4 *>(p.dout.row(b, h, q)) + part);
-        const float4 o = __ldg(reinterpret_cast<const float4 *>(p.o_in.row(b, h, q)) + part);
-        d = fmaf(u.w, o.w, fmaf(u.z, o.z, fmaf(u.y, o.y, u.x * o.x)));
-        reinterpret_cast<float4 *>(p.dq + row * 32)[part] = make_float4(0.f, 0.f, 0.f, 0.f);
+// Column pre-pass: one CTA per 64-query tile of a (batch, head), eight threads per query (four
+// features each). delta_i = sum_c dO_ic O_ic to p.delta, dQ_i = 0, and into the workspace: the
+// tile's scale Q and dO rows split (scaled by 2^e1, 2^e2: the tile maxima brought into
+// [2^14, 2^15)) as FP16 [x0 | x1], and its TileRecord.
+constexpr int kPrepassThreads = kCols * 8;
+__global__ void __launch_bounds__(kPrepassThreads) prepass_kernel(const AttentionParams p, uint8_t *workspace, long long tiles_per_head,
+                                                                  long long record_offset, long long dout_offset) {
+    __shared__ float maxima[kPrepassThreads / 32][3];
+    const long long tile_id = blockIdx.x;
+    const long long bh = tile_id / tiles_per_head;
+    const int tile = static_cast<int>(tile_id % tiles_per_head);
+    const int h = static_cast<int>(bh % p.heads), b = static_cast<int>(bh / p.heads);
+    const int row = threadIdx.x >> 3, part = threadIdx.x & 7;
+    const int query = tile * kCols + row;
+    const bool valid = query < p.queries;
+    const long long query_row = bh * p.queries + query;  // packed [batch][heads][queries] index
+    float4 x = make_float4(0.f, 0.f, 0.f, 0.f), u = x, o = x;
+    if (valid) {
+        x = __ldg(reinterpret_cast<const float4 *>(p.q.row(b, h, query)) + part);
+        u = __ldg(reinterpret_cast<const float4 *>(p.dout.row(b, h, query)) + part);
+        o = __ldg(reinterpret_cast<const float4 *>(p.o_in.row(b, h, query)) + part);
+        x = make_float4(x.x * p.scale, x.y * p.scale, x.z * p.scale, x.w * p.scale);
+        reinterpret_cast<float4 *>(p.dq + query_row * 32)[part] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    d += __shfl_xor_sync(0xffffffffu, d, 1);
-    d += __shfl_xor_sync(0xffffffffu, d, 2);
-    d += __shfl_xor_sync(0xffffffffu, d, 4);
-    if (row < rows && part == 0) p.delta[row] = d;
+    float delta = fmaf(u.w, o.w, fmaf(u.z, o.z, fmaf(u.y, o.y, u.x * o.x)));
+    delta += __shfl_xor_sync(0xffffffffu, delta, 1);
+    delta += __shfl_xor_sync(0xffffffffu, delta, 2);
+    delta += __shfl_xor_sync(0xffffffffu, delta, 4);
+    const float maximum = valid ? p.lse_in[query_row * 2] : -INFINITY;
+    const float total = valid ? p.lse_in[query_row * 2 + 1] : 0.f;
+    const bool visible = valid && maximum != -INFINITY;
+    const float col_offset = visible ? 14.f - maximum * kLog2e - __log2f(total) : -INFINITY;
+    const float col_delta = visible ? delta : 0.f;
+    float m1 = max3(fabsf(x.x), fabsf(x.y), fmaxf(fabsf(x.z), fabsf(x.w)));
+    float m2 = max3(fabsf(u.x), fabsf(u.y), fmaxf(fabsf(u.z), fabsf(u.w)));
+    float m3 = fabsf(col_delta);
+#pragma unroll
+    for (int offset = 16; offset; offset >>= 1) {
+        m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, offset));
+        m2 = fmaxf(m2, __shfl_xor_sync(0xffffffffu, m2, offset));
+        m3 = fmaxf(m3, __shfl_xor_sync(0xffffffffu, m3, offset));
+    }
+    const int warp = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) {
+        maxima[warp][0] = m1;
+        maxima[warp][1] = m2;
+        maxima[warp][2] = m3;
+    }
+    __syncthreads();
+    m1 = m2 = m3 = 0.f;
+#pragma unroll
+    for (int w = 0; w < kPrepassThreads / 32; ++w) {
+        m1 = fmaxf(m1, maxima[w][0]);
+        m2 = fmaxf(m2, maxima[w][1]);
+        m3 = fmaxf(m3, maxima[w][2]);
+    }
+    const int e1 = fp16_scale_exponent(m1), e2 = fp16_scale_exponent(m2);
+    // Split rows: 32 words per query, x0 pairs in words 0-15, x1 pairs in words 16-31; this
+    // thread's features 4 part .. 4 part + 3 are x0 words 2 part, 2 part + 1 and x1 words 16 + 2 part, ....
+    const long long split_row = bh * tiles_per_head * kCols + tile * kCols + row;
+#pragma unroll
+    for (int which = 0; which < 2; ++which) {
+        const float4 v = which == 0 ? x : u;
+        const float scale = exp2_int(which == 0 ? e1 : e2);
+        uint32_t a0, a1, c0, c1;
+        split_pack2<false>(v.x, v.y, scale, a0, a1);
+        split_pack2<false>(v.z, v.w, scale, c0, c1);
+        uint32_t *dst = reinterpret_cast<uint32_t *>(workspace + (which == 0 ? 0 : dout_offset)) + split_row * 32;
+        *reinterpret_cast<uint2 *>(dst + 2 * part) = make_uint2(a0, c0);
+        *reinterpret_cast<uint2 *>(dst + 16 + 2 * part) = make_uint2(a1, c1);
+    }
+    TileRecord *record = reinterpret_cast<TileRecord *>(workspace + record_offset) + tile_id;
+    if (part == 0) {
+        record->col_offset[row] = col_offset;
+        record->col_delta[row] = col_delta;
+        if (valid) p.delta[query_row] = delta;
+    }
+    if (threadIdx.x == 0) {
+        record->e1 = e1;
+        record->e2 = e2;
+        record->delta_max = m3;
+        record->unused = 0;
+    }
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
-        backward_kernel(const BackwardArgs args, const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_dout) {
+        backward_kernel(const Args args, const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_dout) {
     using S = Storage;
     constexpr int kStages = S::kStages;
     extern __shared__ uint8_t shared_raw[];
@@ -994,8 +1094,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     const AttentionParams &p = args.p;
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const TileWindow window = tile_window<kStages>(p, true, args.blocks_per_head);
-    const int h = window.h, b = window.b;
+    int block = blockIdx.x;
+    const int key_tile = block % args.blocks_per_head;
+    block /= args.blocks_per_head;
+    const int h = block % p.heads, b = block / p.heads;
+    const long long bh = static_cast<long long>(b) * p.heads + h;
+    const int r0 = key_tile * kRows;
+    int first, last;  // queries that can see the key tile
+    key_window(r0, min(r0 + kRows, p.keys), p.queries, p.radius, first, last);
+    first &= ~(kCols - 1);
+    const int window_tiles = last > first ? (last - first + kCols - 1) / kCols : 0;
+    const unsigned char *mask = p.mask + static_cast<long long>(b) * p.keys;
 
     if (warp == 0) {
         tmem_alloc(&s.tmem_base, kTmemColumns);
@@ -1004,8 +1113,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == kProducerWarp * 32) {
         for (int i = 0; i < kStages; ++i) {
             mbar_init(&s.full[i], 1);
-            mbar_init(&s.raw_free[i], kSplitThreads);
-            mbar_init(&s.ready[i], kSplitThreads);
             mbar_init(&s.empty[i], 1);
         }
         mbar_init(&s.s_full[0], 1);
@@ -1023,9 +1130,36 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = s.tmem_base;
 
     if (warp == kProducerWarp) {
-        producer_role<32, true>(s, window, tmap_q, tmap_dout, lane);
-    } else if (warp >= kSplitWarp) {
-        split_role<32, true>(s, p, window, warp - kSplitWarp, lane);
+        // ---------------------------------------------------------------- TMA producer
+        // Tiles of the window, none when every key of the tile is masked (dK = dV = 0).
+        bool visible = false;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int key = r0 + 4 * lane + e;
+            visible = visible || (key < p.keys && mask[key] != 0);
+        }
+        const int tiles = __any_sync(0xffffffffu, visible) ? window_tiles : 0;
+        if (lane == 0) {
+            s.tile_count = tiles;
+            mbar_arrive(&s.range_ready);
+            const int row_base = static_cast<int>(bh * args.tiles_per_head * kCols) + first;
+            const TileRecord *records = args.records + bh * args.tiles_per_head + first / kCols;
+            bool ok = true;
+            int issued = 0;
+            for (int j = 0; j < tiles; ++j) {
+                const int stage = j % kStages;
+                if (j >= kStages && !(ok = mbar_wait(&s.empty[stage], ((j / kStages) - 1) & 1))) break;
+                RK_FTRACE(j, 0);
+                mbar_arrive_expect_tx(&s.full[stage], 2 * kTileBytes + kRecordBytes);
+                tma_load_2d(s.b1[stage], &tmap_q, &s.full[stage], 0, row_base + j * kCols);
+                tma_load_2d(s.b2[stage], &tmap_dout, &s.full[stage], 0, row_base + j * kCols);
+                bulk_load(&s.record[stage], records + j, kRecordBytes, &s.full[stage]);
+                ++issued;
+            }
+            // Every load issued lands before the CTA exits (a failed wait above ends the loop early).
+            if (!ok)
+                for (int j = max(0, issued - kStages); j < issued; ++j) mbar_wait(&s.full[j % kStages], (j / kStages) & 1);
+        }
     } else if (warp == kMmaWarp) {
         // ---------------------------------------------------------------- MMA issuer
         // Per tile j: S(j + 1) and dP(j + 1) go out before waiting for P(j) / dS(j); then dK, dV
@@ -1045,11 +1179,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t k_mn_desc = sw128_mn_descriptor(smem_u32(s.a1), G::kMnChunkBytes);
             const auto issue_scores = [&](int j) -> bool {
                 const int stage = j % kStages;
-                if (!mbar_wait_warp(&s.ready[stage], (j / kStages) & 1)) return false;
+                if (!mbar_wait_warp(&s.full[stage], (j / kStages) & 1)) return false;
                 tc_fence_after();
                 const uint32_t scores = tmem + kScores + 128 * (j & 1);
                 issue_product_smem<32>(scores, k_desc, b1_desc + row_stage * stage, nullptr);
                 issue_product_smem<32>(scores + 64, v_desc, b2_desc + row_stage * stage, &s.s_full[j & 1]);
+                if (lane == 0) RK_FTRACE(j, 4);
                 return true;
             };
             bool ok = mbar_wait_warp(&s.rows_ready, 0) && issue_scores(0);
@@ -1060,6 +1195,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 ok = mbar_wait_warp(&s.p_full, j & 1);
+                if (lane == 0) RK_FTRACE(j, 5);
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t scores = tmem + kScores + 128 * (j & 1);
@@ -1079,17 +1215,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 mma_commit_warp(&s.x_done);
                 mma_commit_warp(&s.empty[stage]);
+                if (lane == 0) RK_FTRACE(j, 12);
             }
             mma_commit_warp(&s.mma_done);
             mbar_wait_warp(&s.mma_done, 0);
         }
     } else {
         // ---------------------------------------------------------------- row warps
-        const int g = warp >> 2;               // warpgroup: column half of each tile, feature half of the outputs
+        const int g = warp >> 2;                  // warpgroup: column half of each tile, feature half of the outputs
         const int r = threadIdx.x & (kRows - 1);  // key row within the tile = TMEM lane
-        const int row = window.r0 + r;
+        const int row = r0 + r;
         const bool row_valid = row < p.keys;
-        const bool row_active = row_valid && window.mask[row] != 0;
+        const bool row_active = row_valid && mask[row] != 0;
         const uint32_t lanes = lane_address(tmem, warp);
         float l1_max;  // max over the CTA's keys of ||v_j||_1
         int ea1, ea2;  // exponents of K (one for the CTA) and of this key's V row
@@ -1128,22 +1265,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         int pending_c0 = 0;
         bool ok = true;
         const int tiles = __shfl_sync(0xffffffffu, visited_tiles(s), 0);
+        float *dq_head = p.dq + bh * p.queries * 32;
         for (int j = 0; j < tiles && ok; ++j) {
             const int stage = j % kStages;
             const uint32_t scores = lanes + kScores + 128 * (j & 1);
-            ok = __all_sync(0xffffffffu, mbar_wait(&s.s_full[j & 1], (j >> 1) & 1) && mbar_wait(&s.ready[stage], (j / kStages) & 1));
+            ok = __all_sync(0xffffffffu, mbar_wait(&s.s_full[j & 1], (j >> 1) & 1) && mbar_wait(&s.full[stage], (j / kStages) & 1));
+            if (lane == 0 && (warp & 3) == 0) RK_FTRACE(j, warp == 0 ? 6 : 9);
             if (!ok) break;
             tc_fence_after();
-            const int c0 = window.first + j * kCols;
-            const int e1 = s.e1[stage], e2 = s.e2[stage];
+            const TileRecord &rec = s.record[stage];
+            const int c0 = first + j * kCols;
+            const int e1 = rec.e1, e2 = rec.e2;
             const float slope = kLog2e * exp2_int(-(ea1 + e1));  // TMEM S -> log2e * score
             const float dp_scale = exp2_int(-(ea2 + e2));        // TMEM dP -> dP
             // One dS exponent for the CTA: |dS| <= max_j ||v_j||_1 max|dO| + max|delta| (P <= 1)
-            const int gs = fp16_scale_exponent(l1_max * exp2_int(15 - e2) + s.col_delta_max[stage]);
+            const int gs = fp16_scale_exponent(l1_max * exp2_int(15 - e2) + rec.delta_max);
             const float to_ds = exp2_int(gs - 14);  // P' (= 2^14 P) * (dP - delta) * to_ds = 2^gs dS
             const float w_scale = dp_scale * to_ds;
-            uint64_t active = row_active ? (static_cast<uint64_t>(s.col_mask[stage][0]) | (static_cast<uint64_t>(s.col_mask[stage][1]) << 32))
-                                         : 0ull;
+            // Columns of queries that see no key have offset -inf (P = 0); the mask and the radius
+            // window are applied here.
+            uint64_t active = row_active ? ~0ull : 0ull;
             if (p.radius >= 0) {
                 const int lo_col = max(0, row - p.radius - c0), hi_col = min(kCols - 1, row + p.radius - c0);
                 active &= lo_col > hi_col ? 0ull : ((~0ull) >> (63 - (hi_col - lo_col))) << lo_col;
@@ -1155,8 +1296,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float sv[16], dv[16];  // scores, then P'; dP, then dS'
                 tmem_load16x2(scores + 16 * chunk, sv, scores + 64 + 16 * chunk, dv);
                 float col_offset[16], col_delta[16];
-                const float4 *o4 = reinterpret_cast<const float4 *>(&s.col_offset[stage][16 * chunk]);
-                const float4 *d4 = reinterpret_cast<const float4 *>(&s.col_delta[stage][16 * chunk]);
+                const float4 *o4 = reinterpret_cast<const float4 *>(&rec.col_offset[16 * chunk]);
+                const float4 *d4 = reinterpret_cast<const float4 *>(&rec.col_delta[16 * chunk]);
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     const float4 o = o4[i], d = d4[i];
@@ -1185,22 +1326,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                 store_split_chunk_dual(scores + 64 + 16 * chunk, dv, s.ds[j & 1][0], s.ds[j & 1][1], r, chunk);
                 store_split_chunk(scores + 16 * chunk, sv);
             }
+            if (lane == 0 && warp == 0) RK_FTRACE(j, 11);
             // Fold the previous tile's products before the P(j)/dS(j) arrival lets the MMA warp
             // overwrite them.
             if (j > 0) {
                 ok = __all_sync(0xffffffffu, mbar_wait(&s.x_done, (j - 1) & 1));
+                if (lane == 0 && warp == 0) RK_FTRACE(j, 13);
                 if (!ok) {
                     tmem_wait_store();
                     break;
                 }
                 tc_fence_after();
                 fold_x_half(acc1, acc2, lanes, g, pending1, pending2);
-                fold_dq(p.dq + (window.query_base + pending_c0) * 32, window.last - pending_c0, lanes, g, warp, lane, pending_dq);
+                fold_dq(dq_head + pending_c0 * 32, p.queries - pending_c0, lanes, g, warp, lane, pending_dq);
             }
+            if (lane == 0 && warp == 0) RK_FTRACE(j, 8);
             tmem_wait_store();
             fence_proxy_async_shared();  // the dS^T stores, visible to the dQ MMAs
             tc_fence_before();
             mbar_arrive(&s.p_full);
+            if (lane == 0 && (warp & 3) == 0) RK_FTRACE(j, warp == 0 ? 7 : 10);
             // dK = 2^-(gs + e1) X1; dV = 2^-(14 + e2) X2; dQ = scale 2^-(gs + ea1) (dS' . K')
             pending1 = exp2_int(-(gs + e1));
             pending2 = exp2_int(-(14 + e2));
@@ -1212,13 +1357,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             if (ok) {
                 fold_x_half(acc1, acc2, lanes, g, pending1, pending2);
-                fold_dq(p.dq + (window.query_base + pending_c0) * 32, window.last - pending_c0, lanes, g, warp, lane, pending_dq);
+                fold_dq(dq_head + pending_c0 * 32, p.queries - pending_c0, lanes, g, warp, lane, pending_dq);
             }
         }
         // dK, dV (packed [batch][heads][keys][32]), features [16 g, 16 g + 16); a failed wait leaves NaN.
         if (row_valid) {
             const float bad = ok ? 1.f : NAN;
-            const long long key_row = (static_cast<long long>(b) * p.heads + h) * p.keys + row;
+            const long long key_row = bh * p.keys + row;
             float4 *dk = reinterpret_cast<float4 *>(p.dk + key_row * 32 + 16 * g);
             float4 *dv = reinterpret_cast<float4 *>(p.dv + key_row * 32 + 16 * g);
 #pragma unroll
@@ -1314,21 +1459,39 @@ int launch_both(const AttentionParams &p, cudaStream_t stream) {
     return launch_pass<D, true>(p, map_q, map_dout, stream);  // dK, dV (reads delta)
 }
 
-// The fused backward: the delta / dQ-zeroing pre-pass, then the key-major pass, ordered on `stream`.
-int launch_fused(const AttentionParams &p, cudaStream_t stream) {
+// 2-D FP16 map of the workspace's split rows: 64 halves (128 bytes) per row, box 64 x 64 rows,
+// 128B swizzle (the row layout the MMAs read).
+bool make_split_map(CUtensorMap *map, void *base, long long rows) {
+    auto encode = encode_function();
+    if (encode == nullptr) return false;
+    const cuuint64_t dims[2] = {64, static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {128};
+    const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(kCols)};
+    const cuuint32_t element_strides[2] = {1, 1};
+    return encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, dims, strides, box, element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The fused backward: the column pre-pass, then the key-major pass, ordered on `stream`.
+int launch_fused(const AttentionParams &p, void *workspace, cudaStream_t stream) {
+    const fused::Workspace w = fused::workspace_layout(static_cast<long long>(p.batch) * p.heads, p.queries);
+    if (w.rows >= (1ll << 31)) return kNotEligible;  // TMA row coordinates are 32-bit
+    uint8_t *base = static_cast<uint8_t *>(workspace);
     CUtensorMap map_q, map_dout;
-    if (!make_tensor_map(&map_q, p.q, 32, p.batch, p.heads, p.queries) ||
-        !make_tensor_map(&map_dout, p.dout, 32, p.batch, p.heads, p.queries))
+    if (!make_split_map(&map_q, base + w.q_offset, w.rows) || !make_split_map(&map_dout, base + w.dout_offset, w.rows))
         return kNotEligible;
     cudaError_t status = prepare_kernel<fused::backward_kernel>(fused::shared_bytes());
     if (status != cudaSuccess) return status;
-    const long long rows = static_cast<long long>(p.batch) * p.heads * p.queries;
-    fused::prepass_kernel<<<static_cast<unsigned>((rows * 8 + 255) / 256), 256, 0, stream>>>(p, rows);
+    const long long tiles = static_cast<long long>(p.batch) * p.heads * w.tiles_per_head;
+    fused::prepass_kernel<<<static_cast<unsigned>(tiles), fused::kPrepassThreads, 0, stream>>>(p, base, w.tiles_per_head, w.record_offset,
+                                                                                               w.dout_offset);
     status = cudaGetLastError();
     if (status != cudaSuccess) return status;
-    BackwardArgs args{};
+    fused::Args args{};
     args.p = p;
     args.blocks_per_head = (p.keys + kRows - 1) / kRows;
+    args.tiles_per_head = w.tiles_per_head;
+    args.records = reinterpret_cast<const fused::TileRecord *>(base + w.record_offset);
     const unsigned blocks = static_cast<unsigned>(args.blocks_per_head) * static_cast<unsigned>(p.heads) * static_cast<unsigned>(p.batch);
     fused::backward_kernel<<<blocks, fused::kThreads, fused::shared_bytes(), stream>>>(args, map_q, map_dout);
     return cudaGetLastError();
@@ -1348,7 +1511,14 @@ int launch_backward(const AttentionParams &p, int head_width, cudaStream_t strea
     return kNotEligible;
 }
 
-int launch_fused_backward(const AttentionParams &p, cudaStream_t stream) { return launch_fused(p, stream); }
+long long fused_backward_workspace_bytes(long long batch_heads, long long queries) {
+    return fused::workspace_layout(batch_heads, queries).bytes;
+}
+
+int launch_fused_backward(const AttentionParams &p, void *workspace, cudaStream_t stream) {
+    if ((reinterpret_cast<uintptr_t>(workspace) & 127u) != 0) return kNotEligible;
+    return launch_fused(p, workspace, stream);
+}
 
 #ifdef RK_TC_TRACE
 extern "C" __attribute__((visibility("default"))) int rocmkernels_attention_backward_trace(long long *out, int capacity) {

@@ -115,16 +115,25 @@ def run_forward(entry, tensors: dict, plan: list[ShardCall], *, heads: int, quer
 
 
 def run_backward(entry, tensors: dict, plan: list[ShardCall], *, heads: int, queries: int, keys: int, width: int, radius: int,
-                 strides: dict, stream=None) -> int:
+                 strides: dict, stream=None, workspace=None) -> int:
     """One rank's backward calls (argument order of attention_fp32_backward); `tensors` holds the
-    full problem's q, k, v, mask, out, lse, upstream, grad_q, grad_k, grad_v, delta."""
+    full problem's q, k, v, mask, out, lse, upstream, grad_q, grad_k, grad_v, delta. `workspace`
+    (attention_fp32_backward_fused: a device buffer sized for the largest call of the plan, see
+    workspace_bytes) is passed to every call, which are ordered on `stream`."""
+    extra = {} if workspace is None else {"workspace": workspace}
     for call in plan:
         offsets = shard_offsets(call, heads=heads, queries=queries, keys=keys, width=width,
                                 strides={r: strides[r] for r in STRIDED})
         p = _shifted(tensors, offsets, {"mask": 1})
         status = entry(p["q"], p["k"], p["v"], p["mask"], p["out"], p["lse"], p["upstream"], p["grad_q"], p["grad_k"],
                        p["grad_v"], p["delta"], call.batch, call.heads, queries, keys, radius, strides["q"], strides["k"],
-                       strides["v"], strides["out"], strides["upstream"], stream)
+                       strides["v"], strides["out"], strides["upstream"], stream, **extra)
         if status != 0:
             return status
     return 0
+
+
+def workspace_bytes(size_of, plan: list[ShardCall], queries: int) -> int:
+    """Workspace for run_backward with the fused backward: `size_of(batch, heads, queries)` (e.g.
+    attention_fp32_backward_fused_workspace_size) of the plan's largest call."""
+    return max((size_of(call.batch, call.heads, queries) for call in plan), default=0)

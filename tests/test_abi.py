@@ -208,3 +208,24 @@ def test_static_delta_row_limit_boundary():
     for (batch, heads, queries) in [(2, 16, 131073), (1, 1, limit + 1), (4097, 1024, 1)]:
         status = api.attention_fp32_backward_static_delta(1, 1, 1, 1, 1, 1, 1, 1, 1, 1, batch, heads, queries, 64, -1, S, S, S, S, S)
         assert status == api.INVALID_VALUE, (batch, heads, queries, status)
+
+
+def test_fused_backward_workspace_size():
+    """256 bytes per query (queries padded to 64 per (batch, head)) plus a 528-byte record per
+    64 queries; 0 for non-positive sizes."""
+    size = api.attention_fp32_backward_fused_workspace_size
+    for batch, heads, queries in [(1, 1, 1), (2, 3, 64), (2, 3, 65), (64, 12, 4096), (1, 1, 1000)]:
+        tiles = batch * heads * ((queries + 63) // 64)
+        assert size(batch, heads, queries) == tiles * (64 * 256 + 528)
+    assert size(0, 1, 1) == 0 and size(1, -1, 1) == 0 and size(1, 1, 0) == 0
+
+
+@pytest.mark.parametrize("null_index", range(12))
+def test_fused_backward_rejects_null_pointers_and_small_workspace(null_index):
+    pointers = [1] * 12  # q, k, v, mask, output, lse, upstream, gradients, delta, workspace
+    pointers[null_index] = None
+    lib = api.lib()
+    needed = api.attention_fp32_backward_fused_workspace_size(1, 1, 4)
+    assert lib.attention_fp32_backward_fused(*pointers, needed, 1, 1, 4, 4, -1, S, S, S, S, S, None) == api.INVALID_VALUE
+    # a workspace smaller than the size query asks for: error 1 before any CUDA call
+    assert lib.attention_fp32_backward_fused(*[1] * 12, needed - 1, 1, 1, 4, 4, -1, S, S, S, S, S, None) == api.INVALID_VALUE
