@@ -872,10 +872,11 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
 // this one. Query tiles are 64-aligned (the window's first tile starts at a multiple of 64; the
 // radius test zeroes the columns outside the window).
 namespace fused {
-constexpr int kThreads = 320;
+constexpr int kThreads = 352;
 constexpr int kRowThreads = 256;
 constexpr int kProducerWarp = 8;
-constexpr int kMmaWarp = 9;
+constexpr int kMmaWarp = 9;    // S, dP, dK and dV products
+constexpr int kDqWarp = 10;    // dQ products (a second issuing warp, on another sub-partition)
 // TMEM columns: S / P and dP / dS of tile parity i at 128 i and 128 i + 64; X1 (dK) and X2 (dV)
 // as [b0 | b1] products; dQ (M = 64: query m at lane (m % 16) + 32 (m / 16)) as [k0 | k1].
 constexpr uint32_t kScores = 0, kX1 = 256, kX2 = 320, kDQ = 384;
@@ -924,9 +925,10 @@ struct alignas(1024) Storage {
     uint64_t empty[kStages];                 // MMAs reading the stage finished (commit)
     uint64_t s_full[2];                      // S and dP of the tile parity in TMEM (commit)
     uint64_t p_full;                         // P / dS stored, the previous products folded (256 arrivals)
-    uint64_t x_done;                         // dK, dV and dQ products of the tile in TMEM (commit)
+    uint64_t x_done;                         // dK, dV and dQ products of the tile in TMEM (two commits)
     uint64_t rows_ready;                     // K and V rows stored (256 arrivals)
     uint64_t mma_done;
+    uint64_t dq_done;
     uint64_t range_ready;
     uint32_t tmem_base;
     int tile_count;
@@ -1118,10 +1120,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(&s.s_full[0], 1);
         mbar_init(&s.s_full[1], 1);
         mbar_init(&s.p_full, kRowThreads);
-        mbar_init(&s.x_done, 1);
+        mbar_init(&s.x_done, 2);
         mbar_init(&s.rows_ready, kRowThreads);
         mbar_init(&s.range_ready, 1);
         mbar_init(&s.mma_done, 1);
+        mbar_init(&s.dq_done, 1);
         mbar_fence_init();
     }
     tc_fence_before();
@@ -1162,21 +1165,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp == kMmaWarp) {
         // ---------------------------------------------------------------- MMA issuer
-        // Per tile j: S(j + 1) and dP(j + 1) go out before waiting for P(j) / dS(j); then dK, dV
-        // and dQ of tile j. The MMAs run in issue order, so S(j + 2) overwrites the buffers of
-        // tile j only after the products that read them.
+        // Per tile j: S(j + 1) and dP(j + 1) go out before waiting for P(j) / dS(j); then dK and
+        // dV of tile j. The MMAs of one thread run in issue order, so S(j + 2) overwrites the
+        // buffers of tile j only after the products that read them.
         const int tiles = __shfl_sync(0xffffffffu, visited_tiles(s), 0);
         if (tiles > 0) {
             using G = Geometry<32>;
             constexpr uint64_t row_stage = G::kRowWords * 4 / 16;
-            constexpr uint64_t k_step = 2048 / 16;  // 16 K rows of an MN-major operand
             const uint64_t b1_desc = sw128_descriptor(smem_u32(s.b1[0]));
             const uint64_t b2_desc = sw128_descriptor(smem_u32(s.b2[0]));
             const uint64_t b1_mn_desc = sw128_mn_descriptor(smem_u32(s.b1[0]), G::kMnChunkBytes);
             const uint64_t b2_mn_desc = sw128_mn_descriptor(smem_u32(s.b2[0]), G::kMnChunkBytes);
             const uint64_t k_desc = sw128_descriptor(smem_u32(s.a1));
             const uint64_t v_desc = sw128_descriptor(smem_u32(s.a2));
-            const uint64_t k_mn_desc = sw128_mn_descriptor(smem_u32(s.a1), G::kMnChunkBytes);
             const auto issue_scores = [&](int j) -> bool {
                 const int stage = j % kStages;
                 if (!mbar_wait_warp(&s.full[stage], (j / kStages) & 1)) return false;
@@ -1194,16 +1195,37 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ok = false;
                     break;
                 }
-                ok = mbar_wait_warp(&s.p_full, j & 1);
+                ok = __all_sync(0xffffffffu, mbar_wait_sleep(&s.p_full, j & 1));
                 if (lane == 0) RK_FTRACE(j, 5);
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t scores = tmem + kScores + 128 * (j & 1);
                 issue_x<32>(tmem + kX1, scores + 64, b1_mn_desc + row_stage * stage, nullptr);
                 issue_x<32>(tmem + kX2, scores, b2_mn_desc + row_stage * stage, nullptr);
+                mma_commit_warp(&s.x_done);
+                mma_commit_warp(&s.empty[stage]);
+                if (lane == 0) RK_FTRACE(j, 12);
+            }
+            mma_commit_warp(&s.mma_done);
+            mbar_wait_warp(&s.mma_done, 0);
+        }
+    } else if (warp == kDqWarp) {
+        // ---------------------------------------------------------------- dQ issuer
+        // dQ(j) = dS^T(j) . K once P(j) / dS(j) are stored (it reads only shared memory and
+        // writes only its own accumulator, whose previous tile the row warps folded before that
+        // arrival); its commit is the second arrival on x_done.
+        const int tiles = __shfl_sync(0xffffffffu, visited_tiles(s), 0);
+        if (tiles > 0) {
+            constexpr uint64_t k_step = 2048 / 16;  // 16 K rows of an MN-major operand
+            const uint64_t k_mn_desc = sw128_mn_descriptor(smem_u32(s.a1), Geometry<32>::kMnChunkBytes);
+            bool ok = true;
+            for (int j = 0; j < tiles && ok; ++j) {
+                ok = __all_sync(0xffffffffu, mbar_wait_sleep(&s.p_full, j & 1));
+                if (!ok) break;
+                tc_fence_after();
 #pragma unroll
                 for (int term = 0; term < 2; ++term) {
-                    const uint64_t ds_desc = sw128_mn_descriptor(smem_u32(s.ds[j & 1][term]), G::kMnChunkBytes);
+                    const uint64_t ds_desc = sw128_mn_descriptor(smem_u32(s.ds[j & 1][term]), Geometry<32>::kMnChunkBytes);
 #pragma unroll
                     for (int half = 0; half < 2; ++half) {
                         const uint64_t a[4] = {ds_desc + (4 * half) * k_step, ds_desc + (4 * half + 1) * k_step,
@@ -1214,11 +1236,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
                 mma_commit_warp(&s.x_done);
-                mma_commit_warp(&s.empty[stage]);
-                if (lane == 0) RK_FTRACE(j, 12);
             }
-            mma_commit_warp(&s.mma_done);
-            mbar_wait_warp(&s.mma_done, 0);
+            mma_commit_warp(&s.dq_done);
+            mbar_wait_warp(&s.dq_done, 0);
         }
     } else {
         // ---------------------------------------------------------------- row warps
@@ -1345,7 +1365,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             fence_proxy_async_shared();  // the dS^T stores, visible to the dQ MMAs
             tc_fence_before();
             mbar_arrive(&s.p_full);
-            if (lane == 0 && (warp & 3) == 0) RK_FTRACE(j, warp == 0 ? 7 : 10);
+            if (lane == 0) RK_FTRACE(j, warp == 0 ? 7 : warp == 4 ? 10 : warp < 4 ? warp : warp == 7 ? 3 : warp + 9);
             // dK = 2^-(gs + e1) X1; dV = 2^-(14 + e2) X2; dQ = scale 2^-(gs + ea1) (dS' . K')
             pending1 = exp2_int(-(gs + e1));
             pending2 = exp2_int(-(14 + e2));

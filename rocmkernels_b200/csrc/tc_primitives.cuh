@@ -59,6 +59,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return done != 0;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete is suspended until it
+// completes or `hint_ns` elapse, instead of returning after the default, short interval.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t done;
+    asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+            : "memory");
+    return done != 0;
+}
+
 // Non-blocking test of the phase with the given parity (never suspends the thread; for polling
 // several barriers from one thread).
 __device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
@@ -79,6 +93,20 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long start = clock64();
     while (!mbar_try_wait(bar, parity)) {
+        if (clock64() - start > kWaitTimeoutCycles) {
+            atomicOr(&g_device_status, kStatusWaitTimeout);
+            return false;
+        }
+    }
+    return true;
+}
+
+// mbar_wait for a warp that waits long and shares its sub-partition with busy warps: the polls
+// suspend (up to 20 us each, woken by the phase's completion) instead of spinning, so they take
+// no issue slots from the other warps. Same bound and status word as mbar_wait.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity) {
+    const long long start = clock64();
+    while (!mbar_try_wait_sleep(bar, parity, 20000u)) {
         if (clock64() - start > kWaitTimeoutCycles) {
             atomicOr(&g_device_status, kStatusWaitTimeout);
             return false;
