@@ -4,7 +4,10 @@ use, README.md:67-81, bound through ctypes like tools/TorchCompare/compare_ops.p
 ``attention(q, k, v, mask=None, radius=-1, cos=None, sin=None)`` returns softmax(Q K^T / sqrt(D),
 masked) V for float32 CUDA tensors shaped [batch, heads, tokens, D] (D = 32 or 64, feature
 stride 1, any other strides) and differentiates with respect to q, k and v through the
-library's backward. With rotary tables cos/sin ([batch, tokens, 32], D = 32) q and k are rotated
+library's backward: for D = 32 the fused single-pass backward (attention_fp32_backward_fused, dQ
+summed with atomics), or the deterministic two-pass attention_fp32_backward when
+torch.are_deterministic_algorithms_enabled(); for D = 64 attention64_fp32_backward. With rotary
+tables cos/sin ([batch, tokens, 32], D = 32) q and k are rotated
 first (rotary_fp32's forward, Positional/Rotary.hip) inside the fused flash forward; the backward
 rebuilds the rotated q and k with rotary_fp32, runs the attention backward on them and applies
 the transposed rotation (rotary_fp32 with backward = 1) to their gradients. The calls run on
@@ -53,8 +56,9 @@ def _rotate(x: torch.Tensor, cos, sin, backward: bool) -> torch.Tensor:
 
 class AttentionFunction(torch.autograd.Function):
     """Forward: the flash entry (D = 32; with rotary tables the fused rotary flash entry) or
-    attention64_fp32_forward (D = 64); backward: the matching backward entry, recomputing P from
-    the saved {max, sum}."""
+    attention64_fp32_forward (D = 64); backward: the fused single-pass backward (D = 32; the
+    two-pass one under torch's deterministic mode) or attention64_fp32_backward, recomputing P
+    from the saved {max, sum}."""
 
     @staticmethod
     def forward(ctx, q, k, v, mask, radius, cos=None, sin=None):
@@ -96,9 +100,15 @@ class AttentionFunction(torch.autograd.Function):
         grad_v = torch.empty(batch, heads, keys, width, device=q.device, dtype=torch.float32)
         delta = torch.empty(batch, heads, queries, device=q.device, dtype=torch.float32)
         stream = torch.cuda.current_stream(q.device)
-        backward(q, k, v, mask, out, lse, grad_out, grad_q, grad_k, grad_v, delta, batch, heads, queries, keys, ctx.radius,
-                 api.strides_of(q), api.strides_of(k), api.strides_of(v), api.strides_of(out), api.strides_of(grad_out),
-                 stream)
+        strides = (api.strides_of(q), api.strides_of(k), api.strides_of(v), api.strides_of(out), api.strides_of(grad_out))
+        if width == 32 and not torch.are_deterministic_algorithms_enabled():
+            status = api.attention_fp32_backward_fused(q, k, v, mask, out, lse, grad_out, grad_q, grad_k, grad_v, delta, batch,
+                                                       heads, queries, keys, ctx.radius, *strides, stream)
+            if status != 0:
+                raise api.HipError(status, "attention_fp32_backward_fused")
+        else:
+            backward(q, k, v, mask, out, lse, grad_out, grad_q, grad_k, grad_v, delta, batch, heads, queries, keys, ctx.radius,
+                     *strides, stream)
         if rotary:
             grad_q, grad_k = _rotate(grad_q, cos, sin, True), _rotate(grad_k, cos, sin, True)
         return grad_q, grad_k, grad_v, None, None, None, None

@@ -67,3 +67,35 @@ def test_autograd_matches_torch(cuda, case):
     for name, got, want in zip("qkv", grads, (q64.grad, k64.grad, v64.grad)):
         assert np.isfinite(got).all(), name
         assert normwise(got, want.cpu().numpy()) <= GRADIENT_TOL, name
+
+
+def test_deterministic_mode_takes_the_two_pass_backward(cuda):
+    """Under torch.use_deterministic_algorithms(True) the D = 32 backward is the two-pass
+    attention_fp32_backward: q.grad is bitwise repeatable; by default it is the fused backward,
+    whose gradients agree with it within the bars."""
+    import torch
+
+    from rocmkernels_b200.autograd import attention
+
+    generator = torch.Generator(device=cuda)
+    generator.manual_seed(77)
+    q, k, v = (torch.randn(2, 4, 700, 32, device=cuda, generator=generator) for _ in range(3))
+    mask = torch.ones(2, 700, dtype=torch.uint8, device=cuda)
+    weights = torch.randn(2, 4, 700, 32, device=cuda, generator=generator)
+
+    def grads():
+        leaves = [t.detach().clone().requires_grad_() for t in (q, k, v)]
+        (attention(*leaves, mask) * weights).sum().backward()
+        return [t.grad.cpu().numpy() for t in leaves]
+
+    previous = torch.are_deterministic_algorithms_enabled()
+    torch.use_deterministic_algorithms(True)
+    try:
+        first, second = grads(), grads()
+    finally:
+        torch.use_deterministic_algorithms(previous)
+    for a, b in zip(first, second):
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    fused = grads()
+    for a, b in zip(fused, first):
+        assert normwise(a, b) <= GRADIENT_TOL
