@@ -97,3 +97,38 @@ def test_fused_backward_strided_and_padded_layouts(dev):
         status, grads = dev.backward(FUSED, q, k, v, mask, upstream, out, lse, radius, layout=layout)
         assert status == 0
         assert_gradients_close(grads, expected, f"fused {layout}")
+
+
+def test_fused_backward_workspace_reuse_and_unaligned_fallback(dev):
+    """One workspace serves calls of different sizes ordered on one stream; a workspace that is not
+    128-byte aligned takes the two-pass path, whose results equal attention_fp32_backward's bit
+    for bit."""
+    import torch
+
+    import rocmkernels_b200.attention as api
+
+    big = api.attention_fp32_backward_fused_workspace_size(2, 3, 900)
+    storage = torch.empty(big + 256, dtype=torch.uint8, device=dev.device)
+    for (B, H, Q, K) in [(2, 3, 900, 700), (1, 2, 130, 260), (2, 3, 900, 700)]:
+        q, k, v, upstream, mask = make_inputs(B, H, Q, K, 32, seed=951 + Q + K, dist="normal", mask_fraction=0.1)
+        expected = oracle.attention(q, k, v, mask, upstream, -1, threads=oracle.cpu_count())
+        status, out, lse = dev.forward("attention_fp32_forward_flash", q, k, v, mask)
+        assert status == 0
+        t = [dev.put(x) for x in (q, k, v, out, upstream)]
+        dmask, dlse = dev.put(mask), dev.put(lse)
+        grads = [torch.full((B, H, n, 32), float("nan"), device=dev.device) for n in (Q, K, K)]
+        delta = torch.full((B, H, Q), float("nan"), device=dev.device)
+        st = [api.strides_of(x) for x in t]
+        assert api.attention_fp32_backward_fused(*t[:3], dmask, t[3], dlse, t[4], *grads, delta, B, H, Q, K, -1, *st,
+                                                 workspace=storage[:big]) == 0
+        torch.cuda.synchronize()
+        got = {n: dev.get(x) for n, x in zip(("grad_q", "grad_k", "grad_v"), grads)}
+        assert_gradients_close(got, expected, f"reused workspace B{B} Q{Q} K{K}")
+    # unaligned (the last call's problem again): the two-pass path
+    status, two_pass = dev.backward("attention_fp32_backward", q, k, v, mask, upstream, out, lse)
+    assert status == 0
+    assert api.attention_fp32_backward_fused(*t[:3], dmask, t[3], dlse, t[4], *grads, delta, B, H, Q, K, -1, *st,
+                                             workspace=storage[16:16 + big]) == 0
+    torch.cuda.synchronize()
+    for name, x in zip(("grad_q", "grad_k", "grad_v"), grads):
+        assert np.array_equal(dev.get(x).view(np.uint32), two_pass[name].view(np.uint32)), name
