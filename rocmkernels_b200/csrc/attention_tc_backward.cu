@@ -967,38 +967,36 @@ __device__ __forceinline__ void store_split_chunk_dual(uint32_t column, const fl
     t1[(2 * chunk + 1) ^ swizzle] = make_uint4(q1[4], q1[5], q1[6], q1[7]);
 }
 
-// acc1 += X1 * scale1, acc2 += X2 * scale2 for features [16 g, 16 g + 16) (warpgroup g).
-__device__ __forceinline__ void fold_x_half(float (&acc1)[16], float (&acc2)[16], uint32_t lanes, int g, float scale1, float scale2) {
+// Folds a finished tile's products, the six 16-column blocks in one TMEM round trip: acc1 += X1 *
+// scale1 and acc2 += X2 * scale2 for features [16 g, 16 g + 16) (warpgroup g), and that feature
+// half of the tile's dQ rows added into the gradient (lanes 0-15 of warp w hold queries
+// 16 (w % 4) + lane). `tile` = the gradient row of the tile's first query, `valid` = queries of
+// the tile that exist.
+__device__ __forceinline__ void fold_all(float (&acc1)[16], float (&acc2)[16], uint32_t lanes, int g, float scale1, float scale2,
+                                         float *tile, int valid, int warp, int lane, float dq_scale) {
+    float v[6][16];
+    const uint32_t x = lanes + kX1 + 16 * g, y = lanes + kX2 + 16 * g, z = lanes + kDQ + 16 * g;
+    const uint32_t at[6] = {x, x + 32, y, y + 32, z, z + 32};
+    tmem_load16x6(at, v);
 #pragma unroll
-    for (int which = 0; which < 2; ++which) {
-        float xa[16], xb[16];
-        const uint32_t x = lanes + (which == 0 ? kX1 : kX2) + 16 * g;
-        tmem_load16x2(x, xa, x + 32, xb);
-        float *acc = which == 0 ? acc1 : acc2;
-        const float s = which == 0 ? scale1 : scale2;
-#pragma unroll
-        for (int c = 0; c < 16; c += 2) {
-            const float2 r = fma_f32x2(add_f32x2(make_float2(xa[c], xa[c + 1]), make_float2(xb[c], xb[c + 1])), make_float2(s, s),
-                                       make_float2(acc[c], acc[c + 1]));
-            acc[c] = r.x;
-            acc[c + 1] = r.y;
-        }
+    for (int c = 0; c < 16; c += 2) {
+        const float2 r1 = fma_f32x2(add_f32x2(make_float2(v[0][c], v[0][c + 1]), make_float2(v[1][c], v[1][c + 1])),
+                                    make_float2(scale1, scale1), make_float2(acc1[c], acc1[c + 1]));
+        const float2 r2 = fma_f32x2(add_f32x2(make_float2(v[2][c], v[2][c + 1]), make_float2(v[3][c], v[3][c + 1])),
+                                    make_float2(scale2, scale2), make_float2(acc2[c], acc2[c + 1]));
+        acc1[c] = r1.x;
+        acc1[c + 1] = r1.y;
+        acc2[c] = r2.x;
+        acc2[c + 1] = r2.y;
     }
-}
-
-// Adds the dQ rows of a finished tile into the gradient: lanes 0-15 of warp w hold queries
-// 16 (w % 4) + lane; warpgroup g adds features [16 g, 16 g + 16). `tile` = the gradient row of the
-// tile's first query, `valid` = queries of the tile that exist.
-__device__ __forceinline__ void fold_dq(float *tile, int valid, uint32_t lanes, int g, int warp, int lane, float scale) {
-    float xa[16], xb[16];
-    tmem_load16x2(lanes + kDQ + 16 * g, xa, lanes + kDQ + 32 + 16 * g, xb);
     const int m = 16 * (warp & 3) + lane;
     if (lane < 16 && m < valid) {
         float4 *dst = reinterpret_cast<float4 *>(tile + m * 32 + 16 * g);
 #pragma unroll
         for (int i = 0; i < 4; ++i)
-            atomicAdd(dst + i, make_float4((xa[4 * i] + xb[4 * i]) * scale, (xa[4 * i + 1] + xb[4 * i + 1]) * scale,
-                                           (xa[4 * i + 2] + xb[4 * i + 2]) * scale, (xa[4 * i + 3] + xb[4 * i + 3]) * scale));
+            atomicAdd(dst + i, make_float4((v[4][4 * i] + v[5][4 * i]) * dq_scale, (v[4][4 * i + 1] + v[5][4 * i + 1]) * dq_scale,
+                                           (v[4][4 * i + 2] + v[5][4 * i + 2]) * dq_scale,
+                                           (v[4][4 * i + 3] + v[5][4 * i + 3]) * dq_scale));
     }
 }
 
@@ -1357,8 +1355,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                fold_x_half(acc1, acc2, lanes, g, pending1, pending2);
-                fold_dq(dq_head + pending_c0 * 32, p.queries - pending_c0, lanes, g, warp, lane, pending_dq);
+                fold_all(acc1, acc2, lanes, g, pending1, pending2, dq_head + pending_c0 * 32, p.queries - pending_c0, warp, lane,
+                         pending_dq);
             }
             if (lane == 0 && warp == 0) RK_FTRACE(j, 8);
             tmem_wait_store();
@@ -1375,10 +1373,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (tiles > 0 && ok) {
             ok = __all_sync(0xffffffffu, mbar_wait(&s.x_done, (tiles - 1) & 1));
             tc_fence_after();
-            if (ok) {
-                fold_x_half(acc1, acc2, lanes, g, pending1, pending2);
-                fold_dq(dq_head + pending_c0 * 32, p.queries - pending_c0, lanes, g, warp, lane, pending_dq);
-            }
+            if (ok)
+                fold_all(acc1, acc2, lanes, g, pending1, pending2, dq_head + pending_c0 * 32, p.queries - pending_c0, warp, lane,
+                         pending_dq);
         }
         // dK, dV (packed [batch][heads][keys][32]), features [16 g, 16 g + 16); a failed wait leaves NaN.
         if (row_valid) {

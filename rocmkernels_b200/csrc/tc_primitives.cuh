@@ -176,6 +176,27 @@ __device__ __forceinline__ void tmem_load16x2(uint32_t a, float (&va)[16], uint3
     }
 }
 
+// 16 columns at each of six addresses with one wait.
+__device__ __forceinline__ void tmem_load16x6(const uint32_t (&at)[6], float (&v)[6][16]) {
+    uint32_t r[96];
+    asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%96];\n\t"
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%97];\n\t"
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47}, [%98];\n\t"
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%99];\n\t"
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%64,%65,%66,%67,%68,%69,%70,%71,%72,%73,%74,%75,%76,%77,%78,%79}, [%100];\n\t"
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%80,%81,%82,%83,%84,%85,%86,%87,%88,%89,%90,%91,%92,%93,%94,%95}, [%101];\n\t"
+            "tcgen05.wait::ld.sync.aligned;"
+            : RK_R8(0), RK_R8(8), RK_R8(16), RK_R8(24), RK_R8(32), RK_R8(40), RK_R8(48), RK_R8(56), RK_R8(64), RK_R8(72),
+              RK_R8(80), RK_R8(88)
+            : "r"(at[0]), "r"(at[1]), "r"(at[2]), "r"(at[3]), "r"(at[4]), "r"(at[5])
+            : "memory");
+#pragma unroll
+    for (int k = 0; k < 6; ++k)
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[k][i] = __uint_as_float(r[16 * k + i]);
+}
+
 // 8 columns at a and 8 columns at b with one wait.
 __device__ __forceinline__ void tmem_load8x2(uint32_t a, float (&va)[8], uint32_t b, float (&vb)[8]) {
     uint32_t r[16];
