@@ -867,10 +867,13 @@ __global__ void __launch_bounds__(kThreads, Geometry<D>::kCtasPerSm)
 // offsets, delta). The main kernel TMA-loads those tiles straight into the operand layout (a 128B-
 // swizzled box of 64 FP16 x 64 rows) and has no split warps: one CTA per SM (512 TMEM columns),
 // warps 0-7 two row warpgroups -- warpgroup g handles columns [32 g, 32 g + 32) of every tile and
-// features [16 g, 16 g + 16) of the outputs -- warp 8 the TMA producer, warp 9 the MMA issuer.
-// S and dP are double-buffered so that the next tile's products run while the row warps work on
-// this one. Query tiles are 64-aligned (the window's first tile starts at a multiple of 64; the
-// radius test zeroes the columns outside the window).
+// features [16 g, 16 g + 16) of the outputs -- warp 8 the TMA producer, warp 9 the issuer of the
+// S^T, dP^T, dK and dV products, warp 10 the issuer of the dQ products (two issuing warps on two
+// sub-partitions; both wait for the row warps with suspending waits, so that they take no issue
+// slots from the row warps beside them). S and dP are double-buffered so that the next tile's
+// products run while the row warps work on this one; the row warps fold a tile's dK, dV and dQ
+// products while they work on the next. Query tiles are 64-aligned (the window's first tile
+// starts at a multiple of 64; the radius test zeroes the columns outside the window).
 namespace fused {
 constexpr int kThreads = 352;
 constexpr int kRowThreads = 256;
