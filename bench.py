@@ -24,10 +24,13 @@ k, 0.5-valued inputs): one ``rotary_fp32`` call per step, GB/s over the referenc
 rotary prologue fused in (``attention_fp32_forward_flash_rotary``); its line also carries the
 time of the unfused sequence (``rotary_fp32`` then ``attention_fp32_forward_flash``).
 
-Timing: W untimed steps, then K steps; before each step a 256 MiB buffer is written to flush
-the 126 MB L2, and the step itself is bracketed by CUDA events on the launching stream (the
-flush is outside the events). Device time is summed over the K steps; the max over ranks is
-taken with an all-reduce. FLOPs follow the reference's convention (4*B*H*Q*K*d forward,
+Timing: W untimed steps, then K steps. Forward-only workloads use inputs larger than L2: the
+steps rotate through copies of the input set totalling at least twice the 126 MB L2 (each step's
+inputs were last touched a whole rotation earlier), run back to back on the launching stream, and
+one CUDA event pair brackets the K steps; the line also carries the per-step-flushed figure
+(``flushed``: a 256 MiB write before every step, events around each step, summed). Forward +
+backward workloads flush before every step and bracket each phase with events. The max over ranks
+is taken with an all-reduce. FLOPs follow the reference's convention (4*B*H*Q*K*d forward,
 8*B*H*Q*K*d backward, AttentionBenchmarks.cpp:141-142).
 
 Also reported: ``e2e`` (the same step through the public C entry points with pinned host
@@ -138,8 +141,11 @@ def active_pairs(seq: int, radius: int, length: int) -> int:
 
 def workload_config(name: str, world: int) -> dict:
     spec = WORKLOADS[name]
+    l2 = ("inputs larger than L2: the steps rotate through input sets totalling >= 2 x the 126 MB L2 and run back to back "
+          "(one event pair around the K steps); the per-step-flushed protocol is reported beside it"
+          if not spec["backward"] else "flushed (256 MiB write) before every step")
     config = {"workload": name, "description": spec["description"], "heads": spec["heads"], "seq_len": spec["seq"],
-              "head_dim": spec["dim"], "radius": spec["radius"], "l2": "flushed (256 MiB write) before every step"}
+              "head_dim": spec["dim"], "radius": spec["radius"], "l2": l2}
     if spec.get("generic"):
         config["storage"] = spec["generic"]
     if spec["backward"]:
@@ -152,6 +158,7 @@ def workload_config(name: str, world: int) -> dict:
                        "parallelism": f"batch-sharded x{world}, no collective"})
     return config
 FLUSH_BYTES = 256 << 20
+L2_BYTES = 126 * 10**6  # B200 L2; rotating input sets total at least twice this
 
 
 def env_int(name: str, default: int) -> int:
@@ -823,7 +830,12 @@ def main() -> None:
         job_flops_per_step = world * flops_forward
         job_effective_forward, job_effective_backward = world * effective_forward, 0.0
     job_effective_per_step = job_effective_forward + job_effective_backward
-    launches_per_step = len(plan) * (1 + (2 if with_backward else 0))
+    # The d = 32 split-FP32 flash forward (headline, rotary and FP32 generic d = 32) is two kernels:
+    # the K/V operand pre-pass and the forward.
+    forward_kernel = ("" if spec.get("entry") == "attention_fp32_forward" or generic == "fp16" or
+                      (generic and dim != 32) else api.flash_kernel_name(batch, heads, seq, seq, dim))
+    forward_launches = 2 if forward_kernel == "tcgen05-f16x2-flash-d32" else 1
+    launches_per_step = len(plan) * (forward_launches + (2 if with_backward else 0))
 
     # The step's device tensors by role (one set for the device-timed steps; the e2e leg uses two).
     tensors = dict(q=q, k=k, v=v, mask=mask, out=out, lse=lse)
@@ -923,9 +935,31 @@ def main() -> None:
         parts = [sum(m[j].elapsed_time(m[j + 1]) for m in marks) / 1e3 for j in range(len(fns))]
         return sum(parts), parts
 
-    for _ in range(args.warmup):
+    # Forward-only workloads: extra input sets so that the rotation over them exceeds L2 twice over
+    # (each step's inputs were last touched a whole rotation earlier, so they come from HBM).
+    rotation = [phases]
+    if not with_backward:
+        set_bytes = sum(x.numel() * x.element_size() for x in tensors.values())
+        copies = max(2, -(-2 * L2_BYTES // set_bytes))
+        for _ in range(copies - 1):
+            copy = {name: x.clone() for name, x in tensors.items()}
+            rotation.append(make_phases(copy, stream, plan, batch))
+        rotation_bytes = set_bytes * copies
+
+    def timed_rotating(steps):
+        """Seconds for `steps` back-to-back steps over the rotating input sets (one event pair)."""
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for i in range(steps):
+            for fn in rotation[i % len(rotation)]:
+                fn()
+        end.record(stream)
+        torch.cuda.synchronize(device)
+        return start.elapsed_time(end) / 1e3
+
+    for i in range(args.warmup):
         flush.fill_(0.0)
-        for phase in phases:
+        for phase in rotation[i % len(rotation)]:
             phase()
     torch.cuda.synchronize(device)
 
@@ -937,7 +971,11 @@ def main() -> None:
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(device)
-    device_seconds, part_seconds = timed(phases, args.steps)
+    if with_backward:
+        device_seconds, part_seconds = timed(phases, args.steps)
+    else:
+        device_seconds = timed_rotating(args.steps)
+        part_seconds = [device_seconds]
     torch.cuda.synchronize(device)
     if world > 1:
         dist.barrier()
@@ -958,16 +996,20 @@ def main() -> None:
     e2e_steps = max(1, min(args.steps, 50))
     e2e_seconds = pipelined_e2e(device, e2e_sets, host_inputs, host_outputs, launch_set, e2e_steps)
 
+    # The per-step-flushed protocol of earlier lines (256 MiB flush, then events around the step), for continuity.
+    flushed_seconds = timed(phases, args.steps)[0] if not with_backward else 0.0
+
     unfused_seconds = 0.0
     if rotary:
         for _ in range(args.warmup):
             unfused_rotary_forward()
         unfused_seconds, _ = timed([unfused_rotary_forward], args.steps)
 
-    times = torch.tensor([device_seconds, e2e_seconds, unfused_seconds] + part_seconds, device=device, dtype=torch.float64)
+    times = torch.tensor([device_seconds, e2e_seconds, unfused_seconds, flushed_seconds] + part_seconds, device=device,
+                         dtype=torch.float64)
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    device_seconds, e2e_seconds, unfused_seconds, *part_seconds = times.tolist()
+    device_seconds, e2e_seconds, unfused_seconds, flushed_seconds, *part_seconds = times.tolist()
 
     value = job_flops_per_step * args.steps / device_seconds / 1e12
     e2e_value = job_flops_per_step * e2e_steps / e2e_seconds / 1e12
@@ -1001,6 +1043,8 @@ def main() -> None:
             peak = float(peaks["bf16_tflops"])
             roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                         "traffic": traffic_from_profiles(path, args.workload), "kernel": path}
+            if forward_launches == 2:
+                roofline["duration"] = "the whole step: K/V operand pre-pass + forward kernel (back to back)"
             if path.startswith("tcgen05-f16x2"):  # FP32 storage: compare with the TF32 dense rate as well
                 roofline["peak_source"] = f"{peak_source} bf16_tflops (burst); the TF32 dense rate is half of it"
                 roofline["frac_of_tf32_dense"] = achieved / (peak / 2)
@@ -1033,6 +1077,11 @@ def main() -> None:
     }
     if generic == "fp16" and arrays is not None:
         line["data"] += ", rounded to FP16 storage"
+    if not with_backward:
+        line["flushed"] = {"ms_per_step": flushed_seconds / args.steps * 1e3,
+                           "value": job_flops_per_step * args.steps / flushed_seconds / 1e12, "unit": "TFLOP/s",
+                           "protocol": "256 MiB written before every step, CUDA events around each step (summed)"}
+        line["config"]["rotation"] = {"sets": len(rotation), "bytes": rotation_bytes}
     if with_backward:
         line["effective"] = {"value": job_effective_per_step * args.steps / device_seconds / 1e12, "unit": "TFLOP/s",
                              "flops": "12*d per active (query, key) pair"}

@@ -132,7 +132,12 @@ ROCMKERNELS_C_EXPORT int attention_fp32_forward_tuned(const float *q, const floa
 
 /* Flash forward, the headline entry: tcgen05/TMEM kernel on sm_100a with split-FP16 operands
  * (kind::f16; each FP32 operand as two FP16 terms, three products) when the tensors are
- * TMA-addressable, else the exact FP32 SIMT kernel; radius < -1 is invalid. Replaces attention_fp32_forward_flash (Attention.hpp:28-30; Attention.hip:372-390). */
+ * TMA-addressable, else the exact FP32 SIMT kernel; radius < -1 is invalid. Replaces attention_fp32_forward_flash (Attention.hpp:28-30; Attention.hip:372-390).
+ * Scratch: the tensor-core path first splits every key tile of K and V once into a workspace of
+ * 16,400 bytes per 64 keys of each (batch, head), taken from a stream-ordered memory pool that the
+ * library keeps per device (acquired and given back on `stream`, so concurrent streams never
+ * share it); when the pool cannot supply it the kernel splits K and V itself. The pool keeps up to
+ * 256 MiB across synchronisations; rocmkernels_attention_release_scratch returns the rest. */
 ROCMKERNELS_C_EXPORT int attention_fp32_forward_flash(const float *q, const float *k, const float *v, const bool *mask,
         float *output, float *lse, int batch, int heads, int queries, int keys, int radius, RocmKernelsStrides qs,
         RocmKernelsStrides ks, RocmKernelsStrides vs, RocmKernelsStrides os, RocmKernelsStream stream);
@@ -257,6 +262,11 @@ ROCMKERNELS_C_EXPORT const char *rocmkernels_attention_generic_kernel(int batch,
  * pipeline wait gave up (a protocol failure; the affected rows are written as NaN). Reading it
  * synchronizes with the device; clear != 0 resets it. No counterpart in the reference. */
 ROCMKERNELS_C_EXPORT unsigned int rocmkernels_attention_device_status(int clear);
+
+/* Returns the memory that the library's scratch pool on the current device holds and no call is
+ * using (cudaMemPoolTrimTo(pool, 0)); cudaSuccess when the library has no pool there. Scratch
+ * still in use by enqueued work stays. No counterpart in the reference. */
+ROCMKERNELS_C_EXPORT int rocmkernels_attention_release_scratch(void);
 
 #ifdef __cplusplus
 } /* extern "C" */

@@ -101,6 +101,8 @@ def lib() -> ctypes.CDLL:
         library.rocmkernels_attention_generic_kernel.restype = ctypes.c_char_p
         library.rocmkernels_attention_device_status.argtypes = [ctypes.c_int]
         library.rocmkernels_attention_device_status.restype = ctypes.c_uint
+        library.rocmkernels_attention_release_scratch.argtypes = []
+        library.rocmkernels_attention_release_scratch.restype = ctypes.c_int
         library.attention_fp32_backward_static_delta.argtypes = [_POINTER] * 10 + [_INT] * 5 + [Strides] * 5 + [_POINTER]
         library.attention_fp32_backward_static_delta.restype = ctypes.c_int
         library.attention_fp32_backward_fused.argtypes = ([_POINTER] * 12 + [ctypes.c_ulonglong] + [_INT] * 5 + [Strides] * 5
@@ -132,6 +134,12 @@ def device_status(clear: bool = True) -> int:
     """Status word of the tensor-core kernels on the current device (0 = no failed pipeline wait).
     Synchronizes with the device."""
     return int(lib().rocmkernels_attention_device_status(int(clear)))
+
+
+def release_scratch() -> int:
+    """Returns the idle memory of the library's scratch pool on the current device to the system
+    (the flash forward's split K/V workspace); a cudaError_t value, 0 on success."""
+    return int(lib().rocmkernels_attention_release_scratch())
 
 
 def _error_name(status: int) -> str:

@@ -7,6 +7,7 @@
 #include "attention_common.cuh"
 #include "attention_simt.cuh"
 #include "attention_tc.cuh"
+#include "scratch.h"
 
 #include <cmath>
 #include <mutex>
@@ -423,6 +424,8 @@ int attention_fp32_query_profile(const float *q, const float *k, const float *v,
 }
 
 const char *rocmkernels_attention_build_info(void) { return rk::tc::build_info(); }
+
+int rocmkernels_attention_release_scratch(void) { return rk::scratch_trim(); }
 
 unsigned int rocmkernels_attention_device_status(int clear) {
     return rk::tc::read_device_status(clear != 0) | rk::tc::read_backward_status(clear != 0);

@@ -15,6 +15,18 @@
 //               [v0^T ; v1^T] FP16 rows, zero masked key rows, publish the tile's key mask and
 //               the two per-tile scale exponents
 //
+// Prepared operands (the d = 32 split-FP32 forward when the library's scratch pool can hold them):
+// prepare_kv_kernel first converts every 64-key tile of every head once, into the byte image of
+// that shared-memory stage plus a 16-byte header (mask bits, exponents); the forward then runs
+//   warps 0-7   softmax + epilogue of Q tiles A and B (as above)
+//   warp  8     producer: three bulk copies per key tile (K rows, V^T rows, header)
+//   warps 9-10  MMA issuers, one per Q tile, each waiting (suspended) for its own P tiles
+// with no split warps: the conversion is not repeated by each of a head's query blocks. The V rows
+// of an image are [v1^T ; v0^T] (the ones follow in shared memory), so P.V accumulates
+// Ot = p1.v0 + p0.v1 + p0.v0 in one 32-column accumulator (N = 48, 32, 48; the p1.v1 term, ~2^-22
+// of the output, is left out) and the softmax threads fold one 33-column TMEM load per tile.
+// TMEM per Q tile: q0 0-15 | q1 16-31 | S/P buffers 32-95, 96-159 | Ot 160-191 | row sums 192-207.
+//
 // Split FP16 operands. Every FP32 operand x is scaled by a power of two 2^e (Q: per row; K, V:
 // per tile; P: 2^14) so that its largest magnitude lies in [2^14, 2^15), then split
 // x' = x0 + x1: for Q, K and V x0 = FP16(x') (cvt.rn: 11 significant bits) and x1 = FP16(x' - x0),
@@ -55,7 +67,9 @@
 #include <type_traits>
 
 #include "rotary.cuh"
+#include "scratch.h"
 #include "tc_operands.cuh"
+
 
 namespace rk {
 namespace tc {
@@ -71,12 +85,12 @@ __device__ long long g_trace[kTraceTiles][kTraceEvents];
     do {                                                                                              \
         if (blockIdx.x == 0 && (tile_index) < kTraceTiles) g_trace[(tile_index)][(event)] = clock64(); \
     } while (0)
-// per softmax warp, tile 5 of CTA 0: events 0 s_full seen, 1 max done, 2 exp and P stores issued,
+// per softmax warp, tile 30 of CTA 0: events 0 s_full seen, 1 max done, 2 exp and P stores issued,
 // 3 fold done, 4 P stores complete
 __device__ long long g_warp_trace[8][8];
 #define RK_WARP_TRACE(tile_index, event)                                                                          \
     do {                                                                                                         \
-        if (blockIdx.x == 0 && (tile_index) == 5 && (threadIdx.x & 31) == 0) g_warp_trace[threadIdx.x >> 5][(event)] = clock64(); \
+        if (blockIdx.x == 0 && (tile_index) == 30 && (threadIdx.x & 31) == 0) g_warp_trace[threadIdx.x >> 5][(event)] = clock64(); \
     } while (0)
 #else
 #define RK_WARP_TRACE(tile_index, event) \
@@ -106,16 +120,21 @@ constexpr uint64_t kDescStep = 2;                      // one K=16 step of FP16 
 // 3 stages) with operands twice as wide. FP16 storage (kHalf true, d = 16, 32 or 64): one Q tile,
 // 3 stages, one FP16 term per operand. The TMEM column layout of a Q tile is the same for one or
 // two Q tiles.
-template <int D, bool kHalf, int kTiles = !kHalf && D == 32 ? 2 : 1>
+// kPrepared (split FP32, d = 32): K and V arrive already split, as the stage images that
+// prepare_kv_kernel wrote once per head (below); the CTA then has no split warps, and one MMA warp
+// per Q tile instead of one for both.
+template <int D, bool kHalf, int kTiles = !kHalf && D == 32 ? 2 : 1, bool kPrepared = false>
 struct Forward {
     static_assert(kTiles == 1 || (kTiles == 2 && !kHalf && D == 32), "two Q tiles per CTA: split FP32, d = 32");
+    static_assert(!kPrepared || (!kHalf && D == 32), "prepared operands: split FP32, d = 32");
     static constexpr int kTerms = kHalf ? 1 : 2;  // FP16 terms per operand
     static constexpr int kQTiles = kTiles;
     static constexpr int kCtaQueries = kQTile * kQTiles;
     static constexpr int kStages = !kHalf && D == 32 ? 4 : 3;
     static constexpr int kSoftmaxWarps = 4 * kQTiles;
-    static constexpr int kProducerWarp = kSoftmaxWarps, kMmaWarp = kSoftmaxWarps + 1, kSplitWarp = kSoftmaxWarps + 2;
-    static constexpr int kThreads = 32 * (kSoftmaxWarps + 4);
+    static constexpr int kMmaWarps = kPrepared ? kQTiles : 1, kSplitWarps = kPrepared ? 0 : 2;
+    static constexpr int kProducerWarp = kSoftmaxWarps, kMmaWarp = kSoftmaxWarps + 1, kSplitWarp = kMmaWarp + kMmaWarps;
+    static constexpr int kThreads = 32 * (kSoftmaxWarps + 1 + kMmaWarps + kSplitWarps);
     static constexpr int kSplitThreads = 64;
     // d = 64: the raw K/V stage is refilled as soon as the split warps have read it into registers
     // (their conversion then waits for the MMAs to release the converted stage). Measured on B200:
@@ -130,39 +149,54 @@ struct Forward {
                                                              // FP16: v^T only
     static constexpr int kVWords = kVRows * 32;              // kVRows x 128 bytes
     // TMEM per Q tile: q0 pairs | q1 pairs | S/P buffer 0 | S/P buffer 1 | Oa | Ob | row sums
+    // (prepared operands: one output accumulator Ot, then the row sums)
     static constexpr uint32_t kColQ0 = 0, kColQ1 = D / 2, kColBuffer = kHalf ? 32 : D, kBufferColumns = 64,
-                              kColO = kColBuffer + 128, kColSum = kColO + kTerms * D,
+                              kColO = kColBuffer + 128, kColSum = kColO + (kPrepared ? D : kTerms * D),
                               kColTile = kHalf || D == 32 ? 256 : 512;
     static constexpr uint32_t kTmemColumns = kHalf ? 256 : 512;
     static constexpr uint64_t kDescStageK = (kHalf ? kRawFloats : kKWords) * 4 / 16, kDescStageV = kVWords * 4 / 16;
 };
 
+// Per key tile: which of its 64 keys are visible and the power-of-two scales of its split K and V
+// (16 bytes, so that a bulk copy can land it beside a prepared stage image).
+struct alignas(16) StageHeader {
+    uint32_t mask[2];  // bit c of mask[c / 32]: key k0 + c visible
+    int k_exponent;    // K tile scaled by 2^k_exponent
+    int v_exponent;    // V tile scaled by 2^v_exponent
+};
+
+// A prepared stage image in global memory: the k16 tile (64 rows [k0 | k1], 8 KB) followed by the
+// v1^T / v0^T rows of the vt16 tile (64 rows of 128 bytes), byte for byte as the shared-memory
+// stage holds them.
+constexpr int kImageKBytes = 64 * 2 * 32 * 2, kImageBytes = kImageKBytes + 64 * 128;
+
 // Operand tiles are rows of 128 bytes in 1024-byte aligned 8-row atoms (the 128B swizzle).
-template <int D, bool kHalf, int kTiles = Forward<D, kHalf>::kQTiles>
+template <int D, bool kHalf, int kTiles = Forward<D, kHalf>::kQTiles, bool kPrepared = false>
 struct alignas(1024) SharedStorage {
-    using F = Forward<D, kHalf, kTiles>;
-    float k_raw[F::kStages][F::kRawFloats];    // K tile as TMA lands it (FP32: swizzled boxes of 64 x 32; FP16: 64 x 64)
-    float v_raw[F::kStages][F::kRawFloats];    // V tile
+    using F = Forward<D, kHalf, kTiles, kPrepared>;
+    // Raw tiles as TMA lands them (FP32: swizzled boxes of 64 x 32; FP16: 64 x 64); prepared
+    // operands have none (a 1 KB placeholder keeps the layout below aligned).
+    static constexpr int kRawStages = kPrepared ? 1 : F::kStages, kRawWords = kPrepared ? 256 : F::kRawFloats;
+    float k_raw[kRawStages][kRawWords];        // K tile
+    float v_raw[kRawStages][kRawWords];        // V tile
     uint32_t k16[F::kStages][F::kKWords > 0 ? F::kKWords : 1];  // 64 key rows as [k0 | k1] FP16 (row layout),
                                                                 // K-major 128B swizzle (unused for FP16 storage)
     alignas(1024) uint32_t vt16[F::kStages][F::kVWords];  // rows 0..D-1 v0^T, D..2D-1 v1^T (64 keys each, 128B
                                                           // swizzle), 2D..2D+15 FP16 ones (written once); FP16: v^T
-    uint32_t key_mask[F::kStages][2];          // bit c: key k0 + c visible
-    int k_exponent[F::kStages];                // K tile scaled by 2^k_exponent
-    int v_exponent[F::kStages];                // V tile scaled by 2^v_exponent
+    StageHeader header[F::kStages];            // the stage's key mask and exponents
     float split_max[2][2];                     // per split warp: max |K|, max |V| of its rows
     int split_ok[2];                           // per split warp: its kv_full wait succeeded
     uint64_t kv_full[F::kStages];              // TMA bytes landed
     uint64_t raw_free[F::kStages];             // kEarlyRawRefill: the raw tiles read by the split warps (64 arrivals)
     uint64_t kv_ready[F::kStages];             // conversion done (64 arrivals)
-    uint64_t kv_empty[F::kStages];             // MMAs reading the stage finished (commit)
+    uint64_t kv_empty[F::kStages];             // MMAs reading the stage finished (a commit per MMA warp)
     uint64_t s_full[F::kQTiles][2];            // S of a buffer is in TMEM (commit)
     uint64_t p_full[F::kQTiles];               // P of the current tile is in TMEM (128 arrivals)
     uint64_t pv_done[F::kQTiles];              // Ot of the current tile is in TMEM (commit)
     uint64_t q_ready;                          // q0/q1 of every Q tile in TMEM (128 arrivals per tile)
     uint64_t range_ready;                      // tile_count written (1 arrival)
     int tile_count;                            // key tiles up to the last visible key of the window
-    uint64_t mma_done;                         // every MMA of the CTA finished (commit)
+    uint64_t mma_done;                         // every MMA of the CTA finished (a commit per MMA warp)
     uint32_t tmem_base;
 };
 
@@ -179,6 +213,11 @@ struct FlashArgs {
     int cta_per_head;  // ceil(queries / queries per CTA)
     int vec_out;       // output rows 16-byte addressable
     int rot_batch;     // rotary tables: 1 = one table per sequence (batch coordinate b), 0 = one shared table
+    // Prepared operands: the stage images and headers of key tile t of head (b, h) at index
+    // (b * heads + h) * tiles_per_head + t.
+    const uint8_t *images;
+    const StageHeader *headers;
+    int tiles_per_head;
 };
 
 __device__ __forceinline__ uint32_t tmem_lane_address(uint32_t base, int warp) {
@@ -239,6 +278,61 @@ __device__ __forceinline__ void issue_values(uint32_t tmem, uint64_t v_desc, int
         mma4_f16_ts_warp(t + F::kColO, a1, bv, kIdescPV, 1);
     }
     mma4_f16_ts_commit_warp(t + F::kColO, a0, bv, kIdescPV, kHalf ? 1 : 0, bar);
+}
+
+// Prepared operands, d = 32: Ot = p1.v0 + p0.v1 + p0.v0 in one accumulator, and the row sums
+// p1.1 + p0.1 beside it, over the 64 keys (four K=16 steps per product), then a commit to `bar`.
+// The stage's V tile holds rows [v1^T ; v0^T ; ones]: B1 = v1^T (N = 32), B0 = [v0^T ; ones]
+// (N = 48, 32 rows = 4 KB further). The two small products go in first, so the accumulator is
+// small while they are added; the p1.v1 term (~2^-22 of the output) is left out.
+template <int kTiles>
+__device__ __forceinline__ void issue_values_prepared(uint32_t tmem, uint64_t v_desc, int tile, int buffer, uint64_t *bar) {
+    using F = Forward<32, false, kTiles, true>;
+    const uint32_t t = tmem + tile * F::kColTile;
+    const uint32_t pbuf = t + F::kColBuffer + buffer * F::kBufferColumns;
+    constexpr uint32_t kIdescOutSums = f16_instr_desc(128, 48), kIdescOut = f16_instr_desc(128, 32);
+    constexpr uint64_t kRowsV0 = 32 * 128 / 16;  // descriptor offset of the v0^T rows
+    const uint64_t b1[4] = {v_desc, v_desc + kDescStep, v_desc + 2 * kDescStep, v_desc + 3 * kDescStep};
+    const uint64_t b0[4] = {v_desc + kRowsV0, v_desc + kRowsV0 + kDescStep, v_desc + kRowsV0 + 2 * kDescStep,
+                            v_desc + kRowsV0 + 3 * kDescStep};
+    const uint32_t a0[4] = {pbuf, pbuf + 8, pbuf + 16, pbuf + 24};       // p0 pairs
+    const uint32_t a1[4] = {pbuf + 32, pbuf + 40, pbuf + 48, pbuf + 56};  // p1 pairs
+    mma4_f16_ts_warp(t + F::kColO, a1, b0, kIdescOutSums, 1);
+    mma4_f16_ts_warp(t + F::kColO, a0, b1, kIdescOut, 0);
+    mma4_f16_ts_commit_warp(t + F::kColO, a0, b0, kIdescOutSums, 0, bar);
+}
+
+// Prepared operands, d = 32: folds a finished key tile's Ot (32 columns, V scaled by 2^c) and row
+// sum into the running output and sum, with the same exponent rule as fold_output.
+__device__ __forceinline__ void fold_prepared(float (&o)[32], float &row_sum, int &o_exp, const float (&ot)[32], float sum,
+                                              float weight, int c) {
+    if (o_exp == kNoExponent) o_exp = c;
+    float out_weight = weight, tile_scale = 1.f;
+    if (c > o_exp) {
+        tile_scale = exp2_int(o_exp - c);
+    } else if (c < o_exp) {
+        out_weight = weight * exp2_int(c - o_exp);
+        o_exp = c;
+    }
+    row_sum = fmaf(row_sum, weight, sum);
+    const float2 weight2 = make_float2(out_weight, out_weight);
+    if (__all_sync(0xffffffffu, tile_scale == 1.f)) {  // uniform anyway
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+            const float2 r = fma_f32x2(make_float2(o[i], o[i + 1]), weight2, make_float2(ot[i], ot[i + 1]));
+            o[i] = r.x;
+            o[i + 1] = r.y;
+        }
+    } else {
+        const float2 scale2 = make_float2(tile_scale, tile_scale);
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+            const float2 u = mul_f32x2(make_float2(ot[i], ot[i + 1]), scale2);
+            const float2 r = fma_f32x2(make_float2(o[i], o[i + 1]), weight2, u);
+            o[i] = r.x;
+            o[i + 1] = r.y;
+        }
+    }
 }
 
 // Folds the last finished key tile into the running output and row sum. In TMEM, Oa + Ob is the
@@ -425,17 +519,25 @@ __device__ __forceinline__ void rotate_row32(float4 (&x)[8], const float4 (&cs)[
 // never go through HBM; the result equals rotary_fp32 followed by this kernel bit for bit.
 // With kRotary the producer also lands the tile's cos and sin rows (tmap_cos, tmap_sin) in the
 // stage; the other instantiations ignore those two maps.
+// kPrepared (D = 32, split FP32, no statistics): the key tiles come from the stage images of
+// prepare_kv_kernel (args.images / args.headers; with kRotary its K rows are already rotated and
+// the kernel rotates only the Q rows) by bulk copies, and the kernel is
+// launched as a programmatic dependent of that pre-pass: every thread passes griddepcontrol.wait
+// before it touches global memory (the TMEM allocation and the barrier set-up overlap the end of
+// the pre-pass).
 template <int D, bool kHalf, int kWidth = D, bool kRotary = false, int kTiles = Forward<D, kHalf>::kQTiles,
-          bool kStats = false>
-__global__ void __launch_bounds__(Forward<D, kHalf, kTiles>::kThreads, 1)
+          bool kStats = false, bool kPrepared = false>
+__global__ void __launch_bounds__(Forward<D, kHalf, kTiles, kPrepared>::kThreads, 1)
         flash_forward_kernel(const FlashArgs args, const __grid_constant__ CUtensorMap tmap_k,
                              const __grid_constant__ CUtensorMap tmap_v, const __grid_constant__ CUtensorMap tmap_cos,
                              const __grid_constant__ CUtensorMap tmap_sin) {
     static_assert(kWidth == D || (!kHalf && kWidth % 4 == 0 && kWidth < D), "narrow rows: FP32 storage only");
     static_assert(!kRotary || (D == 32 && kWidth == 32 && !kHalf), "the rotary prologue is defined for 32-wide FP32 heads");
     static_assert(!kStats || (D == 32 && kWidth == 32 && !kHalf && !kRotary), "statistics: 32-wide FP32 heads");
-    using F = Forward<D, kHalf, kTiles>;
-    using Storage = std::conditional_t<kRotary, RotaryStorage<D, kTiles>, SharedStorage<D, kHalf, kTiles>>;
+    static_assert(!kPrepared || (D == 32 && kWidth == 32 && !kHalf && !kStats), "prepared operands: the d = 32 split-FP32 forward");
+    using F = Forward<D, kHalf, kTiles, kPrepared>;
+    // Prepared operands with the rotary prologue: K arrives rotated, so no table tiles are staged.
+    using Storage = std::conditional_t<kRotary && !kPrepared, RotaryStorage<D, kTiles>, SharedStorage<D, kHalf, kTiles, kPrepared>>;
     constexpr int kStages = F::kStages;
     extern __shared__ uint8_t shared_raw[];
     Storage &s = *reinterpret_cast<Storage *>((reinterpret_cast<uintptr_t>(shared_raw) + 1023) & ~uintptr_t(1023));
@@ -451,10 +553,20 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles>::kThreads, 1)
     const int q0 = cta_tile * F::kCtaQueries;
     int first, last;
     key_window(q0, min(q0 + F::kCtaQueries, p.queries), p.keys, p.radius, first, last);
+    // Prepared images cover the fixed 64-key tiles of the sequence: the window starts on one (the
+    // keys before the true start are outside every row's radius and drop out with the window mask).
+    if constexpr (kPrepared) first &= ~(kKeyTile - 1);
     // Key tiles of the window; trailing tiles whose keys are all masked are dropped after the
     // set-up barrier (visible_tiles below), so that key-padded sequences skip their padding.
     const int window_tiles = last > first ? (last - first + kKeyTile - 1) / kKeyTile : 0;
 
+    if constexpr (kPrepared) {
+        if (warp == 0) {
+            tmem_alloc(&s.tmem_base, F::kTmemColumns);
+            tmem_relinquish();
+        }
+        grid_dependency_wait();
+    }
     // The softmax threads issue the loads of their Q row (and, with the rotary prologue, of its
     // table rows) before the set-up barrier, so their latency overlaps the TMEM allocation and
     // the barrier initialisation.
@@ -480,19 +592,29 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles>::kThreads, 1)
         }
     }
 
-    if (warp == 0) {
+    if (!kPrepared && warp == 0) {
         tmem_alloc(&s.tmem_base, F::kTmemColumns);
         tmem_relinquish();
     }
     // TMA loads of key tile j into its stage, completing on kv_full (producer thread only).
+    // Prepared operands: bulk copies of the tile's stage image and header.
     const auto issue_tile = [&](int j) {
         const int stage = j % kStages;
 #ifdef RK_WAIT_TEST
         if (blockIdx.x == 0 && j == g_withheld_tile) return;  // its kv_full phase never completes
 #endif
         RK_TRACE(j, 12);
+        if constexpr (kPrepared) {
+            const long long tile = (static_cast<long long>(b) * p.heads + h) * args.tiles_per_head + first / kKeyTile + j;
+            const uint8_t *image = args.images + tile * kImageBytes;
+            mbar_arrive_expect_tx(&s.kv_full[stage], kImageBytes + sizeof(StageHeader));
+            bulk_load(s.k16[stage], image, kImageKBytes, &s.kv_full[stage]);
+            bulk_load(s.vt16[stage], image + kImageKBytes, kImageBytes - kImageKBytes, &s.kv_full[stage]);
+            bulk_load(&s.header[stage], args.headers + tile, sizeof(StageHeader), &s.kv_full[stage]);
+            return;
+        }
         mbar_arrive_expect_tx(&s.kv_full[stage], ((kStats ? 1 : 2) * F::kBoxes + (kRotary ? 2 : 0)) * kBoxBytes);
-        if constexpr (kRotary) {
+        if constexpr (kRotary && !kPrepared) {
             const int table = b * args.rot_batch;
             tma_load_4d(s.cos_raw[stage], &tmap_cos, &s.kv_full[stage], 0, first + j * kKeyTile, 0, table);
             tma_load_4d(s.sin_raw[stage], &tmap_sin, &s.kv_full[stage], 0, first + j * kKeyTile, 0, table);
@@ -510,7 +632,7 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles>::kThreads, 1)
             mbar_init(&s.kv_full[i], 1);
             mbar_init(&s.raw_free[i], F::kSplitThreads);
             mbar_init(&s.kv_ready[i], F::kSplitThreads);
-            mbar_init(&s.kv_empty[i], 1);
+            mbar_init(&s.kv_empty[i], F::kMmaWarps);
         }
         for (int t = 0; t < F::kQTiles; ++t) {
             mbar_init(&s.s_full[t][0], 1);
@@ -520,7 +642,7 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles>::kThreads, 1)
         }
         mbar_init(&s.q_ready, kQTile * F::kQTiles);
         mbar_init(&s.range_ready, 1);
-        mbar_init(&s.mma_done, 1);
+        mbar_init(&s.mma_done, F::kMmaWarps);
         mbar_fence_init();
         // The first stages are free: their loads overlap the TMEM allocation and the set-up
         // barrier. Nothing else touches the raw K/V tiles or kv_full before that barrier.
@@ -569,7 +691,50 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles>::kThreads, 1)
             // Prefetched tiles past the last visible key are never converted: wait for them.
             for (int j = tiles; j < prefetched; ++j) mbar_wait(&s.kv_full[j], 0);
         }
-    } else if (warp == F::kMmaWarp) {
+    } else if (kPrepared && warp >= F::kMmaWarp && warp < F::kMmaWarp + F::kMmaWarps) {
+        // ---------------------------------------------------------------- MMA issuers (prepared operands)
+        // Warp kMmaWarp + t issues Q tile t's products: S(t, 0) and S(t, 1) first; then for every
+        // key tile j, once P(t, j) is in TMEM, P(t, j).V (the stage's release follows it) and
+        // S(t, j + 2) into the buffer P(t, j) occupies (the tensor core runs one thread's MMAs in
+        // order, so S(t, j + 2) overwrites P(t, j) only after P(t, j).V has read it). Every wait
+        // suspends the warp, so it takes no issue slots from the softmax warps of its sub-partition.
+        const int t = warp - F::kMmaWarp;
+        const int tiles = __shfl_sync(0xffffffffu, visible_tiles(), 0);
+        if (tiles > 0) {
+            const uint64_t k_desc0 = sw128_descriptor(smem_u32(s.k16[0]));
+            const uint64_t v_desc0 = sw128_descriptor(smem_u32(s.vt16[0]));
+            bool ok = mbar_wait_sleep_warp(&s.q_ready, 0);
+            tc_fence_after();
+            for (int j = 0; j < min(2, tiles) && ok; ++j) {
+                ok = mbar_wait_sleep_warp(&s.kv_full[j], 0);
+                if (!ok) break;
+                tc_fence_after();
+                issue_scores<D, kHalf>(tmem, k_desc0 + F::kDescStageK * j, t, j, &s.s_full[t][j]);
+            }
+            for (int j = 0; j < tiles && ok; ++j) {
+                const int stage = j % kStages, buffer = j & 1;
+                if (lane == 0) RK_TRACE(j, 2 + t);
+                ok = mbar_wait_sleep_warp(&s.p_full[t], j & 1);
+                if (!ok) break;
+                if (lane == 0) RK_TRACE(j, t);
+                tc_fence_after();
+                issue_values_prepared<kTiles>(tmem, v_desc0 + F::kDescStageV * stage, t, buffer, &s.pv_done[t]);
+                mma_commit_warp(&s.kv_empty[stage]);
+                if (lane == 0) RK_TRACE(j, 13 + t);
+                if (j + 2 < tiles) {
+                    const int next = (j + 2) % kStages;
+                    ok = mbar_wait_sleep_warp(&s.kv_full[next], ((j + 2) / kStages) & 1);
+                    if (!ok) break;
+                    tc_fence_after();
+                    issue_scores<D, kHalf>(tmem, k_desc0 + F::kDescStageK * next, t, buffer, &s.s_full[t][buffer]);
+                    if (lane == 0) RK_TRACE(j, 7 + 4 * t);
+                }
+            }
+            // TMEM is released only after every issued MMA of both warps has completed.
+            mma_commit_warp(&s.mma_done);
+            mbar_wait_warp(&s.mma_done, 0);
+        }
+    } else if (!kPrepared && warp == F::kMmaWarp) {
         // ---------------------------------------------------------------- MMA issuer
         // S(t, 0) and S(t, 1) first; then for every key tile j, whichever Q tile's P is ready
         // first gets P(j).V and S(j + 2) (into the buffer P(j) occupied) issued first; the K/V
@@ -635,7 +800,7 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles>::kThreads, 1)
             mma_commit_warp(&s.mma_done);
             mbar_wait_warp(&s.mma_done, 0);
         }
-    } else if (warp >= F::kSplitWarp) {
+    } else if (!kPrepared && warp >= F::kSplitWarp) {
         // ---------------------------------------------------------------- FP16 split
         // Split warp w owns key rows [32w, 32w + 32) of every tile; its ballot is their mask.
         // K: lane = one key row -> its row-layout chunks [k0 | k1]. V: item = (key group of 8 rows,
@@ -660,7 +825,7 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles>::kThreads, 1)
                 if (!__all_sync(0xffffffffu, mbar_wait(&s.kv_full[stage], use & 1))) break;
                 const int key = first + j * kKeyTile + row;
                 const uint32_t bits = __ballot_sync(0xffffffffu, key < last && mask[key] != 0);
-                if (lane == 0) s.key_mask[stage][w] = bits;
+                if (lane == 0) s.header[stage].mask[w] = bits;
                 transpose_values<D>(s.v_raw[stage], s.vt16[stage], w, lane, bits);
                 fence_proxy_async_shared();
                 mbar_arrive(&s.kv_ready[stage]);
@@ -682,7 +847,7 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles>::kThreads, 1)
                 kx[c] = raw_chunk<D>(s.k_raw[stage], row, c);
                 if (!keep_row) kx[c] = make_float4(0.f, 0.f, 0.f, 0.f);
             }
-            if constexpr (kRotary) {
+            if constexpr (kRotary && !kPrepared) {
                 if (keep_row) {
                     float4 cs[8], sn[8];
 #pragma unroll
@@ -724,7 +889,7 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles>::kThreads, 1)
                 s.split_max[w][0] = kmax;
                 s.split_max[w][1] = vmax;
                 s.split_ok[w] = landed && stage_free;
-                s.key_mask[stage][w] = bits;
+                s.header[stage].mask[w] = bits;
             }
             asm volatile("bar.sync 1, 64;" ::: "memory");
             if (!(s.split_ok[0] && s.split_ok[1])) break;
@@ -732,8 +897,8 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles>::kThreads, 1)
             const int v_exponent = fp16_scale_exponent(fmaxf(s.split_max[0][1], s.split_max[1][1]));
             asm volatile("bar.sync 1, 64;" ::: "memory");  // split_max is rewritten for the next tile
             if (threadIdx.x == F::kSplitWarp * 32) {
-                s.k_exponent[stage] = k_exponent;
-                s.v_exponent[stage] = v_exponent;
+                s.header[stage].k_exponent = k_exponent;
+                s.header[stage].v_exponent = v_exponent;
             }
             const float k_scale = exp2_int(k_exponent), v_scale = exp2_int(v_exponent);
             // K row: features 8m..8m+7 -> k0 chunk m and k1 chunk m of the row layout
@@ -851,26 +1016,28 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles>::kThreads, 1)
         for (int j = 0; j < tiles && ok; ++j) {
             const int stage = j % kStages, use = j / kStages, buffer = j & 1;
             const uint32_t pbuf = lane_base + F::kColBuffer + buffer * F::kBufferColumns;
+            // The stage's header: converted by the split warps (kv_ready), or landed with the
+            // prepared image (kv_full).
             ok = __all_sync(0xffffffffu, mbar_wait(&s.s_full[tile][buffer], (j >> 1) & 1) &&
-                                                 mbar_wait(&s.kv_ready[stage], use & 1));
+                                                 mbar_wait(kPrepared ? &s.kv_full[stage] : &s.kv_ready[stage], use & 1));
             if (!ok) break;
-            if (tracer) RK_TRACE(j, 4 + 4 * tile);
-            RK_WARP_TRACE(j, 0);
             tc_fence_after();
             float sc[64];
             tmem_load64(pbuf, sc);
+            if (tracer) RK_TRACE(j, 4 + 4 * tile);
+            RK_WARP_TRACE(j, 0);
             // Visible keys of this row in the tile: key mask x radius window x valid row.
             const int k0 = first + j * kKeyTile;
-            uint64_t active = row_valid ? (static_cast<uint64_t>(s.key_mask[stage][0]) |
-                                           (static_cast<uint64_t>(s.key_mask[stage][1]) << 32))
+            uint64_t active = row_valid ? (static_cast<uint64_t>(s.header[stage].mask[0]) |
+                                           (static_cast<uint64_t>(s.header[stage].mask[1]) << 32))
                                         : 0ull;
             if (p.radius >= 0) {
                 const int lo_col = max(0, query - p.radius - k0), hi_col = min(kKeyTile - 1, query + p.radius - k0);
                 active &= lo_col > hi_col ? 0ull : ((~0ull) >> (63 - (hi_col - lo_col))) << lo_col;
             }
             // TMEM S -> scaled score (FP16 storage: S is the plain dot product)
-            const float s_scale = kHalf ? p.scale : exp2_int(-(q_exponent + s.k_exponent[stage]));
-            const int v_exponent = kHalf ? 0 : s.v_exponent[stage];
+            const float s_scale = kHalf ? p.scale : exp2_int(-(q_exponent + s.header[stage].k_exponent));
+            const int v_exponent = kHalf ? 0 : s.header[stage].v_exponent;
             if constexpr (kStats) {
                 // S and the stage's mask and exponent are in registers: S(j + 2) may overwrite the
                 // buffer and the stage may be refilled. The MMA warp must have seen this tile's
@@ -914,12 +1081,25 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles>::kThreads, 1)
             // warp-collective, so the branch is taken by the whole warp (the explicit path is
             // exact for finite rows too).
             constexpr bool kPackedSplit = kHalf || D == 64 || F::kQTiles == 1;
+            RK_WARP_TRACE(j, 5);
             const float tile_sum = __all_sync(0xffffffffu, isfinite(offset) && slope > 0.f)
                                            ? exp_split_store<true, kHalf, kPackedSplit>(sc, slope, offset, pbuf)
                                            : exp_split_store<false, kHalf, kPackedSplit>(sc, slope, offset, pbuf);
             if constexpr (kHalf) row_sum = fmaf(row_sum, old_weight, tile_sum);  // kept in units of the new max
             RK_WARP_TRACE(j, 2);
-            if (j > 0) {  // fold tile j-1 before P(j).V overwrites its Ot
+            if constexpr (kPrepared) {
+                if (j > 0) {  // fold tile j-1 before P(j).V overwrites its Ot
+                    ok = __all_sync(0xffffffffu, mbar_wait(&s.pv_done[tile], (j - 1) & 1));
+                    if (!ok) {
+                        tmem_wait_store();  // no store may be in flight when TMEM is released
+                        break;
+                    }
+                    tc_fence_after();
+                    float ot[32], sum;
+                    tmem_load32_1(lane_base + F::kColO, ot, lane_base + F::kColSum, sum);
+                    fold_prepared(o, row_sum, o_exp, ot, sum, pending_weight, pending_exponent);
+                }
+            } else if (j > 0) {  // fold tile j-1 before P(j).V overwrites its Ot
                 ok = __all_sync(0xffffffffu, mbar_wait(&s.pv_done[tile], (j - 1) & 1));
                 if (!ok) {
                     tmem_wait_store();  // no store may be in flight when TMEM is released
@@ -943,7 +1123,15 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles>::kThreads, 1)
         if (!kStats && tiles > 0 && ok) {
             ok = __all_sync(0xffffffffu, mbar_wait(&s.pv_done[tile], (tiles - 1) & 1));
             tc_fence_after();
-            if (ok) fold_output<D, kHalf>(o, row_sum, o_exp, lane_base, pending_weight, pending_exponent);
+            if (ok) {
+                if constexpr (kPrepared) {
+                    float ot[32], sum;
+                    tmem_load32_1(lane_base + F::kColO, ot, lane_base + F::kColSum, sum);
+                    fold_prepared(o, row_sum, o_exp, ot, sum, pending_weight, pending_exponent);
+                } else {
+                    fold_output<D, kHalf>(o, row_sum, o_exp, lane_base, pending_weight, pending_exponent);
+                }
+            }
         }
         if (row_valid) {
             const float total = ok ? row_sum : NAN;
@@ -985,6 +1173,134 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles>::kThreads, 1)
     if (warp == 0) {
         tc_fence_after();
         tmem_dealloc(tmem, F::kTmemColumns);
+    }
+}
+
+// Operand pre-pass of the prepared d = 32 forward: one CTA of 256 threads per 64-key tile of one
+// (batch, head). It builds the tile's stage image as the forward's split warps build it in shared
+// memory -- keys that are masked or past the sequence zeroed with their mask bits clear; K and V
+// scaled by the powers of two that bring the tile's largest magnitudes into [2^14, 2^15) and split
+// into FP16 pairs (x0 rounded to nearest, x1 the rounded residual); K as [k0 | k1] rows, V as
+// v1^T / v0^T rows, 128B-swizzled -- and the tile's header. Each head's K and V are thus read and
+// split once, instead of once per query block.
+// Thread = (key row = thread / 4, features 8q .. 8q + 7 with q = thread % 4): warp g holds key rows
+// 8g .. 8g + 7, so the V^T chunk of feature f and key group g (V[8g .. 8g + 7][f]) is gathered by
+// an 8 x 8 register transpose among the warp's lanes with the same q.
+// kRotary: each K row is first rotated by its token's tables (rotate_pair, as rotate_row32 does in
+// the forward's split warps): features f and f + 16 sit in lanes q and q ^ 2 of the same row.
+constexpr int kPrepareThreads = 256;
+
+template <bool kRotary>
+__global__ void __launch_bounds__(kPrepareThreads) prepare_kv_kernel(const AttentionParams p, uint8_t *images, StageHeader *headers,
+                                                                     int tiles_per_head) {
+    grid_launch_dependents();  // the forward may be scheduled now; it waits for this grid to complete
+    __shared__ float warp_max[2][kPrepareThreads / 32];
+    __shared__ uint32_t mask_bits[2];
+    const long long tile = blockIdx.x;
+    const int t = static_cast<int>(tile % tiles_per_head);
+    const int bh = static_cast<int>(tile / tiles_per_head);
+    const int h = bh % p.heads, b = bh / p.heads;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const unsigned char *mask = p.mask + static_cast<long long>(b) * p.keys;
+    const int row = threadIdx.x >> 2, q = threadIdx.x & 3;
+    const int key = t * kKeyTile + row;
+    // The rows are read whether or not the mask shows the key (past the sequence: row 0), so that
+    // the loads do not wait for the mask byte; masked rows are zeroed afterwards.
+    const bool in_range = key < p.keys;
+    const int read_key = in_range ? key : 0;
+    const unsigned char key_byte = in_range ? mask[key] : 0;
+    const float4 *krow = reinterpret_cast<const float4 *>(p.k.row(b, h, read_key)) + 2 * q;
+    const float4 *vrow = reinterpret_cast<const float4 *>(p.v.row(b, h, read_key)) + 2 * q;
+    const float4 k0 = __ldg(krow), k1 = __ldg(krow + 1), v0 = __ldg(vrow), v1 = __ldg(vrow + 1);
+    float kx[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
+    float vx[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    if constexpr (kRotary) {
+        const float4 *c4 = reinterpret_cast<const float4 *>(p.cos_row(b, read_key)) + 2 * q;
+        const float4 *s4 = reinterpret_cast<const float4 *>(p.sin_row(b, read_key)) + 2 * q;
+        const float4 c0 = __ldg(c4), c1 = __ldg(c4 + 1), s0 = __ldg(s4), s1 = __ldg(s4 + 1);
+        const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+        const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+        const bool low = q < 2;  // features 8q.. are the low halves f of the pairs (f, f + 16)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const float partner = __shfl_xor_sync(0xffffffffu, kx[e], 2);
+            float out_lo, out_hi;
+            if (low)
+                rotate_pair<false>(kx[e], partner, cs[e], cs[e], sn[e], sn[e], out_lo, out_hi);
+            else
+                rotate_pair<false>(partner, kx[e], cs[e], cs[e], sn[e], sn[e], out_lo, out_hi);
+            kx[e] = low ? out_lo : out_hi;
+        }
+    }
+    const bool visible = in_range && key_byte != 0;
+    float kmax = 0.f, vmax = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        kx[e] = visible ? kx[e] : 0.f;
+        vx[e] = visible ? vx[e] : 0.f;
+        kmax = fmaxf(kmax, fabsf(kx[e]));
+        vmax = fmaxf(vmax, fabsf(vx[e]));
+    }
+#pragma unroll
+    for (int offset = 16; offset; offset >>= 1) {
+        kmax = fmaxf(kmax, __shfl_xor_sync(0xffffffffu, kmax, offset));
+        vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, offset));
+    }
+    if (lane == 0) {
+        warp_max[0][warp] = kmax;
+        warp_max[1][warp] = vmax;
+    }
+    if (warp < 2) {  // the tile's visible keys, 32 per warp
+        const int mkey = t * kKeyTile + threadIdx.x;
+        const uint32_t bits = __ballot_sync(0xffffffffu, mkey < p.keys && mask[mkey] != 0);
+        if (lane == 0) mask_bits[warp] = bits;
+    }
+    // V^T chunk of feature 8q + lane / 4 and key group `warp`: transpose the 8 x 8 block
+    // (row = lane / 4, element e) among the lanes with this q, three swap stages on lane bits 2-4.
+    const int r_local = lane >> 2;
+#pragma unroll
+    for (int m = 1; m < 8; m <<= 1) {
+        const bool upper = (r_local & m) != 0;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            if (e & m) continue;
+            const float send = upper ? vx[e] : vx[e | m];
+            const float received = __shfl_xor_sync(0xffffffffu, send, 4 * m);
+            if (upper)
+                vx[e] = received;
+            else
+                vx[e | m] = received;
+        }
+    }
+    __syncthreads();
+    float kmax_tile = warp_max[0][0], vmax_tile = warp_max[1][0];
+#pragma unroll
+    for (int w = 1; w < kPrepareThreads / 32; ++w) {
+        kmax_tile = fmaxf(kmax_tile, warp_max[0][w]);
+        vmax_tile = fmaxf(vmax_tile, warp_max[1][w]);
+    }
+    const int k_exponent = fp16_scale_exponent(kmax_tile), v_exponent = fp16_scale_exponent(vmax_tile);
+    uint8_t *image = images + tile * kImageBytes;
+    uint4 c0, c1;
+    // K row: features 8q..8q+7 -> chunk q of k0 and of k1 in the row layout
+    split_pack8<true>(kx, exp2_int(k_exponent), c0, c1);
+    uint32_t *k16 = reinterpret_cast<uint32_t *>(image);
+    *row_chunk<32>(k16, row, 0, q) = c0;
+    *row_chunk<32>(k16, row, 1, q) = c1;
+    // V^T rows f (v1) and 32 + f (v0), the order issue_values_prepared reads them in; the 16-byte
+    // chunk of key group g sits at position g ^ (f % 8) of its row.
+    const int f = 8 * q + r_local, position = warp ^ (f & 7);
+    split_pack8<true>(vx, exp2_int(v_exponent), c0, c1);
+    uint4 *vt16 = reinterpret_cast<uint4 *>(image + kImageKBytes);
+    vt16[(32 + f) * 8 + position] = c0;
+    vt16[f * 8 + position] = c1;
+    if (threadIdx.x == 0) {
+        StageHeader header;
+        header.mask[0] = mask_bits[0];
+        header.mask[1] = mask_bits[1];
+        header.k_exponent = k_exponent;
+        header.v_exponent = v_exponent;
+        headers[tile] = header;
     }
 }
 
@@ -1117,7 +1433,77 @@ int launch(const AttentionParams &p, cudaStream_t stream) {
     return launch_tiles<D, kHalf, kWidth, kRotary, Forward<D, kHalf>::kQTiles, kStats>(p, stream);
 }
 
+// Prepared d = 32 forward, one or two Q tiles per CTA (the same choice as launch()): the operand
+// pre-pass into `workspace`, then the forward as its programmatic dependent.
+template <int kTiles, bool kRotary>
+int launch_prepared_tiles(const AttentionParams &p, uint8_t *workspace, cudaStream_t stream) {
+    using F = Forward<32, false, kTiles, true>;
+    constexpr auto kernel = flash_forward_kernel<32, false, 32, kRotary, kTiles, false, true>;
+    constexpr int bytes = static_cast<int>(sizeof(SharedStorage<32, false, kTiles, true>)) + 1024;
+    static_assert(bytes <= 227 * 1024, "prepared stages fit in shared memory");
+    cudaError_t status = prepare_kernel<kernel>(bytes);
+    if (status != cudaSuccess) return status;
+    const int tiles_per_head = (p.keys + kKeyTile - 1) / kKeyTile;
+    const long long tiles = static_cast<long long>(p.batch) * p.heads * tiles_per_head;
+    StageHeader *headers = reinterpret_cast<StageHeader *>(workspace + tiles * kImageBytes);
+    prepare_kv_kernel<kRotary><<<static_cast<unsigned>(tiles), kPrepareThreads, 0, stream>>>(p, workspace, headers, tiles_per_head);
+    status = cudaGetLastError();
+    if (status != cudaSuccess) return status;
+    FlashArgs args{};
+    args.p = p;
+    args.rot_batch = p.rot_cb > 0 ? 1 : 0;
+    args.cta_per_head = (p.queries + F::kCtaQueries - 1) / F::kCtaQueries;
+    args.vec_out = (reinterpret_cast<uintptr_t>(p.o.data) & 15u) == 0 && p.o.sb % 4 == 0 && p.o.sh % 4 == 0 && p.o.st % 4 == 0;
+    args.images = workspace;
+    args.headers = headers;
+    args.tiles_per_head = tiles_per_head;
+    const CUtensorMap unused{};  // the prepared kernel reads no tensor map
+    cudaLaunchAttribute attribute{};
+    attribute.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attribute.val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t config{};
+    config.gridDim = dim3(static_cast<unsigned>(args.cta_per_head) * static_cast<unsigned>(p.heads) * static_cast<unsigned>(p.batch));
+    config.blockDim = dim3(F::kThreads);
+    config.dynamicSmemBytes = bytes;
+    config.stream = stream;
+    config.attrs = &attribute;
+    config.numAttrs = 1;
+    return cudaLaunchKernelEx(&config, kernel, args, unused, unused, unused, unused);
+}
+
+// The prepared d = 32 forward with its workspace from the library's scratch pool (scratch.h), given
+// back on the same stream after the kernels. kNotEligible when the problem is too large for one
+// pre-pass grid or the pool cannot supply the memory (the caller then runs the forward with split
+// warps, which needs no workspace).
+template <bool kRotary>
+int launch_prepared(const AttentionParams &p, cudaStream_t stream) {
+    const long long tiles = static_cast<long long>(p.batch) * p.heads * ((p.keys + kKeyTile - 1) / kKeyTile);
+    if (tiles <= 0 || tiles >= (1ll << 31)) return kNotEligible;
+    void *workspace = nullptr;
+    if (scratch_acquire(&workspace, static_cast<size_t>(prepared_forward_bytes(p.batch, p.heads, p.keys)), stream) != cudaSuccess) {
+        (void)cudaGetLastError();  // a failed pool allocation leaves no error behind for the next call
+        return kNotEligible;
+    }
+    int device = 0, sms = 0;
+    cudaError_t query = cudaGetDevice(&device);
+    if (query == cudaSuccess) query = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    int status = query;
+    if (query == cudaSuccess) {
+        const long long one_tile_ctas = static_cast<long long>((p.queries + kQTile - 1) / kQTile) * p.heads * p.batch;
+        uint8_t *base = static_cast<uint8_t *>(workspace);
+        status = one_tile_ctas <= sms ? launch_prepared_tiles<1, kRotary>(p, base, stream)
+                                      : launch_prepared_tiles<2, kRotary>(p, base, stream);
+    }
+    const cudaError_t released = scratch_release(workspace, stream);
+    return status != cudaSuccess ? status : released;
+}
+
 }  // namespace
+
+long long prepared_forward_bytes(int batch, int heads, int keys) {
+    const long long tiles = static_cast<long long>(batch) * heads * ((keys + kKeyTile - 1) / kKeyTile);
+    return tiles * (kImageBytes + static_cast<long long>(sizeof(StageHeader)));
+}
 
 bool flash_supported(const AttentionParams &p) {
     return p.vec4 && positive_tma_strides(p.k, 4) && positive_tma_strides(p.v, 4) && (p.q.st % 4 == 0) &&
@@ -1126,7 +1512,10 @@ bool flash_supported(const AttentionParams &p) {
 
 int launch_flash_forward(const AttentionParams &p, int head_width, cudaStream_t stream) {
     if (head_width == 16) return launch<32, false, 16>(p, stream);
-    if (head_width == 32) return launch<32, false>(p, stream);
+    if (head_width == 32) {
+        const int status = launch_prepared<false>(p, stream);
+        return status != kNotEligible ? status : launch<32, false>(p, stream);
+    }
     if (head_width == 64) return launch<64, false>(p, stream);
     return kNotEligible;
 }
@@ -1142,7 +1531,9 @@ int launch_flash_forward_rotary(const AttentionParams &p, cudaStream_t stream) {
         return (reinterpret_cast<uintptr_t>(t) & 15u) == 0 && sb % 4 == 0 && st % 4 == 0;
     };
     if (!aligned(p.rot_cos, p.rot_cb, p.rot_ct) || !aligned(p.rot_sin, p.rot_sb, p.rot_st)) return kNotEligible;
-    return launch<32, false, 32, true>(p, stream);
+    if ((p.rot_cb > 0) != (p.rot_sb > 0)) return kNotEligible;  // both tables per sequence, or both shared
+    const int status = launch_prepared<true>(p, stream);
+    return status != kNotEligible ? status : launch<32, false, 32, true>(p, stream);
 }
 
 bool half_flash_supported(const AttentionParams &p) {

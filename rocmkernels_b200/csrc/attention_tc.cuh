@@ -14,8 +14,14 @@ constexpr int kNotEligible = -1;
 // addressable Q rows).
 bool flash_supported(const AttentionParams &p);
 // Launches the tensor-core flash forward for head width 32 or 64 (16: the 32-wide kernel over
-// zero-filled features 16-31); returns a cudaError_t value or kNotEligible.
+// zero-filled features 16-31); returns a cudaError_t value or kNotEligible. Head width 32 runs the
+// prepared-operand forward (an operand pre-pass, then the forward) with a workspace of
+// prepared_forward_bytes from the library's scratch pool, or the forward with in-kernel split
+// warps when the pool cannot supply it.
 int launch_flash_forward(const AttentionParams &p, int head_width, cudaStream_t stream);
+// Workspace bytes of the prepared d = 32 forward: a 16 KB stage image and a 16-byte header per
+// 64-key tile of each (batch, head).
+long long prepared_forward_bytes(int batch, int heads, int keys);
 // The flash forward for head width 32 with the rotary prologue (q and k rotated by the tables in
 // p.rot_*, which must be 16-byte aligned with strides of 4 floats); cudaError_t or kNotEligible.
 int launch_flash_forward_rotary(const AttentionParams &p, cudaStream_t stream);

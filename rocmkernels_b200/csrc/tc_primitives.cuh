@@ -234,6 +234,22 @@ __device__ __forceinline__ void tmem_load16x2_1(uint32_t a, float (&va)[16], uin
     vc = __uint_as_float(r[32]);
 }
 
+// 32 columns at a and the single column b with one wait.
+__device__ __forceinline__ void tmem_load32_1(uint32_t a, float (&va)[32], uint32_t b, float &vb) {
+    uint32_t r[33];
+    asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+            "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%33];\n\t"
+            "tcgen05.ld.sync.aligned.32x32b.x1.b32 {%32}, [%34];\n\t"
+            "tcgen05.wait::ld.sync.aligned;"
+            : RK_R8(0), RK_R8(8), RK_R8(16), RK_R8(24), "=r"(r[32])
+            : "r"(a), "r"(b)
+            : "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) va[i] = __uint_as_float(r[i]);
+    vb = __uint_as_float(r[32]);
+}
+
 // 16 columns at a with one wait.
 __device__ __forceinline__ void tmem_load16(uint32_t a, float (&va)[16]) {
     uint32_t r[16];
@@ -504,6 +520,19 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_test_wait_warp(uint64_t *bar, uint32_t parity) {
     return __all_sync(0xffffffffu, mbar_test_wait(bar, parity));
 }
+
+// mbar_wait_sleep by every lane of a warp; true only if every lane saw the phase complete.
+__device__ __forceinline__ bool mbar_wait_sleep_warp(uint64_t *bar, uint32_t parity) {
+    return __all_sync(0xffffffffu, mbar_wait_sleep(bar, parity));
+}
+
+// Programmatic dependent launch. A grid launched with programmatic stream serialization may start
+// while the grid before it in the stream still runs; grid_dependency_wait() returns once that grid
+// has completed and its memory operations are visible (immediately for a grid launched without
+// the attribute). launch_dependents() lets the next such grid be scheduled once every CTA of this
+// grid has executed it or exited; it orders no memory (the dependent still waits for completion).
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 
 // Packs two FP32 values as FP16 (round to nearest): a in the low half, b in the high half (the
 // order a K-major fp16 operand stores consecutive elements in one 32-bit word).
