@@ -123,15 +123,18 @@ constexpr uint64_t kDescStep = 2;                      // one K=16 step of FP16 
 // kPrepared (split FP32, d = 32): K and V arrive already split, as the stage images that
 // prepare_kv_kernel wrote once per head (below); the CTA then has no split warps, and one MMA warp
 // per Q tile instead of one for both.
-template <int D, bool kHalf, int kTiles = !kHalf && D == 32 ? 2 : 1, bool kPrepared = false>
+// kRowThreads = 2 (prepared, one Q tile): two softmax threads per query row, each taking half of
+// every key tile and half of the output columns (8 softmax warps per Q tile), and two CTAs per SM.
+template <int D, bool kHalf, int kTiles = !kHalf && D == 32 ? 2 : 1, bool kPrepared = false, int kRowThreads = 1>
 struct Forward {
     static_assert(kTiles == 1 || (kTiles == 2 && !kHalf && D == 32), "two Q tiles per CTA: split FP32, d = 32");
     static_assert(!kPrepared || (!kHalf && D == 32), "prepared operands: split FP32, d = 32");
+    static_assert(kRowThreads == 1 || (kRowThreads == 2 && kPrepared && kTiles == 1), "two threads per row: prepared, one Q tile");
     static constexpr int kTerms = kHalf ? 1 : 2;  // FP16 terms per operand
     static constexpr int kQTiles = kTiles;
     static constexpr int kCtaQueries = kQTile * kQTiles;
     static constexpr int kStages = !kHalf && D == 32 ? 4 : 3;
-    static constexpr int kSoftmaxWarps = 4 * kQTiles;
+    static constexpr int kSoftmaxWarps = 4 * kQTiles * kRowThreads;
     static constexpr int kMmaWarps = kPrepared ? kQTiles : 1, kSplitWarps = kPrepared ? 0 : 2;
     static constexpr int kProducerWarp = kSoftmaxWarps, kMmaWarp = kSoftmaxWarps + 1, kSplitWarp = kMmaWarp + kMmaWarps;
     static constexpr int kThreads = 32 * (kSoftmaxWarps + 1 + kMmaWarps + kSplitWarps);
@@ -153,7 +156,8 @@ struct Forward {
     static constexpr uint32_t kColQ0 = 0, kColQ1 = D / 2, kColBuffer = kHalf ? 32 : D, kBufferColumns = 64,
                               kColO = kColBuffer + 128, kColSum = kColO + (kPrepared ? D : kTerms * D),
                               kColTile = kHalf || D == 32 ? 256 : 512;
-    static constexpr uint32_t kTmemColumns = kHalf ? 256 : 512;
+    // One prepared Q tile uses 208 columns: 256, so that two such CTAs share an SM's TMEM.
+    static constexpr uint32_t kTmemColumns = kHalf || (kPrepared && kQTiles == 1) ? 256 : 512;
     static constexpr uint64_t kDescStageK = (kHalf ? kRawFloats : kKWords) * 4 / 16, kDescStageV = kVWords * 4 / 16;
 };
 
@@ -171,9 +175,9 @@ struct alignas(16) StageHeader {
 constexpr int kImageKBytes = 64 * 2 * 32 * 2, kImageBytes = kImageKBytes + 64 * 128;
 
 // Operand tiles are rows of 128 bytes in 1024-byte aligned 8-row atoms (the 128B swizzle).
-template <int D, bool kHalf, int kTiles = Forward<D, kHalf>::kQTiles, bool kPrepared = false>
+template <int D, bool kHalf, int kTiles = Forward<D, kHalf>::kQTiles, bool kPrepared = false, int kRowThreads = 1>
 struct alignas(1024) SharedStorage {
-    using F = Forward<D, kHalf, kTiles, kPrepared>;
+    using F = Forward<D, kHalf, kTiles, kPrepared, kRowThreads>;
     // Raw tiles as TMA lands them (FP32: swizzled boxes of 64 x 32; FP16: 64 x 64); prepared
     // operands have none (a 1 KB placeholder keeps the layout below aligned).
     static constexpr int kRawStages = kPrepared ? 1 : F::kStages, kRawWords = kPrepared ? 256 : F::kRawFloats;
@@ -193,7 +197,11 @@ struct alignas(1024) SharedStorage {
     uint64_t s_full[F::kQTiles][2];            // S of a buffer is in TMEM (commit)
     uint64_t p_full[F::kQTiles];               // P of the current tile is in TMEM (128 arrivals)
     uint64_t pv_done[F::kQTiles];              // Ot of the current tile is in TMEM (commit)
-    uint64_t q_ready;                          // q0/q1 of every Q tile in TMEM (128 arrivals per tile)
+    uint64_t q_ready;                          // q0/q1 of every Q tile in TMEM (128 arrivals per tile and row thread)
+    // kRowThreads = 2: each thread's partial row max of a tile, [tile parity][half][row], and per
+    // lane quarter the barrier the quarter's two warps meet at once both halves are written.
+    float row_exchange[kRowThreads == 2 ? 2 : 1][kRowThreads][kRowThreads == 2 ? kQTile : 1];
+    uint64_t pair_bar[kRowThreads == 2 ? 4 : 1];
     uint64_t range_ready;                      // tile_count written (1 arrival)
     int tile_count;                            // key tiles up to the last visible key of the window
     uint64_t mma_done;                         // every MMA of the CTA finished (a commit per MMA warp)
@@ -304,7 +312,8 @@ __device__ __forceinline__ void issue_values_prepared(uint32_t tmem, uint64_t v_
 
 // Prepared operands, d = 32: folds a finished key tile's Ot (32 columns, V scaled by 2^c) and row
 // sum into the running output and sum, with the same exponent rule as fold_output.
-__device__ __forceinline__ void fold_prepared(float (&o)[32], float &row_sum, int &o_exp, const float (&ot)[32], float sum,
+template <int N>
+__device__ __forceinline__ void fold_prepared(float (&o)[N], float &row_sum, int &o_exp, const float (&ot)[N], float sum,
                                               float weight, int c) {
     if (o_exp == kNoExponent) o_exp = c;
     float out_weight = weight, tile_scale = 1.f;
@@ -318,7 +327,7 @@ __device__ __forceinline__ void fold_prepared(float (&o)[32], float &row_sum, in
     const float2 weight2 = make_float2(out_weight, out_weight);
     if (__all_sync(0xffffffffu, tile_scale == 1.f)) {  // uniform anyway
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
+        for (int i = 0; i < N; i += 2) {
             const float2 r = fma_f32x2(make_float2(o[i], o[i + 1]), weight2, make_float2(ot[i], ot[i + 1]));
             o[i] = r.x;
             o[i + 1] = r.y;
@@ -326,7 +335,7 @@ __device__ __forceinline__ void fold_prepared(float (&o)[32], float &row_sum, in
     } else {
         const float2 scale2 = make_float2(tile_scale, tile_scale);
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
+        for (int i = 0; i < N; i += 2) {
             const float2 u = mul_f32x2(make_float2(ot[i], ot[i + 1]), scale2);
             const float2 r = fma_f32x2(make_float2(o[i], o[i + 1]), weight2, u);
             o[i] = r.x;
@@ -419,11 +428,13 @@ __device__ __forceinline__ void fold_output(float (&o)[D], float &row_sum, int &
 // for two values). Used where registers allow: the split d = 32 kernel with two Q tiles (168
 // registers a thread) spills with it and is faster without (36.9 against 36.2 us at B8 H3 S1024);
 // d = 64 gains 8 %, the one-Q-tile d = 32 kernel 6-7 %.
-template <bool kPlain, bool kHalf, bool kPacked>
-__device__ __forceinline__ float exp_split_store(const float (&sc)[64], float slope, float offset, uint32_t pbuf) {
+// kValues = 32 (two threads per row): the 32 scores of this thread's half of the tile; pbuf then
+// addresses its 16 p0 columns (its p1 columns follow 32 columns further, as for a whole row).
+template <bool kPlain, bool kHalf, bool kPacked, int kValues = 64>
+__device__ __forceinline__ float exp_split_store(const float (&sc)[kValues], float slope, float offset, uint32_t pbuf) {
     float sum[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int chunk = 0; chunk < 4; ++chunk) {
+    for (int chunk = 0; chunk < kValues / 16; ++chunk) {
         float p0[8], p1[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -526,8 +537,8 @@ __device__ __forceinline__ void rotate_row32(float4 (&x)[8], const float4 (&cs)[
 // before it touches global memory (the TMEM allocation and the barrier set-up overlap the end of
 // the pre-pass).
 template <int D, bool kHalf, int kWidth = D, bool kRotary = false, int kTiles = Forward<D, kHalf>::kQTiles,
-          bool kStats = false, bool kPrepared = false>
-__global__ void __launch_bounds__(Forward<D, kHalf, kTiles, kPrepared>::kThreads, 1)
+          bool kStats = false, bool kPrepared = false, int kRowThreads = 1>
+__global__ void __launch_bounds__(Forward<D, kHalf, kTiles, kPrepared, kRowThreads>::kThreads, kRowThreads == 2 ? 2 : 1)
         flash_forward_kernel(const FlashArgs args, const __grid_constant__ CUtensorMap tmap_k,
                              const __grid_constant__ CUtensorMap tmap_v, const __grid_constant__ CUtensorMap tmap_cos,
                              const __grid_constant__ CUtensorMap tmap_sin) {
@@ -535,9 +546,10 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles, kPrepared>::kThreads
     static_assert(!kRotary || (D == 32 && kWidth == 32 && !kHalf), "the rotary prologue is defined for 32-wide FP32 heads");
     static_assert(!kStats || (D == 32 && kWidth == 32 && !kHalf && !kRotary), "statistics: 32-wide FP32 heads");
     static_assert(!kPrepared || (D == 32 && kWidth == 32 && !kHalf && !kStats), "prepared operands: the d = 32 split-FP32 forward");
-    using F = Forward<D, kHalf, kTiles, kPrepared>;
+    using F = Forward<D, kHalf, kTiles, kPrepared, kRowThreads>;
     // Prepared operands with the rotary prologue: K arrives rotated, so no table tiles are staged.
-    using Storage = std::conditional_t<kRotary && !kPrepared, RotaryStorage<D, kTiles>, SharedStorage<D, kHalf, kTiles, kPrepared>>;
+    using Storage = std::conditional_t<kRotary && !kPrepared, RotaryStorage<D, kTiles>,
+                                       SharedStorage<D, kHalf, kTiles, kPrepared, kRowThreads>>;
     constexpr int kStages = F::kStages;
     extern __shared__ uint8_t shared_raw[];
     Storage &s = *reinterpret_cast<Storage *>((reinterpret_cast<uintptr_t>(shared_raw) + 1023) & ~uintptr_t(1023));
@@ -573,7 +585,7 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles, kPrepared>::kThreads
     constexpr int kQChunks = kHalf ? D / 8 : D / 4;  // 16-byte chunks of a Q row
     uint4 q_chunks[kQChunks];
     float4 q_cos[kRotary ? 8 : 1], q_sin[kRotary ? 8 : 1];
-    const int query = q0 + (warp >> 2) * kQTile + (threadIdx.x & (kQTile - 1));  // softmax threads' row
+    const int query = q0 + (kRowThreads == 2 ? 0 : warp >> 2) * kQTile + (threadIdx.x & (kQTile - 1));  // softmax threads' row
     const bool row_valid = warp < F::kSoftmaxWarps && query < p.queries;
     {
         const uint4 *src = kHalf ? reinterpret_cast<const uint4 *>(p.q.row_as<__half>(b, h, row_valid ? query : 0))
@@ -637,10 +649,13 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles, kPrepared>::kThreads
         for (int t = 0; t < F::kQTiles; ++t) {
             mbar_init(&s.s_full[t][0], 1);
             mbar_init(&s.s_full[t][1], 1);
-            mbar_init(&s.p_full[t], kQTile);
+            mbar_init(&s.p_full[t], kQTile * kRowThreads);
             mbar_init(&s.pv_done[t], 1);
         }
-        mbar_init(&s.q_ready, kQTile * F::kQTiles);
+        mbar_init(&s.q_ready, kQTile * F::kQTiles * kRowThreads);
+        if constexpr (kRowThreads == 2) {
+            for (int quarter = 0; quarter < 4; ++quarter) mbar_init(&s.pair_bar[quarter], 64);
+        }
         mbar_init(&s.range_ready, 1);
         mbar_init(&s.mma_done, F::kMmaWarps);
         mbar_fence_init();
@@ -939,7 +954,8 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles, kPrepared>::kThreads
         }
     } else {
         // ---------------------------------------------------------------- softmax / epilogue
-        const int tile = warp >> 2;  // Q tile (0 = A, 1 = B)
+        const int tile = kRowThreads == 2 ? 0 : warp >> 2;  // Q tile (0 = A, 1 = B)
+        const int part = kRowThreads == 2 ? warp >> 2 : 0;  // two threads per row: this thread's half
         const int row_in_tile = threadIdx.x & (kQTile - 1);
         // query and row_valid: this thread's row, computed with the Q prefetch above
         const uint32_t lane_base = tmem_lane_address(tmem, warp) + tile * F::kColTile;
@@ -998,173 +1014,294 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles, kPrepared>::kThreads
                     packed0[c] = __uint_as_float(p0);
                     packed1[c] = __uint_as_float(p1);
                 }
-                tmem_store16x2(lane_base + F::kColQ0 + 16 * half, packed0, lane_base + F::kColQ1 + 16 * half, packed1);
+                if constexpr (kRowThreads == 2) {  // each of the row's two threads stores half the pairs
+                    if (part == 0)
+                        tmem_store8x2_async(lane_base + F::kColQ0, packed0, lane_base + F::kColQ1, packed1);
+                    else
+                        tmem_store8x2_async(lane_base + F::kColQ0 + 8, packed0 + 8, lane_base + F::kColQ1 + 8, packed1 + 8);
+                    tmem_wait_store();
+                } else {
+                    tmem_store16x2(lane_base + F::kColQ0 + 16 * half, packed0, lane_base + F::kColQ1 + 16 * half, packed1);
+                }
             }
             tc_fence_before();
             mbar_arrive(&s.q_ready);
         }
 
-        float row_max = -INFINITY, row_sum = 0.f;  // row_sum carries the 2^14 of P
-        float o[D];                                // running output, scaled by 2^o_exp
+        if constexpr (kRowThreads == 2) {
+            // Two threads per row: this thread takes keys 32 part .. 32 part + 31 of every tile and
+            // output columns 16 part .. 16 part + 15. The row's two threads (warps w and w + 4, the
+            // same TMEM lanes) exchange their partial row max each tile through shared memory and
+            // keep the same row max, sum and exponent (both read the row-sum column).
+            const int quarter = warp & 3;
+            float row_max = -INFINITY, row_sum = 0.f;  // row_sum carries the 2^14 of P
+            float o[16];                               // this thread's output columns, scaled by 2^o_exp
 #pragma unroll
-        for (int c = 0; c < D; ++c) o[c] = 0.f;
-        int o_exp = kNoExponent;
-        float pending_weight = 0.f;  // exp(m_(j-2) - m_(j-1)), applied when tile j-1 is folded
-        int pending_exponent = 0;    // c_(j-1): the V exponent of tile j-1
-        bool ok = true;
-        const int tiles = __shfl_sync(0xffffffffu, visible_tiles(), 0);
-        for (int j = 0; j < tiles && ok; ++j) {
-            const int stage = j % kStages, use = j / kStages, buffer = j & 1;
-            const uint32_t pbuf = lane_base + F::kColBuffer + buffer * F::kBufferColumns;
-            // The stage's header: converted by the split warps (kv_ready), or landed with the
-            // prepared image (kv_full).
-            ok = __all_sync(0xffffffffu, mbar_wait(&s.s_full[tile][buffer], (j >> 1) & 1) &&
-                                                 mbar_wait(kPrepared ? &s.kv_full[stage] : &s.kv_ready[stage], use & 1));
-            if (!ok) break;
-            tc_fence_after();
-            float sc[64];
-            tmem_load64(pbuf, sc);
-            if (tracer) RK_TRACE(j, 4 + 4 * tile);
-            RK_WARP_TRACE(j, 0);
-            // Visible keys of this row in the tile: key mask x radius window x valid row.
-            const int k0 = first + j * kKeyTile;
-            uint64_t active = row_valid ? (static_cast<uint64_t>(s.header[stage].mask[0]) |
-                                           (static_cast<uint64_t>(s.header[stage].mask[1]) << 32))
-                                        : 0ull;
-            if (p.radius >= 0) {
-                const int lo_col = max(0, query - p.radius - k0), hi_col = min(kKeyTile - 1, query + p.radius - k0);
-                active &= lo_col > hi_col ? 0ull : ((~0ull) >> (63 - (hi_col - lo_col))) << lo_col;
-            }
-            // TMEM S -> scaled score (FP16 storage: S is the plain dot product)
-            const float s_scale = kHalf ? p.scale : exp2_int(-(q_exponent + s.header[stage].k_exponent));
-            const int v_exponent = kHalf ? 0 : s.header[stage].v_exponent;
-            if constexpr (kStats) {
-                // S and the stage's mask and exponent are in registers: S(j + 2) may overwrite the
-                // buffer and the stage may be refilled. The MMA warp must have seen this tile's
-                // release of buffer j - 1 before this arrival (two arrivals it has not seen would
-                // complete two phases of p_full, which its parity wait cannot tell from none); it
-                // issues S(j + 1) only after seeing that release, so wait for S(j + 1) first.
-                if (j + 1 < tiles)
-                    ok = __all_sync(0xffffffffu, mbar_wait(&s.s_full[tile][buffer ^ 1], ((j + 1) >> 1) & 1));
+            for (int c = 0; c < 16; ++c) o[c] = 0.f;
+            int o_exp = kNoExponent;
+            float pending_weight = 0.f;
+            int pending_exponent = 0;
+            bool ok = true;
+            const int tiles = __shfl_sync(0xffffffffu, visible_tiles(), 0);
+            for (int j = 0; j < tiles && ok; ++j) {
+                const int stage = j % kStages, use = j / kStages, buffer = j & 1;
+                const uint32_t pbuf = lane_base + F::kColBuffer + buffer * F::kBufferColumns;
+                ok = __all_sync(0xffffffffu, mbar_wait(&s.s_full[0][buffer], (j >> 1) & 1) && mbar_wait(&s.kv_full[stage], use & 1));
                 if (!ok) break;
-                tc_fence_before();
-                mbar_arrive(&s.p_full[tile]);
-            }
-            // Row max (four independent three-input max chains).
-            if (active != ~0ull) {
+                if (tracer && part == 0) RK_TRACE(j, 4);
+                tc_fence_after();
+                float sc[32];
+                tmem_load32(pbuf + 32 * part, sc);
+                const int k0 = first + j * kKeyTile + 32 * part;
+                uint32_t active = row_valid ? s.header[stage].mask[part] : 0u;
+                if (p.radius >= 0) {
+                    const int lo_col = max(0, query - p.radius - k0), hi_col = min(31, query + p.radius - k0);
+                    active &= lo_col > hi_col ? 0u : ((~0u) >> (31 - (hi_col - lo_col))) << lo_col;
+                }
+                const float s_scale = exp2_int(-(q_exponent + s.header[stage].k_exponent));
+                const int v_exponent = s.header[stage].v_exponent;
+                if (active != ~0u) {
 #pragma unroll
-                for (int c = 0; c < 64; ++c) sc[c] = (active >> c) & 1 ? sc[c] : -INFINITY;
-            }
-            float partial_max[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+                    for (int c = 0; c < 32; ++c) sc[c] = (active >> c) & 1 ? sc[c] : -INFINITY;
+                }
+                float partial_max[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-            for (int c = 0; c < 64; c += 2) partial_max[(c >> 1) & 3] = max3(partial_max[(c >> 1) & 3], sc[c], sc[c + 1]);
-            const float raw_max = max3(partial_max[0], partial_max[1], fmaxf(partial_max[2], partial_max[3]));
-            const float tile_max = raw_max == -INFINITY ? -INFINITY : raw_max * s_scale;
-            if (tracer) RK_TRACE(j, 5 + 4 * tile);
-            RK_WARP_TRACE(j, 1);
-            const float next = fmaxf(row_max, tile_max);
-            const float old_weight = isfinite(row_max) ? fast_exp2((row_max - next) * kLog2e) : 0.f;
-            const float slope = s_scale * kLog2e;
-            const float offset = fmaf(-next, kLog2e, 14.f);  // P' = 2^14 exp(S - max) = exp2(S * slope + offset)
-            if constexpr (kStats) {
-                // Statistics only: the row sum of P' in FP32, no P, no output.
-                float partial[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-                for (int c = 0; c < 64; ++c)
-                    partial[c & 3] += sc[c] == -INFINITY ? 0.f : fast_exp2(fmaf(sc[c], slope, offset));
-                row_sum = fmaf(row_sum, old_weight, (partial[0] + partial[1]) + (partial[2] + partial[3]));
-                row_max = next;
-                continue;
-            }
-            // P(j) may be written before Ot(j - 1) is folded: only the p_full arrival below lets
-            // the MMA warp start P(j).V, which overwrites Ot. The TMEM stores inside are
-            // warp-collective, so the branch is taken by the whole warp (the explicit path is
-            // exact for finite rows too).
-            constexpr bool kPackedSplit = kHalf || D == 64 || F::kQTiles == 1;
-            RK_WARP_TRACE(j, 5);
-            const float tile_sum = __all_sync(0xffffffffu, isfinite(offset) && slope > 0.f)
-                                           ? exp_split_store<true, kHalf, kPackedSplit>(sc, slope, offset, pbuf)
-                                           : exp_split_store<false, kHalf, kPackedSplit>(sc, slope, offset, pbuf);
-            if constexpr (kHalf) row_sum = fmaf(row_sum, old_weight, tile_sum);  // kept in units of the new max
-            RK_WARP_TRACE(j, 2);
-            if constexpr (kPrepared) {
+                for (int c = 0; c < 32; c += 2) partial_max[(c >> 1) & 3] = max3(partial_max[(c >> 1) & 3], sc[c], sc[c + 1]);
+                const float half_max = max3(partial_max[0], partial_max[1], fmaxf(partial_max[2], partial_max[3]));
+                // The other half's maximum: written for tile parity j & 1, read after both threads of
+                // the quarter arrived (a thread rewrites this slot only two tiles later, after the
+                // next meeting, which needs the partner's arrival after its read).
+                s.row_exchange[j & 1][part][row_in_tile] = half_max;
+                mbar_arrive(&s.pair_bar[quarter]);
+                ok = __all_sync(0xffffffffu, mbar_wait(&s.pair_bar[quarter], j & 1));
+                if (!ok) break;
+                const float raw_max = fmaxf(half_max, s.row_exchange[j & 1][part ^ 1][row_in_tile]);
+                const float tile_max = raw_max == -INFINITY ? -INFINITY : raw_max * s_scale;
+                if (tracer && part == 0) RK_TRACE(j, 5);
+                const float next = fmaxf(row_max, tile_max);
+                const float old_weight = isfinite(row_max) ? fast_exp2((row_max - next) * kLog2e) : 0.f;
+                const float slope = s_scale * kLog2e;
+                const float offset = fmaf(-next, kLog2e, 14.f);  // P' = 2^14 exp(S - max) = exp2(S * slope + offset)
+                // P(j) may be written before Ot(j - 1) is folded: only the p_full arrival below lets
+                // the MMA warp start P(j).V, which overwrites Ot.
+                const uint32_t pcols = pbuf + 16 * part;
+                if (__all_sync(0xffffffffu, isfinite(offset) && slope > 0.f))
+                    exp_split_store<true, false, true, 32>(sc, slope, offset, pcols);
+                else
+                    exp_split_store<false, false, true, 32>(sc, slope, offset, pcols);
                 if (j > 0) {  // fold tile j-1 before P(j).V overwrites its Ot
+                    ok = __all_sync(0xffffffffu, mbar_wait(&s.pv_done[0], (j - 1) & 1));
+                    if (!ok) {
+                        tmem_wait_store();  // no store may be in flight when TMEM is released
+                        break;
+                    }
+                    tc_fence_after();
+                    float ot[16], sum;
+                    tmem_load16_1(lane_base + F::kColO + 16 * part, ot, lane_base + F::kColSum, sum);
+                    fold_prepared<16>(o, row_sum, o_exp, ot, sum, pending_weight, pending_exponent);
+                }
+                tmem_wait_store();
+                tc_fence_before();
+                if (tracer && part == 0) RK_TRACE(j, 6);
+                mbar_arrive(&s.p_full[0]);
+                row_max = next;
+                pending_weight = old_weight;
+                pending_exponent = v_exponent;
+            }
+            // Epilogue (AttentionFlash32.h:157-169): O / total; fully masked rows give 0 and {-inf, 0}.
+            if (tiles > 0 && ok) {
+                ok = __all_sync(0xffffffffu, mbar_wait(&s.pv_done[0], (tiles - 1) & 1));
+                tc_fence_after();
+                if (ok) {
+                    float ot[16], sum;
+                    tmem_load16_1(lane_base + F::kColO + 16 * part, ot, lane_base + F::kColSum, sum);
+                    fold_prepared<16>(o, row_sum, o_exp, ot, sum, pending_weight, pending_exponent);
+                }
+            }
+            if (row_valid) {
+                const float total = ok ? row_sum : NAN;
+                const bool nan_out = isnan(total) && !p.zero_nan_rows;
+                const float out_scale = exp2_int(-o_exp) / total;
+#pragma unroll
+                for (int c = 0; c < 16; ++c) o[c] = total > 0.f ? o[c] * out_scale : nan_out ? NAN : 0.f;
+                float *out = p.o.row(b, h, query) + 16 * part;
+                if (args.vec_out) {
+#pragma unroll
+                    for (int c = 0; c < 4; ++c)
+                        reinterpret_cast<float4 *>(out)[c] = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+                } else {
+#pragma unroll
+                    for (int c = 0; c < 16; ++c) out[c] = o[c];
+                }
+                if (part == 0) {
+                    const long long row = (static_cast<long long>(b) * p.heads + h) * p.queries + query;
+                    p.lse[row * 2] = total > 0.f ? row_max : nan_out ? NAN : -INFINITY;
+                    p.lse[row * 2 + 1] = total > 0.f ? total * (1.f / kPScale) : nan_out ? NAN : 0.f;
+                }
+            }
+        } else {
+            float row_max = -INFINITY, row_sum = 0.f;  // row_sum carries the 2^14 of P
+            float o[D];                                // running output, scaled by 2^o_exp
+    #pragma unroll
+            for (int c = 0; c < D; ++c) o[c] = 0.f;
+            int o_exp = kNoExponent;
+            float pending_weight = 0.f;  // exp(m_(j-2) - m_(j-1)), applied when tile j-1 is folded
+            int pending_exponent = 0;    // c_(j-1): the V exponent of tile j-1
+            bool ok = true;
+            const int tiles = __shfl_sync(0xffffffffu, visible_tiles(), 0);
+            for (int j = 0; j < tiles && ok; ++j) {
+                const int stage = j % kStages, use = j / kStages, buffer = j & 1;
+                const uint32_t pbuf = lane_base + F::kColBuffer + buffer * F::kBufferColumns;
+                // The stage's header: converted by the split warps (kv_ready), or landed with the
+                // prepared image (kv_full).
+                ok = __all_sync(0xffffffffu, mbar_wait(&s.s_full[tile][buffer], (j >> 1) & 1) &&
+                                                     mbar_wait(kPrepared ? &s.kv_full[stage] : &s.kv_ready[stage], use & 1));
+                if (!ok) break;
+                tc_fence_after();
+                float sc[64];
+                tmem_load64(pbuf, sc);
+                if (tracer) RK_TRACE(j, 4 + 4 * tile);
+                RK_WARP_TRACE(j, 0);
+                // Visible keys of this row in the tile: key mask x radius window x valid row.
+                const int k0 = first + j * kKeyTile;
+                uint64_t active = row_valid ? (static_cast<uint64_t>(s.header[stage].mask[0]) |
+                                               (static_cast<uint64_t>(s.header[stage].mask[1]) << 32))
+                                            : 0ull;
+                if (p.radius >= 0) {
+                    const int lo_col = max(0, query - p.radius - k0), hi_col = min(kKeyTile - 1, query + p.radius - k0);
+                    active &= lo_col > hi_col ? 0ull : ((~0ull) >> (63 - (hi_col - lo_col))) << lo_col;
+                }
+                // TMEM S -> scaled score (FP16 storage: S is the plain dot product)
+                const float s_scale = kHalf ? p.scale : exp2_int(-(q_exponent + s.header[stage].k_exponent));
+                const int v_exponent = kHalf ? 0 : s.header[stage].v_exponent;
+                if constexpr (kStats) {
+                    // S and the stage's mask and exponent are in registers: S(j + 2) may overwrite the
+                    // buffer and the stage may be refilled. The MMA warp must have seen this tile's
+                    // release of buffer j - 1 before this arrival (two arrivals it has not seen would
+                    // complete two phases of p_full, which its parity wait cannot tell from none); it
+                    // issues S(j + 1) only after seeing that release, so wait for S(j + 1) first.
+                    if (j + 1 < tiles)
+                        ok = __all_sync(0xffffffffu, mbar_wait(&s.s_full[tile][buffer ^ 1], ((j + 1) >> 1) & 1));
+                    if (!ok) break;
+                    tc_fence_before();
+                    mbar_arrive(&s.p_full[tile]);
+                }
+                // Row max (four independent three-input max chains).
+                if (active != ~0ull) {
+    #pragma unroll
+                    for (int c = 0; c < 64; ++c) sc[c] = (active >> c) & 1 ? sc[c] : -INFINITY;
+                }
+                float partial_max[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    #pragma unroll
+                for (int c = 0; c < 64; c += 2) partial_max[(c >> 1) & 3] = max3(partial_max[(c >> 1) & 3], sc[c], sc[c + 1]);
+                const float raw_max = max3(partial_max[0], partial_max[1], fmaxf(partial_max[2], partial_max[3]));
+                const float tile_max = raw_max == -INFINITY ? -INFINITY : raw_max * s_scale;
+                if (tracer) RK_TRACE(j, 5 + 4 * tile);
+                RK_WARP_TRACE(j, 1);
+                const float next = fmaxf(row_max, tile_max);
+                const float old_weight = isfinite(row_max) ? fast_exp2((row_max - next) * kLog2e) : 0.f;
+                const float slope = s_scale * kLog2e;
+                const float offset = fmaf(-next, kLog2e, 14.f);  // P' = 2^14 exp(S - max) = exp2(S * slope + offset)
+                if constexpr (kStats) {
+                    // Statistics only: the row sum of P' in FP32, no P, no output.
+                    float partial[4] = {0.f, 0.f, 0.f, 0.f};
+    #pragma unroll
+                    for (int c = 0; c < 64; ++c)
+                        partial[c & 3] += sc[c] == -INFINITY ? 0.f : fast_exp2(fmaf(sc[c], slope, offset));
+                    row_sum = fmaf(row_sum, old_weight, (partial[0] + partial[1]) + (partial[2] + partial[3]));
+                    row_max = next;
+                    continue;
+                }
+                // P(j) may be written before Ot(j - 1) is folded: only the p_full arrival below lets
+                // the MMA warp start P(j).V, which overwrites Ot. The TMEM stores inside are
+                // warp-collective, so the branch is taken by the whole warp (the explicit path is
+                // exact for finite rows too).
+                constexpr bool kPackedSplit = kHalf || D == 64 || F::kQTiles == 1;
+                RK_WARP_TRACE(j, 5);
+                const float tile_sum = __all_sync(0xffffffffu, isfinite(offset) && slope > 0.f)
+                                               ? exp_split_store<true, kHalf, kPackedSplit>(sc, slope, offset, pbuf)
+                                               : exp_split_store<false, kHalf, kPackedSplit>(sc, slope, offset, pbuf);
+                if constexpr (kHalf) row_sum = fmaf(row_sum, old_weight, tile_sum);  // kept in units of the new max
+                RK_WARP_TRACE(j, 2);
+                if constexpr (kPrepared) {
+                    if (j > 0) {  // fold tile j-1 before P(j).V overwrites its Ot
+                        ok = __all_sync(0xffffffffu, mbar_wait(&s.pv_done[tile], (j - 1) & 1));
+                        if (!ok) {
+                            tmem_wait_store();  // no store may be in flight when TMEM is released
+                            break;
+                        }
+                        tc_fence_after();
+                        float ot[32], sum;
+                        tmem_load32_1(lane_base + F::kColO, ot, lane_base + F::kColSum, sum);
+                        fold_prepared(o, row_sum, o_exp, ot, sum, pending_weight, pending_exponent);
+                    }
+                } else if (j > 0) {  // fold tile j-1 before P(j).V overwrites its Ot
                     ok = __all_sync(0xffffffffu, mbar_wait(&s.pv_done[tile], (j - 1) & 1));
                     if (!ok) {
                         tmem_wait_store();  // no store may be in flight when TMEM is released
                         break;
                     }
                     tc_fence_after();
-                    float ot[32], sum;
-                    tmem_load32_1(lane_base + F::kColO, ot, lane_base + F::kColSum, sum);
-                    fold_prepared(o, row_sum, o_exp, ot, sum, pending_weight, pending_exponent);
-                }
-            } else if (j > 0) {  // fold tile j-1 before P(j).V overwrites its Ot
-                ok = __all_sync(0xffffffffu, mbar_wait(&s.pv_done[tile], (j - 1) & 1));
-                if (!ok) {
-                    tmem_wait_store();  // no store may be in flight when TMEM is released
-                    break;
-                }
-                tc_fence_after();
-                fold_output<D, kHalf>(o, row_sum, o_exp, lane_base, pending_weight, pending_exponent);
-            }
-            RK_WARP_TRACE(j, 3);
-            tmem_wait_store();
-            RK_WARP_TRACE(j, 4);
-            tc_fence_before();
-            if (tracer) RK_TRACE(j, 6 + 4 * tile);
-            mbar_arrive(&s.p_full[tile]);
-            row_max = next;
-            pending_weight = old_weight;
-            pending_exponent = v_exponent;
-        }
-
-        // Epilogue (AttentionFlash32.h:157-169): O / total; fully masked rows give 0 and {-inf, 0}.
-        if (!kStats && tiles > 0 && ok) {
-            ok = __all_sync(0xffffffffu, mbar_wait(&s.pv_done[tile], (tiles - 1) & 1));
-            tc_fence_after();
-            if (ok) {
-                if constexpr (kPrepared) {
-                    float ot[32], sum;
-                    tmem_load32_1(lane_base + F::kColO, ot, lane_base + F::kColSum, sum);
-                    fold_prepared(o, row_sum, o_exp, ot, sum, pending_weight, pending_exponent);
-                } else {
                     fold_output<D, kHalf>(o, row_sum, o_exp, lane_base, pending_weight, pending_exponent);
                 }
+                RK_WARP_TRACE(j, 3);
+                tmem_wait_store();
+                RK_WARP_TRACE(j, 4);
+                tc_fence_before();
+                if (tracer) RK_TRACE(j, 6 + 4 * tile);
+                mbar_arrive(&s.p_full[tile]);
+                row_max = next;
+                pending_weight = old_weight;
+                pending_exponent = v_exponent;
             }
-        }
-        if (row_valid) {
-            const float total = ok ? row_sum : NAN;
-            const bool nan_out = isnan(total) && !p.zero_nan_rows;
-            const float out_scale = exp2_int(-o_exp) / total;
-#pragma unroll
-            for (int c = 0; c < D; ++c) o[c] = total > 0.f ? o[c] * out_scale : nan_out ? NAN : 0.f;
-            if constexpr (kHalf) {
-                __half *out = p.o.row_as<__half>(b, h, query);
-                if (args.vec_out) {
-#pragma unroll
-                    for (int c = 0; c < D / 8; ++c)
-                        reinterpret_cast<uint4 *>(out)[c] =
-                                make_uint4(pack_half2(o[8 * c], o[8 * c + 1]), pack_half2(o[8 * c + 2], o[8 * c + 3]),
-                                           pack_half2(o[8 * c + 4], o[8 * c + 5]), pack_half2(o[8 * c + 6], o[8 * c + 7]));
-                } else {
-#pragma unroll
-                    for (int c = 0; c < D; ++c) out[c] = __float2half_rn(o[c]);
-                }
-            } else if constexpr (!kStats) {  // statistics: no output rows
-                float *out = p.o.row(b, h, query);
-                if (args.vec_out) {
-#pragma unroll
-                    for (int c = 0; c < kWidth / 4; ++c)
-                        reinterpret_cast<float4 *>(out)[c] = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
-                } else {
-#pragma unroll
-                    for (int c = 0; c < kWidth; ++c) out[c] = o[c];
+
+            // Epilogue (AttentionFlash32.h:157-169): O / total; fully masked rows give 0 and {-inf, 0}.
+            if (!kStats && tiles > 0 && ok) {
+                ok = __all_sync(0xffffffffu, mbar_wait(&s.pv_done[tile], (tiles - 1) & 1));
+                tc_fence_after();
+                if (ok) {
+                    if constexpr (kPrepared) {
+                        float ot[32], sum;
+                        tmem_load32_1(lane_base + F::kColO, ot, lane_base + F::kColSum, sum);
+                        fold_prepared(o, row_sum, o_exp, ot, sum, pending_weight, pending_exponent);
+                    } else {
+                        fold_output<D, kHalf>(o, row_sum, o_exp, lane_base, pending_weight, pending_exponent);
+                    }
                 }
             }
-            const long long row = (static_cast<long long>(b) * p.heads + h) * p.queries + query;
-            p.lse[row * 2] = total > 0.f ? row_max : nan_out ? NAN : -INFINITY;
-            p.lse[row * 2 + 1] = total > 0.f ? total * (1.f / kPScale) : nan_out ? NAN : 0.f;
+            if (row_valid) {
+                const float total = ok ? row_sum : NAN;
+                const bool nan_out = isnan(total) && !p.zero_nan_rows;
+                const float out_scale = exp2_int(-o_exp) / total;
+    #pragma unroll
+                for (int c = 0; c < D; ++c) o[c] = total > 0.f ? o[c] * out_scale : nan_out ? NAN : 0.f;
+                if constexpr (kHalf) {
+                    __half *out = p.o.row_as<__half>(b, h, query);
+                    if (args.vec_out) {
+    #pragma unroll
+                        for (int c = 0; c < D / 8; ++c)
+                            reinterpret_cast<uint4 *>(out)[c] =
+                                    make_uint4(pack_half2(o[8 * c], o[8 * c + 1]), pack_half2(o[8 * c + 2], o[8 * c + 3]),
+                                               pack_half2(o[8 * c + 4], o[8 * c + 5]), pack_half2(o[8 * c + 6], o[8 * c + 7]));
+                    } else {
+    #pragma unroll
+                        for (int c = 0; c < D; ++c) out[c] = __float2half_rn(o[c]);
+                    }
+                } else if constexpr (!kStats) {  // statistics: no output rows
+                    float *out = p.o.row(b, h, query);
+                    if (args.vec_out) {
+    #pragma unroll
+                        for (int c = 0; c < kWidth / 4; ++c)
+                            reinterpret_cast<float4 *>(out)[c] = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+                    } else {
+    #pragma unroll
+                        for (int c = 0; c < kWidth; ++c) out[c] = o[c];
+                    }
+                }
+                const long long row = (static_cast<long long>(b) * p.heads + h) * p.queries + query;
+                p.lse[row * 2] = total > 0.f ? row_max : nan_out ? NAN : -INFINITY;
+                p.lse[row * 2 + 1] = total > 0.f ? total * (1.f / kPScale) : nan_out ? NAN : 0.f;
+            }
         }
     }
 
@@ -1435,11 +1572,11 @@ int launch(const AttentionParams &p, cudaStream_t stream) {
 
 // Prepared d = 32 forward, one or two Q tiles per CTA (the same choice as launch()): the operand
 // pre-pass into `workspace`, then the forward as its programmatic dependent.
-template <int kTiles, bool kRotary>
+template <int kTiles, bool kRotary, int kRowThreads = 1>
 int launch_prepared_tiles(const AttentionParams &p, uint8_t *workspace, cudaStream_t stream) {
-    using F = Forward<32, false, kTiles, true>;
-    constexpr auto kernel = flash_forward_kernel<32, false, 32, kRotary, kTiles, false, true>;
-    constexpr int bytes = static_cast<int>(sizeof(SharedStorage<32, false, kTiles, true>)) + 1024;
+    using F = Forward<32, false, kTiles, true, kRowThreads>;
+    constexpr auto kernel = flash_forward_kernel<32, false, 32, kRotary, kTiles, false, true, kRowThreads>;
+    constexpr int bytes = static_cast<int>(sizeof(SharedStorage<32, false, kTiles, true, kRowThreads>)) + 1024;
     static_assert(bytes <= 227 * 1024, "prepared stages fit in shared memory");
     cudaError_t status = prepare_kernel<kernel>(bytes);
     if (status != cudaSuccess) return status;
@@ -1491,8 +1628,17 @@ int launch_prepared(const AttentionParams &p, cudaStream_t stream) {
     if (query == cudaSuccess) {
         const long long one_tile_ctas = static_cast<long long>((p.queries + kQTile - 1) / kQTile) * p.heads * p.batch;
         uint8_t *base = static_cast<uint8_t *>(workspace);
-        status = one_tile_ctas <= sms ? launch_prepared_tiles<1, kRotary>(p, base, stream)
-                                      : launch_prepared_tiles<2, kRotary>(p, base, stream);
+        // CTA form by grid size (measured on B200, us per launch, flushed): a grid of one-tile CTAs
+        // that fills two CTAs per SM runs two threads per row (B4 H12 S4096 543 -> 506, C4-shaped
+        // 187 -> 166); below that one thread per row, one Q tile per CTA when that grid fits in one
+        // wave, else two (B8 H3 S1024: 37.1 against 39.2 with two threads per row; B1 H8 S2048
+        // 45.3 against 59.6).
+        if (!kRotary && one_tile_ctas >= 2ll * sms)
+            status = launch_prepared_tiles<1, false, 2>(p, base, stream);
+        else if (one_tile_ctas <= sms)
+            status = launch_prepared_tiles<1, kRotary>(p, base, stream);
+        else
+            status = launch_prepared_tiles<2, kRotary>(p, base, stream);
     }
     const cudaError_t released = scratch_release(workspace, stream);
     return status != cudaSuccess ? status : released;

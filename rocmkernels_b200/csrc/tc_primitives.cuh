@@ -250,6 +250,35 @@ __device__ __forceinline__ void tmem_load32_1(uint32_t a, float (&va)[32], uint3
     vb = __uint_as_float(r[32]);
 }
 
+// 16 columns at a and the single column b with one wait.
+__device__ __forceinline__ void tmem_load16_1(uint32_t a, float (&va)[16], uint32_t b, float &vb) {
+    uint32_t r[17];
+    asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%17];\n\t"
+            "tcgen05.ld.sync.aligned.32x32b.x1.b32 {%16}, [%18];\n\t"
+            "tcgen05.wait::ld.sync.aligned;"
+            : RK_R8(0), RK_R8(8), "=r"(r[16])
+            : "r"(a), "r"(b)
+            : "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) va[i] = __uint_as_float(r[i]);
+    vb = __uint_as_float(r[16]);
+}
+
+// 32 columns at a with one wait.
+__device__ __forceinline__ void tmem_load32(uint32_t a, float (&va)[32]) {
+    uint32_t r[32];
+    asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+            "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
+            "tcgen05.wait::ld.sync.aligned;"
+            : RK_R8(0), RK_R8(8), RK_R8(16), RK_R8(24)
+            : "r"(a)
+            : "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) va[i] = __uint_as_float(r[i]);
+}
+
 // 16 columns at a with one wait.
 __device__ __forceinline__ void tmem_load16(uint32_t a, float (&va)[16]) {
     uint32_t r[16];

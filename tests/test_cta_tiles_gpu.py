@@ -1,7 +1,9 @@
 """The d = 32 split-FP32 flash forward runs 128-query CTAs when that grid fits in one wave (at most
-one CTA per SM) and 256-query CTAs (two Q tiles sharing each K/V tile) otherwise. The shapes here
-sit just below and just above that threshold, computed from the device's SM count, so both CTA
-shapes are checked. Entries: attention_fp32_forward_flash (the plain kernel), the fused rotary
+one CTA per SM), 256-query CTAs (two Q tiles sharing each K/V tile) above that, and -- when the
+grid of 128-query CTAs fills two per SM -- 128-query CTAs with two threads per query row, two CTAs
+per SM (not with the rotary prologue). The shapes here sit just below and just above the one-wave
+threshold and just above the two-per-SM one, computed from the device's SM count, so every CTA
+form is checked. Entries: attention_fp32_forward_flash (the plain kernel), the fused rotary
 forward and attention_generic_forward with 16-wide FP32 heads (the narrow-row instantiation).
 
 Bars: the forward's (attention_cases.py) against the oracle, selection bit-exact on rows without
@@ -19,16 +21,20 @@ from test_rotary_gpu import composition, fused, tables
 
 pytestmark = pytest.mark.gpu
 
-SIDES = ["one_wave", "two_waves"]
+SIDES = ["one_wave", "two_waves", "two_per_sm"]
 
 
 def batch_for(cuda, side, heads, queries):
-    """Batch so that the 128-query grid has at most / just over one CTA per SM."""
+    """Batch so that the 128-query grid has at most / just over one CTA per SM, or at least two."""
     import torch
 
     sms = torch.cuda.get_device_properties(cuda).multi_processor_count
     per_batch = heads * ((queries + 127) // 128)
-    return sms // per_batch if side == "one_wave" else sms // per_batch + 1
+    if side == "one_wave":
+        return sms // per_batch
+    if side == "two_waves":
+        return sms // per_batch + 1
+    return -(-2 * sms // per_batch)
 
 
 def padded_mask(batch, keys, seed):

@@ -72,10 +72,13 @@ print("REPORT " + json.dumps(report))
 """
 
 
-# (batch, heads, seq, withheld key tile, rows of CTA 0): the one-Q-tile CTA (a grid that fits one
-# wave; tile 5 is loaded after the prefetch, when its stage is released) and the two-Q-tile CTA
-# (tile 2 is one of the prefetched stages).
-@pytest.mark.parametrize("batch,heads,seq,withheld,cta_rows", [(1, 1, 512, 5, 128), (1, 160, 256, 2, 256)])
+# (batch, heads, seq, withheld key tile, rows of CTA 0), one case per CTA form of the d = 32
+# forward on a 148-SM B200: one Q tile per CTA (a grid that fits one wave; tile 5 is loaded after
+# the prefetch, when its stage is released), two Q tiles per CTA (200 one-tile CTAs: more than one
+# wave, fewer than two per SM; tile 2 is one of the prefetched stages), and two threads per row
+# (320 one-tile CTAs, two per SM).
+@pytest.mark.parametrize("batch,heads,seq,withheld,cta_rows", [(1, 1, 512, 5, 128), (1, 100, 256, 2, 256),
+                                                               (1, 160, 256, 2, 128)])
 def test_withheld_tile_runs_a_wait_out(cuda, batch, heads, seq, withheld, cta_rows):
     assert WAIT_TEST_LIBRARY.exists(), "build it with `python -m rocmkernels_b200.build --wait-test`"
     env = dict(os.environ, ROCMKERNELS_ATTENTION_LIBRARY=str(WAIT_TEST_LIBRARY))
