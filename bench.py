@@ -834,7 +834,7 @@ def main() -> None:
     # the K/V operand pre-pass and the forward.
     forward_kernel = ("" if spec.get("entry") == "attention_fp32_forward" or generic == "fp16" or
                       (generic and dim != 32) else api.flash_kernel_name(batch, heads, seq, seq, dim))
-    forward_launches = 2 if forward_kernel == "tcgen05-f16x2-flash-d32" else 1
+    forward_launches = 2 if forward_kernel.endswith("-prepared") else 1
     launches_per_step = len(plan) * (forward_launches + (2 if with_backward else 0))
 
     # The step's device tensors by role (one set for the device-timed steps; the e2e leg uses two).

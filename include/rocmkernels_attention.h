@@ -137,7 +137,7 @@ ROCMKERNELS_C_EXPORT int attention_fp32_forward_tuned(const float *q, const floa
  * 16,400 bytes per 64 keys of each (batch, head), taken from a stream-ordered memory pool that the
  * library keeps per device (acquired and given back on `stream`, so concurrent streams never
  * share it); when the pool cannot supply it the kernel splits K and V itself. The pool keeps up to
- * 256 MiB across synchronisations; rocmkernels_attention_release_scratch returns the rest. */
+ * 4 GiB across synchronisations; rocmkernels_attention_release_scratch returns the rest. */
 ROCMKERNELS_C_EXPORT int attention_fp32_forward_flash(const float *q, const float *k, const float *v, const bool *mask,
         float *output, float *lse, int batch, int heads, int queries, int keys, int radius, RocmKernelsStrides qs,
         RocmKernelsStrides ks, RocmKernelsStrides vs, RocmKernelsStrides os, RocmKernelsStream stream);

@@ -445,7 +445,7 @@ const char *rocmkernels_attention_flash_kernel(int batch, int heads, int queries
     p.k = rk::Tensor{nullptr, (long long)heads * keys * w, (long long)keys * w, w};
     p.v = p.k;
     p.o = rk::OutTensor{nullptr, p.q.sb, p.q.sh, p.q.st};
-    if (rk::tc::flash_supported(p)) return rk::tc::kernel_name(head_width);
+    if (rk::tc::flash_supported(p)) return rk::tc::kernel_name(p, head_width);
     return head_width == 64 ? "simt-fp32-forward-d64" : "simt-fp32-forward-d32";
 }
 
@@ -515,7 +515,7 @@ const char *rocmkernels_attention_generic_kernel(int batch, int heads, int queri
     if (half && rk::tc::half_flash_supported(p) && rk::tc::tensor_maps_encodable(p, head_width, true))
         return rk::tc::half_kernel_name(head_width);
     if (!half && rk::tc::flash_supported(p) && rk::tc::tensor_maps_encodable(p, head_width, false))
-        return rk::tc::kernel_name(head_width);
+        return rk::tc::kernel_name(p, head_width);
     if (half) return head_width == 16 ? "simt-fp16-forward-d16" : head_width == 32 ? "simt-fp16-forward-d32" : "simt-fp16-forward-d64";
     return head_width == 16 ? "simt-fp32-forward-d16" : head_width == 32 ? "simt-fp32-forward-d32" : "simt-fp32-forward-d64";
 }

@@ -1644,6 +1644,25 @@ int launch_prepared(const AttentionParams &p, cudaStream_t stream) {
     return status != cudaSuccess ? status : released;
 }
 
+// Whether the prepared-operand forward pays for its pre-pass. The pre-pass costs a few
+// microseconds whatever the shape; the forward it enables saves ~10 % per key tile. A grid that
+// fits in one wave of the split-warp kernel's CTAs with fewer than 24 key tiles per window keeps
+// the split-warp kernel (measured on B200, us per launch flushed / back to back, split warps vs
+// prepared: B8 H3 S1024 36.3 / 30.9 vs 37.2 / 33.0; B2 H8 S512 20.5 / 16.4 vs 20.8 / 16.4;
+// B1 H8 S2048 51.3 / 47.2 vs 45.3 / 39.6).
+bool use_prepared(const AttentionParams &p) {
+    int device = 0, sms = 0;
+    if (cudaGetDevice(&device) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
+        return false;  // no device to run on: the launch reports the error
+    const long long one_tile_ctas = static_cast<long long>((p.queries + kQTile - 1) / kQTile) * p.heads * p.batch;
+    const long long split_warp_ctas = one_tile_ctas <= sms ? one_tile_ctas
+                                                           : static_cast<long long>((p.queries + 2 * kQTile - 1) / (2 * kQTile)) * p.heads * p.batch;
+    int first = 0, last = 0;
+    key_window(0, min(p.queries, 2 * kQTile), p.keys, p.radius, first, last);
+    const int window_tiles = p.radius < 0 ? (p.keys + kKeyTile - 1) / kKeyTile : (last - first + kKeyTile - 1) / kKeyTile + 1;
+    return split_warp_ctas > sms || window_tiles >= 24;
+}
+
 }  // namespace
 
 long long prepared_forward_bytes(int batch, int heads, int keys) {
@@ -1659,7 +1678,7 @@ bool flash_supported(const AttentionParams &p) {
 int launch_flash_forward(const AttentionParams &p, int head_width, cudaStream_t stream) {
     if (head_width == 16) return launch<32, false, 16>(p, stream);
     if (head_width == 32) {
-        const int status = launch_prepared<false>(p, stream);
+        const int status = use_prepared(p) ? launch_prepared<false>(p, stream) : kNotEligible;
         return status != kNotEligible ? status : launch<32, false>(p, stream);
     }
     if (head_width == 64) return launch<64, false>(p, stream);
@@ -1678,7 +1697,7 @@ int launch_flash_forward_rotary(const AttentionParams &p, cudaStream_t stream) {
     };
     if (!aligned(p.rot_cos, p.rot_cb, p.rot_ct) || !aligned(p.rot_sin, p.rot_sb, p.rot_st)) return kNotEligible;
     if ((p.rot_cb > 0) != (p.rot_sb > 0)) return kNotEligible;  // both tables per sequence, or both shared
-    const int status = launch_prepared<true>(p, stream);
+    const int status = use_prepared(p) ? launch_prepared<true>(p, stream) : kNotEligible;
     return status != kNotEligible ? status : launch<32, false, 32, true>(p, stream);
 }
 
@@ -1716,8 +1735,10 @@ unsigned int read_device_status(bool clear) {
     return value;
 }
 
-const char *kernel_name(int head_width) {
-    return head_width == 64 ? "tcgen05-f16x2-flash-d64" : head_width == 16 ? "tcgen05-f16x2-flash-d16" : "tcgen05-f16x2-flash-d32";
+const char *kernel_name(const AttentionParams &p, int head_width) {
+    if (head_width == 64) return "tcgen05-f16x2-flash-d64";
+    if (head_width == 16) return "tcgen05-f16x2-flash-d16";
+    return use_prepared(p) ? "tcgen05-f16x2-flash-d32-prepared" : "tcgen05-f16x2-flash-d32";
 }
 
 #ifdef RK_WAIT_TEST

@@ -47,8 +47,9 @@ const char *build_info();
 // Reads (and optionally clears) the device status word set by a failed bounded wait;
 // synchronizes with the device. 0 = no failure recorded.
 unsigned int read_device_status(bool clear);
-// Name of the tensor-core flash kernel for a head width (for benchmarks and profiles).
-const char *kernel_name(int head_width);
+// Name of the tensor-core flash kernel that a problem of these sizes runs at this head width (for
+// benchmarks and profiles); "-prepared" marks the d = 32 path of an operand pre-pass and the forward.
+const char *kernel_name(const AttentionParams &p, int head_width);
 
 // True when the tensor-core backward accepts the tensors (TMA-addressable q, k, v, dO; 16-byte
 // addressable O and gradients).

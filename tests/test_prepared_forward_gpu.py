@@ -2,9 +2,13 @@
 K and V once into scratch from the library's stream-ordered pool, then the forward (launched as the
 pre-pass's programmatic dependent) bulk-copies those stage images.
 
+The path runs when it pays for its pre-pass: grids beyond one wave of the split-warp kernel, or
+windows of at least 24 key tiles. The shapes below are chosen to take it (on a 148-SM B200) in each
+CTA form: one Q tile, two Q tiles, and two threads per row.
+
 Checked here, on the GPU:
 * results against the oracle at shapes whose key windows do not start on a 64-key tile (radius),
-  with padded keys, key counts that are not a multiple of 64, one- and two-Q-tile CTAs;
+  with padded keys, key counts that are not a multiple of 64, every CTA form;
 * capture in a CUDA graph: the pool allocation, both kernels and the release are recorded, and
   replays on new inputs give the eager call's bits;
 * two streams running forwards at the same time: each stream's scratch is its own (results equal
@@ -49,9 +53,10 @@ def run_forward(cuda, tensors, queries, keys, radius, stream=None):
 
 
 # (batch, heads, queries, keys, radius, mask fraction): radius windows that start inside a key
-# tile, ragged key counts, padded keys; small grids run one Q tile per CTA, the last case two.
-CASES = [(2, 3, 300, 300, 100, 0.0), (1, 2, 200, 333, 37, 0.2), (3, 4, 129, 1000, -1, 0.3), (2, 2, 777, 517, 250, 0.1),
-         (16, 12, 256, 320, 70, 0.15)]
+# tile, ragged key counts, padded keys. Forms: two threads per row (cases 1, 2, 6), one Q tile
+# (cases 3, 4), two Q tiles (case 5).
+CASES = [(40, 4, 300, 300, 100, 0.0), (3, 60, 200, 333, 37, 0.2), (3, 4, 129, 2000, -1, 0.3), (2, 2, 777, 1600, 800, 0.1),
+         (1, 100, 256, 2000, -1, 0.1), (16, 12, 256, 320, 70, 0.15)]
 
 
 @pytest.mark.parametrize("case", CASES, ids=lambda c: "b{}h{}q{}k{}r{}m{}".format(*c))
@@ -66,7 +71,7 @@ def test_prepared_forward_matches_oracle(cuda, case):
 
 
 def test_graph_capture_replays_the_forward(cuda):
-    batch, heads, seq = 4, 3, 512
+    batch, heads, seq = 4, 3, 2048
     (_, _, _, _), tensors = device_problem(cuda, batch, heads, seq, seq, 711)
     stream = torch.cuda.Stream(cuda)
     with torch.cuda.stream(stream):
@@ -93,10 +98,10 @@ def test_graph_capture_replays_the_forward(cuda):
 
 
 def test_two_streams_keep_their_scratch_apart(cuda):
-    problems = [device_problem(cuda, 8, 3, 1024, 1024, seed)[1] for seed in (721, 722)]
+    problems = [device_problem(cuda, 2, 12, 2048, 2048, seed)[1] for seed in (721, 722)]
     expected = []
     for tensors in problems:
-        status, out, lse = run_forward(cuda, tensors, 1024, 1024, -1)
+        status, out, lse = run_forward(cuda, tensors, 2048, 2048, -1)
         assert status == 0
         expected.append((out, lse))
     torch.cuda.synchronize(cuda)
@@ -105,7 +110,7 @@ def test_two_streams_keep_their_scratch_apart(cuda):
     for _ in range(6):  # interleaved launches, no synchronisation between the streams
         for i, (tensors, st) in enumerate(zip(problems, streams)):
             with torch.cuda.stream(st):
-                status, out, lse = run_forward(cuda, tensors, 1024, 1024, -1, st)
+                status, out, lse = run_forward(cuda, tensors, 2048, 2048, -1, st)
                 assert status == 0
                 results[i].append((out, lse))
     torch.cuda.synchronize(cuda)
@@ -117,13 +122,13 @@ def test_two_streams_keep_their_scratch_apart(cuda):
 
 
 def test_release_scratch_then_forward(cuda):
-    (q, k, v, mask), tensors = device_problem(cuda, 2, 2, 256, 256, 731)
-    status, _, _ = run_forward(cuda, tensors, 256, 256, -1)
+    (q, k, v, mask), tensors = device_problem(cuda, 1, 8, 2048, 2048, 731)
+    status, _, _ = run_forward(cuda, tensors, 2048, 2048, -1)
     assert status == 0
     torch.cuda.synchronize(cuda)
     assert api().release_scratch() == 0
-    status, out, lse = run_forward(cuda, tensors, 256, 256, -1)
+    status, out, lse = run_forward(cuda, tensors, 2048, 2048, -1)
     assert status == 0
-    expected = oracle.attention(q, k, v, mask, None, -1, forward_only=True)
+    expected = oracle.attention(q, k, v, mask, None, -1, forward_only=True, threads=oracle.cpu_count())
     assert_forward_close(out.cpu().numpy(), lse.cpu().numpy(), expected, "after release")
     assert np.isfinite(out.cpu().numpy()).all()

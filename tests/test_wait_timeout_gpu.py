@@ -77,9 +77,10 @@ print("REPORT " + json.dumps(report))
 # the prefetch, when its stage is released), two Q tiles per CTA (200 one-tile CTAs: more than one
 # wave, fewer than two per SM; tile 2 is one of the prefetched stages), and two threads per row
 # (320 one-tile CTAs, two per SM).
-@pytest.mark.parametrize("batch,heads,seq,withheld,cta_rows", [(1, 1, 512, 5, 128), (1, 100, 256, 2, 256),
-                                                               (1, 160, 256, 2, 128)])
-def test_withheld_tile_runs_a_wait_out(cuda, batch, heads, seq, withheld, cta_rows):
+@pytest.mark.parametrize("batch,heads,seq,withheld,cta_rows,kernel", [(1, 1, 512, 5, 128, "tcgen05-f16x2-flash-d32"),
+                                                                      (1, 100, 256, 2, 256, "tcgen05-f16x2-flash-d32"),
+                                                                      (1, 160, 256, 2, 128, "tcgen05-f16x2-flash-d32-prepared")])
+def test_withheld_tile_runs_a_wait_out(cuda, batch, heads, seq, withheld, cta_rows, kernel):
     assert WAIT_TEST_LIBRARY.exists(), "build it with `python -m rocmkernels_b200.build --wait-test`"
     env = dict(os.environ, ROCMKERNELS_ATTENTION_LIBRARY=str(WAIT_TEST_LIBRARY))
     args = [str(REPO), str(batch), str(heads), str(seq), str(withheld), str(cta_rows)]
@@ -87,8 +88,7 @@ def test_withheld_tile_runs_a_wait_out(cuda, batch, heads, seq, withheld, cta_ro
     assert result.returncode == 0, result.stdout[-2000:] + result.stderr[-4000:]
     line = next(l for l in result.stdout.splitlines() if l.startswith("REPORT "))
     report = json.loads(line[len("REPORT "):])
-    expected_kernel = "tcgen05-f16x2-flash-d32"
-    assert report["kernel"] == expected_kernel
+    assert report["kernel"] == kernel
     assert report["failed_status"] == 0            # the launch itself succeeded
     assert report["failed_seconds"] < 30.0         # every wait gave up; nothing hung
     assert report["device_status"] == 1           # kStatusWaitTimeout recorded
