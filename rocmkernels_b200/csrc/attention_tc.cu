@@ -532,10 +532,9 @@ __device__ __forceinline__ void rotate_row32(float4 (&x)[8], const float4 (&cs)[
 // stage; the other instantiations ignore those two maps.
 // kPrepared (D = 32, split FP32, no statistics): the key tiles come from the stage images of
 // prepare_kv_kernel (args.images / args.headers; with kRotary its K rows are already rotated and
-// the kernel rotates only the Q rows) by bulk copies, and the kernel is
-// launched as a programmatic dependent of that pre-pass: every thread passes griddepcontrol.wait
-// before it touches global memory (the TMEM allocation and the barrier set-up overlap the end of
-// the pre-pass).
+// the kernel rotates only the Q rows) by bulk copies, and the kernel is launched as a programmatic
+// dependent of that pre-pass: the producer thread passes griddepcontrol.wait before its first copy,
+// while the other threads allocate TMEM, set up the barriers and split their Q rows.
 template <int D, bool kHalf, int kWidth = D, bool kRotary = false, int kTiles = Forward<D, kHalf>::kQTiles,
           bool kStats = false, bool kPrepared = false, int kRowThreads = 1>
 __global__ void __launch_bounds__(Forward<D, kHalf, kTiles, kPrepared, kRowThreads>::kThreads, kRowThreads == 2 ? 2 : 1)
@@ -577,7 +576,6 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles, kPrepared, kRowThrea
             tmem_alloc(&s.tmem_base, F::kTmemColumns);
             tmem_relinquish();
         }
-        grid_dependency_wait();
     }
     // The softmax threads issue the loads of their Q row (and, with the rotary prologue, of its
     // table rows) before the set-up barrier, so their latency overlaps the TMEM allocation and
@@ -659,6 +657,10 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles, kPrepared, kRowThrea
         mbar_init(&s.range_ready, 1);
         mbar_init(&s.mma_done, F::kMmaWarps);
         mbar_fence_init();
+        // Prepared operands: the stage images are the pre-pass's output, the one thing this grid
+        // reads that the grid before it writes (its other inputs were written before the pre-pass
+        // started), so only this thread waits for the pre-pass, right before its first copy.
+        if constexpr (kPrepared) grid_dependency_wait();
         // The first stages are free: their loads overlap the TMEM allocation and the set-up
         // barrier. Nothing else touches the raw K/V tiles or kv_full before that barrier.
         for (int j = 0; j < prefetched; ++j) issue_tile(j);
