@@ -625,7 +625,7 @@ def c5_strong(args, device, world: int, rank: int, dist, api) -> dict:
     (0, 0) slice, which it computes itself, against the oracle."""
     import torch
 
-    from rocmkernels_b200.sharding import run_backward, run_forward, shard_plan, workspace_bytes
+    from rocmkernels_b200.sharding import forward_workspace_bytes, run_backward, run_forward, shard_plan, workspace_bytes
 
     spec = WORKLOADS["c5_fwd_bwd_b64h12s4096d32"]
     B, H, S, D = spec["batch"], spec["heads"], spec["seq"], spec["dim"]
@@ -649,10 +649,15 @@ def c5_strong(args, device, world: int, rank: int, dist, api) -> dict:
     stream = torch.cuda.current_stream(device)
     fwd_t = {r: t[r] for r in ("q", "k", "v", "mask", "out", "lse")}
 
+    # The forward with a workspace: K and V split once per head by the operand pre-pass.
+    forward_workspace = torch.empty(max(1, forward_workspace_bytes(api.attention_fp32_forward_flash_workspace_size, plan, S)),
+                                    dtype=torch.uint8, device=device)
+
     def forward():
-        status = run_forward(api.attention_fp32_forward_flash, fwd_t, plan, stream=stream, **geometry)
+        status = run_forward(api.attention_fp32_forward_flash_workspace, fwd_t, plan, stream=stream, workspace=forward_workspace,
+                             **geometry)
         if status != 0:
-            raise api.HipError(status, "attention_fp32_forward_flash")
+            raise api.HipError(status, "attention_fp32_forward_flash_workspace")
 
     two_pass, fused = "attention_fp32_backward", "attention_fp32_backward_fused"
     workspace = torch.empty(max(1, workspace_bytes(api.attention_fp32_backward_fused_workspace_size, plan, S)), dtype=torch.uint8,
@@ -692,12 +697,13 @@ def c5_strong(args, device, world: int, rank: int, dist, api) -> dict:
     record = {"workload": "c5_fwd_bwd_b64h12s4096d32", "description": spec["description"], "scaling": "strong",
               "ranks": world, "steps": steps,
               "ms_per_step": step_ms, "tflops": flops / (step_ms * 1e-3) / 1e12,
-              "step": "attention_fp32_forward_flash + attention_fp32_backward_fused (the single-pass backward)",
+              "step": "attention_fp32_forward_flash_workspace + attention_fp32_backward_fused (the single-pass backward)",
               "ms_per_step_two_pass": step_two_pass_ms, "tflops_two_pass": flops / (step_two_pass_ms * 1e-3) / 1e12,
               "forward_ms": forward_ms, "backward_two_pass_ms": backward_ms, "backward_fused_ms": backward_fused_ms,
               "rank0_slices": sum(slices), "rank0_active_pairs": sum(slices) * S * S,
               "partition": "rocmkernels_b200.sharding.shard_plan: contiguous batch ranges, no collective on the data path",
-              "gpu_launches_per_rank": steps * 5 * len(plan), "data": data,
+              "gpu_launches_per_rank": steps * len(plan) * (4 + (2 if api.flash_workspace_kernel_name(plan[0].batch, plan[0].heads, S, S)
+                                                                      .endswith("-prepared") else 1)), "data": data,
               "time": "CUDA events per rank around each call, mean over steps, max over ranks; inputs > L2; both "
                       "backward forms run every step on the same forward output"}
     if rank == 0 and arrays is not None:

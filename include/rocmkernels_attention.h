@@ -133,14 +133,27 @@ ROCMKERNELS_C_EXPORT int attention_fp32_forward_tuned(const float *q, const floa
 /* Flash forward, the headline entry: tcgen05/TMEM kernel on sm_100a with split-FP16 operands
  * (kind::f16; each FP32 operand as two FP16 terms, three products) when the tensors are
  * TMA-addressable, else the exact FP32 SIMT kernel; radius < -1 is invalid. Replaces attention_fp32_forward_flash (Attention.hpp:28-30; Attention.hip:372-390).
- * Scratch: the tensor-core path first splits every key tile of K and V once into a workspace of
- * 16,400 bytes per 64 keys of each (batch, head), taken from a stream-ordered memory pool that the
- * library keeps per device (acquired and given back on `stream`, so concurrent streams never
- * share it); when the pool cannot supply it the kernel splits K and V itself. The pool keeps up to
- * 4 GiB across synchronisations; rocmkernels_attention_release_scratch returns the rest. */
+ * Allocates nothing: the kernel splits each K/V tile itself. */
 ROCMKERNELS_C_EXPORT int attention_fp32_forward_flash(const float *q, const float *k, const float *v, const bool *mask,
         float *output, float *lse, int batch, int heads, int queries, int keys, int radius, RocmKernelsStrides qs,
         RocmKernelsStrides ks, RocmKernelsStrides vs, RocmKernelsStrides os, RocmKernelsStream stream);
+
+/* Workspace bytes attention_fp32_forward_flash_workspace needs: 16,400 per 64 keys (rounded up) of
+ * each (batch, head); 0 for non-positive sizes. No counterpart in the reference. */
+ROCMKERNELS_C_EXPORT unsigned long long attention_fp32_forward_flash_workspace_size(int batch, int heads, int keys);
+
+/* attention_fp32_forward_flash with caller scratch (no counterpart in the reference, whose ABI has
+ * no workspace argument): where it pays -- grids beyond one wave of CTAs or key windows of at
+ * least 24 tiles of 64 keys -- an operand pre-pass first splits every K/V tile once into
+ * `workspace` (the split-FP16 stage images and their headers), and the forward copies them instead
+ * of splitting each tile in every CTA; elsewhere, or when `workspace` is not 128-byte aligned, the
+ * call runs attention_fp32_forward_flash's kernel. Same results within the same tolerances.
+ * `workspace_bytes` below attention_fp32_forward_flash_workspace_size, or a null workspace: error 1.
+ * The workspace is in use until the call's work on `stream` completes. */
+ROCMKERNELS_C_EXPORT int attention_fp32_forward_flash_workspace(const float *q, const float *k, const float *v,
+        const bool *mask, float *output, float *lse, int batch, int heads, int queries, int keys, int radius,
+        RocmKernelsStrides qs, RocmKernelsStrides ks, RocmKernelsStrides vs, RocmKernelsStrides os, void *workspace,
+        unsigned long long workspace_bytes, RocmKernelsStream stream);
 
 /* Flash forward with a variant selector 0..18, else error 1; radius < -1 is invalid.
  * Replaces attention_fp32_forward_flash_tuned (Attention.hpp:31-33; Attention.hip:392-417). */
@@ -243,6 +256,14 @@ ROCMKERNELS_C_EXPORT int attention_fp32_forward_flash_rotary(const float *q, con
         int keys, int radius, RocmKernelsStrides qs, RocmKernelsStrides ks, RocmKernelsStrides vs, RocmKernelsStrides cs,
         RocmKernelsStrides ss, RocmKernelsStrides os, RocmKernelsStream stream);
 
+/* attention_fp32_forward_flash_rotary with caller scratch, as attention_fp32_forward_flash_workspace
+ * (the pre-pass rotates the K rows as it splits them). No counterpart in the reference. */
+ROCMKERNELS_C_EXPORT int attention_fp32_forward_flash_rotary_workspace(const float *q, const float *k, const float *v,
+        const float *cos, const float *sin, const bool *mask, float *output, float *lse, int batch, int heads, int queries,
+        int keys, int radius, RocmKernelsStrides qs, RocmKernelsStrides ks, RocmKernelsStrides vs, RocmKernelsStrides cs,
+        RocmKernelsStrides ss, RocmKernelsStrides os, void *workspace, unsigned long long workspace_bytes,
+        RocmKernelsStream stream);
+
 /* Library build identification: a static string naming the architecture the kernels were
  * compiled for ("sm_100a") and the kernel families present. No counterpart in the reference. */
 ROCMKERNELS_C_EXPORT const char *rocmkernels_attention_build_info(void);
@@ -253,6 +274,11 @@ ROCMKERNELS_C_EXPORT const char *rocmkernels_attention_build_info(void);
 ROCMKERNELS_C_EXPORT const char *rocmkernels_attention_flash_kernel(int batch, int heads, int queries, int keys,
         int head_width);
 
+/* Name of the kernel attention_fp32_forward_flash_workspace selects for contiguous, 16-byte aligned
+ * tensors of this shape ("...-prepared" for the operand pre-pass and the forward). No counterpart
+ * in the reference. */
+ROCMKERNELS_C_EXPORT const char *rocmkernels_attention_flash_workspace_kernel(int batch, int heads, int queries, int keys);
+
 /* Name of the kernel attention_generic_forward runs for contiguous [batch][heads][tokens][head_width]
  * tensors of the given dtype (no reference counterpart; for benchmarks and tests). */
 ROCMKERNELS_C_EXPORT const char *rocmkernels_attention_generic_kernel(int batch, int heads, int queries, int keys,
@@ -262,11 +288,6 @@ ROCMKERNELS_C_EXPORT const char *rocmkernels_attention_generic_kernel(int batch,
  * pipeline wait gave up (a protocol failure; the affected rows are written as NaN). Reading it
  * synchronizes with the device; clear != 0 resets it. No counterpart in the reference. */
 ROCMKERNELS_C_EXPORT unsigned int rocmkernels_attention_device_status(int clear);
-
-/* Returns the memory that the library's scratch pool on the current device holds and no call is
- * using (cudaMemPoolTrimTo(pool, 0)); cudaSuccess when the library has no pool there. Scratch
- * still in use by enqueued work stays. No counterpart in the reference. */
-ROCMKERNELS_C_EXPORT int rocmkernels_attention_release_scratch(void);
 
 #ifdef __cplusplus
 } /* extern "C" */

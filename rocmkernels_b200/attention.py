@@ -101,8 +101,16 @@ def lib() -> ctypes.CDLL:
         library.rocmkernels_attention_generic_kernel.restype = ctypes.c_char_p
         library.rocmkernels_attention_device_status.argtypes = [ctypes.c_int]
         library.rocmkernels_attention_device_status.restype = ctypes.c_uint
-        library.rocmkernels_attention_release_scratch.argtypes = []
-        library.rocmkernels_attention_release_scratch.restype = ctypes.c_int
+        library.attention_fp32_forward_flash_workspace.argtypes = ([_POINTER] * 6 + [_INT] * 5 + [Strides] * 4 +
+                                                                   [_POINTER, ctypes.c_ulonglong, _POINTER])
+        library.attention_fp32_forward_flash_workspace.restype = ctypes.c_int
+        library.attention_fp32_forward_flash_rotary_workspace.argtypes = ([_POINTER] * 8 + [_INT] * 5 + [Strides] * 6 +
+                                                                          [_POINTER, ctypes.c_ulonglong, _POINTER])
+        library.attention_fp32_forward_flash_rotary_workspace.restype = ctypes.c_int
+        library.attention_fp32_forward_flash_workspace_size.argtypes = [_INT] * 3
+        library.attention_fp32_forward_flash_workspace_size.restype = ctypes.c_ulonglong
+        library.rocmkernels_attention_flash_workspace_kernel.argtypes = [ctypes.c_int] * 4
+        library.rocmkernels_attention_flash_workspace_kernel.restype = ctypes.c_char_p
         library.attention_fp32_backward_static_delta.argtypes = [_POINTER] * 10 + [_INT] * 5 + [Strides] * 5 + [_POINTER]
         library.attention_fp32_backward_static_delta.restype = ctypes.c_int
         library.attention_fp32_backward_fused.argtypes = ([_POINTER] * 12 + [ctypes.c_ulonglong] + [_INT] * 5 + [Strides] * 5
@@ -134,12 +142,6 @@ def device_status(clear: bool = True) -> int:
     """Status word of the tensor-core kernels on the current device (0 = no failed pipeline wait).
     Synchronizes with the device."""
     return int(lib().rocmkernels_attention_device_status(int(clear)))
-
-
-def release_scratch() -> int:
-    """Returns the idle memory of the library's scratch pool on the current device to the system
-    (the flash forward's split K/V workspace); a cudaError_t value, 0 on success."""
-    return int(lib().rocmkernels_attention_release_scratch())
 
 
 def _error_name(status: int) -> str:
@@ -306,6 +308,46 @@ def attention_generic_forward(q, k, v, mask, output, lse, batch, heads, queries,
 def rotary_fp32(q, k, cos, sin, oq, ok, batch, heads, length, backward, qs, ks, cs, ss, stream=None):
     return _call("rotary_fp32", ptr(q), ptr(k), ptr(cos), ptr(sin), ptr(oq), ptr(ok), batch, heads, length, int(bool(backward)),
                  strides(qs), strides(ks), strides(cs), strides(ss), _stream(stream))
+
+
+def attention_fp32_forward_flash_workspace_size(batch, heads, keys) -> int:
+    """Bytes of device workspace attention_fp32_forward_flash_workspace needs for these sizes."""
+    return int(lib().attention_fp32_forward_flash_workspace_size(batch, heads, keys))
+
+
+def flash_workspace_kernel_name(batch: int, heads: int, queries: int, keys: int) -> str:
+    """Name of the kernel attention_fp32_forward_flash_workspace runs for contiguous, 16-byte
+    aligned inputs ("...-prepared": the operand pre-pass and the forward)."""
+    return lib().rocmkernels_attention_flash_workspace_kernel(batch, heads, queries, keys).decode()
+
+
+def _forward_workspace(q, workspace, size):
+    if workspace is None:
+        import torch
+
+        workspace = torch.empty(max(size, 1), dtype=torch.uint8, device=q.device)
+    capacity = workspace.numel() * workspace.element_size() if hasattr(workspace, "numel") else size
+    return workspace, capacity
+
+
+def attention_fp32_forward_flash_workspace(q, k, v, mask, output, lse, batch, heads, queries, keys, radius, qs, ks, vs, os_,
+                                           stream=None, workspace=None):
+    """attention_fp32_forward_flash with caller scratch for the split K/V operands (see the C
+    header). `workspace`: a device buffer (a torch tensor or a pointer) of
+    attention_fp32_forward_flash_workspace_size bytes; None allocates one with torch on q's device."""
+    workspace, capacity = _forward_workspace(q, workspace, attention_fp32_forward_flash_workspace_size(batch, heads, keys))
+    return _call("attention_fp32_forward_flash_workspace", ptr(q), ptr(k), ptr(v), ptr(mask), ptr(output), ptr(lse), batch, heads,
+                 queries, keys, radius, strides(qs), strides(ks), strides(vs), strides(os_), ptr(workspace), capacity,
+                 _stream(stream))
+
+
+def attention_fp32_forward_flash_rotary_workspace(q, k, v, cos, sin, mask, output, lse, batch, heads, queries, keys, radius, qs, ks,
+                                                  vs, cs, ss, os_, stream=None, workspace=None):
+    """attention_fp32_forward_flash_rotary with caller scratch, as attention_fp32_forward_flash_workspace."""
+    workspace, capacity = _forward_workspace(q, workspace, attention_fp32_forward_flash_workspace_size(batch, heads, keys))
+    return _call("attention_fp32_forward_flash_rotary_workspace", ptr(q), ptr(k), ptr(v), ptr(cos), ptr(sin), ptr(mask), ptr(output),
+                 ptr(lse), batch, heads, queries, keys, radius, strides(qs), strides(ks), strides(vs), strides(cs), strides(ss),
+                 strides(os_), ptr(workspace), capacity, _stream(stream))
 
 
 def attention_fp32_forward_flash_rotary(q, k, v, cos, sin, mask, output, lse, batch, heads, queries, keys, radius, qs, ks, vs, cs,

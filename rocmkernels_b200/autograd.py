@@ -10,8 +10,10 @@ torch.are_deterministic_algorithms_enabled(); for D = 64 attention64_fp32_backwa
 tables cos/sin ([batch, tokens, 32], D = 32) q and k are rotated
 first (rotary_fp32's forward, Positional/Rotary.hip) inside the fused flash forward; the backward
 rebuilds the rotated q and k with rotary_fp32, runs the attention backward on them and applies
-the transposed rotation (rotary_fp32 with backward = 1) to their gradients. The calls run on
-torch's current stream and allocate their outputs through torch.
+the transposed rotation (rotary_fp32 with backward = 1) to their gradients. For D = 32 the
+forward is the flash entry with a workspace (attention_fp32_forward_flash_workspace: K and V split
+once by an operand pre-pass where that pays). The calls run on torch's current stream and
+allocate their outputs and workspaces through torch.
 """
 from __future__ import annotations
 
@@ -70,16 +72,22 @@ class AttentionFunction(torch.autograd.Function):
         out = torch.empty(batch, heads, queries, width, device=q.device, dtype=torch.float32)
         lse = torch.empty(batch, heads, queries, 2, device=q.device, dtype=torch.float32)
         stream = torch.cuda.current_stream(q.device)
-        if cos is None:
+        if cos is None and width == 32:
+            status = api.attention_fp32_forward_flash_workspace(q, k, v, mask, out, lse, batch, heads, queries, keys, radius,
+                                                                api.strides_of(q), api.strides_of(k), api.strides_of(v),
+                                                                api.strides_of(out), stream)
+            if status != 0:
+                raise api.HipError(status, "attention_fp32_forward_flash_workspace")
+        elif cos is None:
             forward(q, k, v, mask, out, lse, batch, heads, queries, keys, radius, api.strides_of(q), api.strides_of(k),
                     api.strides_of(v), api.strides_of(out), stream)
         else:
-            status = api.attention_fp32_forward_flash_rotary(q, k, v, cos, sin, mask, out, lse, batch, heads, queries, keys,
-                                                             radius, api.strides_of(q), api.strides_of(k), api.strides_of(v),
-                                                             _table_strides(cos), _table_strides(sin), api.strides_of(out),
-                                                             stream)
+            status = api.attention_fp32_forward_flash_rotary_workspace(q, k, v, cos, sin, mask, out, lse, batch, heads, queries, keys,
+                                                                       radius, api.strides_of(q), api.strides_of(k),
+                                                                       api.strides_of(v), _table_strides(cos), _table_strides(sin),
+                                                                       api.strides_of(out), stream)
             if status != 0:
-                raise api.HipError(status, "attention_fp32_forward_flash_rotary")
+                raise api.HipError(status, "attention_fp32_forward_flash_rotary_workspace")
         ctx.save_for_backward(q, k, v, mask, out, lse, cos, sin)
         ctx.radius = radius
         return out

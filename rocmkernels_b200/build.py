@@ -30,7 +30,6 @@ SOURCES = [
     "csrc/rotary.cu",
     "csrc/device.cpp",
     "csrc/context.cpp",
-    "csrc/scratch.cpp",
 ]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -7,7 +7,6 @@
 #include "attention_common.cuh"
 #include "attention_simt.cuh"
 #include "attention_tc.cuh"
-#include "scratch.h"
 
 #include <cmath>
 #include <mutex>
@@ -124,10 +123,11 @@ int launch_backward(const AttentionParams &p, cudaStream_t stream, bool softmax_
 }
 
 // The flash entry: the tcgen05 tensor-core kernel when the problem fits its contract, else the
-// exact SIMT kernel (same results within the documented tolerance; no CPU path exists).
-int launch_flash(const AttentionParams &p, cudaStream_t stream) {
+// exact SIMT kernel (same results within the documented tolerance; no CPU path exists). With a
+// workspace the tensor-core kernel may take prepared operands (attention_tc.cuh).
+int launch_flash(const AttentionParams &p, void *workspace, cudaStream_t stream) {
     if (rk::tc::flash_supported(p)) {
-        const int status = rk::tc::launch_flash_forward(p, 32, stream);
+        const int status = rk::tc::launch_flash_forward(p, 32, workspace, stream);
         if (status != rk::tc::kNotEligible) return status;
     }
     return launch_simt_forward<32, false>(p, stream);
@@ -167,7 +167,7 @@ template <class T>
 int launch_generic(const AttentionParams &p, int D, cudaStream_t stream) {
     if constexpr (std::is_same_v<T, float>) {
         if (rk::tc::flash_supported(p)) {
-            const int status = rk::tc::launch_flash_forward(p, D, stream);
+            const int status = rk::tc::launch_flash_forward(p, D, nullptr, stream);
             if (status != rk::tc::kNotEligible) return status;
         }
     } else {
@@ -326,7 +326,24 @@ int attention_fp32_forward_flash(const float *q, const float *k, const float *v,
     if (forward_args_bad(q, k, v, mask, output, lse, batch, heads, queries, keys) || radius < -1)
         return cudaErrorInvalidValue;
     const AttentionParams p = forward_params(32, q, k, v, mask, output, lse, batch, heads, queries, keys, radius, qs, ks, vs, os);
-    return launch_flash(p, stream);
+    return launch_flash(p, nullptr, stream);
+}
+
+unsigned long long attention_fp32_forward_flash_workspace_size(int batch, int heads, int keys) {
+    if (batch <= 0 || heads <= 0 || keys <= 0) return 0;
+    return static_cast<unsigned long long>(rk::tc::prepared_forward_bytes(batch, heads, keys));
+}
+
+int attention_fp32_forward_flash_workspace(const float *q, const float *k, const float *v, const bool *mask, float *output,
+                                           float *lse, int batch, int heads, int queries, int keys, int radius,
+                                           RocmKernelsStrides qs, RocmKernelsStrides ks, RocmKernelsStrides vs,
+                                           RocmKernelsStrides os, void *workspace, unsigned long long workspace_bytes,
+                                           RocmKernelsStream stream) {
+    if (forward_args_bad(q, k, v, mask, output, lse, batch, heads, queries, keys) || radius < -1 || !workspace ||
+        workspace_bytes < attention_fp32_forward_flash_workspace_size(batch, heads, keys))
+        return cudaErrorInvalidValue;
+    const AttentionParams p = forward_params(32, q, k, v, mask, output, lse, batch, heads, queries, keys, radius, qs, ks, vs, os);
+    return launch_flash(p, workspace, stream);
 }
 
 int attention_fp32_forward_flash_tuned(const float *q, const float *k, const float *v, const bool *mask, float *output,
@@ -340,7 +357,7 @@ int attention_fp32_forward_flash_tuned(const float *q, const float *k, const flo
     // Variants 0-18 were the reference's register/LDS tiling sweep; on sm_100a the even
     // variants run the tensor-core kernel and the odd ones the exact SIMT kernel, so both
     // implementations stay reachable through the reference's selector.
-    if (variant % 2 == 0 || variant == 13) return launch_flash(p, stream);
+    if (variant % 2 == 0 || variant == 13) return launch_flash(p, nullptr, stream);
     return launch_simt_forward<32, false>(p, stream);
 }
 
@@ -366,7 +383,7 @@ int attention64_fp32_forward(const float *q, const float *k, const float *v, con
     if (forward_args_bad(q, k, v, mask, output, lse, batch, heads, queries, keys)) return cudaErrorInvalidValue;
     const AttentionParams p = forward_params(64, q, k, v, mask, output, lse, batch, heads, queries, keys, radius, qs, ks, vs, os);
     if (rk::tc::flash_supported(p)) {  // else (tensors not TMA-addressable) the exact SIMT kernel
-        const int status = rk::tc::launch_flash_forward(p, 64, stream);
+        const int status = rk::tc::launch_flash_forward(p, 64, nullptr, stream);
         if (status != rk::tc::kNotEligible) return status;
     }
     return launch_simt_forward<64, false>(p, stream);
@@ -425,13 +442,12 @@ int attention_fp32_query_profile(const float *q, const float *k, const float *v,
 
 const char *rocmkernels_attention_build_info(void) { return rk::tc::build_info(); }
 
-int rocmkernels_attention_release_scratch(void) { return rk::scratch_trim(); }
-
 unsigned int rocmkernels_attention_device_status(int clear) {
     return rk::tc::read_device_status(clear != 0) | rk::tc::read_backward_status(clear != 0);
 }
 
-const char *rocmkernels_attention_flash_kernel(int batch, int heads, int queries, int keys, int head_width) {
+namespace {
+const char *flash_kernel_of(int batch, int heads, int queries, int keys, int head_width, bool workspace) {
     if (head_width != 32 && head_width != 64) return "unsupported";
     AttentionParams p{};
     p.batch = batch;
@@ -445,17 +461,24 @@ const char *rocmkernels_attention_flash_kernel(int batch, int heads, int queries
     p.k = rk::Tensor{nullptr, (long long)heads * keys * w, (long long)keys * w, w};
     p.v = p.k;
     p.o = rk::OutTensor{nullptr, p.q.sb, p.q.sh, p.q.st};
-    if (rk::tc::flash_supported(p)) return rk::tc::kernel_name(p, head_width);
+    if (rk::tc::flash_supported(p)) return rk::tc::kernel_name(p, head_width, workspace);
     return head_width == 64 ? "simt-fp32-forward-d64" : "simt-fp32-forward-d32";
 }
+}  // namespace
 
-int attention_fp32_forward_flash_rotary(const float *q, const float *k, const float *v, const float *cos, const float *sin,
-                                        const bool *mask, float *output, float *lse, int batch, int heads, int queries,
-                                        int keys, int radius, RocmKernelsStrides qs, RocmKernelsStrides ks,
-                                        RocmKernelsStrides vs, RocmKernelsStrides cs, RocmKernelsStrides ss,
-                                        RocmKernelsStrides os, RocmKernelsStream stream) {
-    if (forward_args_bad(q, k, v, mask, output, lse, batch, heads, queries, keys) || !cos || !sin || radius < -1)
-        return cudaErrorInvalidValue;
+const char *rocmkernels_attention_flash_kernel(int batch, int heads, int queries, int keys, int head_width) {
+    return flash_kernel_of(batch, heads, queries, keys, head_width, false);
+}
+
+const char *rocmkernels_attention_flash_workspace_kernel(int batch, int heads, int queries, int keys) {
+    return flash_kernel_of(batch, heads, queries, keys, 32, true);
+}
+
+namespace {
+int flash_rotary(const float *q, const float *k, const float *v, const float *cos, const float *sin, const bool *mask, float *output,
+                 float *lse, int batch, int heads, int queries, int keys, int radius, RocmKernelsStrides qs, RocmKernelsStrides ks,
+                 RocmKernelsStrides vs, RocmKernelsStrides cs, RocmKernelsStrides ss, RocmKernelsStrides os, void *workspace,
+                 RocmKernelsStream stream) {
     AttentionParams p = forward_params(32, q, k, v, mask, output, lse, batch, heads, queries, keys, radius, qs, ks, vs, os);
     p.rot_cos = cos;
     p.rot_sin = sin;
@@ -464,10 +487,35 @@ int attention_fp32_forward_flash_rotary(const float *q, const float *k, const fl
     p.rot_sb = ss.batch;
     p.rot_st = ss.token;
     if (rk::tc::flash_supported(p)) {  // else (tensors or tables not 16-byte addressable) the exact SIMT kernel
-        const int status = rk::tc::launch_flash_forward_rotary(p, stream);
+        const int status = rk::tc::launch_flash_forward_rotary(p, workspace, stream);
         if (status != rk::tc::kNotEligible) return status;
     }
     return launch_simt_forward<32, false, float, true>(p, stream);
+}
+}  // namespace
+
+int attention_fp32_forward_flash_rotary(const float *q, const float *k, const float *v, const float *cos, const float *sin,
+                                        const bool *mask, float *output, float *lse, int batch, int heads, int queries,
+                                        int keys, int radius, RocmKernelsStrides qs, RocmKernelsStrides ks,
+                                        RocmKernelsStrides vs, RocmKernelsStrides cs, RocmKernelsStrides ss,
+                                        RocmKernelsStrides os, RocmKernelsStream stream) {
+    if (forward_args_bad(q, k, v, mask, output, lse, batch, heads, queries, keys) || !cos || !sin || radius < -1)
+        return cudaErrorInvalidValue;
+    return flash_rotary(q, k, v, cos, sin, mask, output, lse, batch, heads, queries, keys, radius, qs, ks, vs, cs, ss, os, nullptr,
+                        stream);
+}
+
+int attention_fp32_forward_flash_rotary_workspace(const float *q, const float *k, const float *v, const float *cos,
+                                                  const float *sin, const bool *mask, float *output, float *lse, int batch,
+                                                  int heads, int queries, int keys, int radius, RocmKernelsStrides qs,
+                                                  RocmKernelsStrides ks, RocmKernelsStrides vs, RocmKernelsStrides cs,
+                                                  RocmKernelsStrides ss, RocmKernelsStrides os, void *workspace,
+                                                  unsigned long long workspace_bytes, RocmKernelsStream stream) {
+    if (forward_args_bad(q, k, v, mask, output, lse, batch, heads, queries, keys) || !cos || !sin || radius < -1 || !workspace ||
+        workspace_bytes < attention_fp32_forward_flash_workspace_size(batch, heads, keys))
+        return cudaErrorInvalidValue;
+    return flash_rotary(q, k, v, cos, sin, mask, output, lse, batch, heads, queries, keys, radius, qs, ks, vs, cs, ss, os, workspace,
+                        stream);
 }
 
 int attention_generic_forward(const void *q, const void *k, const void *v, const bool *mask, void *output, float *lse,
@@ -515,7 +563,7 @@ const char *rocmkernels_attention_generic_kernel(int batch, int heads, int queri
     if (half && rk::tc::half_flash_supported(p) && rk::tc::tensor_maps_encodable(p, head_width, true))
         return rk::tc::half_kernel_name(head_width);
     if (!half && rk::tc::flash_supported(p) && rk::tc::tensor_maps_encodable(p, head_width, false))
-        return rk::tc::kernel_name(p, head_width);
+        return rk::tc::kernel_name(p, head_width, false);
     if (half) return head_width == 16 ? "simt-fp16-forward-d16" : head_width == 32 ? "simt-fp16-forward-d32" : "simt-fp16-forward-d64";
     return head_width == 16 ? "simt-fp32-forward-d16" : head_width == 32 ? "simt-fp32-forward-d32" : "simt-fp32-forward-d64";
 }

@@ -15,7 +15,7 @@
 //               [v0^T ; v1^T] FP16 rows, zero masked key rows, publish the tile's key mask and
 //               the two per-tile scale exponents
 //
-// Prepared operands (the d = 32 split-FP32 forward when the library's scratch pool can hold them):
+// Prepared operands (the d = 32 split-FP32 forward given a caller workspace, where it pays):
 // prepare_kv_kernel first converts every 64-key tile of every head once, into the byte image of
 // that shared-memory stage plus a 16-byte header (mask bits, exponents); the forward then runs
 //   warps 0-7   softmax + epilogue of Q tiles A and B (as above)
@@ -67,7 +67,6 @@
 #include <type_traits>
 
 #include "rotary.cuh"
-#include "scratch.h"
 #include "tc_operands.cuh"
 
 
@@ -1610,40 +1609,27 @@ int launch_prepared_tiles(const AttentionParams &p, uint8_t *workspace, cudaStre
     return cudaLaunchKernelEx(&config, kernel, args, unused, unused, unused, unused);
 }
 
-// The prepared d = 32 forward with its workspace from the library's scratch pool (scratch.h), given
-// back on the same stream after the kernels. kNotEligible when the problem is too large for one
-// pre-pass grid or the pool cannot supply the memory (the caller then runs the forward with split
-// warps, which needs no workspace).
+// The prepared d = 32 forward in the caller's workspace (prepared_forward_bytes, 128-byte aligned).
+// kNotEligible when the workspace is not aligned or the problem is too large for one pre-pass grid
+// (the caller then runs the forward with split warps, which needs no workspace).
 template <bool kRotary>
-int launch_prepared(const AttentionParams &p, cudaStream_t stream) {
+int launch_prepared(const AttentionParams &p, void *workspace, cudaStream_t stream) {
     const long long tiles = static_cast<long long>(p.batch) * p.heads * ((p.keys + kKeyTile - 1) / kKeyTile);
-    if (tiles <= 0 || tiles >= (1ll << 31)) return kNotEligible;
-    void *workspace = nullptr;
-    if (scratch_acquire(&workspace, static_cast<size_t>(prepared_forward_bytes(p.batch, p.heads, p.keys)), stream) != cudaSuccess) {
-        (void)cudaGetLastError();  // a failed pool allocation leaves no error behind for the next call
-        return kNotEligible;
-    }
+    if (tiles <= 0 || tiles >= (1ll << 31) || (reinterpret_cast<uintptr_t>(workspace) & 127u) != 0) return kNotEligible;
     int device = 0, sms = 0;
-    cudaError_t query = cudaGetDevice(&device);
-    if (query == cudaSuccess) query = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-    int status = query;
-    if (query == cudaSuccess) {
-        const long long one_tile_ctas = static_cast<long long>((p.queries + kQTile - 1) / kQTile) * p.heads * p.batch;
-        uint8_t *base = static_cast<uint8_t *>(workspace);
-        // CTA form by grid size (measured on B200, us per launch, flushed): a grid of one-tile CTAs
-        // that fills two CTAs per SM runs two threads per row (B4 H12 S4096 543 -> 506, C4-shaped
-        // 187 -> 166); below that one thread per row, one Q tile per CTA when that grid fits in one
-        // wave, else two (B8 H3 S1024: 37.1 against 39.2 with two threads per row; B1 H8 S2048
-        // 45.3 against 59.6).
-        if (!kRotary && one_tile_ctas >= 2ll * sms)
-            status = launch_prepared_tiles<1, false, 2>(p, base, stream);
-        else if (one_tile_ctas <= sms)
-            status = launch_prepared_tiles<1, kRotary>(p, base, stream);
-        else
-            status = launch_prepared_tiles<2, kRotary>(p, base, stream);
-    }
-    const cudaError_t released = scratch_release(workspace, stream);
-    return status != cudaSuccess ? status : released;
+    cudaError_t status = cudaGetDevice(&device);
+    if (status == cudaSuccess) status = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    if (status != cudaSuccess) return status;
+    const long long one_tile_ctas = static_cast<long long>((p.queries + kQTile - 1) / kQTile) * p.heads * p.batch;
+    uint8_t *base = static_cast<uint8_t *>(workspace);
+    // CTA form by grid size (measured on B200, us per launch, flushed): a grid of one-tile CTAs
+    // that fills two CTAs per SM runs two threads per row (B4 H12 S4096 543 -> 506, C4-shaped
+    // 187 -> 166); below that one thread per row, one Q tile per CTA when that grid fits in one
+    // wave, else two (B8 H3 S1024: 37.1 against 39.2 with two threads per row; B1 H8 S2048
+    // 45.3 against 59.6).
+    if (!kRotary && one_tile_ctas >= 2ll * sms) return launch_prepared_tiles<1, false, 2>(p, base, stream);
+    if (one_tile_ctas <= sms) return launch_prepared_tiles<1, kRotary>(p, base, stream);
+    return launch_prepared_tiles<2, kRotary>(p, base, stream);
 }
 
 // Whether the prepared-operand forward pays for its pre-pass. The pre-pass costs a few
@@ -1677,10 +1663,10 @@ bool flash_supported(const AttentionParams &p) {
            (reinterpret_cast<uintptr_t>(p.q.data) & 15u) == 0;
 }
 
-int launch_flash_forward(const AttentionParams &p, int head_width, cudaStream_t stream) {
+int launch_flash_forward(const AttentionParams &p, int head_width, void *workspace, cudaStream_t stream) {
     if (head_width == 16) return launch<32, false, 16>(p, stream);
     if (head_width == 32) {
-        const int status = use_prepared(p) ? launch_prepared<false>(p, stream) : kNotEligible;
+        const int status = workspace != nullptr && use_prepared(p) ? launch_prepared<false>(p, workspace, stream) : kNotEligible;
         return status != kNotEligible ? status : launch<32, false>(p, stream);
     }
     if (head_width == 64) return launch<64, false>(p, stream);
@@ -1693,13 +1679,13 @@ bool statistics_supported(const AttentionParams &p) {
 
 int launch_statistics(const AttentionParams &p, cudaStream_t stream) { return launch<32, false, 32, false, true>(p, stream); }
 
-int launch_flash_forward_rotary(const AttentionParams &p, cudaStream_t stream) {
+int launch_flash_forward_rotary(const AttentionParams &p, void *workspace, cudaStream_t stream) {
     const auto aligned = [](const float *t, long long sb, long long st) {
         return (reinterpret_cast<uintptr_t>(t) & 15u) == 0 && sb % 4 == 0 && st % 4 == 0;
     };
     if (!aligned(p.rot_cos, p.rot_cb, p.rot_ct) || !aligned(p.rot_sin, p.rot_sb, p.rot_st)) return kNotEligible;
     if ((p.rot_cb > 0) != (p.rot_sb > 0)) return kNotEligible;  // both tables per sequence, or both shared
-    const int status = use_prepared(p) ? launch_prepared<true>(p, stream) : kNotEligible;
+    const int status = workspace != nullptr && use_prepared(p) ? launch_prepared<true>(p, workspace, stream) : kNotEligible;
     return status != kNotEligible ? status : launch<32, false, 32, true>(p, stream);
 }
 
@@ -1737,10 +1723,10 @@ unsigned int read_device_status(bool clear) {
     return value;
 }
 
-const char *kernel_name(const AttentionParams &p, int head_width) {
+const char *kernel_name(const AttentionParams &p, int head_width, bool workspace) {
     if (head_width == 64) return "tcgen05-f16x2-flash-d64";
     if (head_width == 16) return "tcgen05-f16x2-flash-d16";
-    return use_prepared(p) ? "tcgen05-f16x2-flash-d32-prepared" : "tcgen05-f16x2-flash-d32";
+    return workspace && use_prepared(p) ? "tcgen05-f16x2-flash-d32-prepared" : "tcgen05-f16x2-flash-d32";
 }
 
 #ifdef RK_WAIT_TEST

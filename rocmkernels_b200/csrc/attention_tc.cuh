@@ -14,17 +14,18 @@ constexpr int kNotEligible = -1;
 // addressable Q rows).
 bool flash_supported(const AttentionParams &p);
 // Launches the tensor-core flash forward for head width 32 or 64 (16: the 32-wide kernel over
-// zero-filled features 16-31); returns a cudaError_t value or kNotEligible. Head width 32 runs the
-// prepared-operand forward (an operand pre-pass, then the forward) with a workspace of
-// prepared_forward_bytes from the library's scratch pool, or the forward with in-kernel split
-// warps when the pool cannot supply it.
-int launch_flash_forward(const AttentionParams &p, int head_width, cudaStream_t stream);
+// zero-filled features 16-31); returns a cudaError_t value or kNotEligible. Head width 32 with a
+// workspace (prepared_forward_bytes, 128-byte aligned; nullptr for none) runs, where it pays, the
+// prepared-operand forward (an operand pre-pass into the workspace, then the forward), else the
+// forward with in-kernel split warps.
+int launch_flash_forward(const AttentionParams &p, int head_width, void *workspace, cudaStream_t stream);
 // Workspace bytes of the prepared d = 32 forward: a 16 KB stage image and a 16-byte header per
 // 64-key tile of each (batch, head).
 long long prepared_forward_bytes(int batch, int heads, int keys);
 // The flash forward for head width 32 with the rotary prologue (q and k rotated by the tables in
-// p.rot_*, which must be 16-byte aligned with strides of 4 floats); cudaError_t or kNotEligible.
-int launch_flash_forward_rotary(const AttentionParams &p, cudaStream_t stream);
+// p.rot_*, which must be 16-byte aligned with strides of 4 floats), with an optional workspace as
+// launch_flash_forward; cudaError_t or kNotEligible.
+int launch_flash_forward_rotary(const AttentionParams &p, void *workspace, cudaStream_t stream);
 
 // Statistics only ({row max, sum} per query, no V and no output): the split-FP16 flash forward
 // without the P.V products; the row sums are taken in FP32 by the softmax threads. Eligible when
@@ -47,9 +48,10 @@ const char *build_info();
 // Reads (and optionally clears) the device status word set by a failed bounded wait;
 // synchronizes with the device. 0 = no failure recorded.
 unsigned int read_device_status(bool clear);
-// Name of the tensor-core flash kernel that a problem of these sizes runs at this head width (for
-// benchmarks and profiles); "-prepared" marks the d = 32 path of an operand pre-pass and the forward.
-const char *kernel_name(const AttentionParams &p, int head_width);
+// Name of the tensor-core flash kernel that a problem of these sizes runs at this head width, with
+// or without a workspace (for benchmarks and profiles); "-prepared" marks the d = 32 path of an
+// operand pre-pass and the forward.
+const char *kernel_name(const AttentionParams &p, int head_width, bool workspace);
 
 // True when the tensor-core backward accepts the tensors (TMA-addressable q, k, v, dO; 16-byte
 // addressable O and gradients).

@@ -99,16 +99,20 @@ def _shifted(tensors: dict, offsets: dict, element_bytes: dict) -> dict:
 
 
 def run_forward(entry, tensors: dict, plan: list[ShardCall], *, heads: int, queries: int, keys: int, width: int, radius: int,
-                strides: dict, stream=None) -> int:
+                strides: dict, stream=None, workspace=None) -> int:
     """One rank's forward calls: `entry` is a forward entry point of rocmkernels_b200.attention
     (same argument order as attention_fp32_forward_flash); `tensors` holds the full problem's q,
-    k, v, mask, out, lse (torch tensors or device addresses). Returns the first non-zero status."""
+    k, v, mask, out, lse (torch tensors or device addresses). `workspace`
+    (attention_fp32_forward_flash_workspace: a device buffer sized for the largest call of the
+    plan, see forward_workspace_bytes) is passed to every call, which are ordered on `stream`.
+    Returns the first non-zero status."""
+    extra = {} if workspace is None else {"workspace": workspace}
     for call in plan:
         offsets = shard_offsets(call, heads=heads, queries=queries, keys=keys, width=width,
                                 strides={r: strides[r] for r in ("q", "k", "v", "out")})
         p = _shifted(tensors, offsets, {"mask": 1})
         status = entry(p["q"], p["k"], p["v"], p["mask"], p["out"], p["lse"], call.batch, call.heads, queries, keys, radius,
-                       strides["q"], strides["k"], strides["v"], strides["out"], stream)
+                       strides["q"], strides["k"], strides["v"], strides["out"], stream, **extra)
         if status != 0:
             return status
     return 0
@@ -131,6 +135,12 @@ def run_backward(entry, tensors: dict, plan: list[ShardCall], *, heads: int, que
         if status != 0:
             return status
     return 0
+
+
+def forward_workspace_bytes(size_of, plan: list[ShardCall], keys: int) -> int:
+    """Workspace for run_forward with attention_fp32_forward_flash_workspace: `size_of(batch,
+    heads, keys)` (attention_fp32_forward_flash_workspace_size) of the plan's largest call."""
+    return max((size_of(call.batch, call.heads, keys) for call in plan), default=0)
 
 
 def workspace_bytes(size_of, plan: list[ShardCall], queries: int) -> int:

@@ -229,3 +229,33 @@ def test_fused_backward_rejects_null_pointers_and_small_workspace(null_index):
     assert lib.attention_fp32_backward_fused(*pointers, needed, 1, 1, 4, 4, -1, S, S, S, S, S, None) == api.INVALID_VALUE
     # a workspace smaller than the size query asks for: error 1 before any CUDA call
     assert lib.attention_fp32_backward_fused(*[1] * 12, needed - 1, 1, 1, 4, 4, -1, S, S, S, S, S, None) == api.INVALID_VALUE
+
+
+def test_forward_workspace_size():
+    """16,400 bytes per 64-key tile of every (batch, head): the split K and V images (16,384) and
+    a 16-byte stage header; 0 for non-positive sizes."""
+    size = api.attention_fp32_forward_flash_workspace_size
+    for batch, heads, keys in [(1, 1, 1), (2, 3, 64), (2, 3, 65), (8, 3, 1024), (64, 12, 4096)]:
+        assert size(batch, heads, keys) == batch * heads * ((keys + 63) // 64) * 16400
+    assert size(0, 1, 1) == 0 and size(1, -1, 1) == 0 and size(1, 1, 0) == 0
+
+
+@pytest.mark.parametrize("rotary", [False, True], ids=["plain", "rotary"])
+@pytest.mark.parametrize("null_index", range(9))
+def test_forward_workspace_entries_reject_null_pointers_and_small_workspace(null_index, rotary):
+    count = 9 if rotary else 7  # q, k, v, [cos, sin,] mask, output, lse, workspace
+    if null_index >= count:
+        pytest.skip("no such pointer")
+    lib = api.lib()
+    needed = api.attention_fp32_forward_flash_workspace_size(1, 1, 4)
+    pointers = [1] * count
+    pointers[null_index] = None
+    if rotary:
+        call = lambda ptrs, capacity: lib.attention_fp32_forward_flash_rotary_workspace(
+            *ptrs[:8], 1, 1, 4, 4, -1, S, S, S, S, S, S, ptrs[8], capacity, None)
+    else:
+        call = lambda ptrs, capacity: lib.attention_fp32_forward_flash_workspace(
+            *ptrs[:6], 1, 1, 4, 4, -1, S, S, S, S, ptrs[6], capacity, None)
+    assert call(pointers, needed) == api.INVALID_VALUE
+    # a workspace smaller than the size query asks for: error 1 before any CUDA call
+    assert call([1] * count, needed - 1) == api.INVALID_VALUE

@@ -3,7 +3,9 @@ one CTA per SM), 256-query CTAs (two Q tiles sharing each K/V tile) above that, 
 grid of 128-query CTAs fills two per SM -- 128-query CTAs with two threads per query row, two CTAs
 per SM (not with the rotary prologue). The shapes here sit just below and just above the one-wave
 threshold and just above the two-per-SM one, computed from the device's SM count, so every CTA
-form is checked. Entries: attention_fp32_forward_flash (the plain kernel), the fused rotary
+form is checked. Entries: attention_fp32_forward_flash (the plain kernel),
+attention_fp32_forward_flash_workspace (above one wave: the operand pre-pass and the prepared
+kernel in the same three forms; the Python wrapper allocates the workspace), the fused rotary
 forward and attention_generic_forward with 16-wide FP32 heads (the narrow-row instantiation).
 
 Bars: the forward's (attention_cases.py) against the oracle, selection bit-exact on rows without
@@ -58,17 +60,19 @@ def dev(cuda):
     return Device(cuda)
 
 
+@pytest.mark.parametrize("entry", ["attention_fp32_forward_flash", "attention_fp32_forward_flash_workspace"],
+                         ids=["plain", "workspace"])
 @pytest.mark.parametrize("side", SIDES)
 @pytest.mark.parametrize("case", FLASH_CASES, ids=lambda c: "h{}q{}k{}r{}".format(*c))
-def test_flash_forward_either_cta_shape(dev, cuda, side, case):
+def test_flash_forward_either_cta_shape(dev, cuda, side, case, entry):
     H, Q, K, radius = case
     B = batch_for(cuda, side, H, Q)
     q, k, v, _, _ = make_inputs(B, H, Q, K, 32, seed=611 + Q, dist="normal", mask3=False)
     mask = padded_mask(B, K, 613 + Q)
     expected = oracle.attention(q, k, v, mask, None, radius, forward_only=True, threads=oracle.cpu_count())
-    status, out, lse = dev.forward("attention_fp32_forward_flash", q, k, v, mask, radius)
+    status, out, lse = dev.forward(entry, q, k, v, mask, radius)
     assert status == 0
-    assert_forward_close(out, lse, expected, f"B{B} {side}")
+    assert_forward_close(out, lse, expected, f"B{B} {side} {entry}")
     dead = expected["lse"][..., 1] == 0
     assert np.all(lse[..., 0][dead] == -np.inf) and np.all(lse[..., 1][dead] == 0.0)
     assert not np.any(out[dead])

@@ -37,6 +37,7 @@ from oracle import oracle
 from rocmkernels_b200 import attention as api
 
 batch, heads, seq, withheld, cta_rows = (int(x) for x in sys.argv[2:7])
+entry = sys.argv[7]
 library = api.lib()
 withhold = library.rocmkernels_attention_test_withhold_tile
 withhold.argtypes, withhold.restype = [ctypes.c_int], ctypes.c_int
@@ -45,16 +46,22 @@ q, k, v, upstream, mask = make_inputs(batch, heads, seq, seq, 32, dist="normal",
 expected = oracle.attention(q, k, v, mask, None, -1, threads=8, forward_only=True)
 dq, dk, dv, dmask = (torch.from_numpy(x).to(cuda) for x in (q, k, v, mask))
 st = api.Strides(heads * seq * 32, seq * 32, 32)
+workspace = torch.empty(api.attention_fp32_forward_flash_workspace_size(batch, heads, seq), dtype=torch.uint8, device=cuda)
 
 def run():
     out = torch.full((batch, heads, seq, 32), 7.0, device=cuda)
     lse = torch.full((batch, heads, seq, 2), 7.0, device=cuda)
     start = time.perf_counter()
-    status = api.attention_fp32_forward_flash(dq, dk, dv, dmask, out, lse, batch, heads, seq, seq, -1, st, st, st, st)
+    if entry == "workspace":
+        status = api.attention_fp32_forward_flash_workspace(dq, dk, dv, dmask, out, lse, batch, heads, seq, seq, -1, st, st, st, st,
+                                                            workspace=workspace)
+    else:
+        status = api.attention_fp32_forward_flash(dq, dk, dv, dmask, out, lse, batch, heads, seq, seq, -1, st, st, st, st)
     torch.cuda.synchronize(cuda)
     return status, time.perf_counter() - start, out.cpu().numpy(), lse.cpu().numpy()
 
-report = {"kernel": api.flash_kernel_name(batch, heads, seq, seq)}
+name_of = api.flash_workspace_kernel_name if entry == "workspace" else api.flash_kernel_name
+report = {"kernel": name_of(batch, heads, seq, seq)}
 assert api.device_status(clear=True) == 0
 assert withhold(withheld) == 0
 status, seconds, out, lse = run()
@@ -72,18 +79,19 @@ print("REPORT " + json.dumps(report))
 """
 
 
-# (batch, heads, seq, withheld key tile, rows of CTA 0), one case per CTA form of the d = 32
+# (batch, heads, seq, withheld key tile, rows of CTA 0, entry), one case per CTA form of the d = 32
 # forward on a 148-SM B200: one Q tile per CTA (a grid that fits one wave; tile 5 is loaded after
 # the prefetch, when its stage is released), two Q tiles per CTA (200 one-tile CTAs: more than one
-# wave, fewer than two per SM; tile 2 is one of the prefetched stages), and two threads per row
-# (320 one-tile CTAs, two per SM).
-@pytest.mark.parametrize("batch,heads,seq,withheld,cta_rows,kernel", [(1, 1, 512, 5, 128, "tcgen05-f16x2-flash-d32"),
-                                                                      (1, 100, 256, 2, 256, "tcgen05-f16x2-flash-d32"),
-                                                                      (1, 160, 256, 2, 128, "tcgen05-f16x2-flash-d32-prepared")])
-def test_withheld_tile_runs_a_wait_out(cuda, batch, heads, seq, withheld, cta_rows, kernel):
+# wave, fewer than two per SM; tile 2 is one of the prefetched stages), and, through the workspace
+# entry, the prepared kernel with two threads per row (320 one-tile CTAs, two per SM).
+@pytest.mark.parametrize("batch,heads,seq,withheld,cta_rows,entry,kernel",
+                         [(1, 1, 512, 5, 128, "plain", "tcgen05-f16x2-flash-d32"),
+                          (1, 100, 256, 2, 256, "plain", "tcgen05-f16x2-flash-d32"),
+                          (1, 160, 256, 2, 128, "workspace", "tcgen05-f16x2-flash-d32-prepared")])
+def test_withheld_tile_runs_a_wait_out(cuda, batch, heads, seq, withheld, cta_rows, entry, kernel):
     assert WAIT_TEST_LIBRARY.exists(), "build it with `python -m rocmkernels_b200.build --wait-test`"
     env = dict(os.environ, ROCMKERNELS_ATTENTION_LIBRARY=str(WAIT_TEST_LIBRARY))
-    args = [str(REPO), str(batch), str(heads), str(seq), str(withheld), str(cta_rows)]
+    args = [str(REPO), str(batch), str(heads), str(seq), str(withheld), str(cta_rows), entry]
     result = subprocess.run([sys.executable, "-c", _CHILD, *args], capture_output=True, text=True, timeout=300, env=env)
     assert result.returncode == 0, result.stdout[-2000:] + result.stderr[-4000:]
     line = next(l for l in result.stdout.splitlines() if l.startswith("REPORT "))
