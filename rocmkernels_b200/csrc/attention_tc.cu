@@ -91,7 +91,27 @@ __device__ long long g_warp_trace[8][8];
     do {                                                                                                         \
         if (blockIdx.x == 0 && (tile_index) == 30 && (threadIdx.x & 31) == 0) g_warp_trace[threadIdx.x >> 5][(event)] = clock64(); \
     } while (0)
+// per CTA (thread 0): events 0 entry, 1 set-up barrier passed, 2 results written (before the
+// final barrier), 3 exit; 4 the SM; globaltimer nanoseconds, so CTAs on different SMs compare.
+constexpr int kTraceCtas = 1024;
+__device__ unsigned long long g_cta_trace[kTraceCtas][5];
+#define RK_CTA_TRACE(event)                                                            \
+    do {                                                                               \
+        if (threadIdx.x == 0 && blockIdx.x < kTraceCtas) {                             \
+            unsigned long long now;                                                    \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));                    \
+            g_cta_trace[blockIdx.x][(event)] = now;                                    \
+            if ((event) == 0) {                                                        \
+                unsigned sm;                                                           \
+                asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));                        \
+                g_cta_trace[blockIdx.x][4] = sm;                                       \
+            }                                                                          \
+        }                                                                              \
+    } while (0)
 #else
+#define RK_CTA_TRACE(event) \
+    do {                   \
+    } while (0)
 #define RK_WARP_TRACE(tile_index, event) \
     do {                                \
     } while (0)
@@ -554,6 +574,7 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles, kPrepared, kRowThrea
     const AttentionParams &p = args.p;
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    RK_CTA_TRACE(0);
 
     int block = blockIdx.x;
     const int cta_tile = block % args.cta_per_head;
@@ -673,6 +694,7 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles, kPrepared, kRowThrea
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    RK_CTA_TRACE(1);
     const uint32_t tmem = s.tmem_base;
     // The window's tiles up to its last visible key (published by the producer warp).
     const auto visible_tiles = [&]() { return mbar_wait(&s.range_ready, 0) ? s.tile_count : 0; };
@@ -1306,12 +1328,14 @@ __global__ void __launch_bounds__(Forward<D, kHalf, kTiles, kPrepared, kRowThrea
         }
     }
 
+    RK_CTA_TRACE(2);
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
         tmem_dealloc(tmem, F::kTmemColumns);
     }
+    RK_CTA_TRACE(3);
 }
 
 // Operand pre-pass of the prepared d = 32 forward: one CTA of 256 threads per 64-key tile of one
@@ -1743,6 +1767,14 @@ extern "C" __attribute__((visibility("default"))) int rocmkernels_attention_trac
     if (capacity < count) return -1;
     if (cudaMemcpyFromSymbol(out, g_trace, sizeof(long long) * count) != cudaSuccess) return -2;
     if (capacity >= count + 64 && cudaMemcpyFromSymbol(out + count, g_warp_trace, sizeof(long long) * 64) != cudaSuccess) return -3;
+    return count;
+}
+
+// Per-CTA globaltimer stamps (kTraceCtas x 5: entry, set-up done, results written, exit, SM).
+extern "C" __attribute__((visibility("default"))) int rocmkernels_attention_cta_trace(unsigned long long *out, int capacity) {
+    const int count = kTraceCtas * 5;
+    if (capacity < count) return -1;
+    if (cudaMemcpyFromSymbol(out, g_cta_trace, sizeof(unsigned long long) * count) != cudaSuccess) return -2;
     return count;
 }
 #endif
