@@ -1603,17 +1603,16 @@ int launch_tiles(const AttentionParams &p, cudaStream_t stream) {
 // B8 H3 S1024 (192 one-tile CTAs, two waves) 35.8 -> 56.3, so two tiles stay there.
 template <int D, bool kHalf, int kWidth = D, bool kRotary = false, bool kStats = false>
 int launch(const AttentionParams &p, cudaStream_t stream) {
-    if constexpr (Forward<D, kHalf>::kQTiles == 2) {
-        int device = 0, sms = 0;
-        cudaError_t status = cudaGetDevice(&device);
-        if (status == cudaSuccess) status = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-        if (status != cudaSuccess) return status;
-        const long long one_tile_ctas = static_cast<long long>((p.queries + kQTile - 1) / kQTile) * p.heads * p.batch;
-        // One-wave one-tile grids are launched chained (kChained): measured on B200, B2 H8 S512
-        // back to back 16.4 -> 15.7 us. Two-tile grids are not: their CTAs then start on the SMs
-        // the grid ahead left free and ran their tiles ~6 % slower (B8 H3 S1024 31.1 -> 33.4 us).
-        if (one_tile_ctas <= sms) return launch_tiles<D, kHalf, kWidth, kRotary, 1, kStats, true>(p, stream);
-    }
+    int device = 0, sms = 0;
+    cudaError_t status = cudaGetDevice(&device);
+    if (status == cudaSuccess) status = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    if (status != cudaSuccess) return status;
+    const long long one_tile_ctas = static_cast<long long>((p.queries + kQTile - 1) / kQTile) * p.heads * p.batch;
+    // One-wave one-tile grids (every storage mode and width) are launched chained (kChained):
+    // measured on B200, B2 H8 S512 d = 32 back to back 16.4 -> 15.6 us. Two-tile and multi-wave
+    // grids are not: two-tile CTAs then start on the SMs the grid ahead left free and ran their
+    // tiles ~6 % slower (B8 H3 S1024 31.1 -> 33.4 us).
+    if (one_tile_ctas <= sms) return launch_tiles<D, kHalf, kWidth, kRotary, 1, kStats, true>(p, stream);
     return launch_tiles<D, kHalf, kWidth, kRotary, Forward<D, kHalf>::kQTiles, kStats>(p, stream);
 }
 
