@@ -6,8 +6,9 @@ runs, and they touch global memory only after it has completed. Checked here wit
 forwards on one stream, each one's output the next one's Q (read after write), written back into
 the buffer the call before read (write after read), with torch kernels between some calls; the
 chain is run once without any synchronisation and once with a synchronise after every call, and
-the two must agree bit for bit. Shapes: 32-wide split FP32, 64-wide, and the 16-wide FP16 generic
-forward, all one-wave grids on a 148-SM B200 (the kernel-name query shows the form).
+the two must agree bit for bit. The same chain captured in a CUDA graph (where the launches become
+programmatic edges) replays to the same bits. Shapes: 32-wide split FP32, 64-wide, and the 16-wide
+FP16 generic forward, all one-wave grids on a 148-SM B200.
 """
 from __future__ import annotations
 
@@ -26,7 +27,7 @@ def api():
     return attention
 
 
-def run_chain(cuda, width, start, k, v, mask, steps, synchronise):
+def run_chain(cuda, width, start, k, v, mask, steps, synchronise, torch_ops=True):
     a = api()
     batch, heads, seq, _ = start.shape
     buffers = [start.clone(), torch.empty_like(start)]
@@ -36,7 +37,7 @@ def run_chain(cuda, width, start, k, v, mask, steps, synchronise):
     for i in range(steps):
         q, out = buffers[i % 2], buffers[(i + 1) % 2]
         assert entry(q, k, v, mask, out, lse, batch, heads, seq, seq, -1, st, st, st, st) == 0
-        if i % 3 == 2:
+        if torch_ops and i % 3 == 2:
             out.mul_(1.5)  # a torch kernel (not a programmatic dependent) between two forwards
         if synchronise:
             torch.cuda.synchronize(cuda)
@@ -82,4 +83,39 @@ def test_generic_fp16_chain_keeps_stream_order(cuda):
     ordered, ordered_lse = chain(True)
     assert torch.equal(chained.view(torch.int16), ordered.view(torch.int16))
     assert torch.equal(chained_lse.view(torch.int32), ordered_lse.view(torch.int32))
+    assert a.device_status(clear=True) == 0
+
+
+def test_chained_forwards_in_a_graph(cuda):
+    """A chain of one-wave forwards captured in a CUDA graph (the launches become programmatic
+    edges) replays to the bits of the same chain run eagerly with a synchronise after every call."""
+    a = api()
+    batch, heads, seq, width = 2, 8, 512, 32
+    gen = torch.Generator(device="cpu").manual_seed(921)
+    q, k, v = (torch.randn(batch, heads, seq, width, generator=gen).to(cuda) for _ in range(3))
+    mask = torch.ones(batch, seq, dtype=torch.uint8, device=cuda)
+    st = a.strides_of(q)
+    buffers = [q.clone(), torch.empty_like(q)]
+    lse = torch.empty(batch, heads, seq, 2, device=cuda)
+
+    def chain(stream):
+        for i in range(6):
+            src, dst = buffers[i % 2], buffers[(i + 1) % 2]
+            assert a.attention_fp32_forward_flash(src, k, v, mask, dst, lse, batch, heads, seq, seq, -1, st, st, st, st, stream) == 0
+
+    side = torch.cuda.Stream(cuda)
+    with torch.cuda.stream(side):
+        chain(side)  # kernel attributes are set outside the capture
+        side.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            chain(torch.cuda.current_stream(cuda))
+    buffers[0].copy_(q)
+    graph.replay()
+    torch.cuda.synchronize(cuda)
+    replayed, replayed_lse = buffers[0].clone(), lse.clone()
+    expected, expected_lse = run_chain(cuda, width, q, k, v, mask, 6, synchronise=True, torch_ops=False)
+    assert torch.equal(replayed.view(torch.int32), expected.view(torch.int32))
+    assert torch.equal(replayed_lse.view(torch.int32), expected_lse.view(torch.int32))
+    del graph
     assert a.device_status(clear=True) == 0
