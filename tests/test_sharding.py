@@ -139,3 +139,34 @@ def test_two_gloo_ranks_reassemble_the_single_process_result():
     assert all(proc.exitcode == 0 for proc in procs)
     assert queue.get(timeout=5) is True
     assert queue.get(timeout=5) is True
+
+
+@pytest.mark.parametrize("batch,heads,world,rank", [(64, 12, 8, 3), (8, 3, 2, 1), (3, 1, 8, 2)])
+def test_forward_workspace_covers_every_call(batch, heads, world, rank):
+    from rocmkernels_b200 import attention as api
+    from rocmkernels_b200.sharding import forward_workspace_bytes
+
+    plan = shard_plan(batch, heads, world, rank)
+    size = api.attention_fp32_forward_flash_workspace_size
+    need = forward_workspace_bytes(size, plan, 4096)
+    assert need == max((size(c.batch, c.heads, 4096) for c in plan), default=0)
+    assert all(size(c.batch, c.heads, 4096) <= need for c in plan)
+
+
+@pytest.mark.parametrize("workspace", [None, 0x7000])
+def test_run_forward_hands_the_workspace_to_every_call(workspace):
+    from rocmkernels_b200.sharding import run_forward
+
+    calls = []
+
+    def entry(*args, **kwargs):
+        calls.append(kwargs)
+        return 0
+
+    plan = shard_plan(8, 3, 2, 0)
+    tensors = {name: 0x100000 for name in ("q", "k", "v", "mask", "out", "lse")}
+    strides = {name: (3 * 1024 * 32, 1024 * 32, 32) for name in ("q", "k", "v", "out")}
+    status = run_forward(entry, tensors, plan, heads=3, queries=1024, keys=1024, width=32, radius=-1, strides=strides,
+                         workspace=workspace)
+    assert status == 0 and len(calls) == len(plan)
+    assert all(c == ({} if workspace is None else {"workspace": workspace}) for c in calls)
